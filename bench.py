@@ -1,0 +1,431 @@
+#!/usr/bin/env python
+"""Decode and prefill throughput of the SLM.use token loop on B200.
+
+Workload ("C2"): the 86M-class looped hybrid
+(d 768, 12 heads × 64, FFN 3072, vocab 32000, window 4096, layout S | LS | S,
+fp32, N(0, 0.02) random init, seed 0) at R = 4 loops.  A 4096-id uniform
+random prompt is read in 256-token chunks, so every sliding-window ring is
+full; then greedy decode.  One bench step = one decoded token (one m = 1
+advance through prelude, R loops of the core and coda, tied logits, and the
+on-device pick).
+
+Printed on one JSON line (rank 0):
+  value     decode tok/s over all ranks, inputs resident on the device
+            (`slm_decode`: ids stay on the GPU), CUDA events on the library's
+            stream, max over ranks;
+  e2e       the same decode through the per-token C ABI (`slm_step` with a
+            host id + `slm_sample` returning a host id), host clock;
+  prefill   tok/s of the 4096-token prompt (feed + logits read back);
+  extra     R = 8 and R = 16 decode with the sampling of configs[2];
+  roofline  the dominant decode kernel (GEMV) against measured HBM bandwidth;
+  cpu_baseline  the CPU oracle (a C++ restatement of the reference's CPU
+            backend) on a bounded sample, rank 0 only, N = 1 only.
+
+--impl reference runs only the CPU oracle on the host cores (rank 0), since
+the reference itself (Rust) cannot be built on this image.
+
+Multi-GPU (torchrun): each rank decodes its own sequence on its own GPU, no
+collective on the data path ("weak" scaling); NCCL only for the barrier and
+the max-over-ranks of the timed region.
+"""
+from __future__ import annotations
+
+import argparse
+import hashlib
+import importlib.util
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+MODEL_BYTES_NOTE = "inputs larger than L2: 640 MB of weights and KV read per token at R=4"
+
+
+def load_pkg():
+    if "slm_b200" in sys.modules:
+        return sys.modules["slm_b200"]
+    pkg = ROOT / "slm.use_b200"
+    spec = importlib.util.spec_from_file_location("slm_b200", pkg / "__init__.py",
+                                                  submodule_search_locations=[str(pkg)])
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules["slm_b200"] = mod
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def model_dir(cfg: dict, seed: int) -> Path:
+    import slm_b200.synthetic as syn  # noqa: F401  (package registered by load_pkg)
+    tag = hashlib.sha1(json.dumps([cfg, seed], sort_keys=True).encode()).hexdigest()[:12]
+    folder = Path(os.environ.get("SLM_BENCH_DIR", "/tmp/slm_b200_bench")) / tag
+    if not (folder / "done").exists():
+        syn.write_model(folder, cfg, seed)
+        (folder / "done").write_text("ok")
+    return folder
+
+
+# ---------------------------------------------------------------------------
+# Algorithmic bytes per decoded token (fp32), full window
+# ---------------------------------------------------------------------------
+
+def decode_bytes(cfg: dict, loops: int) -> dict:
+    d, h, f, v, w = cfg["d_model"], cfg["n_heads"], cfg["hidden"], cfg["vocab_size"], cfg["window"]
+    dh = d // h
+    s_par = 3 * d * d + d * d + 2 * f * d + f * d + 2 * d
+    l_par = 4 * d * d + h * d + d * d + 2 * f * d + f * d + 2 * d + h + dh
+    n_s = cfg["prelude"].count("S") + cfg["coda"].count("S") + loops * cfg["core"].count("S")
+    n_l = loops * cfg["core"].count("L")
+    weights = 4 * (cfg["prelude"].count("S") * s_par + cfg["coda"].count("S") * s_par
+                   + loops * (cfg["core"].count("S") * s_par + cfg["core"].count("L") * l_par)
+                   + d * d + v * d + d)
+    kv = n_s * 2 * h * w * dh * 4
+    gla = n_l * 2 * h * dh * dh * 4
+    return {"weights": weights, "kv": kv, "gla_state": gla, "total": weights + kv + gla}
+
+
+# ---------------------------------------------------------------------------
+# Clocks during the timed region
+# ---------------------------------------------------------------------------
+
+class Clocks:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: int):
+        self.device = device
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "100",
+                 "-i", str(self.device)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        self.lines = []
+        if self.proc:
+            time.sleep(0.2)
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [l for l in out.splitlines() if l.strip()]
+        return False
+
+    def summary(self) -> dict:
+        sm, mx, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in getattr(self, "lines", []):
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = max(mx, float(parts[2]))
+            except ValueError:
+                continue
+            for name, val in zip(names, parts[5:9]):
+                if val.lower().startswith("active"):
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx or None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------
+# CPU oracle (the reference's CPU path restated) — baseline only
+# ---------------------------------------------------------------------------
+
+def cpu_measure(folder: Path, loops: int, steps: int, warmup: int, budget_s: float) -> dict:
+    sys.path.insert(0, str(ROOT))
+    from oracle import oracle as O
+
+    cores = O.lib().orc_threads(os.cpu_count() or 1)
+    model = O.Model(folder)
+    se = model.session(loops)
+    se.fill(4096, seed=0)
+    tok = 1
+    for _ in range(warmup):
+        se.step(tok)
+        tok = int(np.argmax(se.logits()))
+    done, t0 = 0, time.perf_counter()
+    while done < steps:
+        se.step(tok)
+        tok = int(np.argmax(se.logits()))
+        done += 1
+        if time.perf_counter() - t0 > budget_s:
+            break
+    dec_s = time.perf_counter() - t0
+    # One 256-token prompt chunk whose queries all see a full window.
+    pre = model.session(loops)
+    pre.fill(3840, seed=1)
+    ids = np.random.default_rng(0).integers(0, model.cfg["vocab_size"], 256)
+    t1 = time.perf_counter()
+    pre.feed(ids, 256)
+    pre.logits()
+    pre_s = time.perf_counter() - t1
+    return {"decode_tok_s": done / dec_s, "decode_steps": done, "prefill_tok_s": 256 / pre_s, "cores": cores,
+            "sample": f"{done} greedy decode steps at position 4096 (full window, R={loops}) from a seeded "
+                      f"filled state; prefill: one 256-token chunk at positions 3840-4095"}
+
+
+# ---------------------------------------------------------------------------
+# The B200 arm
+# ---------------------------------------------------------------------------
+
+def run_b200(args, rank: int, world: int, local: int) -> dict | None:
+    import torch
+    import torch.distributed as dist
+
+    slm = load_pkg()
+    syn = __import__("slm_b200.synthetic").synthetic
+    cfg = syn.BASE
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    if local == 0:
+        folder = model_dir(cfg, 0)
+    if world > 1:
+        dist.barrier()
+    folder = model_dir(cfg, 0)
+
+    ctx = slm.Context(local)
+    model = slm.Model(ctx, folder)
+    stream = torch.cuda.ExternalStream(ctx.stream, device=dev)
+    V = cfg["vocab_size"]
+    greedy = slm.Sampling()
+    rng = np.random.default_rng(rank)
+    prompt = rng.integers(0, V, args.prompt).astype(np.uint32)
+
+    def events():
+        return torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+
+    # Warm-up: load modules, capture the step graph once.
+    w = model.session(args.loops)
+    w.feed(prompt[:512])
+    w.decode(w.sample(greedy), 8, greedy)
+    w.close()
+
+    se = model.session(args.loops)
+    clocks = Clocks(local)
+    with clocks:
+        # Prefill (feed + logits read, src/main.rs:200-205).
+        a, b = events()
+        torch.cuda.synchronize(dev)
+        t0 = time.perf_counter()
+        a.record(stream)
+        se.feed(prompt, 256)
+        logits = se.logits()
+        b.record(stream)
+        torch.cuda.synchronize(dev)
+        prefill_host_s = time.perf_counter() - t0
+        prefill_ms = a.elapsed_time(b)
+        tok = int(np.argmax(logits))
+
+        # Decode, device-resident ids.
+        se.decode(tok, args.warmup, greedy)
+        tok = int(se.sample(greedy))
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+        a, b = events()
+        a.record(stream)
+        out = se.decode(tok, args.steps, greedy)
+        b.record(stream)
+        torch.cuda.synchronize(dev)
+        if world > 1:
+            dist.barrier()
+        dec_ms = a.elapsed_time(b)
+
+        # End to end through the per-token C ABI with host ids.
+        tok = int(out[-1])
+        for _ in range(min(args.warmup, 4)):
+            se.step(tok)
+            tok = se.sample(greedy)
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            se.step(tok)
+            tok = se.sample(greedy)
+        e2e_s = time.perf_counter() - t0
+        torch.cuda.synchronize(dev)
+
+        # Dominant kernel: the m = 1 GEMV on a 32000 × 768 matrix (the tied
+        # logits head, the largest decode weight); four copies rotate so each
+        # launch streams its matrix from HBM, not L2.
+        ops = slm.Ops(ctx)
+        mats = [ops.upload(np.random.default_rng(9 + i).standard_normal(V * cfg["d_model"], dtype=np.float32))
+                for i in range(4)]
+        xv = ops.upload(np.ones(cfg["d_model"], dtype=np.float32))
+        yv = ops.zeros(V)
+        for i in range(8):
+            ops.linear(yv, mats[i % 4], V, cfg["d_model"], xv, 1)
+        reps = 40
+        a, b = events()
+        a.record(stream)
+        for i in range(reps):
+            ops.linear(yv, mats[i % 4], V, cfg["d_model"], xv, 1)
+        b.record(stream)
+        torch.cuda.synchronize(dev)
+        gemv_us = a.elapsed_time(b) * 1000.0 / reps
+        for mbuf in mats:
+            mbuf.close()
+
+    extra = {}
+    if not args.quick:
+        c3 = slm.Sampling(temperature=0.8, top_k=40, repeat_penalty=1.1, repeat_window=256)
+        for loops in (8, 16):
+            s2 = model.session(loops)
+            torch.cuda.synchronize(dev)
+            a, b = events()
+            a.record(stream)
+            s2.feed(prompt, 256)
+            lg = s2.logits()
+            b.record(stream)
+            torch.cuda.synchronize(dev)
+            pre_ms = a.elapsed_time(b)
+            st = [slm.rng_seed(0)]
+            hist = list(prompt[-256:])
+            first = s2.sample(c3, hist, st)
+            hist.append(first)
+            s2.decode(first, 8, c3, hist, st)
+            n2 = min(args.steps, 256)
+            a, b = events()
+            a.record(stream)
+            s2.decode(first, n2, c3, hist, st)
+            b.record(stream)
+            torch.cuda.synchronize(dev)
+            extra[f"R{loops}"] = {"decode_tok_s": n2 / (a.elapsed_time(b) / 1000.0),
+                                  "prefill_tok_s": len(prompt) / (pre_ms / 1000.0), "decode_steps": n2,
+                                  "sampling": "T=0.8 top-k 40 repeat-penalty 1.1 (window 256) seed 0"}
+            s2.close()
+
+    step_kernels = se.step_kernels
+    res = {"dec_ms": dec_ms, "e2e_s": e2e_s, "prefill_ms": prefill_ms, "prefill_host_s": prefill_host_s,
+           "gemv_us": gemv_us, "clocks": clocks.summary(), "extra": extra, "step_kernels": step_kernels,
+           "device": ctx.name, "state_bytes": se.state_bytes()}
+    if world > 1:
+        t = torch.tensor([dec_ms, e2e_s, prefill_ms], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        res["dec_ms"], res["e2e_s"], res["prefill_ms"] = t.tolist()
+    se.close()
+    model.close()
+    ctx.close()
+    return res
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=1024)
+    ap.add_argument("--warmup", type=int, default=8)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--loops", type=int, default=4)
+    ap.add_argument("--prompt", type=int, default=4096)
+    ap.add_argument("--quick", action="store_true", help="skip the R=8/16 lines")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    load_pkg()
+    syn = __import__("slm_b200.synthetic").synthetic
+    cfg = syn.BASE
+    byts = decode_bytes(cfg, args.loops)
+    workload = (f"C2 decode: 86M-class S|LS|S (d768, 12x64, FFN 3072, V32000, window 4096) fp32, R={args.loops}, "
+                f"{args.prompt}-id prompt in 256-chunks then greedy decode at a full window")
+    config = {"workload": workload, "model": "86M-class looped hybrid (synthetic)", "loops": args.loops,
+              "prompt": args.prompt, "global_batch": world, "seq_len": args.prompt,
+              "parallelism": f"independent sequences, 1 per GPU x{world}", "l2": MODEL_BYTES_NOTE}
+
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        folder = model_dir(cfg, 0)
+        c = cpu_measure(folder, args.loops, args.steps, args.warmup, budget_s=120.0)
+        line = {"metric": f"decode tok/s, R={args.loops}, 4096 ctx full", "value": c["decode_tok_s"],
+                "unit": "tok/s", "n_gpus": world, "steps": c["decode_steps"], "warmup": args.warmup,
+                "ms_per_step": 1000.0 / c["decode_tok_s"], "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "f32", "data": "synthetic (N(0,0.02) init, seed 0)",
+                "config": config, "impl": "reference",
+                "cpu_baseline": {"value": c["decode_tok_s"], "unit": "tok/s", "cores": c["cores"], "kind": "port",
+                                 "sample": c["sample"]},
+                "e2e": {"value": c["decode_tok_s"], "unit": "tok/s", "h2d_bytes_per_step": 0,
+                        "d2h_bytes_per_step": 0},
+                "prefill": {"value": c["prefill_tok_s"], "unit": "tok/s"},
+                "note": "the reference (Rust) has no toolchain here; this arm runs the C++ restatement of its "
+                        "CPU backend (oracle/slm_oracle.cpp) on all host cores"}
+        print(json.dumps(line), flush=True)
+        return
+
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+
+    if world > 1:
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
+    res = run_b200(args, rank, world, local)
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        cpu = cpu_measure(model_dir(cfg, 0), args.loops, 64, 2, budget_s=20.0)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+
+    peaks = {}
+    try:
+        peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text())
+    except (OSError, ValueError):
+        pass
+    hbm = peaks.get("hbm_gbs") or 6650.0
+    peak_src = "measured" if peaks.get("hbm_gbs") else "fallback"
+    K = args.steps
+    value = world * K / (res["dec_ms"] / 1000.0)
+    gemv_bytes = (cfg["vocab_size"] * cfg["d_model"] + cfg["d_model"] + cfg["vocab_size"]) * 4
+    gemv_gbs = gemv_bytes / (res["gemv_us"] * 1e-6) / 1e9
+    step_gbs = byts["total"] / (res["dec_ms"] / 1000.0 / K) / 1e9
+    line = {
+        "metric": f"decode tok/s, R={args.loops}, 4096 ctx full", "value": value, "unit": "tok/s",
+        "n_gpus": world, "steps": K, "warmup": args.warmup, "ms_per_step": res["dec_ms"] / K,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (N(0,0.02) random init, uniform random ids, seed 0 / rank)", "config": config,
+        "e2e": {"value": world * K / res["e2e_s"], "unit": "tok/s", "h2d_bytes_per_step": 12,
+                "d2h_bytes_per_step": 16,
+                "how": "per token slm_step(host id) + slm_sample -> host id, host clock"},
+        "prefill": {"value": world * args.prompt / (res["prefill_ms"] / 1000.0), "unit": "tok/s",
+                    "e2e_value": world * args.prompt / res["prefill_host_s"], "prompt": args.prompt},
+        "roofline": {"bound": "hbm", "kernel": "k_gemv<1,STORE> (32000x768 fp32, m=1)",
+                     "achieved": gemv_gbs, "peak": hbm, "unit": "GB/s", "frac": gemv_gbs / hbm,
+                     "traffic": None, "peak_source": peak_src,
+                     "step": {"bytes_per_token": byts["total"], "achieved": step_gbs, "frac": step_gbs / hbm}},
+        "clocks": res["clocks"],
+        "gpu_launches": K * (res["step_kernels"] + 1),
+        "extra": res["extra"],
+        "device": res["device"],
+        "state_mib": res["state_bytes"] / 2**20,
+    }
+    if cpu:
+        line["cpu_baseline"] = {"value": cpu["decode_tok_s"], "unit": "tok/s", "cores": cpu["cores"], "kind": "port",
+                                "sample": cpu["sample"], "prefill_tok_s": cpu["prefill_tok_s"]}
+    print(json.dumps(line), flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,223 @@
+/*
+ * slm_b200.h — C ABI of the B200 (sm_100a) backend for the SLM.use token loop.
+ *
+ * Two levels, both plain C: opaque handles, pointers and sizes, an int status
+ * on every call (0 = ok; the message of the last failure on this thread comes
+ * from slm_last_error()).  Nothing here throws or aborts.
+ *
+ * 1. Op level: one entry point per method of the reference's `Ops` trait
+ *    (reference src/ops.rs:68-228), on device buffers (`slm_buf`).  A buffer
+ *    stands for `Ops::Buf`; an (slm_buf*, offset) pair stands for `At`
+ *    (src/ops.rs:13-29).  Output buffers that are too small are reallocated,
+ *    as the reference CUDA backend's `ensure` does (src/cuda.rs:122-127).
+ *    Calls are asynchronous on the context's stream; slm_read synchronises
+ *    (src/cuda.rs:160-165).
+ *
+ * 2. Model level: what the reference's `Model`/`Session` offer
+ *    (src/model.rs:225-690) — load, session, feed, step, logits,
+ *    state_bytes — plus on-device sampling (src/sample.rs:33-93) and an
+ *    n-token decode that keeps every id on the device.  This level runs the
+ *    fused sm_100a kernels and captures the m = 1 token step in a CUDA graph.
+ *
+ * Threading: a context owns one device and one stream; use a context from one
+ * host thread at a time (the reference pins its model to one thread,
+ * src/serve.rs:1-3).  Sessions of one model may live on different contexts.
+ */
+#ifndef SLM_B200_H
+#define SLM_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes. */
+#define SLM_OK 0
+#define SLM_ERR_INVALID 1  /* bad argument or shape */
+#define SLM_ERR_CUDA 2     /* a CUDA call failed */
+#define SLM_ERR_IO 3       /* a model file could not be read or parsed */
+#define SLM_ERR_NOMEM 4    /* device allocation failed */
+#define SLM_ERR_DEVICE 5   /* a kernel reported an error word (bounded wait expired, bad id) */
+
+typedef struct slm_ctx slm_ctx;
+typedef struct slm_buf slm_buf;
+typedef struct slm_model slm_model;
+typedef struct slm_session slm_session;
+
+/* Message of the last failed call on this thread ("" if none). */
+const char* slm_last_error(void);
+/* Library version string. */
+const char* slm_version(void);
+
+/* ---------------------------------------------------------------------- */
+/* Context (replaces Cuda::probe, reference src/cuda.rs:71-120).           */
+/* ---------------------------------------------------------------------- */
+
+/* Number of visible CUDA devices (0 when there is no driver or GPU). */
+int slm_device_count(int* out);
+/* Binds `device`, creates a stream.  Fails with SLM_ERR_CUDA when the device
+ * is not an sm_100 part or cannot be opened. */
+int slm_ctx_new(int device, slm_ctx** out);
+int slm_ctx_free(slm_ctx* ctx);
+/* Device name, as Ops::name (src/ops.rs:71, src/cuda.rs:145-150). */
+int slm_ctx_name(slm_ctx* ctx, char* out, size_t cap);
+/* Waits for all work on the context's stream. */
+int slm_ctx_sync(slm_ctx* ctx);
+/* The context's cudaStream_t (as void*), for callers that time or order work
+ * around the library's launches. */
+int slm_ctx_stream(slm_ctx* ctx, void** out);
+
+/* ---------------------------------------------------------------------- */
+/* Buffers: Ops::zeros / upload / read / flush (src/ops.rs:72-91).         */
+/* ---------------------------------------------------------------------- */
+
+int slm_zeros(slm_ctx* ctx, size_t n, slm_buf** out);
+int slm_upload(slm_ctx* ctx, const float* data, size_t n, slm_buf** out);
+/* Waits for pending work and copies the first n values to `out`. */
+int slm_read(slm_ctx* ctx, const slm_buf* buf, size_t n, float* out);
+int slm_buf_free(slm_buf* buf);
+size_t slm_buf_len(const slm_buf* buf);
+/* Device address of the buffer's first value (valid until it is resized). */
+float* slm_buf_ptr(slm_buf* buf);
+/* Ops::flush: a no-op, kept for the trait's shape (src/cuda.rs:167-169). */
+int slm_flush(slm_ctx* ctx);
+
+/* ---------------------------------------------------------------------- */
+/* Op level: one call per Ops method.  Offsets are in floats.              */
+/* ---------------------------------------------------------------------- */
+
+/* Ops::gather (src/ops.rs:94): y[i] = w[ids[i]], ids on the host. */
+int slm_op_gather(slm_ctx* ctx, slm_buf* y, const slm_buf* w, const uint32_t* ids, size_t m, size_t d);
+/* Ops::copy (src/ops.rs:95). */
+int slm_op_copy(slm_ctx* ctx, slm_buf* y, const slm_buf* x, size_t xoff, size_t n);
+/* Ops::shift (src/ops.rs:97-104): y[0] = first, y[i] = x[i-1]. */
+int slm_op_shift(slm_ctx* ctx, slm_buf* y, const slm_buf* first, const slm_buf* x, size_t xoff,
+                 size_t m, size_t d);
+/* Ops::columns (src/ops.rs:107-115). */
+int slm_op_columns(slm_ctx* ctx, slm_buf* y, const slm_buf* x, size_t m, size_t stride, size_t off,
+                   size_t len);
+/* Ops::linear (src/ops.rs:118-126): y[i] = w·x[i], w rows × cols row-major. */
+int slm_op_linear(slm_ctx* ctx, slm_buf* y, const slm_buf* w, size_t rows, size_t cols,
+                  const slm_buf* x, size_t xoff, size_t m);
+/* Ops::add (src/ops.rs:127). */
+int slm_op_add(slm_ctx* ctx, slm_buf* y, const slm_buf* a, size_t aoff, const slm_buf* b, size_t boff,
+               size_t n);
+/* Ops::add_row (src/ops.rs:129-136). */
+int slm_op_add_row(slm_ctx* ctx, slm_buf* y, const slm_buf* x, size_t xoff, const slm_buf* row,
+                   size_t rowoff, size_t m, size_t d);
+/* Ops::scale_rows (src/ops.rs:138): factors on the host, m = number of factors. */
+int slm_op_scale_rows(slm_ctx* ctx, slm_buf* y, const slm_buf* x, size_t xoff, const float* f, size_t m,
+                      size_t d);
+/* Ops::mix (src/ops.rs:140-147): y = a + t·(b − a). */
+int slm_op_mix(slm_ctx* ctx, slm_buf* y, const slm_buf* a, size_t aoff, const slm_buf* b, size_t boff,
+               size_t n, float t);
+/* Ops::rms (src/ops.rs:150-158). */
+int slm_op_rms(slm_ctx* ctx, slm_buf* y, const slm_buf* x, size_t xoff, const slm_buf* w, size_t groups,
+               size_t size, float eps);
+/* Ops::silu_mul (src/ops.rs:160-166): y = silu(g)·u. */
+int slm_op_silu_mul(slm_ctx* ctx, slm_buf* y, const slm_buf* g, size_t goff, const slm_buf* u,
+                    size_t uoff, size_t n);
+/* Ops::rope_table (src/ops.rs:169-177). */
+int slm_op_rope_table(slm_ctx* ctx, slm_buf* cos_out, slm_buf* sin_out, const slm_buf* inv, size_t pos,
+                      size_t m, size_t half);
+/* Ops::rope (src/ops.rs:179-188). */
+int slm_op_rope(slm_ctx* ctx, slm_buf* y, const slm_buf* x, size_t xoff, const slm_buf* cos_in,
+                const slm_buf* sin_in, size_t m, size_t heads, size_t dh);
+/* Ops::l2norm (src/ops.rs:190). */
+int slm_op_l2norm(slm_ctx* ctx, slm_buf* y, const slm_buf* x, size_t xoff, size_t heads, size_t dh);
+/* Ops::gla (src/ops.rs:191-205). */
+int slm_op_gla(slm_ctx* ctx, slm_buf* y, slm_buf* s, const slm_buf* q, size_t qoff, const slm_buf* k,
+               size_t koff, const slm_buf* v, size_t voff, const slm_buf* decay, const slm_buf* bias,
+               size_t m, size_t heads, size_t dh);
+/* Ops::store (src/ops.rs:207-217). */
+int slm_op_store(slm_ctx* ctx, slm_buf* cache, const slm_buf* src, size_t srcoff, size_t pos, size_t m,
+                 size_t cap, size_t heads, size_t dh);
+
+/* Attn (src/ops.rs:31-46).  reach = SIZE_MAX means unbounded. */
+typedef struct slm_attn {
+  size_t pos, m, reach, gap, cap, heads, key_heads, dh;
+  float scale;
+} slm_attn;
+/* Ops::attend (src/ops.rs:218-227).  `scores` is scratch (resized as needed). */
+int slm_op_attend(slm_ctx* ctx, slm_buf* y, slm_buf* scores, const slm_buf* q, size_t qoff,
+                  const slm_buf* k, const slm_buf* v, const slm_attn* a);
+
+/* ---------------------------------------------------------------------- */
+/* Model level (src/model.rs, src/sample.rs).                              */
+/* ---------------------------------------------------------------------- */
+
+typedef struct slm_model_info {
+  size_t vocab, d_model, heads, head_dim, kv_heads, hidden, window, max_loops, default_loops;
+  size_t params; /* Model::params (src/model.rs:275-302) */
+  char prelude[32], core[32], coda[32];
+} slm_model_info;
+
+/* Model::load (src/model.rs:226-269): `dir` holds config.json and model.safetensors (f32). */
+int slm_model_load(slm_ctx* ctx, const char* dir, slm_model** out);
+int slm_model_free(slm_model* model);
+int slm_model_info_get(const slm_model* model, slm_model_info* out);
+
+/* Model::session (src/model.rs:333-381); loops = 0 takes the default. */
+int slm_session_new(slm_model* model, size_t loops, slm_session** out);
+int slm_session_free(slm_session* se);
+int slm_session_pos(const slm_session* se, size_t* out);
+int slm_session_loops(const slm_session* se, size_t* out);
+/* Model::feed (src/model.rs:658-667): chunks of at most `limit` (≤ 256). */
+int slm_feed(slm_session* se, const uint32_t* ids, size_t n, size_t limit);
+/* Model::step (src/model.rs:643-645). */
+int slm_step(slm_session* se, uint32_t id);
+/* Model::logits (src/model.rs:669-671): copies vocab floats, synchronises. */
+int slm_logits(slm_session* se, float* out);
+/* Model::state_bytes (src/model.rs:674-690). */
+int slm_state_bytes(const slm_session* se, size_t* out);
+
+/* Sampling (src/sample.rs:3-15). */
+typedef struct slm_sampling {
+  float temperature;      /* 0 picks the most likely token */
+  uint32_t top_k;         /* 0 keeps every token */
+  float top_p;            /* 1 keeps them all */
+  float repeat_penalty;   /* 1 disables the penalty */
+  uint32_t repeat_window; /* how many recent tokens the penalty looks at */
+} slm_sampling;
+
+/* xorshift64* seeding, Rng::new (src/sample.rs:21-23). */
+uint64_t slm_rng_seed(uint64_t seed);
+
+/* pick (src/sample.rs:33-93) on the device, from the session's logits.
+ * `recent` (host, n_recent ids) is the history the repeat penalty reads;
+ * `rng_state` is read and advanced.  Candidates after top-k are kept in a
+ * canonical order (logit descending, then id ascending).  Synchronises. */
+int slm_sample(slm_session* se, const slm_sampling* s, const uint32_t* recent, size_t n_recent,
+               uint64_t* rng_state, uint32_t* out_id);
+
+/* pick (src/sample.rs:33-93) on any device logits: `logits` holds at least
+ * `vocab` floats; otherwise as slm_sample.  Synchronises. */
+int slm_pick(slm_ctx* ctx, const slm_buf* logits, size_t vocab, const slm_sampling* s, const uint32_t* recent,
+             size_t n_recent, uint64_t* rng_state, uint32_t* out_id);
+
+/* n decode steps without leaving the device: feeds `first`, then each
+ * sampled id, and writes the n sampled ids to `out` (host).  `recent` seeds
+ * the penalty history; sampled ids join it.  Equivalent to n rounds of
+ * slm_step + slm_sample.  Synchronises once at the end. */
+int slm_decode(slm_session* se, uint32_t first, size_t n, const slm_sampling* s, const uint32_t* recent,
+               size_t n_recent, uint64_t* rng_state, uint32_t* out);
+
+/* Execution switches of a session (for tests and measurement):
+ *   SLM_OPT_GRAPH    1 = replay the m = 1 step as a CUDA graph (default 1) */
+#define SLM_OPT_GRAPH 1
+int slm_session_set(slm_session* se, int option, int64_t value);
+
+/* Counters of a session:
+ *   SLM_STAT_STEP_KERNELS  kernels one m = 1 step launches (graph nodes)
+ *   SLM_STAT_GRAPHS        step graphs captured so far */
+#define SLM_STAT_STEP_KERNELS 1
+#define SLM_STAT_GRAPHS 2
+int slm_session_stat(const slm_session* se, int what, int64_t* out);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SLM_B200_H */

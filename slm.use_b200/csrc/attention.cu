@@ -1,0 +1,351 @@
+// Softmax attention over ring caches (reference Ops::attend, src/ops.rs:218-227;
+// CPU arithmetic src/cpu.rs:352-403; window geometry src/ops.rs:31-66).
+//
+// The query at position p reads cached positions lo..hi-1 with
+// lo = max(0, p - reach + 1) (reach 0 = unbounded) and hi = p + 1 - gap, kept
+// in ring slots p % cap of a [key_head][cap][dh] cache.  A query that sees
+// nothing yields zeros.
+//
+// Scores are never materialised.  Each (query, head) range is cut into
+// `nsplit` contiguous slices; a CTA folds its slice into a running
+// (max, sum, acc[dh]) with online softmax and writes that partial, and
+// k_attn_combine merges the slices.  Two shapes of the slice pass:
+//  * k_attn_split (m ≤ 8, decode): 8-float lane groups walk the slice, one
+//    cache row per group per step, K and V read once with 16-byte loads.
+//  * k_attn_tile (m > 8, prefill chunks): 16 queries share 32-position K/V
+//    tiles staged in shared memory.
+// The position of the first query comes from device memory, so the same
+// launch (and a CUDA graph holding it) serves every decode step.
+#include "common.cuh"
+#include "kernels.cuh"
+
+namespace slm {
+
+namespace {
+
+struct Range {
+  long long lo, hi;
+};
+
+__device__ __forceinline__ Range visible(long long p, long long reach, long long gap) {
+  Range r;
+  r.lo = (reach <= 0 || p < reach - 1) ? 0 : p - (reach - 1);
+  r.hi = p + 1 - gap;
+  if (r.hi < r.lo) r.hi = r.lo;
+  return r;
+}
+
+// Merge two online-softmax partials (m, l, acc) into the first.
+__device__ __forceinline__ void merge(float& m, float& l, float* acc, float om, float ol, const float* oacc, int n) {
+  float M = fmaxf(m, om);
+  float ca = m == -INFINITY ? 0.0f : expf(m - M);
+  float cb = om == -INFINITY ? 0.0f : expf(om - M);
+  l = l * ca + ol * cb;
+  for (int e = 0; e < n; e++) acc[e] = acc[e] * ca + oacc[e] * cb;
+  m = M;
+}
+
+// ---------------------------------------------------------------------------
+// Slice pass for a few queries.  grid (nsplit, heads, m), 128 threads.
+// ---------------------------------------------------------------------------
+template <int DH>
+__global__ void __launch_bounds__(128)
+    k_attn_split(const float* __restrict__ q, int ldq, const float* __restrict__ K, const float* __restrict__ V,
+                 AttnGeom g, const long long* __restrict__ pos_ptr, int nsplit, float* __restrict__ part) {
+  constexpr int G = DH / 8;        // lanes per cache row
+  constexpr int PPW = 32 / G;      // rows per warp step
+  constexpr int WARPS = 4;
+  const int s = blockIdx.x, h = blockIdx.y, i = blockIdx.z;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int sub = lane % G, grp = lane / G;
+  const long long p = pos_ptr[0] + i;
+  Range r = visible(p, g.reach, g.gap);
+  long long count = r.hi - r.lo;
+  long long chunk = (count + nsplit - 1) / nsplit;
+  long long start = r.lo + (long long)s * chunk;
+  long long end = min(r.hi, start + chunk);
+
+  const int kvh = h / (g.heads / g.key_heads);
+  const float* Kb = K + (size_t)kvh * g.cap * DH + sub * 8;
+  const float* Vb = V + (size_t)kvh * g.cap * DH + sub * 8;
+  const float* qp = q + (size_t)i * ldq + (size_t)h * DH + sub * 8;
+  float qv[8];
+  {
+    float4 a = *reinterpret_cast<const float4*>(qp), b = *reinterpret_cast<const float4*>(qp + 4);
+    qv[0] = a.x, qv[1] = a.y, qv[2] = a.z, qv[3] = a.w, qv[4] = b.x, qv[5] = b.y, qv[6] = b.z, qv[7] = b.w;
+  }
+  float mx = -INFINITY, l = 0.0f, acc[8];
+#pragma unroll
+  for (int e = 0; e < 8; e++) acc[e] = 0.0f;
+
+  const long long slot0 = start < end ? start % g.cap : 0;
+  for (long long base = start + warp * PPW; base < end; base += (long long)WARPS * PPW) {
+    long long pp = base + grp;
+    bool ok = pp < end;
+    float sc = 0.0f;
+    float4 v0 = make_float4(0.f, 0.f, 0.f, 0.f), v1 = v0;
+    if (ok) {
+      long long sl = slot0 + (pp - start);
+      if (sl >= g.cap) sl -= g.cap;
+      if (sl >= g.cap) sl %= g.cap;
+      size_t slot = (size_t)sl;
+      const float4* kr = reinterpret_cast<const float4*>(Kb + slot * DH);
+      const float4* vr = reinterpret_cast<const float4*>(Vb + slot * DH);
+      float4 k0 = ld_stream(kr), k1 = ld_stream(kr + 1);
+      v0 = ld_stream(vr);
+      v1 = ld_stream(vr + 1);
+      sc = qv[0] * k0.x + qv[1] * k0.y + qv[2] * k0.z + qv[3] * k0.w + qv[4] * k1.x + qv[5] * k1.y +
+           qv[6] * k1.z + qv[7] * k1.w;
+    }
+#pragma unroll
+    for (int o = 1; o < G; o <<= 1) sc += __shfl_xor_sync(0xffffffffu, sc, o);
+    if (ok) {
+      sc *= g.scale;
+      float M = fmaxf(mx, sc);
+      float corr = mx == -INFINITY ? 0.0f : expf(mx - M);
+      float pe = expf(sc - M);
+      l = l * corr + pe;
+      float vv[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+#pragma unroll
+      for (int e = 0; e < 8; e++) acc[e] = acc[e] * corr + pe * vv[e];
+      mx = M;
+    }
+  }
+  // Merge the lane groups of the warp (they hold the same `sub` slices).
+#pragma unroll
+  for (int o = G; o < 32; o <<= 1) {
+    float om = __shfl_xor_sync(0xffffffffu, mx, o);
+    float ol = __shfl_xor_sync(0xffffffffu, l, o);
+    float oacc[8];
+#pragma unroll
+    for (int e = 0; e < 8; e++) oacc[e] = __shfl_xor_sync(0xffffffffu, acc[e], o);
+    merge(mx, l, acc, om, ol, oacc, 8);
+  }
+  // Merge the warps through shared memory.
+  __shared__ float sm[WARPS][DH + 2];
+  if (grp == 0) {
+#pragma unroll
+    for (int e = 0; e < 8; e++) sm[warp][sub * 8 + e] = acc[e];
+    if (sub == 0) {
+      sm[warp][DH] = mx;
+      sm[warp][DH + 1] = l;
+    }
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < DH; e += blockDim.x) {
+    float m0 = sm[0][DH], l0 = sm[0][DH + 1], a0 = sm[0][e];
+    for (int w = 1; w < WARPS; w++) merge(m0, l0, &a0, sm[w][DH], sm[w][DH + 1], &sm[w][e], 1);
+    float* out = part + (((size_t)s * g.m + i) * g.heads + h) * (DH + 2);
+    out[e] = a0;
+    if (e == 0) {
+      out[DH] = m0;
+      out[DH + 1] = l0;
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Slice pass for query tiles.  grid (nsplit, ceil(m/16), heads), 128 threads;
+// each warp owns 4 queries; 32-position K/V tiles in shared memory.
+// ---------------------------------------------------------------------------
+template <int DH>
+__global__ void __launch_bounds__(128)
+    k_attn_tile(const float* __restrict__ q, int ldq, const float* __restrict__ K, const float* __restrict__ V,
+                AttnGeom g, const long long* __restrict__ pos_ptr, int nsplit, float* __restrict__ part) {
+  constexpr int QT = 16, QW = 4, KT = 32, LD = DH + 1;
+  constexpr int DPL = (DH + 31) / 32;  // output dims per lane
+  __shared__ float Ks[KT][LD], Vs[KT][LD];
+  __shared__ __align__(16) float Qs[4][DH][QW];  // per warp, transposed: [warp][d][query]
+  const int s = blockIdx.x, i0 = blockIdx.y * QT, h = blockIdx.z;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const long long pos = pos_ptr[0];
+  const int kvh = h / (g.heads / g.key_heads);
+  const float* Kb = K + (size_t)kvh * g.cap * DH;
+  const float* Vb = V + (size_t)kvh * g.cap * DH;
+
+  // Union of the tile's ranges (ranges grow with the query position).
+  int ilast = min(i0 + QT, g.m) - 1;
+  Range r0 = visible(pos + i0, g.reach, g.gap), r1 = visible(pos + ilast, g.reach, g.gap);
+  long long ulo = r0.lo, uhi = max(r1.hi, r0.hi);
+  long long count = uhi - ulo;
+  long long chunk = (count + nsplit - 1) / nsplit;
+  long long start = ulo + (long long)s * chunk, end = min(uhi, start + chunk);
+
+  // This warp's queries.
+  long long qlo[QW], qhi[QW];
+  bool qok[QW];
+#pragma unroll
+  for (int j = 0; j < QW; j++) {
+    int i = i0 + warp * QW + j;
+    qok[j] = i < g.m;
+    Range rr = visible(pos + i, g.reach, g.gap);
+    qlo[j] = qok[j] ? rr.lo : 0;
+    qhi[j] = qok[j] ? rr.hi : 0;
+    for (int d = lane; d < DH; d += 32)
+      Qs[warp][d][j] = qok[j] ? q[(size_t)i * ldq + (size_t)h * DH + d] : 0.0f;
+  }
+  float mx[QW], l[QW], acc[QW][DPL];
+#pragma unroll
+  for (int j = 0; j < QW; j++) {
+    mx[j] = -INFINITY;
+    l[j] = 0.0f;
+#pragma unroll
+    for (int t = 0; t < DPL; t++) acc[j][t] = 0.0f;
+  }
+  __syncwarp();
+
+  for (long long t0 = start; t0 < end; t0 += KT) {
+    __syncthreads();
+    // Stage K/V rows t0 .. t0+KT-1 (zeros past `end`).
+    for (int e = threadIdx.x; e < KT * (DH / 4); e += blockDim.x) {
+      int row = e / (DH / 4), c = (e % (DH / 4)) * 4;
+      long long pp = t0 + row;
+      float4 kv = make_float4(0.f, 0.f, 0.f, 0.f), vv = kv;
+      if (pp < end) {
+        size_t slot = (size_t)(pp % g.cap);
+        kv = ld_stream(reinterpret_cast<const float4*>(Kb + slot * DH + c));
+        vv = ld_stream(reinterpret_cast<const float4*>(Vb + slot * DH + c));
+      }
+      Ks[row][c] = kv.x, Ks[row][c + 1] = kv.y, Ks[row][c + 2] = kv.z, Ks[row][c + 3] = kv.w;
+      Vs[row][c] = vv.x, Vs[row][c + 1] = vv.y, Vs[row][c + 2] = vv.z, Vs[row][c + 3] = vv.w;
+    }
+    __syncthreads();
+    // Scores: lane ↔ position t0 + lane.
+    float sc[QW];
+#pragma unroll
+    for (int j = 0; j < QW; j++) sc[j] = 0.0f;
+#pragma unroll 8
+    for (int d = 0; d < DH; d++) {
+      float kd = Ks[lane][d];
+      float4 qd = *reinterpret_cast<const float4*>(&Qs[warp][d][0]);
+      sc[0] = fmaf(qd.x, kd, sc[0]);
+      sc[1] = fmaf(qd.y, kd, sc[1]);
+      sc[2] = fmaf(qd.z, kd, sc[2]);
+      sc[3] = fmaf(qd.w, kd, sc[3]);
+    }
+    long long pp = t0 + lane;
+    float pe[QW];
+#pragma unroll
+    for (int j = 0; j < QW; j++) {
+      bool vis = qok[j] && pp < end && pp >= qlo[j] && pp < qhi[j];
+      float sj = vis ? sc[j] * g.scale : -INFINITY;
+      float tmax = warp_max(sj);
+      if (tmax == -INFINITY) {
+        pe[j] = 0.0f;
+        continue;
+      }
+      float M = fmaxf(mx[j], tmax);
+      float corr = mx[j] == -INFINITY ? 0.0f : expf(mx[j] - M);
+      pe[j] = vis ? expf(sj - M) : 0.0f;
+      l[j] = l[j] * corr + warp_sum(pe[j]);
+#pragma unroll
+      for (int t = 0; t < DPL; t++) acc[j][t] *= corr;
+      mx[j] = M;
+    }
+    // P·V: lane owns output dims lane + 32t.
+    for (int k = 0; k < KT; k++) {
+      float pk[QW];
+#pragma unroll
+      for (int j = 0; j < QW; j++) pk[j] = __shfl_sync(0xffffffffu, pe[j], k);
+#pragma unroll
+      for (int t = 0; t < DPL; t++) {
+        int d = lane + 32 * t;
+        float vd = d < DH ? Vs[k][d] : 0.0f;
+#pragma unroll
+        for (int j = 0; j < QW; j++) acc[j][t] = fmaf(pk[j], vd, acc[j][t]);
+      }
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < QW; j++) {
+    int i = i0 + warp * QW + j;
+    if (i >= g.m) continue;
+    float* out = part + (((size_t)s * g.m + i) * g.heads + h) * (DH + 2);
+#pragma unroll
+    for (int t = 0; t < DPL; t++) {
+      int d = lane + 32 * t;
+      if (d < DH) out[d] = acc[j][t];
+    }
+    if (lane == 0) {
+      out[DH] = mx[j];
+      out[DH + 1] = l[j];
+    }
+  }
+}
+
+// Merge the slices: y[i][h] = Σ_s e^{m_s - M} acc_s / Σ_s e^{m_s - M} l_s.
+// grid m·heads, block 32·ceil(dh/32).
+__global__ void k_attn_combine(const float* __restrict__ part, int nsplit, int m, int heads, int dh,
+                               float* __restrict__ y, int ldy) {
+  int pair = blockIdx.x, i = pair / heads, h = pair % heads, e = threadIdx.x;
+  size_t stride = (size_t)m * heads * (dh + 2);
+  const float* p0 = part + ((size_t)i * heads + h) * (dh + 2);
+  float M = -INFINITY;
+  for (int s = 0; s < nsplit; s++) M = fmaxf(M, p0[s * stride + dh]);
+  float L = 0.0f, a = 0.0f;
+  if (M != -INFINITY) {
+    for (int s = 0; s < nsplit; s++) {
+      const float* ps = p0 + s * stride;
+      float ms = ps[dh];
+      if (ms == -INFINITY) continue;
+      float c = expf(ms - M);
+      L += ps[dh + 1] * c;
+      if (e < dh) a += ps[e] * c;
+    }
+  }
+  if (e < dh) y[(size_t)i * ldy + (size_t)h * dh + e] = L > 0.0f ? a / L : 0.0f;
+}
+
+template <int DH>
+void launch_tile(const float* q, int ldq, const float* K, const float* V, const AttnGeom& g, const long long* pos_ptr,
+                 int nsplit, float* part, cudaStream_t st) {
+  if constexpr (DH <= 128) {
+    k_attn_tile<DH><<<dim3(nsplit, cdiv(g.m, 16), g.heads), 128, 0, st>>>(q, ldq, K, V, g, pos_ptr, nsplit, part);
+    SLM_LAUNCHED("k_attn_tile");
+  }
+}
+
+template <int DH>
+void launch_dh(const float* q, int ldq, const float* K, const float* V, const AttnGeom& g, const long long* pos_ptr,
+               int nsplit, float* part, cudaStream_t st) {
+  if (g.m <= 8 || DH > 128) {
+    k_attn_split<DH><<<dim3(nsplit, g.heads, g.m), 128, 0, st>>>(q, ldq, K, V, g, pos_ptr, nsplit, part);
+    SLM_LAUNCHED("k_attn_split");
+  } else {
+    launch_tile<DH>(q, ldq, K, V, g, pos_ptr, nsplit, part, st);
+  }
+}
+
+}  // namespace
+
+int attn_splits(const AttnGeom& g, long long max_span) {
+  if (max_span < 1) max_span = 1;
+  long long ctas = (g.m <= 8 || g.dh > 128) ? (long long)g.heads * g.m : (long long)g.heads * ((g.m + 15) / 16);
+  long long want = (2 * 148 + ctas - 1) / ctas;             // two CTAs per SM
+  long long most = (max_span + 127) / 128;                 // at least 128 positions per slice
+  long long n = want < most ? want : most;
+  if (n < 1) n = 1;
+  if (n > 256) n = 256;
+  return (int)n;
+}
+
+size_t attn_part_floats(const AttnGeom& g, int nsplit) { return (size_t)nsplit * g.m * g.heads * (g.dh + 2); }
+
+void attention(const float* q, int ldq, const float* K, const float* V, const AttnGeom& g, const long long* pos_ptr,
+               int nsplit, float* part, float* y, int ldy, cudaStream_t st) {
+  if (g.m == 0) return;
+  SLM_REQUIRE(g.key_heads > 0 && g.heads % g.key_heads == 0, "attend: heads must be a multiple of key_heads");
+  switch (g.dh) {
+    case 8: launch_dh<8>(q, ldq, K, V, g, pos_ptr, nsplit, part, st); break;
+    case 16: launch_dh<16>(q, ldq, K, V, g, pos_ptr, nsplit, part, st); break;
+    case 32: launch_dh<32>(q, ldq, K, V, g, pos_ptr, nsplit, part, st); break;
+    case 64: launch_dh<64>(q, ldq, K, V, g, pos_ptr, nsplit, part, st); break;
+    case 128: launch_dh<128>(q, ldq, K, V, g, pos_ptr, nsplit, part, st); break;
+    case 256: launch_dh<256>(q, ldq, K, V, g, pos_ptr, nsplit, part, st); break;
+    default: fail(SLM_ERR_INVALID, "attend: head size must be one of 8, 16, 32, 64, 128, 256");
+  }
+  k_attn_combine<<<g.m * g.heads, 32 * cdiv(g.dh, 32), 0, st>>>(part, nsplit, g.m, g.heads, g.dh, y, ldy);
+  SLM_LAUNCHED("k_attn_combine");
+}
+
+}  // namespace slm

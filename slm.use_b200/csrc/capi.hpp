@@ -1,0 +1,66 @@
+// Internal definitions behind the opaque handles of include/slm_b200.h.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <new>
+#include <string>
+
+#include "../../include/slm_b200.h"
+#include "common.cuh"
+
+struct slm_ctx {
+  int device = 0;
+  int sms = 0;
+  std::string name;
+  cudaStream_t stream = nullptr;
+  int* err = nullptr;           // device error word (bad ids, sampler limits)
+  void* stage = nullptr;        // staging buffer for host arrays (ids, factors)
+  size_t stage_bytes = 0;
+};
+
+struct slm_buf {
+  slm_ctx* ctx;
+  float* ptr;
+  size_t len;
+};
+
+extern "C" int slm_ctx_stream(slm_ctx* c, void** out);
+
+namespace slm {
+
+void set_error(const std::string& s);
+
+// Makes the context's device current for the lifetime of the object.
+struct Device {
+  int prev;
+  explicit Device(slm_ctx* c);
+  ~Device();
+};
+
+void* dev_alloc(size_t bytes);
+void dev_free(void* p);
+void ensure(slm_buf* y, size_t n);
+const float* view(const slm_buf* b, size_t off, size_t n, const char* what);
+void* stage(slm_ctx* c, const void* host, size_t bytes);
+
+// Runs f, turning failures into a status code and the thread's error message.
+template <class F>
+int guard(F&& f) {
+  try {
+    f();
+    set_error("");
+    return SLM_OK;
+  } catch (const Error& e) {
+    set_error(e.what());
+    return e.code;
+  } catch (const std::bad_alloc&) {
+    set_error("host allocation failed");
+    return SLM_ERR_NOMEM;
+  } catch (const std::exception& e) {
+    set_error(e.what());
+    return SLM_ERR_INVALID;
+  }
+}
+
+}  // namespace slm

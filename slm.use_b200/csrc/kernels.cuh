@@ -1,0 +1,96 @@
+// Host-side launchers of the sm_100a kernels (one .cu file per family).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace slm {
+
+// y[i][r] = epi(W[r]·x[i]) for i < m; see common.cuh:Epi.
+struct LinearArgs {
+  const float* w = nullptr;
+  int rows = 0, cols = 0;
+  const float* x = nullptr;
+  int ldx = 0, m = 0;
+  float* y = nullptr;
+  int ldy = 0;
+  const float* res = nullptr;  // EPI_ADD
+  int ldres = 0;
+  int epi = 0;
+};
+void linear(const LinearArgs& a, cudaStream_t st);
+void linear_prepare();
+
+// Attention geometry (reference Attn, src/ops.rs:31-46).  reach 0 = unbounded.
+struct AttnGeom {
+  int m;
+  long long reach, gap, cap;
+  int heads, key_heads, dh;
+  float scale;
+};
+int attn_splits(const AttnGeom& g, long long max_span);
+size_t attn_part_floats(const AttnGeom& g, int nsplit);
+// y[i][h·dh + e]; part holds attn_part_floats(g, nsplit) floats.
+void attention(const float* q, int ldq, const float* K, const float* V, const AttnGeom& g, const long long* pos_ptr,
+               int nsplit, float* part, float* y, int ldy, cudaStream_t st);
+
+struct GlaArgs {
+  float* S;
+  const float *q, *k, *v, *g, *dec, *bias, *hnw;
+  int ldq, ldk, ldv, ldg, lddec;
+  float eps;
+  int m, heads, dh;
+  float* out;
+  int ldo;
+  int fuse;  // 1: out = silu(g)·head_norm(y); 0: out = y (the bare Ops::gla)
+};
+void gla(const GlaArgs& a, cudaStream_t st);
+
+struct SampleArgs {
+  const float* logits;
+  float* work;  // vocab floats
+  int vocab;
+  float temperature, top_p, penalty;
+  uint32_t top_k, window;
+  const uint32_t* recent;  // device history
+  long long nrecent;
+  unsigned long long* rng;  // device xorshift64* state
+  uint32_t* out;            // chosen id
+  uint32_t* hist_out;       // optional: history array, written at [nrecent]
+  uint32_t* next_id;        // optional: the next step's input id
+  int* err;
+};
+void sample(const SampleArgs& a, cudaStream_t st);
+
+// elementwise.cu
+void ew_gather(float* y, const float* w, const uint32_t* ids, size_t m, size_t d, size_t vocab, int* err,
+               cudaStream_t st);
+void ew_embed(float* e0, float* x, const float* w, const uint32_t* ids, size_t m, size_t d, size_t vocab, int* err,
+              cudaStream_t st);
+void ew_copy(float* y, const float* x, size_t n, cudaStream_t st);
+void ew_shift(float* y, const float* first, const float* x, size_t m, size_t d, cudaStream_t st);
+void ew_columns(float* y, const float* x, size_t m, size_t stride, size_t off, size_t len, cudaStream_t st);
+void ew_add(float* y, const float* a, const float* b, size_t n, cudaStream_t st);
+void ew_add_row(float* y, const float* x, const float* row, size_t m, size_t d, cudaStream_t st);
+void ew_scale_rows(float* y, const float* x, const float* f, size_t m, size_t d, cudaStream_t st);
+void ew_mix(float* y, const float* a, const float* b, size_t n, float t, cudaStream_t st);
+void ew_silu_mul(float* y, const float* g, const float* u, size_t n, cudaStream_t st);
+void ew_loop_in(float* x, const float* s, const float* e, const float* row, size_t m, size_t d, cudaStream_t st);
+void ew_rms(float* y, const float* x, const float* w, size_t groups, size_t size, float eps, const float* base,
+            cudaStream_t st);
+void ew_l2norm(float* y, size_t ldy, const float* x, size_t ldx, size_t rows, size_t heads, size_t dh,
+               cudaStream_t st);
+void ew_rope_table(float* c, float* s, const float* inv, long long pos, size_t m, size_t half, cudaStream_t st);
+void ew_rope(float* y, const float* x, const float* c, const float* s, size_t m, size_t heads, size_t dh,
+             cudaStream_t st);
+void ew_store(float* cache, const float* src, size_t ldsrc, const long long* pos_ptr, long long pos, size_t m,
+              size_t cap, size_t heads, size_t dh, cudaStream_t st);
+void ew_rope_store(const float* mix, size_t ldmix, const float* inv, const long long* pos_ptr, size_t m,
+                   size_t heads, size_t dh, size_t cap, float* qout, float* kc, float* vc, cudaStream_t st);
+void ew_g_post(float* q, size_t d, size_t m, const long long* pos_ptr, float inv_log, int logn, const float* keys,
+               size_t ldk, const float* vals, size_t ldv, size_t kd, size_t cap, size_t dh, float* kc, float* vc,
+               cudaStream_t st);
+void ew_advance_pos(long long* pos, long long m, cudaStream_t st);
+
+}  // namespace slm

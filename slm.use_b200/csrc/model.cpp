@@ -1,0 +1,814 @@
+// The looped hybrid model on the device: weights, per-session state and the
+// m-token advance (reference Model/Session, src/model.rs:196-690), with the
+// fused kernels of this library in place of the reference's ~17 launches per
+// block.  The m = 1 step is captured once as a CUDA graph and replayed: every
+// kernel reads the position from device memory and the next token id from a
+// device slot that the on-device sampler writes.
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "capi.hpp"
+#include "common.cuh"
+#include "kernels.cuh"
+#include "loader.hpp"
+
+namespace slm {
+
+constexpr size_t CHUNK = 256;            // src/model.rs:27
+constexpr size_t MAX_SCORES = 1u << 28;  // src/model.rs:30
+constexpr size_t G_CAP0 = 1u << 13;      // first global cache capacity, src/model.rs:320
+
+struct Mat {
+  const float* w = nullptr;
+  size_t rows = 0, cols = 0;
+};
+
+struct Block {
+  char kind = 'S';
+  const float *norm1 = nullptr, *norm2 = nullptr;
+  Mat up, down;
+  Mat qkv, o;                                               // S (o: every kind)
+  Mat qkvg, decay;                                          // L
+  const float *bias = nullptr, *head_norm = nullptr;        // L
+  Mat q, kv;                                                // G
+  const float* norm_e = nullptr;                            // G with global_emb
+};
+
+struct LState {
+  char kind = 'S';
+  float *k = nullptr, *v = nullptr, *s = nullptr, *prev = nullptr;
+  size_t cap = 0;
+};
+
+}  // namespace slm
+
+using namespace slm;
+
+struct slm_model {
+  slm_ctx* ctx = nullptr;
+  Config cfg;
+  float* arena = nullptr;
+  std::vector<Block> prelude, core, coda;
+  Mat embed, inject, loop_embed;
+  bool looped = false;
+  const float* norm_f = nullptr;
+  const float* inv_freq = nullptr;
+  size_t params = 0, hidden = 0, mix_cols = 0;
+};
+
+struct slm_session {
+  slm_model* model = nullptr;
+  slm_ctx* ctx = nullptr;
+  size_t loops = 0, pos = 0;
+  std::vector<LState> pre, coda;
+  std::vector<std::vector<LState>> core;
+  std::vector<float*> owned;  // device allocations of this session
+  float *xa = nullptr, *xb = nullptr, *e0 = nullptr, *e_proj = nullptr, *n = nullptr, *mix = nullptr, *q = nullptr,
+        *kb = nullptr, *kin = nullptr, *kvs = nullptr, *y = nullptr, *mid = nullptr, *dec = nullptr, *part = nullptr,
+        *logits = nullptr, *work = nullptr, *nlast = nullptr;
+  long long* pos_dev = nullptr;
+  uint32_t* ids_dev = nullptr;
+  unsigned long long* rng_dev = nullptr;
+  uint32_t* out_dev = nullptr;
+  uint32_t* hist_dev = nullptr;
+  size_t hist_cap = 0;
+  uint32_t* outs_dev = nullptr;
+  size_t outs_cap = 0;
+  cudaGraphExec_t graph = nullptr;
+  bool use_graph = true;
+  bool capturing = false;
+  int64_t step_kernels = 0;  // kernel nodes of the captured step
+  int64_t graphs = 0;
+};
+
+namespace slm {
+namespace {
+
+struct Uploader {
+  std::vector<std::pair<const float*, size_t>> items;  // host data, floats
+  std::vector<size_t> offsets;
+  size_t total = 0;
+  size_t add(const float* data, size_t n) {
+    size_t off = total;
+    offsets.push_back(off);
+    items.emplace_back(data, n);
+    total += (n + 63) / 64 * 64;  // 256-byte aligned tensors
+    return off;
+  }
+};
+
+struct Loading {
+  Tensors t;
+  Uploader up;
+  std::vector<std::pair<const float**, size_t>> fix;  // pointers to patch with arena offsets
+  std::string error;
+};
+
+const TensorView& take(Loading& L, const std::string& name) {
+  auto it = L.t.map.find(name);
+  if (it == L.t.map.end()) fail(SLM_ERR_IO, "missing weight " + name);
+  return it->second;
+}
+
+void vec(Loading& L, const std::string& name, const float** dst, size_t want) {
+  const TensorView& tv = take(L, name);
+  if (want && tv.count != want) fail(SLM_ERR_IO, name + ": expected " + std::to_string(want) + " values");
+  size_t off = L.up.add(tv.data, tv.count);
+  L.fix.emplace_back(dst, off);
+}
+
+void mat(Loading& L, const std::string& name, Mat* m) {
+  const TensorView& tv = take(L, name);
+  if (tv.shape.size() != 2) fail(SLM_ERR_IO, name + ": expected a matrix");
+  m->rows = tv.shape[0];
+  m->cols = tv.shape[1];
+  size_t off = L.up.add(tv.data, tv.count);
+  L.fix.emplace_back(&m->w, off);
+}
+
+// Block::load (src/model.rs:114-153).
+void load_block(Loading& L, const Config& c, Block* b, const std::string& prefix, char kind) {
+  auto n = [&](const char* s) { return prefix + "." + s; };
+  b->kind = kind;
+  size_t d = c.d;
+  if (kind == 'S') {
+    mat(L, n("mixer.qkv.weight"), &b->qkv);
+    mat(L, n("mixer.o.weight"), &b->o);
+    if (b->qkv.rows != 3 * d || b->qkv.cols != d) fail(SLM_ERR_IO, prefix + ": qkv must be 3d × d");
+  } else if (kind == 'L') {
+    mat(L, n("mixer.qkvg.weight"), &b->qkvg);
+    mat(L, n("mixer.decay.weight"), &b->decay);
+    vec(L, n("mixer.decay.bias"), &b->bias, c.heads);
+    vec(L, n("mixer.head_norm.weight"), &b->head_norm, c.dh());
+    mat(L, n("mixer.o.weight"), &b->o);
+    if (b->qkvg.rows != 4 * d || b->qkvg.cols != d) fail(SLM_ERR_IO, prefix + ": qkvg must be 4d × d");
+    if (b->decay.rows != c.heads || b->decay.cols != d) fail(SLM_ERR_IO, prefix + ": decay must be heads × d");
+  } else if (kind == 'G') {
+    mat(L, n("mixer.q.weight"), &b->q);
+    mat(L, n("mixer.kv.weight"), &b->kv);
+    mat(L, n("mixer.o.weight"), &b->o);
+    if (c.emb != 0) vec(L, n("mixer.norm_e.weight"), &b->norm_e, d);
+    if (b->kv.rows != 2 * c.kv_heads * c.dh() || b->kv.cols != d) fail(SLM_ERR_IO, prefix + ": kv has the wrong shape");
+  } else {
+    fail(SLM_ERR_IO, std::string("unknown layer type ") + kind);
+  }
+  if (b->o.rows != d || b->o.cols != d) fail(SLM_ERR_IO, prefix + ": o must be d × d");
+  vec(L, n("norm1.weight"), &b->norm1, d);
+  vec(L, n("norm2.weight"), &b->norm2, d);
+  mat(L, n("mlp.up.weight"), &b->up);
+  mat(L, n("mlp.down.weight"), &b->down);
+  if (b->up.cols != d || b->down.rows != d || b->up.rows != 2 * b->down.cols)
+    fail(SLM_ERR_IO, prefix + ": mlp shapes do not match");
+}
+
+size_t mat_params(const Mat& m) { return m.rows * m.cols; }
+
+void* alloc_zero(slm_session* se, size_t bytes) {
+  void* p = dev_alloc(bytes);
+  se->owned.push_back(static_cast<float*>(p));
+  SLM_CUDA(cudaMemsetAsync(p, 0, bytes, se->ctx->stream));
+  return p;
+}
+
+LState new_state(slm_session* se, const Block& b) {
+  const Config& c = se->model->cfg;
+  size_t h = c.heads, dh = c.dh();
+  LState st;
+  st.kind = b.kind;
+  if (b.kind == 'S') {
+    size_t cap = c.window + CHUNK;  // Model::cap, src/model.rs:304-306
+    st.cap = cap;
+    st.k = static_cast<float*>(alloc_zero(se, h * cap * dh * sizeof(float)));
+    st.v = static_cast<float*>(alloc_zero(se, h * cap * dh * sizeof(float)));
+  } else if (b.kind == 'L') {
+    st.s = static_cast<float*>(alloc_zero(se, h * dh * dh * sizeof(float)));
+  } else {
+    st.cap = G_CAP0;
+    st.k = static_cast<float*>(dev_alloc(c.kv_heads * st.cap * dh * sizeof(float)));
+    st.v = static_cast<float*>(dev_alloc(c.kv_heads * st.cap * dh * sizeof(float)));
+    SLM_CUDA(cudaMemsetAsync(st.k, 0, c.kv_heads * st.cap * dh * sizeof(float), se->ctx->stream));
+    SLM_CUDA(cudaMemsetAsync(st.v, 0, c.kv_heads * st.cap * dh * sizeof(float), se->ctx->stream));
+    st.prev = static_cast<float*>(alloc_zero(se, c.d * sizeof(float)));
+  }
+  return st;
+}
+
+void drop_graph(slm_session* se) {
+  if (se->graph) {
+    cudaGraphExecDestroy(se->graph);
+    se->graph = nullptr;
+  }
+}
+
+// Doubles a global cache on the device (the reference moves it through the
+// host, src/model.rs:384-398).  Positions never wrap in a global cache.
+void grow(slm_session* se, LState& st) {
+  const Config& c = se->model->cfg;
+  size_t kh = c.kv_heads, dh = c.dh(), old = st.cap, nw = old * 2;
+  cudaStream_t s = se->ctx->stream;
+  for (float** buf : {&st.k, &st.v}) {
+    float* p = static_cast<float*>(dev_alloc(kh * nw * dh * sizeof(float)));
+    SLM_CUDA(cudaMemsetAsync(p, 0, kh * nw * dh * sizeof(float), s));
+    SLM_CUDA(cudaMemcpy2DAsync(p, nw * dh * sizeof(float), *buf, old * dh * sizeof(float), old * dh * sizeof(float), kh,
+                               cudaMemcpyDeviceToDevice, s));
+    SLM_CUDA(cudaStreamSynchronize(s));
+    dev_free(*buf);
+    *buf = p;
+  }
+  st.cap = nw;
+  drop_graph(se);
+}
+
+void ensure_caps(slm_session* se, size_t m) {
+  auto one = [&](LState& st) {
+    if (st.kind == 'G')
+      while (se->pos + m > st.cap) grow(se, st);
+  };
+  for (auto& st : se->pre) one(st);
+  for (auto& l : se->core)
+    for (auto& st : l) one(st);
+  for (auto& st : se->coda) one(st);
+}
+
+void run_linear(cudaStream_t s, const Mat& w, const float* x, int ldx, int m, float* y, int ldy, int epi,
+                const float* res = nullptr, int ldres = 0, size_t rows = 0) {
+  LinearArgs a;
+  a.w = w.w;
+  a.rows = (int)(rows ? rows : w.rows);
+  a.cols = (int)w.cols;
+  a.x = x;
+  a.ldx = ldx;
+  a.m = m;
+  a.y = y;
+  a.ldy = ldy;
+  a.res = res;
+  a.ldres = ldres;
+  a.epi = epi;
+  linear(a, s);
+}
+
+// Model::block (src/model.rs:400-560) for m tokens, x updated in place.
+void block(slm_session* se, const Block& b, LState& st, float* x, size_t m) {
+  slm_model* md = se->model;
+  const Config& c = md->cfg;
+  cudaStream_t s = se->ctx->stream;
+  const size_t d = c.d, heads = c.heads, dh = c.dh();
+  const float scale = 1.0f / std::sqrt((float)dh);
+  const int im = (int)m, id = (int)d;
+  ew_rms(se->n, x, b.norm1, m, d, c.eps, nullptr, s);
+  bool has_h = true;
+  if (b.kind == 'S') {
+    run_linear(s, b.qkv, se->n, id, im, se->mix, (int)(3 * d), EPI_STORE);
+    ew_rope_store(se->mix, 3 * d, md->inv_freq, se->pos_dev, m, heads, dh, st.cap, se->q, st.k, st.v, s);
+    AttnGeom g{im, (long long)c.window, 0, (long long)st.cap, (int)heads, (int)heads, (int)dh, scale};
+    int ns = attn_splits(g, (long long)(c.window + m - 1));
+    attention(se->q, id, st.k, st.v, g, se->pos_dev, ns, se->part, se->y, id, s);
+  } else if (b.kind == 'L') {
+    run_linear(s, b.qkvg, se->n, id, im, se->mix, (int)(4 * d), EPI_STORE);
+    run_linear(s, b.decay, se->n, id, im, se->dec, (int)heads, EPI_STORE);
+    ew_l2norm(se->q, d, se->mix, 4 * d, m, heads, dh, s);
+    ew_l2norm(se->kb, d, se->mix + d, 4 * d, m, heads, dh, s);
+    GlaArgs a{};
+    a.S = st.s;
+    a.q = se->q, a.ldq = id;
+    a.k = se->kb, a.ldk = id;
+    a.v = se->mix + 2 * d, a.ldv = (int)(4 * d);
+    a.g = se->mix + 3 * d, a.ldg = (int)(4 * d);
+    a.dec = se->dec, a.lddec = (int)heads;
+    a.bias = b.bias, a.hnw = b.head_norm, a.eps = c.eps;
+    a.m = im, a.heads = (int)heads, a.dh = (int)dh;
+    a.out = se->y, a.ldo = id, a.fuse = 1;
+    gla(a, s);
+  } else {
+    if (b.norm_e) ew_rms(se->n, se->e0, b.norm_e, m, d, c.eps, se->n, s);  // n += rms(e0)·w_e
+    const size_t kh = c.kv_heads, kd = kh * dh;
+    run_linear(s, b.q, se->n, id, im, se->q, id, EPI_STORE);
+    run_linear(s, b.kv, se->n, id, im, se->mix, (int)(2 * kd), EPI_STORE);
+    const float* keys = se->mix;
+    size_t ldk = 2 * kd;
+    if (c.kshift) {
+      ew_shift(se->kin, st.prev, se->n, m, d, s);
+      run_linear(s, b.kv, se->kin, id, im, se->kvs, (int)kd, EPI_STORE, nullptr, 0, kd);  // key rows only
+      ew_copy(st.prev, se->n + (m - 1) * d, d, s);
+      keys = se->kvs;
+      ldk = kd;
+    }
+    float inv_log = c.logn ? 1.0f / std::log((float)c.logn) : 0.0f;
+    ew_g_post(se->q, d, m, se->pos_dev, inv_log, c.logn ? 1 : 0, keys, ldk, se->mix + kd, 2 * kd, kd, st.cap, dh,
+              st.k, st.v, s);
+    size_t far = c.far ? c.window : 0;
+    if (se->capturing || se->pos + m > far) {
+      AttnGeom g{im, 0, (long long)far, (long long)st.cap, (int)heads, (int)kh, (int)dh, scale};
+      long long span = (long long)(se->capturing ? st.cap : se->pos + m);
+      int ns = attn_splits(g, span);
+      attention(se->q, id, st.k, st.v, g, se->pos_dev, ns, se->part, se->y, id, s);
+    } else {
+      has_h = false;
+    }
+  }
+  if (has_h) run_linear(s, b.o, se->y, id, im, x, id, EPI_ADD, x, id);  // x += o·y
+  ew_rms(se->n, x, b.norm2, m, d, c.eps, nullptr, s);
+  const size_t hidden = b.down.cols;
+  run_linear(s, b.up, se->n, id, im, se->mid, (int)hidden, EPI_SILU);          // silu(gate)·amp
+  run_linear(s, b.down, se->mid, (int)hidden, im, x, id, EPI_ADD, x, id);       // x += down·mid
+}
+
+// Model::advance (src/model.rs:563-640).  Ids are already in se->ids_dev.
+void advance(slm_session* se, size_t m, bool want_logits) {
+  slm_model* md = se->model;
+  const Config& c = md->cfg;
+  cudaStream_t s = se->ctx->stream;
+  const size_t d = c.d;
+  float* x = se->xa;
+  ew_embed(se->e0, x, md->embed.w, se->ids_dev, m, d, c.vocab, se->ctx->err, s);
+  for (size_t i = 0; i < md->prelude.size(); i++) block(se, md->prelude[i], se->pre[i], x, m);
+  if (md->looped) {
+    run_linear(s, md->inject, x, (int)d, (int)m, se->e_proj, (int)d, EPI_STORE);
+    float* sbuf = x;  // s = x (no copy: the loop writes the other buffer)
+    for (size_t r = 0; r < se->loops; r++) {
+      const float* le = md->loop_embed.w + r * d;
+      float* xr = (sbuf == se->xa) ? se->xb : se->xa;
+      ew_loop_in(xr, sbuf, se->e_proj, le, m, d, s);
+      for (size_t i = 0; i < md->core.size(); i++) block(se, md->core[i], se->core[r][i], xr, m);
+      if (c.damp == 1.0f) {
+        sbuf = xr;
+      } else {
+        ew_mix(sbuf, sbuf, xr, m * d, c.damp, s);  // s = s + damp·(x − s), in place
+      }
+    }
+    x = sbuf;
+  }
+  for (size_t i = 0; i < md->coda.size(); i++) block(se, md->coda[i], se->coda[i], x, m);
+  if (want_logits) {
+    ew_rms(se->nlast, x + (m - 1) * d, md->norm_f, 1, d, c.eps, nullptr, s);
+    run_linear(s, md->embed, se->nlast, (int)d, 1, se->logits, (int)c.vocab, EPI_STORE);  // tied head
+  }
+  ew_advance_pos(se->pos_dev, (long long)m, s);
+  se->pos += m;
+}
+
+// One decode step for the id already in ids_dev[0]: graph replay when enabled.
+void step_device(slm_session* se) {
+  ensure_caps(se, 1);
+  cudaStream_t s = se->ctx->stream;
+  if (!se->use_graph) {
+    advance(se, 1, true);
+    return;
+  }
+  if (!se->graph) {
+    cudaGraph_t g = nullptr;
+    SLM_CUDA(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
+    se->capturing = true;
+    size_t pos0 = se->pos;
+    try {
+      advance(se, 1, true);
+    } catch (...) {
+      se->capturing = false;
+      cudaStreamEndCapture(s, &g);
+      if (g) cudaGraphDestroy(g);
+      se->pos = pos0;
+      throw;
+    }
+    se->capturing = false;
+    se->pos = pos0;  // the capture enqueued nothing
+    SLM_CUDA(cudaStreamEndCapture(s, &g));
+    size_t count = 0;
+    cudaGraphGetNodes(g, nullptr, &count);
+    std::vector<cudaGraphNode_t> nodes(count);
+    if (count) cudaGraphGetNodes(g, nodes.data(), &count);
+    int64_t kernels = 0;
+    for (auto nd : nodes) {
+      cudaGraphNodeType t;
+      if (cudaGraphNodeGetType(nd, &t) == cudaSuccess && t == cudaGraphNodeTypeKernel) kernels++;
+    }
+    se->step_kernels = kernels;
+    se->graphs++;
+    cudaError_t e = cudaGraphInstantiate(&se->graph, g, 0);
+    cudaGraphDestroy(g);
+    SLM_CUDA(e);
+  }
+  SLM_CUDA(cudaGraphLaunch(se->graph, s));
+  se->pos += 1;
+}
+
+void check_device_error(slm_ctx* c) {
+  int h = 0;
+  SLM_CUDA(cudaMemcpyAsync(&h, c->err, sizeof(int), cudaMemcpyDeviceToHost, c->stream));
+  SLM_CUDA(cudaStreamSynchronize(c->stream));
+  if (h) {
+    SLM_CUDA(cudaMemsetAsync(c->err, 0, sizeof(int), c->stream));
+    std::string why;
+    if (h & 1) why += " token id out of range;";
+    if (h & 2) why += " top_k above 2048 is not supported on the device;";
+    if (h & 4) why += " top_p set larger than the 2048 largest logits (use top_k);";
+    fail(SLM_ERR_DEVICE, "device reported:" + why);
+  }
+}
+
+void ensure_u32(slm_session* se, uint32_t** p, size_t* cap, size_t n) {
+  if (*cap >= n) return;
+  SLM_CUDA(cudaStreamSynchronize(se->ctx->stream));
+  dev_free(*p);
+  size_t c = n < 1024 ? 1024 : n;
+  *p = static_cast<uint32_t*>(dev_alloc(c * sizeof(uint32_t)));
+  *cap = c;
+}
+
+void check_sampling(const slm_sampling* sp) {
+  SLM_REQUIRE(sp, "sampling is null");
+  SLM_REQUIRE(sp->top_k <= 2048, "top_k above 2048 is not supported on the device");
+  SLM_REQUIRE(!(sp->top_p != sp->top_p), "top_p is NaN");
+}
+
+SampleArgs sample_args(slm_session* se, const slm_sampling* sp) {
+  SampleArgs a{};
+  a.logits = se->logits;
+  a.work = se->work;
+  a.vocab = (int)se->model->cfg.vocab;
+  a.temperature = sp->temperature;
+  a.top_p = sp->top_p;
+  a.penalty = sp->repeat_penalty;
+  a.top_k = sp->top_k;
+  a.window = sp->repeat_window;
+  a.rng = se->rng_dev;
+  a.err = se->ctx->err;
+  return a;
+}
+
+}  // namespace
+}  // namespace slm
+
+extern "C" {
+
+int slm_model_load(slm_ctx* ctx, const char* dir, slm_model** out) {
+  return guard([&] {
+    SLM_REQUIRE(ctx && dir && out, "bad arguments");
+    Device dev(ctx);
+    auto md = std::make_unique<slm_model>();
+    md->ctx = ctx;
+    md->cfg = load_config(dir);
+    const Config& c = md->cfg;
+    Loading L;
+    L.t = load_safetensors(dir);
+    auto blocks = [&](std::vector<Block>& out_b, const char* name, const std::string& kinds) {
+      out_b.resize(kinds.size());
+      for (size_t i = 0; i < kinds.size(); i++)
+        load_block(L, c, &out_b[i], std::string(name) + "." + std::to_string(i), kinds[i]);
+    };
+    blocks(md->prelude, "prelude", c.prelude);
+    blocks(md->core, "core", c.core);
+    blocks(md->coda, "coda", c.coda);
+    md->looped = !c.core.empty();
+    if (md->looped) {
+      mat(L, "inject_e.weight", &md->inject);
+      mat(L, "loop_embed.weight", &md->loop_embed);
+      SLM_REQUIRE(md->loop_embed.rows >= c.max_loops && md->loop_embed.cols == c.d, "loop_embed has the wrong shape");
+    }
+    mat(L, "embed.weight", &md->embed);
+    vec(L, "norm_f.weight", &md->norm_f, c.d);
+    SLM_REQUIRE(md->embed.rows == c.vocab && md->embed.cols == c.d, "embed must be vocab × d");
+    const size_t dh = c.dh();
+    SLM_REQUIRE(dh % 2 == 0 && c.d % 4 == 0, "head size must be even and d_model a multiple of 4");
+    std::vector<float> inv(dh / 2);
+    for (size_t i = 0; i < dh / 2; i++) inv[i] = 1.0f / std::pow(c.rope_base, (float)(2 * i) / (float)dh);
+    L.t.map["__inv_freq"] = TensorView{{dh / 2}, inv.data(), dh / 2};
+    vec(L, "__inv_freq", &md->inv_freq, dh / 2);
+    md->arena = static_cast<float*>(dev_alloc(L.up.total * sizeof(float)));
+    for (size_t i = 0; i < L.up.items.size(); i++)
+      SLM_CUDA(cudaMemcpy(md->arena + L.up.offsets[i], L.up.items[i].first, L.up.items[i].second * sizeof(float),
+                          cudaMemcpyHostToDevice));
+    for (auto& f : L.fix) *f.first = md->arena + f.second;
+    // Model::params (src/model.rs:275-302).
+    size_t p = 0;
+    for (auto* bs : {&md->prelude, &md->core, &md->coda})
+      for (auto& b : *bs) {
+        size_t mixer = 0;
+        if (b.kind == 'S') mixer = mat_params(b.qkv) + mat_params(b.o);
+        if (b.kind == 'L') mixer = mat_params(b.qkvg) + mat_params(b.decay) + mat_params(b.o) + c.heads + dh;
+        if (b.kind == 'G') mixer = mat_params(b.q) + mat_params(b.kv) + mat_params(b.o) + (b.norm_e ? c.d : 0);
+        p += mixer + 2 * c.d + mat_params(b.up) + mat_params(b.down);
+        md->hidden = std::max(md->hidden, b.down.cols);
+      }
+    p += mat_params(md->embed) + c.d + mat_params(md->inject) + mat_params(md->loop_embed);
+    md->params = p;
+    md->mix_cols = std::max({3 * c.d, 4 * c.d, 2 * c.kv_heads * dh});
+    *out = md.release();
+  });
+}
+
+int slm_model_free(slm_model* md) {
+  return guard([&] {
+    if (!md) return;
+    Device dev(md->ctx);
+    cudaStreamSynchronize(md->ctx->stream);
+    dev_free(md->arena);
+    delete md;
+  });
+}
+
+int slm_model_info_get(const slm_model* md, slm_model_info* out) {
+  return guard([&] {
+    SLM_REQUIRE(md && out, "bad arguments");
+    const Config& c = md->cfg;
+    std::memset(out, 0, sizeof(*out));
+    out->vocab = c.vocab, out->d_model = c.d, out->heads = c.heads, out->head_dim = c.dh();
+    out->kv_heads = c.kv_heads, out->hidden = md->hidden, out->window = c.window;
+    out->max_loops = c.max_loops, out->default_loops = c.default_loops, out->params = md->params;
+    std::strncpy(out->prelude, c.prelude.c_str(), sizeof(out->prelude) - 1);
+    std::strncpy(out->core, c.core.c_str(), sizeof(out->core) - 1);
+    std::strncpy(out->coda, c.coda.c_str(), sizeof(out->coda) - 1);
+  });
+}
+
+int slm_session_new(slm_model* md, size_t loops, slm_session** out) {
+  return guard([&] {
+    SLM_REQUIRE(md && out, "bad arguments");
+    const Config& c = md->cfg;
+    // Config::loops (src/config.rs:96-105).
+    if (c.core.empty()) {
+      loops = 0;
+    } else {
+      if (loops == 0) loops = c.default_loops;
+      SLM_REQUIRE(loops >= 1 && loops <= c.max_loops, "loops must be between 1 and " + std::to_string(c.max_loops));
+    }
+    Device dev(md->ctx);
+    auto se = std::make_unique<slm_session>();
+    se->model = md;
+    se->ctx = md->ctx;
+    se->loops = loops;
+    try {
+      for (auto& b : md->prelude) se->pre.push_back(new_state(se.get(), b));
+      se->core.resize(loops);
+      for (size_t r = 0; r < loops; r++)
+        for (auto& b : md->core) se->core[r].push_back(new_state(se.get(), b));
+      for (auto& b : md->coda) se->coda.push_back(new_state(se.get(), b));
+      const size_t d = c.d, dh = c.dh(), kd = c.kv_heads * dh;
+      auto f = [&](size_t n) { return static_cast<float*>(alloc_zero(se.get(), n * sizeof(float))); };
+      se->xa = f(CHUNK * d);
+      se->xb = f(CHUNK * d);
+      se->e0 = f(CHUNK * d);
+      se->e_proj = f(CHUNK * d);
+      se->n = f(CHUNK * d);
+      se->mix = f(CHUNK * md->mix_cols);
+      se->q = f(CHUNK * d);
+      se->kb = f(CHUNK * d);
+      se->kin = f(CHUNK * d);
+      se->kvs = f(CHUNK * kd);
+      se->y = f(CHUNK * d);
+      se->mid = f(CHUNK * std::max<size_t>(md->hidden, 1));
+      se->dec = f(CHUNK * c.heads);
+      se->nlast = f(d);
+      se->logits = f(c.vocab);
+      se->work = f(c.vocab);
+      size_t part = 0;
+      for (size_t m = 1; m <= CHUNK; m++) {
+        AttnGeom g{(int)m, 0, 0, 1, (int)c.heads, 1, (int)dh, 1.0f};
+        part = std::max(part, attn_part_floats(g, attn_splits(g, 1ll << 40)));
+      }
+      se->part = f(part);
+      se->pos_dev = reinterpret_cast<long long*>(alloc_zero(se.get(), sizeof(long long)));
+      se->ids_dev = reinterpret_cast<uint32_t*>(alloc_zero(se.get(), CHUNK * sizeof(uint32_t)));
+      se->rng_dev = reinterpret_cast<unsigned long long*>(alloc_zero(se.get(), sizeof(unsigned long long)));
+      se->out_dev = reinterpret_cast<uint32_t*>(alloc_zero(se.get(), sizeof(uint32_t) * 4));
+      SLM_CUDA(cudaStreamSynchronize(se->ctx->stream));
+    } catch (...) {
+      cudaStreamSynchronize(se->ctx->stream);
+      for (float* p : se->owned) dev_free(p);
+      for (auto* v : {&se->pre, &se->coda})
+        for (auto& st : *v)
+          if (st.kind == 'G') dev_free(st.k), dev_free(st.v);
+      for (auto& l : se->core)
+        for (auto& st : l)
+          if (st.kind == 'G') dev_free(st.k), dev_free(st.v);
+      throw;
+    }
+    *out = se.release();
+  });
+}
+
+int slm_session_free(slm_session* se) {
+  return guard([&] {
+    if (!se) return;
+    Device dev(se->ctx);
+    cudaStreamSynchronize(se->ctx->stream);
+    drop_graph(se);
+    for (float* p : se->owned) dev_free(p);
+    auto g = [&](LState& st) {
+      if (st.kind == 'G') dev_free(st.k), dev_free(st.v);
+    };
+    for (auto& st : se->pre) g(st);
+    for (auto& l : se->core)
+      for (auto& st : l) g(st);
+    for (auto& st : se->coda) g(st);
+    dev_free(se->hist_dev);
+    dev_free(se->outs_dev);
+    delete se;
+  });
+}
+
+int slm_session_pos(const slm_session* se, size_t* out) {
+  return guard([&] {
+    SLM_REQUIRE(se && out, "bad arguments");
+    *out = se->pos;
+  });
+}
+
+int slm_session_loops(const slm_session* se, size_t* out) {
+  return guard([&] {
+    SLM_REQUIRE(se && out, "bad arguments");
+    *out = se->loops;
+  });
+}
+
+int slm_session_set(slm_session* se, int option, int64_t value) {
+  return guard([&] {
+    SLM_REQUIRE(se, "session is null");
+    if (option == SLM_OPT_GRAPH) {
+      Device dev(se->ctx);
+      se->use_graph = value != 0;
+      if (!se->use_graph) drop_graph(se);
+      return;
+    }
+    fail(SLM_ERR_INVALID, "unknown option");
+  });
+}
+
+int slm_session_stat(const slm_session* se, int what, int64_t* out) {
+  return guard([&] {
+    SLM_REQUIRE(se && out, "bad arguments");
+    if (what == SLM_STAT_STEP_KERNELS) *out = se->step_kernels;
+    else if (what == SLM_STAT_GRAPHS) *out = se->graphs;
+    else fail(SLM_ERR_INVALID, "unknown counter");
+  });
+}
+
+int slm_feed(slm_session* se, const uint32_t* ids, size_t n, size_t limit) {
+  return guard([&] {
+    SLM_REQUIRE(se && (ids || n == 0), "bad arguments");
+    SLM_REQUIRE(limit >= 1, "limit must be at least 1");
+    const Config& c = se->model->cfg;
+    for (size_t i = 0; i < n; i++) SLM_REQUIRE(ids[i] < c.vocab, "token id out of range");
+    Device dev(se->ctx);
+    bool global_outside = c.coda.find('G') != std::string::npos || c.prelude.find('G') != std::string::npos;
+    size_t at = 0;
+    while (at < n) {
+      // Model::chunk_at (src/model.rs:647-654).
+      size_t chunk = std::min(limit, CHUNK);
+      if (global_outside) chunk = std::min(chunk, std::max<size_t>(MAX_SCORES / c.heads / (se->pos + 1), 1));
+      size_t m = std::min(chunk, n - at);
+      if (m == 1 && se->use_graph) {
+        SLM_CUDA(cudaMemcpyAsync(se->ids_dev, ids + at, sizeof(uint32_t), cudaMemcpyHostToDevice, se->ctx->stream));
+        step_device(se);  // the last chunk always wants logits; middle ones do too here (harmless)
+      } else {
+        ensure_caps(se, m);
+        SLM_CUDA(cudaMemcpyAsync(se->ids_dev, ids + at, m * sizeof(uint32_t), cudaMemcpyHostToDevice, se->ctx->stream));
+        advance(se, m, at + m == n);
+      }
+      at += m;
+    }
+  });
+}
+
+int slm_step(slm_session* se, uint32_t id) {
+  return guard([&] {
+    SLM_REQUIRE(se, "session is null");
+    SLM_REQUIRE(id < se->model->cfg.vocab, "token id out of range");
+    Device dev(se->ctx);
+    SLM_CUDA(cudaMemcpyAsync(se->ids_dev, &id, sizeof(uint32_t), cudaMemcpyHostToDevice, se->ctx->stream));
+    step_device(se);
+  });
+}
+
+int slm_logits(slm_session* se, float* out) {
+  return guard([&] {
+    SLM_REQUIRE(se && out, "bad arguments");
+    Device dev(se->ctx);
+    SLM_CUDA(cudaMemcpyAsync(out, se->logits, se->model->cfg.vocab * sizeof(float), cudaMemcpyDeviceToHost,
+                             se->ctx->stream));
+    check_device_error(se->ctx);
+  });
+}
+
+int slm_state_bytes(const slm_session* se, size_t* out) {
+  return guard([&] {
+    SLM_REQUIRE(se && out, "bad arguments");
+    const Config& c = se->model->cfg;
+    size_t dh = c.dh(), total = 0;
+    auto one = [&](const LState& st) -> size_t {
+      if (st.kind == 'S') return 2 * c.heads * (c.window + CHUNK) * dh;
+      if (st.kind == 'L') return c.heads * dh * dh;
+      return 2 * c.kv_heads * se->pos * dh + c.d;
+    };
+    for (auto& st : se->pre) total += one(st);
+    for (auto& l : se->core)
+      for (auto& st : l) total += one(st);
+    for (auto& st : se->coda) total += one(st);
+    *out = total * 4;
+  });
+}
+
+uint64_t slm_rng_seed(uint64_t seed) { return seed * 0x9E3779B97F4A7C15ull | 1; }
+
+int slm_sample(slm_session* se, const slm_sampling* sp, const uint32_t* recent, size_t n_recent, uint64_t* rng_state,
+               uint32_t* out_id) {
+  return guard([&] {
+    SLM_REQUIRE(se && rng_state && out_id && (recent || n_recent == 0), "bad arguments");
+    check_sampling(sp);
+    Device dev(se->ctx);
+    cudaStream_t s = se->ctx->stream;
+    ensure_u32(se, &se->hist_dev, &se->hist_cap, n_recent + 1);
+    if (n_recent)
+      SLM_CUDA(cudaMemcpyAsync(se->hist_dev, recent, n_recent * sizeof(uint32_t), cudaMemcpyHostToDevice, s));
+    unsigned long long st = *rng_state;
+    SLM_CUDA(cudaMemcpyAsync(se->rng_dev, &st, sizeof(st), cudaMemcpyHostToDevice, s));
+    SampleArgs a = sample_args(se, sp);
+    a.recent = se->hist_dev;
+    a.nrecent = (long long)n_recent;
+    a.out = se->out_dev;
+    sample(a, s);
+    uint32_t id = 0;
+    SLM_CUDA(cudaMemcpyAsync(&id, se->out_dev, sizeof(id), cudaMemcpyDeviceToHost, s));
+    SLM_CUDA(cudaMemcpyAsync(&st, se->rng_dev, sizeof(st), cudaMemcpyDeviceToHost, s));
+    check_device_error(se->ctx);
+    *out_id = id;
+    *rng_state = st;
+  });
+}
+
+int slm_pick(slm_ctx* c, const slm_buf* logits, size_t vocab, const slm_sampling* sp, const uint32_t* recent,
+             size_t n_recent, uint64_t* rng_state, uint32_t* out_id) {
+  return guard([&] {
+    SLM_REQUIRE(c && rng_state && out_id && (recent || n_recent == 0) && vocab > 0, "bad arguments");
+    SLM_REQUIRE(vocab < (1u << 31), "vocab too large");
+    check_sampling(sp);
+    const float* l = view(logits, 0, vocab, "pick logits");
+    Device dev(c);
+    cudaStream_t s = c->stream;
+    size_t words = vocab + n_recent + 8;
+    float* scratch = static_cast<float*>(dev_alloc(words * sizeof(float)));
+    struct Free {
+      float* p;
+      ~Free() { dev_free(p); }
+    } fr{scratch};
+    auto* hist = reinterpret_cast<uint32_t*>(scratch + vocab);
+    auto* rng = reinterpret_cast<unsigned long long*>(scratch + vocab + n_recent + 2 - ((vocab + n_recent) & 1));
+    auto* outd = reinterpret_cast<uint32_t*>(rng + 2);
+    if (n_recent) SLM_CUDA(cudaMemcpyAsync(hist, recent, n_recent * sizeof(uint32_t), cudaMemcpyHostToDevice, s));
+    unsigned long long st = *rng_state;
+    SLM_CUDA(cudaMemcpyAsync(rng, &st, sizeof(st), cudaMemcpyHostToDevice, s));
+    SampleArgs a{};
+    a.logits = l;
+    a.work = scratch;
+    a.vocab = (int)vocab;
+    a.temperature = sp->temperature, a.top_p = sp->top_p, a.penalty = sp->repeat_penalty;
+    a.top_k = sp->top_k, a.window = sp->repeat_window;
+    a.recent = hist, a.nrecent = (long long)n_recent;
+    a.rng = rng, a.out = outd, a.err = c->err;
+    sample(a, s);
+    uint32_t id = 0;
+    SLM_CUDA(cudaMemcpyAsync(&id, outd, sizeof(id), cudaMemcpyDeviceToHost, s));
+    SLM_CUDA(cudaMemcpyAsync(&st, rng, sizeof(st), cudaMemcpyDeviceToHost, s));
+    check_device_error(c);
+    *out_id = id;
+    *rng_state = st;
+  });
+}
+
+int slm_decode(slm_session* se, uint32_t first, size_t n, const slm_sampling* sp, const uint32_t* recent,
+               size_t n_recent, uint64_t* rng_state, uint32_t* out) {
+  return guard([&] {
+    SLM_REQUIRE(se && rng_state && (out || n == 0) && (recent || n_recent == 0), "bad arguments");
+    SLM_REQUIRE(first < se->model->cfg.vocab, "token id out of range");
+    check_sampling(sp);
+    if (n == 0) return;
+    Device dev(se->ctx);
+    cudaStream_t s = se->ctx->stream;
+    ensure_u32(se, &se->hist_dev, &se->hist_cap, n_recent + n + 1);
+    ensure_u32(se, &se->outs_dev, &se->outs_cap, n);
+    if (n_recent)
+      SLM_CUDA(cudaMemcpyAsync(se->hist_dev, recent, n_recent * sizeof(uint32_t), cudaMemcpyHostToDevice, s));
+    unsigned long long st = *rng_state;
+    SLM_CUDA(cudaMemcpyAsync(se->rng_dev, &st, sizeof(st), cudaMemcpyHostToDevice, s));
+    SLM_CUDA(cudaMemcpyAsync(se->ids_dev, &first, sizeof(first), cudaMemcpyHostToDevice, s));
+    SampleArgs a = sample_args(se, sp);
+    a.recent = se->hist_dev;
+    a.hist_out = se->hist_dev;
+    a.next_id = se->ids_dev;
+    for (size_t t = 0; t < n; t++) {
+      step_device(se);
+      a.nrecent = (long long)(n_recent + t);
+      a.out = se->outs_dev + t;
+      sample(a, s);
+    }
+    SLM_CUDA(cudaMemcpyAsync(out, se->outs_dev, n * sizeof(uint32_t), cudaMemcpyDeviceToHost, s));
+    SLM_CUDA(cudaMemcpyAsync(&st, se->rng_dev, sizeof(st), cudaMemcpyDeviceToHost, s));
+    check_device_error(se->ctx);
+    *rng_state = st;
+  });
+}
+
+}  // extern "C"

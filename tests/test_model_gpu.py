@@ -1,0 +1,137 @@
+"""Model-level parity through the C ABI: the tiny golden fixture (the
+reference's own parity test, tests/parity.rs), synthetic models against the
+CPU oracle, and chunked prefill against token-by-token decode."""
+import numpy as np
+import pytest
+
+from conftest import SPLITS, TINY, TOLERANCE, load_pkg, run_split
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def tiny(slm, ctx):
+    return slm.Model(ctx, TINY)
+
+
+@pytest.mark.parametrize("graph", [True, False])
+def test_tiny_plain_decode(tiny, golden, graph):
+    def factory(loops):
+        se = tiny.session(loops)
+        se.set_graph(graph)
+        return se
+
+    checked, md, same = run_split(factory, golden, 0, 1)
+    assert checked == 40
+    assert md < TOLERANCE and same, md
+
+
+@pytest.mark.parametrize("split,chunk", SPLITS)
+def test_tiny_chunked_prefill(tiny, golden, split, chunk):
+    checked, md, same = run_split(tiny.session, golden, split, chunk)
+    assert checked == 41 - split
+    assert md < TOLERANCE and same, (split, chunk, md)
+
+
+def test_tiny_state_bytes(tiny, oracle):
+    ref = oracle.Model(TINY)
+    a, b = tiny.session(3), ref.session(3)
+    ids = np.arange(13) % 97
+    a.feed(ids, 5)
+    b.feed(ids, 5)
+    assert a.state_bytes() == b.state_bytes()
+    assert a.pos == b.pos == 13
+
+
+def _synthetic(tmp_path_factory, name, base, **kw):
+    syn = __import__("slm_b200.synthetic").synthetic
+    cfg = syn.scaled(getattr(syn, base), **kw)
+    return syn.write_model(tmp_path_factory.mktemp(name), cfg, seed=5)
+
+
+@pytest.fixture(scope="module")
+def small(tmp_path_factory):
+    load_pkg()
+    return _synthetic(tmp_path_factory, "small", "BASE", vocab_size=1000, d_model=128, n_heads=2, hidden=256,
+                      window=48, max_loops=4, default_loops=3)
+
+
+@pytest.fixture(scope="module")
+def small_g(tmp_path_factory):
+    load_pkg()
+    return _synthetic(tmp_path_factory, "small_g", "GLOBAL", vocab_size=500, d_model=64, n_heads=4, hidden=128,
+                      window=16, max_loops=3, default_loops=2, global_kv_heads=2)
+
+
+def compare(dev, ref, ids, limit, steps, atol):
+    dev.feed(ids, limit)
+    ref.feed(ids, limit)
+    worst = float(np.abs(dev.logits() - ref.logits()).max())
+    tok = int(np.argmax(ref.logits()))
+    for _ in range(steps):
+        dev.step(tok)
+        ref.step(tok)
+        a, b = dev.logits(), ref.logits()
+        worst = max(worst, float(np.abs(a - b).max()))
+        tok = int(np.argmax(b))
+    assert worst < atol, worst
+    return worst
+
+
+@pytest.mark.parametrize("limit", [256, 7, 1])
+def test_small_model_matches_oracle(slm, ctx, oracle, small, limit):
+    ids = np.random.default_rng(0).integers(0, 1000, 300)
+    dev = slm.Model(ctx, small).session()
+    ref = oracle.Model(small).session()
+    compare(dev, ref, ids, limit, 20, 2e-4)
+
+
+def test_global_variant_matches_oracle(slm, ctx, oracle, small_g):
+    ids = np.random.default_rng(1).integers(0, 500, 200)
+    dev = slm.Model(ctx, small_g).session()
+    ref = oracle.Model(small_g).session()
+    compare(dev, ref, ids, 64, 20, 2e-4)
+
+
+def test_global_cache_grows_on_device(slm, ctx, oracle, small_g):
+    # 8192 slots first (src/model.rs:320); crossing it doubles the cache.
+    ids = np.random.default_rng(2).integers(0, 500, 8250)
+    dev = slm.Model(ctx, small_g).session(1)
+    ref = oracle.Model(small_g).session(1)
+    compare(dev, ref, ids, 256, 5, 5e-4)
+    assert dev.state_bytes() == ref.state_bytes()
+
+
+def test_chunked_prefill_gives_the_same_greedy_tokens(slm, ctx, small):
+    model = slm.Model(ctx, small)
+    ids = np.random.default_rng(3).integers(0, 1000, 333)
+    a, b = model.session(), model.session()
+    a.feed(ids, 256)
+    for t in ids:
+        b.step(int(t))
+    greedy = slm.Sampling()
+    first_a, first_b = a.sample(greedy), b.sample(greedy)
+    assert first_a == first_b
+    ta = a.decode(first_a, 48, greedy)
+    tb = b.decode(first_b, 48, greedy)
+    np.testing.assert_array_equal(ta, tb)
+
+
+def test_86m_shapes_match_oracle(slm, ctx, oracle, tmp_path_factory):
+    folder = _synthetic(tmp_path_factory, "m86", "BASE", window=128)
+    ids = np.random.default_rng(4).integers(0, 32000, 160)
+    dev = slm.Model(ctx, folder).session(2)
+    ref = oracle.Model(folder).session(2)
+    compare(dev, ref, ids, 64, 4, 1e-3)
+
+
+def test_errors_are_statuses(slm, ctx, tiny):
+    se = tiny.session()
+    with pytest.raises(slm.SlmError):
+        se.step(97)  # vocab is 97
+    with pytest.raises(slm.SlmError):
+        se.feed([1, 2, 500])
+    with pytest.raises(slm.SlmError):
+        tiny.session(7)  # max_loops 6
+    with pytest.raises(slm.SlmError):
+        slm.Model(ctx, TINY.parent / "missing")
