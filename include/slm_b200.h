@@ -205,8 +205,12 @@ int slm_decode(slm_session* se, uint32_t first, size_t n, const slm_sampling* s,
                size_t n_recent, uint64_t* rng_state, uint32_t* out);
 
 /* Execution switches of a session (for tests and measurement):
- *   SLM_OPT_GRAPH    1 = replay the m = 1 step as a CUDA graph (default 1) */
+ *   SLM_OPT_GRAPH    1 = replay the m = 1 step as a CUDA graph (default 1)
+ *   SLM_OPT_MEGA     1 = run the m = 1 step as one persistent kernel (default
+ *                    1 where the model allows it: head size 64, no global
+ *                    layers, damp 1; fails with SLM_ERR_INVALID otherwise) */
 #define SLM_OPT_GRAPH 1
+#define SLM_OPT_MEGA 2
 int slm_session_set(slm_session* se, int option, int64_t value);
 
 /* Counters of a session:
@@ -214,6 +218,8 @@ int slm_session_set(slm_session* se, int option, int64_t value);
  *   SLM_STAT_GRAPHS        step graphs captured so far */
 #define SLM_STAT_STEP_KERNELS 1
 #define SLM_STAT_GRAPHS 2
+#define SLM_STAT_MEGA 3    /* 1 when the persistent decode kernel is in use */
+#define SLM_STAT_PHASES 4  /* phases (grid barriers + 1) of that kernel's step */
 int slm_session_stat(const slm_session* se, int what, int64_t* out);
 
 #ifdef __cplusplus

@@ -34,6 +34,8 @@ _vp = _c.c_void_p
 _sz = _c.c_size_t
 
 SLM_OPT_GRAPH = 1
+SLM_OPT_MEGA = 2
+SLM_STAT_STEP_KERNELS, SLM_STAT_GRAPHS, SLM_STAT_MEGA, SLM_STAT_PHASES = 1, 2, 3, 4
 SIZE_MAX = (1 << 64) - 1
 
 
@@ -427,6 +429,14 @@ class Session:
 
     def set_graph(self, on: bool) -> None:
         _check(lib().slm_session_set(self._h, SLM_OPT_GRAPH, 1 if on else 0))
+
+    def set_mega(self, on: bool) -> None:
+        """Run m = 1 steps as one persistent kernel (where the model allows it)."""
+        _check(lib().slm_session_set(self._h, SLM_OPT_MEGA, 1 if on else 0))
+
+    @property
+    def mega(self) -> bool:
+        return self.stat(SLM_STAT_MEGA) == 1
 
     def feed(self, ids, limit: int = CHUNK) -> None:
         ids = _u32(ids)

@@ -1,0 +1,783 @@
+// The m = 1 token step as one persistent, warp-specialised kernel.
+//
+// Everything a decode step reads from HBM — the weights, the old entries of
+// the sliding-window rings and the recurrent GLA state — is fixed for the
+// whole step; only small activation vectors (x, q, y, mid: a few KB) flow
+// from phase to phase.  So one producer warp per CTA walks the step's static
+// tiles in order and streams them into a 4-stage shared-memory ring with
+// cp.async.bulk (TMA bulk copies, mbarrier completion), never waiting for
+// the grid barriers that separate phases; eight consumer warps wait at each
+// barrier, rebuild the phase's input vector on chip (RMSNorm, loop input,
+// embedding) and consume the tiles.  HBM keeps streaming the next phases'
+// weights while the consumers cross a barrier.
+//
+// Phases follow the reference's block (src/model.rs:400-560) and advance
+// (src/model.rs:563-640) for one token:
+//   S block: [norm1 + qkv + rope + ring store] [window attention, split over
+//            positions, merged by the last arriving CTA of each head]
+//            [o + residual] [norm2 + up + silu] [down + residual]
+//   L block: [norm1 + qkvg + decay] [GLA: l2norm, state update, q·S,
+//            head_norm, silu gate] [o + residual] [norm2 + up] [down]
+//   glue:    embedding in the first prologue, inject after the prelude, the
+//            loop input (s + e + loop_embed[r]) in the first core prologue,
+//            norm_f + tied logits + greedy arg-max at the end.
+// Every wait (mbarrier, grid barrier) is bounded: past ~2 s the kernel sets
+// bit 8 of the error word and returns.
+#include "common.cuh"
+#include "kernels.cuh"
+#include "mega.cuh"
+
+namespace slm {
+namespace mega {
+
+namespace {
+
+__device__ __forceinline__ uint32_t saddr(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ void mbar_init(uint64_t* b, unsigned count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(saddr(b)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* b, unsigned bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(saddr(b)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* b) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(saddr(b)) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* b, unsigned parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(saddr(b)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, unsigned bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   saddr(dst)),
+               "l"(src), "r"(bytes), "r"(saddr(bar))
+               : "memory");
+}
+__device__ __forceinline__ unsigned long long now_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+__device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release(unsigned* p, unsigned v) {
+  asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ int ld_volatile(const int* p) { return *(const volatile int*)p; }
+__device__ __forceinline__ void consumers_sync() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
+// Barrier of the 256 consumer threads that also ANDs a flag over them, so a
+// failed wait in any thread is seen by all of them at the same point.
+__device__ __forceinline__ int consumers_and(int v) {
+  int r;
+  asm volatile(
+      "{\n .reg .pred p, q;\n setp.ne.s32 p, %1, 0;\n bar.red.and.pred q, 1, 256, p;\n selp.s32 %0, 1, 0, q;\n}\n"
+      : "=r"(r)
+      : "r"(v)
+      : "memory");
+  return r;
+}
+
+constexpr unsigned long long kWaitNs = 2000000000ull;  // 2 s per wait
+
+// Bounded wait on an mbarrier phase; false (and the error bit) on expiry or
+// when another CTA has already failed.
+__device__ bool wait_mbar(uint64_t* b, unsigned parity, int* err) {
+  if (mbar_try_wait(b, parity)) return true;
+  unsigned long long t0 = now_ns();
+  for (unsigned it = 1;; it++) {
+    if (mbar_try_wait(b, parity)) return true;
+    if ((it & 63) == 0) {
+      if (ld_volatile(err) & 8) return false;
+      if (now_ns() - t0 > kWaitNs) {
+        atomicOr(err, 8);
+        return false;
+      }
+    }
+  }
+}
+
+__device__ __forceinline__ uint32_t total_key(float f) {
+  uint32_t u = __float_as_uint(f + 0.0f);  // -0 → +0: equal values compare equal
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+// ---------------------------------------------------------------------------
+// Tile walk shared by the producer and the consumers
+// ---------------------------------------------------------------------------
+
+// Logical outputs per tile of a GEMV phase.
+__device__ __forceinline__ int tile_outs(const Phase& ph) {
+  int rows = kStageBytes / (ph.cols * 4);
+  if (rows > 16) rows = 16;
+  bool pair = ph.out_mode == OUT_SILU || ph.out_mode == OUT_ROPE;
+  return pair ? rows / 2 : rows;
+}
+
+__device__ __forceinline__ bool is_pair(const Phase& ph) {
+  return ph.out_mode == OUT_SILU || ph.out_mode == OUT_ROPE;
+}
+
+// First weight row of logical output o (and its partner) of segment s.
+__device__ __forceinline__ void out_rows(const Phase& ph, const Segment& sg, int o, int d, int* r0, int* r1) {
+  if (ph.out_mode == OUT_ROPE) {
+    int sec = o / (d / 2), rem = o % (d / 2), h = rem / 32, j = rem % 32;
+    *r0 = sec * d + h * kDH + j;
+    *r1 = *r0 + 32;
+  } else if (ph.out_mode == OUT_SILU) {
+    *r0 = o;
+    *r1 = o + sg.rows;
+  } else {
+    *r0 = o;
+    *r1 = -1;
+  }
+}
+
+// Item i of a GEMV phase → segment and logical output range.
+__device__ __forceinline__ void gemv_item(const Phase& ph, int i, int* seg, int* o0, int* o1) {
+  int s = 0;
+  if (ph.nseg > 1 && i >= ph.seg[0].items) {
+    i -= ph.seg[0].items;
+    s = 1;
+  }
+  const Segment& sg = ph.seg[s];
+  *seg = s;
+  *o0 = i * sg.per_item;
+  *o1 = min(sg.rows, *o0 + sg.per_item);
+}
+
+// Window range of the step's query and this split's slice of old positions.
+__device__ __forceinline__ void attn_slice(const Phase& ph, long long pos, int s, long long* a, long long* b) {
+  long long lo = ph.window > 0 && pos > ph.window - 1 ? pos - (ph.window - 1) : 0;
+  long long count = pos - lo;  // old positions (the current one is added by the last split)
+  long long chunk = (count + ph.splits - 1) / ph.splits;
+  *a = lo + (long long)s * chunk;
+  *b = min(pos, *a + chunk);
+  if (*b < *a) *b = *a;
+}
+
+struct Smem {
+  uint64_t full[kStages], empty[kStages];
+  float xin[kMaxCols];
+  float acc[2][kMaxItemOut];
+  float part[16][8];
+  float red[32];
+  float wsm[kConsumerWarps][kDH + 2];
+  float vec[4][kDH];
+  float yp[4][kDH];
+  unsigned long long best;
+  int flag;
+};
+
+// ---------------------------------------------------------------------------
+// Producer: one lane walks every tile of every phase in order.
+// ---------------------------------------------------------------------------
+__device__ void producer(const Plan& P, Smem& sm, char* ring, long long pos) {
+  unsigned k = 0;  // tiles issued
+  const int G = gridDim.x, me = blockIdx.x, d = P.d;
+  bool ok = true;
+  auto acquire = [&](unsigned bytes) -> char* {
+    int s = k % kStages;
+    if (k >= (unsigned)kStages && !wait_mbar(&sm.empty[s], ((k / kStages) - 1) & 1, P.err)) {
+      ok = false;
+      return nullptr;
+    }
+    mbar_expect_tx(&sm.full[s], bytes);
+    return ring + (size_t)s * kStageBytes;
+  };
+  for (int p = 0; p < P.nphases && ok; p++) {
+    const Phase& ph = P.phases[p];
+    for (int i = me; i < ph.items && ok; i += G) {
+      if (ph.kind == PH_GEMV) {
+        int s, o0, o1;
+        gemv_item(ph, i, &s, &o0, &o1);
+        const Segment& sg = ph.seg[s];
+        const int T = tile_outs(ph);
+        const unsigned rowb = (unsigned)ph.cols * 4;
+        for (int t0 = o0; t0 < o1 && ok; t0 += T) {
+          int n = min(T, o1 - t0);
+          int r0, r1;
+          out_rows(ph, sg, t0, d, &r0, &r1);
+          unsigned bytes = (unsigned)n * rowb * (is_pair(ph) ? 2 : 1);
+          char* dst = acquire(bytes);
+          if (!dst) break;
+          uint64_t* fb = &sm.full[k % kStages];
+          bulk_g2s(dst, sg.w + (size_t)r0 * ph.cols, n * rowb, fb);
+          if (is_pair(ph)) bulk_g2s(dst + (size_t)n * rowb, sg.w + (size_t)r1 * ph.cols, n * rowb, fb);
+          k++;
+        }
+      } else if (ph.kind == PH_ATTN) {
+        int h = i / ph.splits, s = i % ph.splits;
+        long long a, b;
+        attn_slice(ph, pos, s, &a, &b);
+        const float* kb = ph.kc + (size_t)h * ph.cap * kDH;
+        const float* vb = ph.vc + (size_t)h * ph.cap * kDH;
+        for (long long t0 = a; t0 < b && ok; t0 += kAttnTile) {
+          int n = (int)min((long long)kAttnTile, b - t0);
+          char* dst = acquire((unsigned)n * kDH * 4 * 2);
+          if (!dst) break;
+          uint64_t* fb = &sm.full[k % kStages];
+          long long slot = t0 % ph.cap;
+          int n1 = (int)min((long long)n, ph.cap - slot);
+          bulk_g2s(dst, kb + slot * kDH, n1 * kDH * 4, fb);
+          bulk_g2s(dst + kAttnTile * kDH * 4, vb + slot * kDH, n1 * kDH * 4, fb);
+          if (n1 < n) {
+            bulk_g2s(dst + (size_t)n1 * kDH * 4, kb, (n - n1) * kDH * 4, fb);
+            bulk_g2s(dst + kAttnTile * kDH * 4 + (size_t)n1 * kDH * 4, vb, (n - n1) * kDH * 4, fb);
+          }
+          k++;
+        }
+      } else {  // PH_GLA: the head's state
+        char* dst = acquire(kDH * kDH * 4);
+        if (!dst) break;
+        bulk_g2s(dst, ph.state + (size_t)i * kDH * kDH, kDH * kDH * 4, &sm.full[k % kStages]);
+        k++;
+      }
+    }
+  }
+  // Drain: every copy issued must land before the CTA may exit.
+  unsigned first = k > (unsigned)kStages ? k - kStages : 0;
+  for (unsigned j = first; j < k; j++) wait_mbar(&sm.full[j % kStages], (j / kStages) & 1, P.err);
+}
+
+// ---------------------------------------------------------------------------
+// Consumers
+// ---------------------------------------------------------------------------
+
+struct Cons {
+  const Plan& P;
+  Smem& sm;
+  char* ring;
+  unsigned k = 0;  // tiles consumed
+  bool ok = true;
+  int tid, warp, lane;
+  long long pos;
+
+  __device__ Cons(const Plan& p, Smem& s, char* r, long long ps) : P(p), sm(s), ring(r), pos(ps) {
+    tid = threadIdx.x;
+    warp = tid >> 5;
+    lane = tid & 31;
+  }
+
+  __device__ const float* take() {
+    int s = k % kStages;
+    int got = wait_mbar(&sm.full[s], (k / kStages) & 1, P.err) ? 1 : 0;
+    if (!consumers_and(got)) {
+      ok = false;
+      return nullptr;
+    }
+    return reinterpret_cast<const float*>(ring + (size_t)s * kStageBytes);
+  }
+  __device__ void release() {
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&sm.empty[k % kStages]);
+    k++;
+  }
+
+  // Grid barrier (consumer thread 0 for the CTA), generation counted.
+  __device__ void grid_sync() {
+    consumers_sync();
+    if (tid == 0) {
+      unsigned* bar = P.bar;
+      unsigned gen = ld_acquire(&bar[1]);
+      __threadfence();
+      unsigned arrived = atomicAdd(&bar[0], 1u);
+      if (arrived == gridDim.x - 1) {
+        atomicExch(&bar[0], 0u);
+        __threadfence();
+        st_release(&bar[1], gen + 1);
+      } else {
+        unsigned long long t0 = now_ns();
+        for (unsigned it = 0; ld_acquire(&bar[1]) == gen; it++) {
+          if ((it & 31) == 31) {
+            if (ld_volatile(P.err) & 8) {
+              sm.flag = 1;
+              break;
+            }
+            if (now_ns() - t0 > kWaitNs) {
+              atomicOr(P.err, 8);
+              sm.flag = 1;
+              break;
+            }
+          }
+        }
+      }
+      __threadfence();
+    }
+    consumers_sync();
+    if (sm.flag) ok = false;
+  }
+
+  // Input vector of a GEMV phase into sm.xin.
+  __device__ void prologue(const Phase& ph) {
+    const int n = ph.cols;
+    if (ph.in_mode == IN_PLAIN) {
+      for (int e = tid; e < n; e += 256) sm.xin[e] = __ldcg(ph.in_a + e);
+      consumers_sync();
+      return;
+    }
+    const float* src = ph.in_a;
+    float ss = 0.0f;
+    for (int e = tid; e < n; e += 256) {
+      float v;
+      if (ph.in_mode == IN_EMBED_RMS) {
+        v = __ldg(P.embed + (size_t)P.ids[0] * n + e);
+        if (blockIdx.x == 0) {
+          P.e0[e] = v;
+          P.x0[e] = v;
+        }
+      } else if (ph.in_mode == IN_LOOP_RMS) {
+        v = (__ldcg(ph.in_a + e) + __ldcg(ph.in_b + e)) + __ldg(ph.in_c + e);
+        if (blockIdx.x == 0) ph.xout[e] = v;
+      } else {
+        v = __ldcg(src + e);
+      }
+      sm.xin[e] = v;
+      ss = fmaf(v, v, ss);
+    }
+    ss = warp_sum(ss);
+    if (lane == 0) sm.red[warp] = ss;
+    consumers_sync();
+    float t = 0.0f;
+#pragma unroll
+    for (int w = 0; w < kConsumerWarps; w++) t += sm.red[w];
+    const float r = 1.0f / sqrtf(t / (float)n + P.eps);
+    for (int e = tid; e < n; e += 256) sm.xin[e] = sm.xin[e] * r * __ldg(ph.norm_w + e);
+    consumers_sync();
+  }
+
+  // Dot products of one tile: `rows` weight rows of `cols` in smem → sm.acc.
+  __device__ void gemv_tile(const float* w, int rows, int cols, int acc_base, int pair_n, int n) {
+    // rows ≤ 16.  With fewer than 8 rows, warps split the columns.
+    const int seg = rows >= 8 ? 1 : 8 / rows;
+    const int span = cols / seg;
+    const float4* x4 = reinterpret_cast<const float4*>(sm.xin);
+    for (int r = warp % (rows >= 8 ? 8 : rows); r < rows; r += (rows >= 8 ? 8 : rows)) {
+      const int sgi = rows >= 8 ? 0 : warp / rows;
+      if (rows < 8 && sgi >= seg) break;
+      const float4* w4 = reinterpret_cast<const float4*>(w + (size_t)r * cols + sgi * span);
+      const int c0 = sgi * span / 4;
+      float a = 0.0f;
+#pragma unroll 4
+      for (int c = lane; c < span / 4; c += 32) a = dot4(w4[c], x4[c0 + c], a);
+      a = warp_sum(a);
+      if (lane == 0) {
+        if (seg == 1) {
+          // row r of the tile → logical output and pair half
+          int half = pair_n ? r / n : 0, o = pair_n ? r % n : r;
+          sm.acc[half][acc_base + o] = a;
+        } else {
+          sm.part[r][sgi] = a;
+        }
+      }
+    }
+    if (seg > 1) {
+      consumers_sync();
+      if (tid < rows) {
+        float a = 0.0f;
+        for (int g = 0; g < seg; g++) a += sm.part[tid][g];
+        int half = pair_n ? tid / n : 0, o = pair_n ? tid % n : tid;
+        sm.acc[half][acc_base + o] = a;
+      }
+    }
+  }
+
+  __device__ void gemv_phase(const Phase& ph, int item_phase_index) {
+    const int G = gridDim.x;
+    bool any = blockIdx.x < ph.items;
+    if (!any) return;
+    prologue(ph);
+    const int T = tile_outs(ph);
+    const bool pair = is_pair(ph);
+    for (int i = blockIdx.x; i < ph.items && ok; i += G) {
+      int s, o0, o1;
+      gemv_item(ph, i, &s, &o0, &o1);
+      const Segment& sg = ph.seg[s];
+      for (int t0 = o0; t0 < o1; t0 += T) {
+        int n = min(T, o1 - t0);
+        const float* w = take();
+        if (!w) return;
+        gemv_tile(w, pair ? 2 * n : n, ph.cols, t0 - o0, pair ? 1 : 0, n);
+        consumers_sync();  // every warp done with the stage and sm.acc written
+        release();
+      }
+      epilogue(ph, sg, o0, o1, i);
+      consumers_sync();
+    }
+    (void)item_phase_index;
+  }
+
+  __device__ void epilogue(const Phase& ph, const Segment& sg, int o0, int o1, int item) {
+    const int n = o1 - o0;
+    if (ph.out_mode == OUT_ROPE) {
+      const int d = P.d;
+      for (int t = tid; t < n; t += 256) {
+        int o = o0 + t;
+        int sec = o / (d / 2), rem = o % (d / 2), h = rem / 32, j = rem % 32;
+        float a = sm.acc[0][t], b = sm.acc[1][t];
+        size_t slot = (size_t)(pos % ph.cap);
+        if (sec < 2) {
+          float ang = (float)pos * __ldg(ph.inv_freq + j);
+          float sn, cs;
+          sincosf(ang, &sn, &cs);
+          float u = a * cs - b * sn, v = a * sn + b * cs;
+          if (sec == 0) {
+            ph.q[h * kDH + j] = u;
+            ph.q[h * kDH + 32 + j] = v;
+          } else {
+            float* kr = ph.kc + ((size_t)h * ph.cap + slot) * kDH;
+            kr[j] = u;
+            kr[32 + j] = v;
+          }
+        } else {
+          float* vr = ph.vc + ((size_t)h * ph.cap + slot) * kDH;
+          vr[j] = a;
+          vr[32 + j] = b;
+        }
+      }
+      return;
+    }
+    for (int t = tid; t < n; t += 256) {
+      int o = o0 + t;
+      float a = sm.acc[0][t];
+      if (ph.out_mode == OUT_ADD)
+        sg.out[o] = __ldcg(sg.out + o) + a;
+      else if (ph.out_mode == OUT_SILU)
+        sg.out[o] = silu_mul(a, sm.acc[1][t]);
+      else
+        sg.out[o] = a;
+    }
+    if (ph.out_mode == OUT_LOGITS) logits_argmax(sg, o0, n, item, ph.items);
+  }
+
+  __device__ void logits_argmax(const Segment& sg, int o0, int n, int item, int items) {
+    unsigned long long best = 0;
+    for (int t = tid; t < n; t += 256) {
+      float v = sm.acc[0][t];
+      if (v != v) continue;
+      unsigned long long c = ((unsigned long long)total_key(v) << 32) | (0xFFFFFFFFu - (uint32_t)(o0 + t));
+      if (c > best) best = c;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      unsigned long long other = __shfl_xor_sync(0xffffffffu, best, o);
+      if (other > best) best = other;
+    }
+    if (tid == 0) sm.best = 0;
+    consumers_sync();
+    if (lane == 0 && best) atomicMax(&sm.best, best);
+    consumers_sync();
+    if (tid == 0) {
+      P.arg_part[item] = sm.best;
+      __threadfence();
+      unsigned prev = atomicAdd(P.arg_count, 1u);
+      sm.flag = prev == (unsigned)items - 1 ? 2 : 0;
+    }
+    consumers_sync();
+    if (sm.flag == 2) {
+      __threadfence();
+      unsigned long long b = 0;
+      for (int j = tid; j < items; j += 256) {
+        unsigned long long c = __ldcg(P.arg_part + j);
+        if (c > b) b = c;
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        unsigned long long other = __shfl_xor_sync(0xffffffffu, b, o);
+        if (other > b) b = other;
+      }
+      consumers_sync();
+      if (tid == 0) sm.best = 0;
+      consumers_sync();
+      if (lane == 0 && b) atomicMax(&sm.best, b);
+      consumers_sync();
+      if (tid == 0) {
+        uint32_t id = sm.best ? 0xFFFFFFFFu - (uint32_t)(sm.best & 0xFFFFFFFFu) : 0;
+        if (P.greedy) {
+          P.next_id[0] = id;
+          unsigned at = *P.out_index;
+          if (P.out_ids) P.out_ids[at] = id;
+          if (P.hist) P.hist[P.hist_base + at] = id;
+          *P.out_index = at + 1;
+        }
+        *P.arg_count = 0;
+        P.pos[0] = pos + 1;  // every CTA read the position at entry
+        sm.flag = 0;
+      }
+      consumers_sync();
+    }
+  }
+
+  // Window attention for head h, split s (one query at `pos`).
+  __device__ void attn_item(const Phase& ph, int item) {
+    const int h = item / ph.splits, s = item % ph.splits;
+    const int sub = lane & 7, grp = lane >> 3;
+    // Lane `sub` of a group owns dims sub*4 .. sub*4+3 and 32+sub*4 .. 32+sub*4+3,
+    // so a group reads each cached row as two contiguous 128-byte runs.
+    const int d0 = sub * 4, d1 = 32 + sub * 4;
+    float qv[8];
+    {
+      const float* qp = ph.q + h * kDH;
+#pragma unroll
+      for (int e = 0; e < 4; e++) qv[e] = __ldcg(qp + d0 + e), qv[4 + e] = __ldcg(qp + d1 + e);
+    }
+    float mx = -INFINITY, l = 0.0f, acc[8];
+#pragma unroll
+    for (int e = 0; e < 8; e++) acc[e] = 0.0f;
+    auto fold = [&](const float* kr) {
+      float4 k0 = *reinterpret_cast<const float4*>(kr + d0), k1 = *reinterpret_cast<const float4*>(kr + d1);
+      float sc = qv[0] * k0.x + qv[1] * k0.y + qv[2] * k0.z + qv[3] * k0.w + qv[4] * k1.x + qv[5] * k1.y +
+                 qv[6] * k1.z + qv[7] * k1.w;
+      sc += __shfl_xor_sync(0xffffffffu, sc, 1);
+      sc += __shfl_xor_sync(0xffffffffu, sc, 2);
+      sc += __shfl_xor_sync(0xffffffffu, sc, 4);
+      return sc * ph.scale;
+    };
+    auto update = [&](float sc, const float* vr) {
+      float M = fmaxf(mx, sc);
+      float corr = mx == -INFINITY ? 0.0f : expf(mx - M);
+      float pe = expf(sc - M);
+      l = l * corr + pe;
+      float4 v0 = *reinterpret_cast<const float4*>(vr + d0), v1 = *reinterpret_cast<const float4*>(vr + d1);
+      float vv[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+#pragma unroll
+      for (int e = 0; e < 8; e++) acc[e] = acc[e] * corr + pe * vv[e];
+      mx = M;
+    };
+    long long a, b;
+    attn_slice(ph, pos, s, &a, &b);
+    for (long long t0 = a; t0 < b; t0 += kAttnTile) {
+      const int n = (int)min((long long)kAttnTile, b - t0);
+      const float* tile = take();
+      if (!tile) return;
+      const float* Kt = tile;
+      const float* Vt = tile + kAttnTile * kDH;
+      // warp w: rows w*8 .. w*8+7; lane group: rows +grp and +4+grp.
+#pragma unroll
+      for (int half = 0; half < 2; half++) {
+        int r = warp * 8 + half * 4 + grp;
+        bool valid = r < n;
+        int rr = valid ? r : 0;
+        float sc = fold(Kt + rr * kDH);
+        if (valid) update(sc, Vt + rr * kDH);
+      }
+      consumers_sync();
+      release();
+    }
+    if (s == ph.splits - 1 && warp == 0 && grp == 0) {
+      // The step's own position, stored by the qkv phase.
+      size_t slot = (size_t)(pos % ph.cap);
+      const float* kr = ph.kc + ((size_t)h * ph.cap + slot) * kDH;
+      const float* vr = ph.vc + ((size_t)h * ph.cap + slot) * kDH;
+      float kk[8], vv[8];
+#pragma unroll
+      for (int e = 0; e < 4; e++) {
+        kk[e] = __ldcg(kr + d0 + e), kk[4 + e] = __ldcg(kr + d1 + e);
+        vv[e] = __ldcg(vr + d0 + e), vv[4 + e] = __ldcg(vr + d1 + e);
+      }
+      float sc = 0.0f;
+#pragma unroll
+      for (int e = 0; e < 8; e++) sc += qv[e] * kk[e];
+      sc += __shfl_xor_sync(0x000000ffu, sc, 1);
+      sc += __shfl_xor_sync(0x000000ffu, sc, 2);
+      sc += __shfl_xor_sync(0x000000ffu, sc, 4);
+      sc *= ph.scale;
+      float M = fmaxf(mx, sc);
+      float corr = mx == -INFINITY ? 0.0f : expf(mx - M);
+      float pe = expf(sc - M);
+      l = l * corr + pe;
+#pragma unroll
+      for (int e = 0; e < 8; e++) acc[e] = acc[e] * corr + pe * vv[e];
+      mx = M;
+    }
+    // Merge the four lane groups of each warp, then the warps.
+#pragma unroll
+    for (int o = 8; o < 32; o <<= 1) {
+      float om = __shfl_xor_sync(0xffffffffu, mx, o), ol = __shfl_xor_sync(0xffffffffu, l, o);
+      float M = fmaxf(mx, om);
+      float ca = mx == -INFINITY ? 0.0f : expf(mx - M), cb = om == -INFINITY ? 0.0f : expf(om - M);
+      l = l * ca + ol * cb;
+#pragma unroll
+      for (int e = 0; e < 8; e++) acc[e] = acc[e] * ca + __shfl_xor_sync(0xffffffffu, acc[e], o) * cb;
+      mx = M;
+    }
+    if (grp == 0) {
+#pragma unroll
+      for (int e = 0; e < 4; e++) sm.wsm[warp][d0 + e] = acc[e], sm.wsm[warp][d1 + e] = acc[4 + e];
+      if (sub == 0) sm.wsm[warp][kDH] = mx, sm.wsm[warp][kDH + 1] = l;
+    }
+    consumers_sync();
+    float* out = ph.part + (size_t)item * (kDH + 2);
+    if (tid < kDH) {
+      float m0 = sm.wsm[0][kDH], l0 = sm.wsm[0][kDH + 1], a0 = sm.wsm[0][tid];
+      for (int w = 1; w < kConsumerWarps; w++) {
+        float om = sm.wsm[w][kDH], ol = sm.wsm[w][kDH + 1];
+        float M = fmaxf(m0, om);
+        float ca = m0 == -INFINITY ? 0.0f : expf(m0 - M), cb = om == -INFINITY ? 0.0f : expf(om - M);
+        l0 = l0 * ca + ol * cb;
+        a0 = a0 * ca + sm.wsm[w][tid] * cb;
+        m0 = M;
+      }
+      out[tid] = a0;
+      if (tid == 0) out[kDH] = m0, out[kDH + 1] = l0;
+    }
+    consumers_sync();
+    if (tid == 0) {
+      __threadfence();
+      unsigned prev = atomicAdd(ph.counters + h, 1u);
+      sm.flag = prev == (unsigned)ph.splits - 1 ? 2 : 0;
+    }
+    consumers_sync();
+    if (sm.flag == 2) {
+      __threadfence();
+      if (tid < kDH) {
+        const float* p0 = ph.part + (size_t)h * ph.splits * (kDH + 2);
+        float M = -INFINITY;
+        for (int j = 0; j < ph.splits; j++) M = fmaxf(M, __ldcg(p0 + j * (kDH + 2) + kDH));
+        float L = 0.0f, A = 0.0f;
+        if (M != -INFINITY)
+          for (int j = 0; j < ph.splits; j++) {
+            float mj = __ldcg(p0 + j * (kDH + 2) + kDH);
+            if (mj == -INFINITY) continue;
+            float c = expf(mj - M);
+            L += __ldcg(p0 + j * (kDH + 2) + kDH + 1) * c;
+            A += __ldcg(p0 + j * (kDH + 2) + tid) * c;
+          }
+        ph.y[h * kDH + tid] = L > 0.0f ? A / L : 0.0f;
+      }
+      if (tid == 0) {
+        ph.counters[h] = 0;
+        sm.flag = 0;
+      }
+      consumers_sync();
+    }
+  }
+
+  // GLA for head h: l2norm q, k; S = d·S + kᵀv; y = q·S; head_norm; silu gate.
+  __device__ void gla_item(const Phase& ph, int h) {
+    const int d = P.d;
+    const float* row = ph.mix;  // [q | k | v | g], each d wide
+    if (tid < kDH) {
+      sm.vec[0][tid] = __ldcg(row + h * kDH + tid);
+      sm.vec[1][tid] = __ldcg(row + d + h * kDH + tid);
+      sm.vec[2][tid] = __ldcg(row + 2 * d + h * kDH + tid);
+      sm.vec[3][tid] = __ldcg(row + 3 * d + h * kDH + tid);
+    }
+    consumers_sync();
+    if (warp < 2) {  // warp 0: |q|, warp 1: |k|
+      float a = sm.vec[warp][lane], b = sm.vec[warp][lane + 32];
+      float ss = warp_sum(a * a + b * b);
+      float r = 1.0f / fmaxf(sqrtf(ss), 1e-12f);
+      sm.vec[warp][lane] = a * r;
+      sm.vec[warp][lane + 32] = b * r;
+    }
+    const float dcy = 1.0f / (1.0f + expf(__ldcg(ph.dec + h) + __ldg(ph.bias + h)));
+    float* tile = const_cast<float*>(take());
+    consumers_sync();
+    if (!tile) return;
+    const int b = tid & 63, qa = tid >> 6;
+    const float vb = sm.vec[2][b];
+    float yp = 0.0f;
+#pragma unroll
+    for (int a = qa * 16; a < qa * 16 + 16; a++) {
+      float s = dcy * tile[a * kDH + b] + sm.vec[1][a] * vb;
+      tile[a * kDH + b] = s;
+      yp = fmaf(sm.vec[0][a], s, yp);
+    }
+    sm.yp[qa][b] = yp;
+    consumers_sync();
+    // State back to HBM (coalesced), then the gated, normalised output.
+    float* Sg = ph.state + (size_t)h * kDH * kDH;
+    for (int e = tid; e < kDH * kDH; e += 256) Sg[e] = tile[e];
+    if (warp < 2) {
+      int bb = tid;
+      float y = ((sm.yp[0][bb] + sm.yp[1][bb]) + sm.yp[2][bb]) + sm.yp[3][bb];
+      float ss = warp_sum(y * y);
+      if (lane == 0) sm.red[warp] = ss;
+      asm volatile("bar.sync 2, 64;" ::: "memory");
+      float tot = sm.red[0] + sm.red[1];
+      float r = 1.0f / sqrtf(tot / (float)kDH + P.eps);
+      ph.y[h * kDH + bb] = silu_mul(sm.vec[3][bb], y * r * __ldg(ph.hnw + bb));
+    }
+    consumers_sync();
+    release();
+  }
+
+  __device__ void run(const Plan& Pl) {
+    for (int p = 0; p < Pl.nphases && ok; p++) {
+      const Phase& ph = Pl.phases[p];
+      if (p > 0) {
+        grid_sync();
+        if (!ok) return;
+      }
+      if (ph.kind == PH_GEMV) {
+        gemv_phase(ph, p);
+      } else if (ph.kind == PH_ATTN) {
+        for (int i = blockIdx.x; i < ph.items && ok; i += gridDim.x) attn_item(ph, i);
+      } else {
+        for (int i = blockIdx.x; i < ph.items && ok; i += gridDim.x) gla_item(ph, i);
+      }
+    }
+  }
+};
+
+__global__ void __launch_bounds__(kThreads, 1) k_decode_mega(const Plan* __restrict__ plan) {
+  extern __shared__ __align__(1024) char smem_raw[];
+  const Plan& P = *plan;
+  Smem& sm = *reinterpret_cast<Smem*>(smem_raw);
+  char* ring = smem_raw + ((sizeof(Smem) + 1023) / 1024) * 1024;
+  const long long pos = P.pos[0];
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; s++) {
+      mbar_init(&sm.full[s], 1);
+      mbar_init(&sm.empty[s], kConsumerWarps);
+    }
+    sm.flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+  if (threadIdx.x >= kConsumerWarps * 32) {
+    if (threadIdx.x == kConsumerWarps * 32) producer(P, sm, ring, pos);
+    return;
+  }
+  Cons c(P, sm, ring, pos);
+  c.run(P);
+}
+
+}  // namespace
+
+size_t smem_bytes() { return ((sizeof(Smem) + 1023) / 1024) * 1024 + (size_t)kStages * kStageBytes; }
+
+void prepare() {
+  SLM_CUDA(cudaFuncSetAttribute(k_decode_mega, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_bytes()));
+}
+
+int blocks_per_sm() {
+  int n = 0;
+  SLM_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k_decode_mega, kThreads, smem_bytes()));
+  return n;
+}
+
+void launch(const Plan* plan_dev, int grid, cudaStream_t st) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem_bytes();
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  SLM_CUDA(cudaLaunchKernelEx(&cfg, k_decode_mega, plan_dev));
+}
+
+}  // namespace mega
+}  // namespace slm

@@ -49,7 +49,7 @@ void gla(const GlaArgs& a, cudaStream_t st);
 
 struct SampleArgs {
   const float* logits;
-  float* work;  // vocab floats
+  float* work;  // 3·vocab words: logits after the penalty, sorted weights, sorted ids
   int vocab;
   float temperature, top_p, penalty;
   uint32_t top_k, window;

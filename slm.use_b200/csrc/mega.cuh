@@ -1,0 +1,96 @@
+// Plan of the persistent decode kernel (decode_mega.cu): the m = 1 token step
+// as a list of phases separated by grid barriers.  Built once per session on
+// the host (model.cpp) and read by every CTA.
+#pragma once
+
+#include <stdint.h>
+
+namespace slm {
+namespace mega {
+
+constexpr int kConsumerWarps = 8;
+constexpr int kThreads = (kConsumerWarps + 1) * 32;  // + one producer warp
+constexpr int kStages = 4;
+constexpr int kStageBytes = 48 * 1024;
+constexpr int kMaxCols = 3072;       // widest GEMV input held on chip
+constexpr int kMaxItemOut = 256;     // logical outputs per GEMV item
+constexpr int kDH = 64;              // head size of the kernel
+constexpr int kAttnTile = 64;        // cache positions per attention tile
+
+enum PhaseKind : int { PH_GEMV = 0, PH_ATTN = 1, PH_GLA = 2 };
+
+// How a GEMV phase forms its input vector.
+enum InMode : int {
+  IN_PLAIN = 0,      // v = a
+  IN_RMS = 1,        // v = rms(a)·w
+  IN_EMBED_RMS = 2,  // x = embed[ids[0]] (written to a and b), v = rms(x)·w
+  IN_LOOP_RMS = 3,   // x = (a + b) + c, written to xout; v = rms(x)·w
+};
+
+// What a GEMV phase does with its dot products.
+enum OutMode : int {
+  OUT_STORE = 0,   // y[r] = acc
+  OUT_ADD = 1,     // y[r] += acc (the residual)
+  OUT_SILU = 2,    // pairs (j, j + n): y[j] = silu(acc_j)·acc_{j+n}
+  OUT_ROPE = 3,    // S qkv: rotate q, k pairs (j, j+32) of each head, write q, store k, v in the ring
+  OUT_LOGITS = 4,  // y[r] = acc and a per-item arg-max partial
+};
+
+struct Segment {
+  const float* w;   // weight rows, row-major, `cols` wide
+  int rows;         // logical outputs (pairs count for SILU / ROPE)
+  int per_item;     // logical outputs per item
+  int items;
+  float* out;       // output (OUT_STORE/ADD/SILU/LOGITS)
+};
+
+struct Phase {
+  int kind;
+  // GEMV
+  int cols;
+  int in_mode, out_mode;
+  const float *in_a, *in_b, *in_c, *norm_w;
+  float* xout;
+  int nseg;
+  Segment seg[2];
+  // OUT_ROPE / ATTN / GLA
+  float *q, *kc, *vc;  // q buffer and the layer's ring (ATTN, ROPE)
+  long long cap, window;
+  const float* inv_freq;
+  // ATTN: heads × splits items; partials and per-head arrival counters
+  int heads, splits;
+  float* part;
+  unsigned* counters;
+  float* y;
+  float scale;
+  // GLA: state [heads][64][64], raw q|k|v|g rows in `mix`, decay in `dec`
+  float* state;
+  const float *mix, *dec, *bias, *hnw;
+  // items of the phase (all kinds)
+  int items;
+};
+
+struct Plan {
+  int nphases;
+  Phase* phases;       // device array
+  int d, heads, vocab;
+  float eps;
+  const float* embed;
+  const uint32_t* ids;  // ids[0]: the token of this step
+  float *e0, *x0;       // embedding outputs
+  long long* pos;       // position of this step (advanced at the end)
+  unsigned* arg_count;  // arrival counter of the logits arg-max
+  unsigned long long* arg_part;  // per-item arg-max partials
+  int greedy;           // 1: write the arg-max to next_id / out
+  uint32_t* next_id;
+  uint32_t* out_ids;    // out_ids[*out_index] = id, then ++*out_index
+  unsigned* out_index;
+  uint32_t* hist;       // optional history array (same index as out + hist_base)
+  unsigned long long hist_base;
+  unsigned* bar;        // grid barrier: [0] arrivals, [1] generation
+  int* err;             // error word: 8 = a bounded wait expired
+  long long spin_limit;
+};
+
+}  // namespace mega
+}  // namespace slm

@@ -15,6 +15,16 @@
 #include "common.cuh"
 #include "kernels.cuh"
 #include "loader.hpp"
+#include "mega.cuh"
+
+namespace slm {
+namespace mega {
+size_t smem_bytes();
+void prepare();
+int blocks_per_sm();
+void launch(const Plan* plan_dev, int grid, cudaStream_t st);
+}  // namespace mega
+}  // namespace slm
 
 namespace slm {
 
@@ -83,6 +93,14 @@ struct slm_session {
   bool capturing = false;
   int64_t step_kernels = 0;  // kernel nodes of the captured step
   int64_t graphs = 0;
+  // Persistent decode kernel (decode_mega.cu)
+  bool mega_ok = false, use_mega = false;
+  std::string mega_why;                  // why the kernel does not apply, if it does not
+  slm::mega::Plan plan_host{};
+  slm::mega::Plan* plan_dev = nullptr;
+  slm::mega::Phase* phases_dev = nullptr;
+  float* xc = nullptr;
+  int grid = 0;
 };
 
 namespace slm {
@@ -351,10 +369,165 @@ void advance(slm_session* se, size_t m, bool want_logits) {
   se->pos += m;
 }
 
+// Why the persistent decode kernel cannot run this model ("" if it can).
+std::string mega_unsupported(const slm_model* md) {
+  const Config& c = md->cfg;
+  if (c.dh() != (size_t)mega::kDH) return "head size is not 64";
+  if (c.d % 32 != 0 || c.d > (size_t)mega::kMaxCols) return "d_model must be a multiple of 32 and at most 3072";
+  if (md->hidden % 32 != 0 || md->hidden > (size_t)mega::kMaxCols) return "FFN width must be a multiple of 32, <= 3072";
+  if (c.damp != 1.0f) return "damp != 1";
+  if (c.prelude.empty()) return "no prelude block";
+  for (const std::string* part : {&c.prelude, &c.core, &c.coda})
+    if (part->find('G') != std::string::npos) return "global-attention layers";
+  return "";
+}
+
+// The m = 1 step as phases (decode_mega.cu), for this session's buffers.
+void build_plan(slm_session* se) {
+  using namespace mega;
+  slm_model* md = se->model;
+  const Config& c = md->cfg;
+  const int G = se->grid;
+  const int d = (int)c.d, H = (int)c.heads;
+  std::vector<Phase> ph;
+  auto per = [&](int rows, int items_wanted, int multiple) {
+    int p = (rows + items_wanted - 1) / items_wanted;
+    p = (p + multiple - 1) / multiple * multiple;
+    return std::min(p, kMaxItemOut / multiple * multiple);
+  };
+  auto seg = [&](const float* w, int rows, int p, float* out) {
+    Segment sg{};
+    sg.w = w, sg.rows = rows, sg.per_item = p, sg.items = (rows + p - 1) / p, sg.out = out;
+    return sg;
+  };
+  auto gemv = [&](int cols, int in_mode, const float* a, const float* b, const float* cc, const float* nw, float* xout,
+                  int out_mode, Segment s0) {
+    Phase p{};
+    p.kind = PH_GEMV;
+    p.cols = cols;
+    p.in_mode = in_mode, p.in_a = a, p.in_b = b, p.in_c = cc, p.norm_w = nw, p.xout = xout;
+    p.out_mode = out_mode;
+    p.nseg = 1;
+    p.seg[0] = s0;
+    p.items = s0.items;
+    return p;
+  };
+  const int splits = std::max(1, G / H);
+  const float scale = 1.0f / std::sqrt((float)c.dh());
+  // Attention partials (heads × splits × (dh + 2)) and per-head arrival counters.
+  float* attn_part = static_cast<float*>(alloc_zero(se, (size_t)H * splits * (kDH + 2) * sizeof(float)));
+  auto* attn_count = static_cast<unsigned*>(alloc_zero(se, (size_t)H * sizeof(unsigned)));
+  float* X0 = se->xa;
+  struct In {
+    int mode;
+    const float *a, *b, *c;
+    float* xout;
+  };
+  auto block = [&](const Block& b, LState& st, float* X, In in) {
+    const float* ia = in.mode == IN_RMS ? X : in.a;
+    if (b.kind == 'S') {
+      Phase p = gemv(d, in.mode, ia, in.b, in.c, b.norm1, in.xout, OUT_ROPE,
+                     seg(b.qkv.w, 3 * d / 2, per(3 * d / 2, G, 8), nullptr));
+      p.q = se->q, p.kc = st.k, p.vc = st.v, p.cap = (long long)st.cap, p.inv_freq = md->inv_freq;
+      ph.push_back(p);
+      Phase a{};
+      a.kind = PH_ATTN;
+      a.kc = st.k, a.vc = st.v, a.q = se->q, a.cap = (long long)st.cap, a.window = (long long)c.window;
+      a.heads = H, a.splits = splits, a.part = attn_part, a.counters = attn_count;
+      a.y = se->y, a.scale = scale, a.items = H * splits;
+      ph.push_back(a);
+    } else {
+      Phase p = gemv(d, in.mode, ia, in.b, in.c, b.norm1, in.xout, OUT_STORE,
+                     seg(b.qkvg.w, 4 * d, per(4 * d, std::max(1, G - 1), 1), se->mix));
+      p.nseg = 2;
+      p.seg[1] = seg(b.decay.w, H, per(H, 1, 1), se->dec);
+      p.items = p.seg[0].items + p.seg[1].items;
+      ph.push_back(p);
+      Phase g{};
+      g.kind = PH_GLA;
+      g.state = st.s, g.mix = se->mix, g.dec = se->dec, g.bias = b.bias, g.hnw = b.head_norm, g.y = se->y;
+      g.items = H;
+      ph.push_back(g);
+    }
+    ph.push_back(gemv(d, IN_PLAIN, se->y, nullptr, nullptr, nullptr, nullptr, OUT_ADD, seg(b.o.w, d, per(d, G, 1), X)));
+    const int F = (int)b.down.cols;
+    ph.push_back(gemv(d, IN_RMS, X, nullptr, nullptr, b.norm2, nullptr, OUT_SILU,
+                      seg(b.up.w, F, per(F, G, 1), se->mid)));
+    ph.push_back(gemv(F, IN_PLAIN, se->mid, nullptr, nullptr, nullptr, nullptr, OUT_ADD,
+                      seg(b.down.w, d, per(d, G, 1), X)));
+  };
+  for (size_t i = 0; i < md->prelude.size(); i++)
+    block(md->prelude[i], se->pre[i], X0, In{i == 0 ? IN_EMBED_RMS : IN_RMS, nullptr, nullptr, nullptr, nullptr});
+  float* X = X0;
+  if (md->looped) {
+    ph.push_back(gemv(d, IN_PLAIN, X0, nullptr, nullptr, nullptr, nullptr, OUT_STORE,
+                      seg(md->inject.w, d, per(d, G, 1), se->e_proj)));
+    const float* sbuf = X0;
+    for (size_t r = 0; r < se->loops; r++) {
+      float* xr = (r % 2 == 0) ? se->xb : se->xc;
+      for (size_t j = 0; j < md->core.size(); j++) {
+        In in = j == 0 ? In{IN_LOOP_RMS, sbuf, se->e_proj, md->loop_embed.w + r * c.d, xr}
+                       : In{IN_RMS, nullptr, nullptr, nullptr, nullptr};
+        block(md->core[j], se->core[r][j], xr, in);
+      }
+      sbuf = xr;
+    }
+    X = const_cast<float*>(sbuf);
+  }
+  for (size_t i = 0; i < md->coda.size(); i++)
+    block(md->coda[i], se->coda[i], X, In{IN_RMS, nullptr, nullptr, nullptr, nullptr});
+  ph.push_back(gemv(d, IN_RMS, X, nullptr, nullptr, md->norm_f, nullptr, OUT_LOGITS,
+                    seg(md->embed.w, (int)c.vocab, per((int)c.vocab, G, 1), se->logits)));
+  const int logit_items = ph.back().items;
+
+  // Device memory of the plan: phases, arg-max partials, counters, barrier words.
+  se->phases_dev = static_cast<Phase*>(alloc_zero(se, ph.size() * sizeof(Phase)));
+  SLM_CUDA(cudaMemcpyAsync(se->phases_dev, ph.data(), ph.size() * sizeof(Phase), cudaMemcpyHostToDevice,
+                           se->ctx->stream));
+  auto* words = static_cast<unsigned*>(alloc_zero(se, 64 * sizeof(unsigned)));
+  Plan& P = se->plan_host;
+  P = Plan{};
+  P.nphases = (int)ph.size();
+  P.phases = se->phases_dev;
+  P.d = d, P.heads = H, P.vocab = (int)c.vocab, P.eps = c.eps;
+  P.embed = md->embed.w;
+  P.ids = se->ids_dev;
+  P.e0 = se->e0, P.x0 = X0;
+  P.pos = se->pos_dev;
+  P.arg_count = words;
+  P.bar = words + 4;
+  P.out_index = words + 8;
+  P.arg_part = static_cast<unsigned long long*>(alloc_zero(se, logit_items * sizeof(unsigned long long)));
+  P.next_id = se->ids_dev;
+  P.err = se->ctx->err;
+  se->plan_dev = static_cast<Plan*>(alloc_zero(se, sizeof(Plan)));
+  SLM_CUDA(cudaMemcpyAsync(se->plan_dev, &P, sizeof(Plan), cudaMemcpyHostToDevice, se->ctx->stream));
+}
+
+// Points the plan's greedy outputs at `out` (nullptr: logits only).
+void plan_outputs(slm_session* se, bool greedy, uint32_t* out, uint32_t* hist, unsigned long long hist_base) {
+  mega::Plan& P = se->plan_host;
+  P.greedy = greedy ? 1 : 0;
+  P.out_ids = out;
+  P.hist = hist;
+  P.hist_base = hist_base;
+  SLM_CUDA(cudaMemcpyAsync(se->plan_dev, &P, sizeof(P), cudaMemcpyHostToDevice, se->ctx->stream));
+  SLM_CUDA(cudaMemsetAsync(P.out_index, 0, sizeof(unsigned), se->ctx->stream));
+}
+
+void mega_step(slm_session* se) {
+  mega::launch(se->plan_dev, se->grid, se->ctx->stream);
+  se->pos += 1;
+}
+
 // One decode step for the id already in ids_dev[0]: graph replay when enabled.
 void step_device(slm_session* se) {
   ensure_caps(se, 1);
   cudaStream_t s = se->ctx->stream;
+  if (se->use_mega) {
+    mega_step(se);
+    return;
+  }
   if (!se->use_graph) {
     advance(se, 1, true);
     return;
@@ -403,8 +576,7 @@ void check_device_error(slm_ctx* c) {
     SLM_CUDA(cudaMemsetAsync(c->err, 0, sizeof(int), c->stream));
     std::string why;
     if (h & 1) why += " token id out of range;";
-    if (h & 2) why += " top_k above 2048 is not supported on the device;";
-    if (h & 4) why += " top_p set larger than the 2048 largest logits (use top_k);";
+    if (h & 8) why += " a bounded wait in the decode kernel expired (state of this step is undefined);";
     fail(SLM_ERR_DEVICE, "device reported:" + why);
   }
 }
@@ -420,8 +592,7 @@ void ensure_u32(slm_session* se, uint32_t** p, size_t* cap, size_t n) {
 
 void check_sampling(const slm_sampling* sp) {
   SLM_REQUIRE(sp, "sampling is null");
-  SLM_REQUIRE(sp->top_k <= 2048, "top_k above 2048 is not supported on the device");
-  SLM_REQUIRE(!(sp->top_p != sp->top_p), "top_p is NaN");
+  SLM_REQUIRE(!(sp->top_p != sp->top_p) && !(sp->temperature != sp->temperature), "NaN sampling parameter");
 }
 
 SampleArgs sample_args(slm_session* se, const slm_sampling* sp) {
@@ -563,17 +734,36 @@ int slm_session_new(slm_model* md, size_t loops, slm_session** out) {
       se->dec = f(CHUNK * c.heads);
       se->nlast = f(d);
       se->logits = f(c.vocab);
-      se->work = f(c.vocab);
+      se->work = f(3 * c.vocab);  // sampler: logits, sorted weights, sorted ids
       size_t part = 0;
       for (size_t m = 1; m <= CHUNK; m++) {
         AttnGeom g{(int)m, 0, 0, 1, (int)c.heads, 1, (int)dh, 1.0f};
         part = std::max(part, attn_part_floats(g, attn_splits(g, 1ll << 40)));
       }
       se->part = f(part);
+      se->xc = f(CHUNK * d);
       se->pos_dev = reinterpret_cast<long long*>(alloc_zero(se.get(), sizeof(long long)));
       se->ids_dev = reinterpret_cast<uint32_t*>(alloc_zero(se.get(), CHUNK * sizeof(uint32_t)));
       se->rng_dev = reinterpret_cast<unsigned long long*>(alloc_zero(se.get(), sizeof(unsigned long long)));
       se->out_dev = reinterpret_cast<uint32_t*>(alloc_zero(se.get(), sizeof(uint32_t) * 4));
+      se->mega_why = mega_unsupported(md);
+      if (se->mega_why.empty()) {
+        int coop = 0;
+        SLM_CUDA(cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, se->ctx->device));
+        if (coop) {
+          mega::prepare();
+          if (mega::blocks_per_sm() >= 1) {
+            se->grid = se->ctx->sms;  // one CTA per SM, all resident (cooperative launch)
+            build_plan(se.get());
+            se->mega_ok = true;
+            se->use_mega = true;
+          } else {
+            se->mega_why = "the decode kernel does not fit on an SM";
+          }
+        } else {
+          se->mega_why = "device has no cooperative launch";
+        }
+      }
       SLM_CUDA(cudaStreamSynchronize(se->ctx->stream));
     } catch (...) {
       cudaStreamSynchronize(se->ctx->stream);
@@ -633,6 +823,11 @@ int slm_session_set(slm_session* se, int option, int64_t value) {
       if (!se->use_graph) drop_graph(se);
       return;
     }
+    if (option == SLM_OPT_MEGA) {
+      if (value && !se->mega_ok) fail(SLM_ERR_INVALID, "persistent decode kernel unavailable: " + se->mega_why);
+      se->use_mega = value != 0;
+      return;
+    }
     fail(SLM_ERR_INVALID, "unknown option");
   });
 }
@@ -640,8 +835,10 @@ int slm_session_set(slm_session* se, int option, int64_t value) {
 int slm_session_stat(const slm_session* se, int what, int64_t* out) {
   return guard([&] {
     SLM_REQUIRE(se && out, "bad arguments");
-    if (what == SLM_STAT_STEP_KERNELS) *out = se->step_kernels;
+    if (what == SLM_STAT_STEP_KERNELS) *out = se->use_mega ? 1 : se->step_kernels;
     else if (what == SLM_STAT_GRAPHS) *out = se->graphs;
+    else if (what == SLM_STAT_MEGA) *out = se->use_mega ? 1 : 0;
+    else if (what == SLM_STAT_PHASES) *out = se->mega_ok ? se->plan_host.nphases : 0;
     else fail(SLM_ERR_INVALID, "unknown counter");
   });
 }
@@ -748,14 +945,15 @@ int slm_pick(slm_ctx* c, const slm_buf* logits, size_t vocab, const slm_sampling
     const float* l = view(logits, 0, vocab, "pick logits");
     Device dev(c);
     cudaStream_t s = c->stream;
-    size_t words = vocab + n_recent + 8;
+    const size_t work = 3 * vocab;  // sampler: logits, sorted weights, sorted ids
+    size_t words = work + n_recent + 8;
     float* scratch = static_cast<float*>(dev_alloc(words * sizeof(float)));
     struct Free {
       float* p;
       ~Free() { dev_free(p); }
     } fr{scratch};
-    auto* hist = reinterpret_cast<uint32_t*>(scratch + vocab);
-    auto* rng = reinterpret_cast<unsigned long long*>(scratch + vocab + n_recent + 2 - ((vocab + n_recent) & 1));
+    auto* hist = reinterpret_cast<uint32_t*>(scratch + work);
+    auto* rng = reinterpret_cast<unsigned long long*>(scratch + work + n_recent + 2 - ((work + n_recent) & 1));
     auto* outd = reinterpret_cast<uint32_t*>(rng + 2);
     if (n_recent) SLM_CUDA(cudaMemcpyAsync(hist, recent, n_recent * sizeof(uint32_t), cudaMemcpyHostToDevice, s));
     unsigned long long st = *rng_state;
@@ -798,12 +996,21 @@ int slm_decode(slm_session* se, uint32_t first, size_t n, const slm_sampling* sp
     a.recent = se->hist_dev;
     a.hist_out = se->hist_dev;
     a.next_id = se->ids_dev;
-    for (size_t t = 0; t < n; t++) {
-      step_device(se);
-      a.nrecent = (long long)(n_recent + t);
-      a.out = se->outs_dev + t;
-      sample(a, s);
+    const bool fused = se->use_mega && sp->temperature <= 0.0f && sp->repeat_penalty == 1.0f;
+    if (fused) plan_outputs(se, true, se->outs_dev, se->hist_dev, n_recent);
+    try {
+      for (size_t t = 0; t < n; t++) {
+        step_device(se);
+        if (fused) continue;  // the step's own arg-max wrote the id
+        a.nrecent = (long long)(n_recent + t);
+        a.out = se->outs_dev + t;
+        sample(a, s);
+      }
+    } catch (...) {
+      if (fused) plan_outputs(se, false, nullptr, nullptr, 0);
+      throw;
     }
+    if (fused) plan_outputs(se, false, nullptr, nullptr, 0);
     SLM_CUDA(cudaMemcpyAsync(out, se->outs_dev, n * sizeof(uint32_t), cudaMemcpyDeviceToHost, s));
     SLM_CUDA(cudaMemcpyAsync(&st, se->rng_dev, sizeof(st), cudaMemcpyDeviceToHost, s));
     check_device_error(se->ctx);

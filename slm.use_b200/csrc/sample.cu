@@ -5,16 +5,18 @@
 //
 // One CTA of 1024 threads:
 //   1. copy the logits to a work buffer and apply the repeat penalty once per
-//      distinct id of the last `window` history entries;
+//      distinct id of the last `window` history entries (sample.rs:34-47);
 //   2. temperature ≤ 0: arg-max, first index on ties (sample.rs:48-53);
-//   3. otherwise top-k by an MSB-first radix select over the total order of
-//      f32 (Rust's total_cmp), ties at the threshold broken by smaller id; the
-//      k candidates are bitonic-sorted (logit descending, then id ascending —
+//   3. top-k and/or top-p: candidates come out in rounds of up to 2048, each
+//      round the next-largest by (logit in f32 total order, then smaller id) —
 //      the canonical order that stands in for select_nth_unstable's
-//      unspecified one); weights e^((l - top)/T), top-p cut on the running
-//      sum, then the cumulative walk with r = u·Σw (sample.rs:61-92).
-// Sequential sums and the walk run in candidate order on one thread, as the
-// reference does, whenever the candidate set is a sorted list (≤ 2048).
+//      unspecified one — found by an MSB-first radix select over that 64-bit
+//      composite key and bitonic-sorted in shared memory.  Weights
+//      e^((l - top)/T), the top-p cut on the running sum, then the cumulative
+//      walk with r = u·Σw (sample.rs:54-92), sequentially in candidate order
+//      on one thread as the reference does;
+//   4. no top-k and no top-p: every id in id order (the reference leaves the
+//      ids unsorted), with a block scan in place of the sequential walk.
 #include "common.cuh"
 #include "kernels.cuh"
 
@@ -22,13 +24,20 @@ namespace slm {
 
 namespace {
 
-constexpr int ST = 1024;      // threads
-constexpr int MAXC = 2048;    // candidates kept in shared memory
+constexpr int ST = 1024;    // threads
+constexpr int MAXC = 2048;  // candidates per round, in shared memory
 
 __device__ __forceinline__ uint32_t total_key(float f) {
   uint32_t u = __float_as_uint(f);
   return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
 }
+
+// Larger composite = earlier in the canonical order.
+__device__ __forceinline__ unsigned long long composite(float f, uint32_t id) {
+  return ((unsigned long long)total_key(f) << 32) | (0xFFFFFFFFu - id);
+}
+
+__device__ __forceinline__ uint32_t comp_id(unsigned long long c) { return 0xFFFFFFFFu - (uint32_t)(c & 0xFFFFFFFFu); }
 
 __device__ __forceinline__ float rng_next(unsigned long long* st) {
   unsigned long long x = *st;
@@ -49,44 +58,115 @@ __device__ float block_max(float v, float* red) {
   return warp_max(t);
 }
 
-// Exclusive block scan of one uint per thread (ST threads).
-__device__ uint32_t block_excl_scan(uint32_t v, uint32_t* warp_tot, uint32_t* total) {
-  int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
-  uint32_t x = v;
-#pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    uint32_t y = __shfl_up_sync(0xffffffffu, x, o);
-    if (lane >= o) x += y;
+struct Shared {
+  uint32_t hist[256];
+  unsigned long long cand[MAXC];
+  float wts[MAXC];
+  float red[32];
+  float wpre[32];
+  unsigned long long best, prefix, thresh;
+  uint32_t remaining, count, found, keep, nsorted;
+  float held, enough, s_sum, s_r, top;
+};
+
+// The c largest composites below `bound` (all when bound == 0): sets
+// sh.thresh so that exactly c composites c satisfy thresh ≤ c < bound.
+__device__ void select_round(const float* work, int V, unsigned long long bound, uint32_t c, Shared& sh) {
+  const int tid = threadIdx.x, lane = tid & 31;
+  if (tid == 0) {
+    sh.prefix = 0;
+    sh.remaining = c;
+    sh.found = 0;
   }
-  __syncthreads();
-  if (lane == 31) warp_tot[w] = x;
-  __syncthreads();
-  if (w == 0) {
-    uint32_t t = warp_tot[lane];
-    uint32_t s = t;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      uint32_t y = __shfl_up_sync(0xffffffffu, s, o);
-      if (lane >= o) s += y;
+  unsigned long long mask = 0;
+  for (int shift = 56; shift >= 0; shift -= 8) {
+    for (int b = tid; b < 256; b += ST) sh.hist[b] = 0;
+    if (tid == 0) sh.count = 0;
+    __syncthreads();
+    if (sh.found) break;
+    const unsigned long long prefix = sh.prefix;
+    for (int base = 0; base < V; base += ST) {
+      int i = base + tid;
+      bool act = false;
+      uint32_t digit = 0;
+      if (i < V) {
+        unsigned long long k = composite(work[i], (uint32_t)i);
+        act = (!bound || k < bound) && (k & mask) == prefix;
+        digit = (uint32_t)(k >> shift) & 0xFFu;
+      }
+      unsigned am = __ballot_sync(0xffffffffu, act);
+      if (act) {
+        unsigned peers = __match_any_sync(am, digit);
+        if (lane == __ffs(peers) - 1) atomicAdd(&sh.hist[digit], (uint32_t)__popc(peers));
+      }
     }
-    warp_tot[lane] = s - t;
-    if (lane == 31) *total = s;
+    __syncthreads();
+    if (tid == 0) {
+      uint32_t rem = sh.remaining, cum = 0;
+      int b = 255;
+      for (; b >= 0; b--) {
+        if (cum + sh.hist[b] >= rem) break;
+        cum += sh.hist[b];
+      }
+      if (b < 0) b = 0;
+      sh.remaining = rem - cum;
+      sh.prefix = prefix | ((unsigned long long)b << shift);
+      // Every composite under the new prefix is taken: stop here.
+      if (sh.hist[b] == sh.remaining || shift == 0) sh.found = 1;
+    }
+    mask |= 0xFFull << shift;
+    __syncthreads();
+  }
+  if (tid == 0) sh.thresh = sh.prefix;  // low bits zero: the smallest composite under the prefix
+  __syncthreads();
+}
+
+// Collects the selected composites and sorts them, descending.
+__device__ void gather_sort(const float* work, int V, unsigned long long bound, uint32_t c, Shared& sh) {
+  const int tid = threadIdx.x;
+  if (tid == 0) sh.count = 0;
+  __syncthreads();
+  const unsigned long long th = sh.thresh;
+  for (int i = tid; i < V; i += ST) {
+    unsigned long long k = composite(work[i], (uint32_t)i);
+    if (k >= th && (!bound || k < bound)) {
+      uint32_t slot = atomicAdd(&sh.count, 1u);
+      if (slot < (uint32_t)MAXC) sh.cand[slot] = k;
+    }
   }
   __syncthreads();
-  return warp_tot[w] + x - v;
+  uint32_t P = 1;
+  while (P < c) P <<= 1;
+  for (uint32_t i = c + tid; i < P; i += ST) sh.cand[i] = 0;
+  __syncthreads();
+  for (uint32_t size = 2; size <= P; size <<= 1) {
+    for (uint32_t stride = size >> 1; stride > 0; stride >>= 1) {
+      for (uint32_t i = tid; i < P; i += ST) {
+        uint32_t j = i ^ stride;
+        if (j > i) {
+          bool desc = (i & size) == 0;
+          unsigned long long x = sh.cand[i], y = sh.cand[j];
+          if (desc ? (x < y) : (x > y)) sh.cand[i] = y, sh.cand[j] = x;
+        }
+      }
+      __syncthreads();
+    }
+  }
+}
+
+__device__ void finish(const SampleArgs& a, uint32_t chosen) {
+  a.out[0] = chosen;
+  if (a.hist_out) a.hist_out[a.nrecent] = chosen;
+  if (a.next_id) a.next_id[0] = chosen;
 }
 
 __global__ void __launch_bounds__(ST) k_sample(SampleArgs a) {
-  __shared__ uint32_t hist[256];
-  __shared__ uint32_t warp_tot[32];
-  __shared__ uint32_t s_total, s_count, s_prefix, s_remaining;
-  __shared__ unsigned long long cand[MAXC];
-  __shared__ float wts[MAXC];
-  __shared__ float redf[32];
-  __shared__ unsigned long long s_best;
-  const int tid = threadIdx.x;
+  __shared__ Shared sh;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int V = a.vocab;
   float* work = a.work;
+  float* sw = a.work + V;                                    // sorted weights (multi-round)
+  uint32_t* sid = reinterpret_cast<uint32_t*>(a.work + 2 * (size_t)V);  // their ids
 
   for (int i = tid; i < V; i += ST) work[i] = a.logits[i];
   __syncthreads();
@@ -109,238 +189,176 @@ __global__ void __launch_bounds__(ST) k_sample(SampleArgs a) {
   }
   __syncthreads();
 
-  uint32_t chosen = 0;
   if (a.temperature <= 0.0f) {
-    // Arg-max; (key, ~index) packs "larger value, then smaller index".
     unsigned long long best = 0;
-    bool have = false;
     for (int i = tid; i < V; i += ST) {
       float v = work[i];
       if (v != v) continue;  // NaN never wins a `>` comparison
-      unsigned long long c = ((unsigned long long)total_key(v) << 32) | (0xFFFFFFFFu - (uint32_t)i);
-      if (!have || c > best) best = c, have = true;
+      unsigned long long c = composite(v, (uint32_t)i);
+      if (c > best) best = c;
     }
-    if (tid == 0) s_best = 0;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      unsigned long long other = __shfl_xor_sync(0xffffffffu, best, o);
+      if (other > best) best = other;
+    }
+    if (tid == 0) sh.best = 0;
     __syncthreads();
-    if (have) atomicMax(&s_best, best);
+    if (lane == 0 && best) atomicMax(&sh.best, best);
     __syncthreads();
-    chosen = s_best ? 0xFFFFFFFFu - (uint32_t)(s_best & 0xFFFFFFFFu) : 0;
     if (tid == 0) {
-      // -0.0 and +0.0 compare equal in the reference's `>`: keep the first.
+      uint32_t chosen = sh.best ? comp_id(sh.best) : 0;
       float bv = work[chosen];
+      // -0.0 and +0.0 compare equal under the reference's `>`: keep the first.
       if (bv == 0.0f)
         for (uint32_t i = 0; i < chosen; i++)
           if (work[i] == bv) {
             chosen = i;
             break;
           }
-      a.out[0] = chosen;
-      if (a.hist_out) a.hist_out[a.nrecent] = chosen;
-      if (a.next_id) a.next_id[0] = chosen;
+      finish(a, chosen);
     }
     return;
   }
 
   const bool use_k = a.top_k > 0 && a.top_k < (uint32_t)V;
-  const bool sorted = use_k || a.top_p < 1.0f;
-  if (!sorted) {
-    // Every id, in id order: weights, a block sum, then the walk.
-    float top = -INFINITY;
-    for (int i = tid; i < V; i += ST) top = fmaxf(top, work[i]);
-    top = block_max(top, redf);
-    // Contiguous slices per thread keep the walk in id order.
+  float top = -INFINITY;
+  for (int i = tid; i < V; i += ST) top = fmaxf(top, work[i]);
+  top = block_max(top, sh.red);
+  const float invT = a.temperature;
+
+  if (!use_k && !(a.top_p < 1.0f)) {
+    // Every id, in id order.  Contiguous slices per thread keep the order.
     int per = (V + ST - 1) / ST, lo = tid * per, hi = min(V, lo + per);
     float part = 0.0f;
-    for (int i = lo; i < hi; i++) part += expf((work[i] - top) / a.temperature);
-    __syncthreads();
-    // Exclusive scan of the float partials (via warp shuffles + shared).
+    for (int i = lo; i < hi; i++) part += expf((work[i] - top) / invT);
     float x = part;
-    int lane = tid & 31, w = tid >> 5;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
       float y = __shfl_up_sync(0xffffffffu, x, o);
       if (lane >= o) x += y;
     }
-    if (lane == 31) redf[w] = x;
     __syncthreads();
-    __shared__ float wpre[32];
-    __shared__ float s_sum, s_r;
-    if (w == 0) {
-      float t = redf[lane], s = t;
+    if (lane == 31) sh.red[warp] = x;
+    __syncthreads();
+    if (warp == 0) {
+      float t = sh.red[lane], s = t;
 #pragma unroll
       for (int o = 1; o < 32; o <<= 1) {
         float y = __shfl_up_sync(0xffffffffu, s, o);
         if (lane >= o) s += y;
       }
-      wpre[lane] = s - t;
-      if (lane == 31) s_sum = s;
+      sh.wpre[lane] = s - t;
+      if (lane == 31) sh.s_sum = s;
     }
     __syncthreads();
-    float before = wpre[w] + x - part;
+    float before = sh.wpre[warp] + x - part;
     if (tid == 0) {
       unsigned long long st = *a.rng;
-      s_r = rng_next(&st) * s_sum;
+      sh.s_r = rng_next(&st) * sh.s_sum;
       *a.rng = st;
-      s_count = 0xFFFFFFFFu;
+      sh.count = 0xFFFFFFFFu;
     }
     __syncthreads();
-    float r = s_r - before;
+    float r = sh.s_r - before;
     if (r > 0.0f && r <= part) {
       for (int i = lo; i < hi; i++) {
-        r -= expf((work[i] - top) / a.temperature);
+        r -= expf((work[i] - top) / invT);
         if (r <= 0.0f) {
-          atomicMin(&s_count, (uint32_t)i);
+          atomicMin(&sh.count, (uint32_t)i);
           break;
         }
       }
     }
     __syncthreads();
-    if (tid == 0) {
-      chosen = s_count == 0xFFFFFFFFu ? (uint32_t)(V - 1) : s_count;
-      a.out[0] = chosen;
-      if (a.hist_out) a.hist_out[a.nrecent] = chosen;
-      if (a.next_id) a.next_id[0] = chosen;
-    }
+    if (tid == 0) finish(a, sh.count == 0xFFFFFFFFu ? (uint32_t)(V - 1) : sh.count);
     return;
   }
 
-  // Candidate set: the K largest by total order (K ≤ MAXC).
-  const uint32_t K = use_k ? a.top_k : (uint32_t)min(V, MAXC);
-  if (K > (uint32_t)MAXC) {
-    if (tid == 0 && a.err) atomicOr(a.err, 2);
-    return;
+  // Sorted candidates, in rounds.
+  const uint32_t K = use_k ? a.top_k : (uint32_t)V;
+  const bool multi = K > (uint32_t)MAXC;
+  if (!use_k) {  // the top-p cut needs Σ over every id
+    float part = 0.0f;
+    for (int i = tid; i < V; i += ST) part += expf((work[i] - top) / invT);
+    float total = block_sum(part, sh.red);
+    if (tid == 0) sh.enough = a.top_p * total;
   }
   if (tid == 0) {
-    s_prefix = 0;
-    s_remaining = K;
+    sh.nsorted = 0;
+    sh.keep = 0;
+    sh.held = 0.0f;
   }
-  uint32_t mask = 0;
-  for (int shift = 24; shift >= 0; shift -= 8) {
-    for (int b = tid; b < 256; b += ST) hist[b] = 0;
-    __syncthreads();
-    uint32_t prefix = s_prefix;
-    for (int i = tid; i < V; i += ST) {
-      uint32_t k = total_key(work[i]);
-      if ((k & mask) == prefix) atomicAdd(&hist[(k >> shift) & 0xFF], 1u);
+  __syncthreads();
+  unsigned long long bound = 0;
+  while (true) {
+    const uint32_t done = sh.nsorted;
+    if (done >= K || sh.keep) break;
+    const uint32_t c = min((uint32_t)MAXC, K - done);
+    select_round(work, V, bound, c, sh);
+    gather_sort(work, V, bound, c, sh);
+    for (uint32_t i = tid; i < c; i += ST) {
+      uint32_t id = comp_id(sh.cand[i]);
+      float w = expf((work[id] - top) / invT);
+      sh.wts[i] = w;
+      if (multi) {
+        sw[done + i] = w;
+        sid[done + i] = id;
+      }
     }
     __syncthreads();
     if (tid == 0) {
-      uint32_t rem = s_remaining, cum = 0;
-      int b = 255;
-      for (; b >= 0; b--) {
-        if (cum + hist[b] >= rem) break;
-        cum += hist[b];
+      if (!use_k && a.top_p < 1.0f) {
+        float held = sh.held;
+        for (uint32_t i = 0; i < c; i++) {
+          held += sh.wts[i];
+          if (held >= sh.enough) {
+            sh.keep = done + i + 1;
+            break;
+          }
+        }
+        sh.held = held;
       }
-      if (b < 0) b = 0;
-      s_remaining = rem - cum;
-      s_prefix = prefix | ((uint32_t)b << shift);
+      sh.nsorted = done + c;
     }
-    mask |= 0xFFu << shift;
+    bound = sh.cand[c - 1];
     __syncthreads();
   }
-  const uint32_t T = s_prefix, need_eq = s_remaining;
-  if (tid == 0) s_count = 0;
-  __syncthreads();
-  // Above the threshold: any order (sorted below).
-  for (int i = tid; i < V; i += ST) {
-    uint32_t k = total_key(work[i]);
-    if (k > T) {
-      uint32_t slot = atomicAdd(&s_count, 1u);
-      if (slot < (uint32_t)MAXC) cand[slot] = ((unsigned long long)k << 32) | (0xFFFFFFFFu - (uint32_t)i);
-    }
-  }
-  __syncthreads();
-  const uint32_t n_gt = s_count;
-  // At the threshold: the need_eq smallest ids.
-  {
-    int per = (V + ST - 1) / ST, lo = tid * per, hi = min(V, lo + per);
-    uint32_t c = 0;
-    for (int i = lo; i < hi; i++) c += total_key(work[i]) == T;
-    uint32_t rank = block_excl_scan(c, warp_tot, &s_total);
-    for (int i = lo; i < hi && rank < need_eq; i++) {
-      if (total_key(work[i]) == T) {
-        uint32_t slot = n_gt + rank;
-        if (slot < (uint32_t)MAXC) cand[slot] = ((unsigned long long)T << 32) | (0xFFFFFFFFu - (uint32_t)i);
-        rank++;
-      }
-    }
-  }
-  __syncthreads();
-  // Bitonic sort, descending, over the next power of two.
-  uint32_t P = 1;
-  while (P < K) P <<= 1;
-  for (uint32_t i = K + tid; i < P; i += ST) cand[i] = 0;
-  __syncthreads();
-  for (uint32_t size = 2; size <= P; size <<= 1) {
-    for (uint32_t stride = size >> 1; stride > 0; stride >>= 1) {
-      for (uint32_t i = tid; i < P; i += ST) {
-        uint32_t j = i ^ stride;
-        if (j > i) {
-          bool desc = (i & size) == 0;
-          unsigned long long x = cand[i], y = cand[j];
-          if (desc ? (x < y) : (x > y)) cand[i] = y, cand[j] = x;
-        }
-      }
-      __syncthreads();
-    }
-  }
-  // Weights in candidate order.
-  const float top = work[0xFFFFFFFFu - (uint32_t)(cand[0] & 0xFFFFFFFFu)];
-  for (uint32_t i = tid; i < K; i += ST) {
-    uint32_t id = 0xFFFFFFFFu - (uint32_t)(cand[i] & 0xFFFFFFFFu);
-    wts[i] = expf((work[id] - top) / a.temperature);
-  }
-  // Without top-k the top-p cut needs Σ over every id.
-  float all_sum = 0.0f;
-  if (!use_k) {
-    float part = 0.0f;
-    for (int i = tid; i < V; i += ST) part += expf((work[i] - top) / a.temperature);
-    all_sum = block_sum(part, redf);
-  }
-  __syncthreads();
   if (tid == 0) {
-    uint32_t keep = K;
-    if (a.top_p < 1.0f) {
-      float total = 0.0f;
-      if (use_k)
-        for (uint32_t i = 0; i < K; i++) total += wts[i];
-      else
-        total = all_sum;
-      float enough = a.top_p * total, held = 0.0f;
-      keep = 0;
-      for (uint32_t i = 0; i < K; i++) {
-        held += wts[i];
-        if (held >= enough) {
-          keep = i + 1;
-          break;
+    auto W = [&](uint32_t i) { return multi ? sw[i] : sh.wts[i]; };
+    auto ID = [&](uint32_t i) { return multi ? sid[i] : comp_id(sh.cand[i]); };
+    uint32_t keep = sh.keep;
+    if (use_k) {
+      keep = K;
+      if (a.top_p < 1.0f) {
+        float total = 0.0f;
+        for (uint32_t i = 0; i < K; i++) total += W(i);
+        float enough = a.top_p * total, held = 0.0f;
+        for (uint32_t i = 0; i < K; i++) {
+          held += W(i);
+          if (held >= enough) {
+            keep = i + 1;
+            break;
+          }
         }
       }
-      if (keep == 0) {
-        if (use_k) {
-          keep = K;
-        } else {
-          if (a.err) atomicOr(a.err, 4);  // top-p set larger than the candidates held on chip
-          keep = K;
-        }
-      }
+    } else if (keep == 0) {
+      keep = sh.nsorted;
     }
     float total = 0.0f;
-    for (uint32_t i = 0; i < keep; i++) total += wts[i];
+    for (uint32_t i = 0; i < keep; i++) total += W(i);
     unsigned long long st = *a.rng;
     float r = rng_next(&st) * total;
     *a.rng = st;
     uint32_t pick = keep - 1;
     for (uint32_t i = 0; i < keep; i++) {
-      r -= wts[i];
+      r -= W(i);
       if (r <= 0.0f) {
         pick = i;
         break;
       }
     }
-    chosen = 0xFFFFFFFFu - (uint32_t)(cand[pick] & 0xFFFFFFFFu);
-    a.out[0] = chosen;
-    if (a.hist_out) a.hist_out[a.nrecent] = chosen;
-    if (a.next_id) a.next_id[0] = chosen;
+    finish(a, ID(pick));
   }
 }
 

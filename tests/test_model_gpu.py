@@ -135,3 +135,47 @@ def test_errors_are_statuses(slm, ctx, tiny):
         tiny.session(7)  # max_loops 6
     with pytest.raises(slm.SlmError):
         slm.Model(ctx, TINY.parent / "missing")
+
+
+def test_persistent_kernel_matches_graph_path(slm, ctx, small):
+    model = slm.Model(ctx, small)
+    ids = np.random.default_rng(6).integers(0, 1000, 360)
+    a, b = model.session(), model.session()
+    b.set_mega(False)
+    assert a.mega and not b.mega
+    assert a.stat(slm.SLM_STAT_PHASES) == 5 * (2 + 3 * 2) + 2  # 8 blocks of 5 phases + inject + logits
+    a.feed(ids[:300])
+    b.feed(ids[:300])
+    worst = 0.0
+    for t in ids[300:]:  # crosses the ring's wrap (cap = 48 + 256)
+        a.step(int(t))
+        b.step(int(t))
+        worst = max(worst, float(np.abs(a.logits() - b.logits()).max()))
+    assert worst < 2e-5, worst
+    greedy = slm.Sampling()
+    first = a.sample(greedy)
+    assert first == b.sample(greedy)
+    np.testing.assert_array_equal(a.decode(first, 64, greedy), b.decode(first, 64, greedy))
+    assert a.pos == b.pos
+
+
+def test_persistent_kernel_sampling_path(slm, ctx, small):
+    model = slm.Model(ctx, small)
+    s = slm.Sampling(temperature=0.8, top_k=40, repeat_penalty=1.1, repeat_window=64)
+    prompt = np.random.default_rng(7).integers(0, 1000, 70)
+    a, b = model.session(), model.session()
+    b.set_mega(False)
+    a.feed(prompt)
+    b.feed(prompt)
+    sa, sb = [slm.rng_seed(5)], [slm.rng_seed(5)]
+    first = a.sample(s, list(prompt), sa)
+    assert first == b.sample(s, list(prompt), sb)
+    hist = list(prompt) + [first]
+    np.testing.assert_array_equal(a.decode(first, 40, s, hist, sa), b.decode(first, 40, s, hist, sb))
+
+
+def test_persistent_kernel_is_refused_where_it_does_not_apply(slm, tiny):
+    se = tiny.session()
+    assert not se.mega  # head size 8 and a global layer
+    with pytest.raises(slm.SlmError):
+        se.set_mega(True)

@@ -28,6 +28,9 @@ CASES = [
     dict(temperature=0.9, top_k=100, top_p=0.8),
     dict(temperature=1.3),
     dict(temperature=1.0, top_k=2048),
+    dict(temperature=1.0, top_k=5000),
+    dict(temperature=1.0, top_k=5000, top_p=0.9),
+    dict(temperature=1.0, top_p=0.99),
 ]
 
 
