@@ -211,6 +211,7 @@ int slm_decode(slm_session* se, uint32_t first, size_t n, const slm_sampling* s,
  *                    layers, damp 1; fails with SLM_ERR_INVALID otherwise) */
 #define SLM_OPT_GRAPH 1
 #define SLM_OPT_MEGA 2
+#define SLM_OPT_TRACE 3 /* 1 = record the per-phase timeline of each persistent step */
 int slm_session_set(slm_session* se, int option, int64_t value);
 
 /* Counters of a session:
@@ -221,6 +222,12 @@ int slm_session_set(slm_session* se, int option, int64_t value);
 #define SLM_STAT_MEGA 3    /* 1 when the persistent decode kernel is in use */
 #define SLM_STAT_PHASES 4  /* phases (grid barriers + 1) of that kernel's step */
 int slm_session_stat(const slm_session* se, int what, int64_t* out);
+
+/* Timeline of the last persistent step (SLM_OPT_TRACE on): for each phase p
+ * and CTA c, out[(p·grid + c)·2] is the globaltimer (ns) when the CTA began
+ * the phase's work and out[(p·grid + c)·2 + 1] when it reached the next grid
+ * barrier.  *n_out receives the count; nothing is copied when cap < count. */
+int slm_session_trace(slm_session* se, uint64_t* out, size_t cap, size_t* n_out);
 
 #ifdef __cplusplus
 }

@@ -35,6 +35,7 @@ _sz = _c.c_size_t
 
 SLM_OPT_GRAPH = 1
 SLM_OPT_MEGA = 2
+SLM_OPT_TRACE = 3
 SLM_STAT_STEP_KERNELS, SLM_STAT_GRAPHS, SLM_STAT_MEGA, SLM_STAT_PHASES = 1, 2, 3, 4
 SIZE_MAX = (1 << 64) - 1
 
@@ -106,6 +107,7 @@ _SIGS = {
     "slm_session_loops": (_c.c_int, [_vp, _c.POINTER(_sz)]),
     "slm_session_set": (_c.c_int, [_vp, _c.c_int, _c.c_int64]),
     "slm_session_stat": (_c.c_int, [_vp, _c.c_int, _c.POINTER(_c.c_int64)]),
+    "slm_session_trace": (_c.c_int, [_vp, _u64p, _sz, _c.POINTER(_sz)]),
     "slm_feed": (_c.c_int, [_vp, _u32p, _sz, _sz]),
     "slm_step": (_c.c_int, [_vp, _c.c_uint32]),
     "slm_logits": (_c.c_int, [_vp, _f32p]),
@@ -433,6 +435,18 @@ class Session:
     def set_mega(self, on: bool) -> None:
         """Run m = 1 steps as one persistent kernel (where the model allows it)."""
         _check(lib().slm_session_set(self._h, SLM_OPT_MEGA, 1 if on else 0))
+
+    def set_trace(self, on: bool) -> None:
+        _check(lib().slm_session_set(self._h, SLM_OPT_TRACE, 1 if on else 0))
+
+    def trace(self) -> np.ndarray:
+        """Timeline of the last persistent step: [phase][cta][start, barrier] in ns."""
+        n = _sz(0)
+        _check(lib().slm_session_trace(self._h, None, 0, _c.byref(n)))
+        out = np.empty(n.value, dtype=np.uint64)
+        _check(lib().slm_session_trace(self._h, out.ctypes.data_as(_u64p), n.value, _c.byref(n)))
+        phases = self.stat(SLM_STAT_PHASES)
+        return out.reshape(phases, -1, 2)
 
     @property
     def mega(self) -> bool:

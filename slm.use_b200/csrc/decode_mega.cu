@@ -3,13 +3,16 @@
 // Everything a decode step reads from HBM — the weights, the old entries of
 // the sliding-window rings and the recurrent GLA state — is fixed for the
 // whole step; only small activation vectors (x, q, y, mid: a few KB) flow
-// from phase to phase.  So one producer warp per CTA walks the step's static
-// tiles in order and streams them into a 4-stage shared-memory ring with
-// cp.async.bulk (TMA bulk copies, mbarrier completion), never waiting for
-// the grid barriers that separate phases; eight consumer warps wait at each
-// barrier, rebuild the phase's input vector on chip (RMSNorm, loop input,
-// embedding) and consume the tiles.  HBM keeps streaming the next phases'
-// weights while the consumers cross a barrier.
+// from phase to phase.  So one producer thread per CTA walks the step's
+// static tiles in order:
+//   * a ring cursor streams them into a 4-stage shared-memory ring with
+//     cp.async.bulk (TMA bulk copies, mbarrier completion), never waiting for
+//     the grid barriers that separate phases;
+//   * a lookahead cursor, kLookahead tiles further on, issues
+//     cp.async.bulk.prefetch.L2 for the same tiles, so HBM keeps streaming
+//     while the ring is full and the consumers sit at a barrier.
+// Eight consumer warps wait at each barrier, rebuild the phase's input vector
+// on chip (RMSNorm, loop input, embedding) and consume the tiles.
 //
 // Phases follow the reference's block (src/model.rs:400-560) and advance
 // (src/model.rs:563-640) for one token:
@@ -58,6 +61,9 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, unsigned by
                "l"(src), "r"(bytes), "r"(saddr(bar))
                : "memory");
 }
+__device__ __forceinline__ void prefetch_l2(const void* src, unsigned bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
 __device__ __forceinline__ unsigned long long now_ns() {
   unsigned long long t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
@@ -68,8 +74,8 @@ __device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
   asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
-__device__ __forceinline__ void st_release(unsigned* p, unsigned v) {
-  asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+__device__ __forceinline__ void red_release_add(unsigned* p, unsigned v) {
+  asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 __device__ __forceinline__ int ld_volatile(const int* p) { return *(const volatile int*)p; }
 __device__ __forceinline__ void consumers_sync() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
@@ -110,22 +116,21 @@ __device__ __forceinline__ uint32_t total_key(float f) {
 }
 
 // ---------------------------------------------------------------------------
-// Tile walk shared by the producer and the consumers
+// Tile geometry shared by the producer and the consumers
 // ---------------------------------------------------------------------------
-
-// Logical outputs per tile of a GEMV phase.
-__device__ __forceinline__ int tile_outs(const Phase& ph) {
-  int rows = kStageBytes / (ph.cols * 4);
-  if (rows > 16) rows = 16;
-  bool pair = ph.out_mode == OUT_SILU || ph.out_mode == OUT_ROPE;
-  return pair ? rows / 2 : rows;
-}
 
 __device__ __forceinline__ bool is_pair(const Phase& ph) {
   return ph.out_mode == OUT_SILU || ph.out_mode == OUT_ROPE;
 }
 
-// First weight row of logical output o (and its partner) of segment s.
+// Logical outputs per tile of a GEMV phase.
+__device__ __forceinline__ int tile_outs(const Phase& ph) {
+  int rows = kStageBytes / (ph.cols * 4);
+  if (rows > 16) rows = 16;
+  return is_pair(ph) ? rows / 2 : rows;
+}
+
+// First weight row of logical output o (and its partner).
 __device__ __forceinline__ void out_rows(const Phase& ph, const Segment& sg, int o, int d, int* r0, int* r1) {
   if (ph.out_mode == OUT_ROPE) {
     int sec = o / (d / 2), rem = o % (d / 2), h = rem / 32, j = rem % 32;
@@ -153,23 +158,124 @@ __device__ __forceinline__ void gemv_item(const Phase& ph, int i, int* seg, int*
   *o1 = min(sg.rows, *o0 + sg.per_item);
 }
 
-// Window range of the step's query and this split's slice of old positions.
+// The step's query sees positions lo..pos; split s takes a slice of the old
+// positions lo..pos-1 (the last split also takes `pos` itself, from the ring
+// the qkv phase just wrote).
 __device__ __forceinline__ void attn_slice(const Phase& ph, long long pos, int s, long long* a, long long* b) {
   long long lo = ph.window > 0 && pos > ph.window - 1 ? pos - (ph.window - 1) : 0;
-  long long count = pos - lo;  // old positions (the current one is added by the last split)
+  long long count = pos - lo;
   long long chunk = (count + ph.splits - 1) / ph.splits;
   *a = lo + (long long)s * chunk;
   *b = min(pos, *a + chunk);
   if (*b < *a) *b = *a;
 }
 
+struct Tile {
+  int n;
+  const void* src[4];
+  unsigned bytes[4];
+  unsigned off[4];
+  unsigned total;
+};
+
+// Resumable walk over this CTA's tiles, phase by phase (the order in which
+// the consumers take them).
+struct Walker {
+  const Plan* P;
+  long long pos;
+  int me, G;
+  int p = 0, i = -1, seg = 0;
+  long long t = 0, tend = 0;
+
+  __device__ Walker(const Plan* pl, long long ps) : P(pl), pos(ps) {
+    me = blockIdx.x;
+    G = gridDim.x;
+  }
+
+  __device__ void start_item(const Phase& ph) {
+    if (ph.kind == PH_GEMV) {
+      int o0, o1;
+      gemv_item(ph, i, &seg, &o0, &o1);
+      t = o0, tend = o1;
+    } else if (ph.kind == PH_ATTN) {
+      attn_slice(ph, pos, i % ph.splits, &t, &tend);
+    } else {
+      t = 0, tend = 1;
+    }
+  }
+
+  __device__ bool next(Tile& T) {
+    while (p < P->nphases) {
+      const Phase& ph = P->phases[p];
+      if (i < 0) {
+        i = me;
+        if (i >= ph.items) {
+          p++, i = -1;
+          continue;
+        }
+        start_item(ph);
+      }
+      if (t < tend) {
+        make(ph, T);
+        return true;
+      }
+      i += G;
+      if (i >= ph.items) {
+        p++, i = -1;
+        continue;
+      }
+      start_item(ph);
+    }
+    return false;
+  }
+
+  __device__ void make(const Phase& ph, Tile& T) {
+    T.n = 0;
+    if (ph.kind == PH_GEMV) {
+      const Segment& sg = ph.seg[seg];
+      const int Tn = tile_outs(ph);
+      int n = (int)min((long long)Tn, tend - t);
+      int r0, r1;
+      out_rows(ph, sg, (int)t, P->d, &r0, &r1);
+      const unsigned rowb = (unsigned)ph.cols * 4;
+      T.src[0] = sg.w + (size_t)r0 * ph.cols, T.bytes[0] = n * rowb, T.off[0] = 0, T.n = 1;
+      if (is_pair(ph)) T.src[1] = sg.w + (size_t)r1 * ph.cols, T.bytes[1] = n * rowb, T.off[1] = n * rowb, T.n = 2;
+      t += n;
+    } else if (ph.kind == PH_ATTN) {
+      const int h = i / ph.splits;
+      const float* kb = ph.kc + (size_t)h * ph.cap * kDH;
+      const float* vb = ph.vc + (size_t)h * ph.cap * kDH;
+      int n = (int)min((long long)kAttnTile, tend - t);
+      long long slot = t % ph.cap;
+      int n1 = (int)min((long long)n, ph.cap - slot);
+      const unsigned vo = kAttnTile * kDH * 4;
+      T.src[0] = kb + slot * kDH, T.bytes[0] = n1 * kDH * 4, T.off[0] = 0;
+      T.src[1] = vb + slot * kDH, T.bytes[1] = n1 * kDH * 4, T.off[1] = vo;
+      T.n = 2;
+      if (n1 < n) {
+        T.src[2] = kb, T.bytes[2] = (n - n1) * kDH * 4, T.off[2] = n1 * kDH * 4;
+        T.src[3] = vb, T.bytes[3] = (n - n1) * kDH * 4, T.off[3] = vo + n1 * kDH * 4;
+        T.n = 4;
+      }
+      t += n;
+    } else {
+      T.src[0] = ph.state + (size_t)i * kDH * kDH, T.bytes[0] = kDH * kDH * 4, T.off[0] = 0, T.n = 1;
+      t += 1;
+    }
+    T.total = 0;
+    for (int j = 0; j < T.n; j++) T.total += T.bytes[j];
+  }
+};
+
 struct Smem {
   uint64_t full[kStages], empty[kStages];
   float xin[kMaxCols];
+  float xraw[kMaxD];
   float acc[2][kMaxItemOut];
   float part[16][8];
   float red[32];
   float wsm[kConsumerWarps][kDH + 2];
+  float cmb[kMaxSplits][kDH + 2];
   float vec[4][kDH];
   float yp[4][kDH];
   unsigned long long best;
@@ -177,70 +283,26 @@ struct Smem {
 };
 
 // ---------------------------------------------------------------------------
-// Producer: one lane walks every tile of every phase in order.
+// Producer: one thread, two cursors over the same tile sequence.
 // ---------------------------------------------------------------------------
 __device__ void producer(const Plan& P, Smem& sm, char* ring, long long pos) {
-  unsigned k = 0;  // tiles issued
-  const int G = gridDim.x, me = blockIdx.x, d = P.d;
-  bool ok = true;
-  auto acquire = [&](unsigned bytes) -> char* {
-    int s = k % kStages;
-    if (k >= (unsigned)kStages && !wait_mbar(&sm.empty[s], ((k / kStages) - 1) & 1, P.err)) {
-      ok = false;
-      return nullptr;
-    }
-    mbar_expect_tx(&sm.full[s], bytes);
-    return ring + (size_t)s * kStageBytes;
-  };
-  for (int p = 0; p < P.nphases && ok; p++) {
-    const Phase& ph = P.phases[p];
-    for (int i = me; i < ph.items && ok; i += G) {
-      if (ph.kind == PH_GEMV) {
-        int s, o0, o1;
-        gemv_item(ph, i, &s, &o0, &o1);
-        const Segment& sg = ph.seg[s];
-        const int T = tile_outs(ph);
-        const unsigned rowb = (unsigned)ph.cols * 4;
-        for (int t0 = o0; t0 < o1 && ok; t0 += T) {
-          int n = min(T, o1 - t0);
-          int r0, r1;
-          out_rows(ph, sg, t0, d, &r0, &r1);
-          unsigned bytes = (unsigned)n * rowb * (is_pair(ph) ? 2 : 1);
-          char* dst = acquire(bytes);
-          if (!dst) break;
-          uint64_t* fb = &sm.full[k % kStages];
-          bulk_g2s(dst, sg.w + (size_t)r0 * ph.cols, n * rowb, fb);
-          if (is_pair(ph)) bulk_g2s(dst + (size_t)n * rowb, sg.w + (size_t)r1 * ph.cols, n * rowb, fb);
-          k++;
-        }
-      } else if (ph.kind == PH_ATTN) {
-        int h = i / ph.splits, s = i % ph.splits;
-        long long a, b;
-        attn_slice(ph, pos, s, &a, &b);
-        const float* kb = ph.kc + (size_t)h * ph.cap * kDH;
-        const float* vb = ph.vc + (size_t)h * ph.cap * kDH;
-        for (long long t0 = a; t0 < b && ok; t0 += kAttnTile) {
-          int n = (int)min((long long)kAttnTile, b - t0);
-          char* dst = acquire((unsigned)n * kDH * 4 * 2);
-          if (!dst) break;
-          uint64_t* fb = &sm.full[k % kStages];
-          long long slot = t0 % ph.cap;
-          int n1 = (int)min((long long)n, ph.cap - slot);
-          bulk_g2s(dst, kb + slot * kDH, n1 * kDH * 4, fb);
-          bulk_g2s(dst + kAttnTile * kDH * 4, vb + slot * kDH, n1 * kDH * 4, fb);
-          if (n1 < n) {
-            bulk_g2s(dst + (size_t)n1 * kDH * 4, kb, (n - n1) * kDH * 4, fb);
-            bulk_g2s(dst + kAttnTile * kDH * 4 + (size_t)n1 * kDH * 4, vb, (n - n1) * kDH * 4, fb);
-          }
-          k++;
-        }
-      } else {  // PH_GLA: the head's state
-        char* dst = acquire(kDH * kDH * 4);
-        if (!dst) break;
-        bulk_g2s(dst, ph.state + (size_t)i * kDH * kDH, kDH * kDH * 4, &sm.full[k % kStages]);
-        k++;
-      }
-    }
+  Walker ring_w(&P, pos), ahead(&P, pos);
+  Tile T;
+  for (int j = 0; j < kLookahead; j++) {
+    if (!ahead.next(T)) break;
+    for (int s = 0; s < T.n; s++) prefetch_l2(T.src[s], T.bytes[s]);
+  }
+  unsigned k = 0;
+  while (ring_w.next(T)) {
+    const int s = k % kStages;
+    if (k >= (unsigned)kStages && !wait_mbar(&sm.empty[s], ((k / kStages) - 1) & 1, P.err)) break;
+    mbar_expect_tx(&sm.full[s], T.total);
+    char* dst = ring + (size_t)s * kStageBytes;
+    for (int j = 0; j < T.n; j++) bulk_g2s(dst + T.off[j], T.src[j], T.bytes[j], &sm.full[s]);
+    k++;
+    Tile A;
+    if (ahead.next(A))
+      for (int j = 0; j < A.n; j++) prefetch_l2(A.src[j], A.bytes[j]);
   }
   // Drain: every copy issued must land before the CTA may exit.
   unsigned first = k > (unsigned)kStages ? k - kStages : 0;
@@ -255,7 +317,8 @@ struct Cons {
   const Plan& P;
   Smem& sm;
   char* ring;
-  unsigned k = 0;  // tiles consumed
+  unsigned k = 0;         // tiles consumed
+  unsigned barriers = 0;  // grid barriers passed in this step
   bool ok = true;
   int tid, warp, lane;
   long long pos;
@@ -281,41 +344,38 @@ struct Cons {
     k++;
   }
 
-  // Grid barrier (consumer thread 0 for the CTA), generation counted.
+  // Grid barrier: a monotonic arrival count (reset at the end of the step);
+  // barrier b of the step completes when the count reaches b · grid.
   __device__ void grid_sync() {
     consumers_sync();
+    barriers++;
     if (tid == 0) {
-      unsigned* bar = P.bar;
-      unsigned gen = ld_acquire(&bar[1]);
+      unsigned* cnt = P.bar;
+      const unsigned target = barriers * gridDim.x;
       __threadfence();
-      unsigned arrived = atomicAdd(&bar[0], 1u);
-      if (arrived == gridDim.x - 1) {
-        atomicExch(&bar[0], 0u);
-        __threadfence();
-        st_release(&bar[1], gen + 1);
-      } else {
-        unsigned long long t0 = now_ns();
-        for (unsigned it = 0; ld_acquire(&bar[1]) == gen; it++) {
-          if ((it & 31) == 31) {
-            if (ld_volatile(P.err) & 8) {
-              sm.flag = 1;
-              break;
-            }
-            if (now_ns() - t0 > kWaitNs) {
-              atomicOr(P.err, 8);
-              sm.flag = 1;
-              break;
-            }
+      red_release_add(cnt, 1u);
+      unsigned long long t0 = 0;
+      for (unsigned it = 0; ld_acquire(cnt) < target; it++) {
+        if ((it & 15) == 15) {
+          if (ld_volatile(P.err) & 8) {
+            sm.flag = 1;
+            break;
+          }
+          if (!t0) {
+            t0 = now_ns();
+          } else if (now_ns() - t0 > kWaitNs) {
+            atomicOr(P.err, 8);
+            sm.flag = 1;
+            break;
           }
         }
       }
-      __threadfence();
     }
     consumers_sync();
-    if (sm.flag) ok = false;
+    if (sm.flag == 1) ok = false;
   }
 
-  // Input vector of a GEMV phase into sm.xin.
+  // Input vector of a GEMV phase into sm.xin (and the raw x into sm.xraw).
   __device__ void prologue(const Phase& ph) {
     const int n = ph.cols;
     if (ph.in_mode == IN_PLAIN) {
@@ -323,9 +383,13 @@ struct Cons {
       consumers_sync();
       return;
     }
-    const float* src = ph.in_a;
     float ss = 0.0f;
-    for (int e = tid; e < n; e += 256) {
+    float wv[kMaxD / 256];
+#pragma unroll
+    for (int j = 0; j < kMaxD / 256; j++) {
+      int e = tid + j * 256;
+      if (e >= n) break;
+      wv[j] = __ldg(ph.norm_w + e);
       float v;
       if (ph.in_mode == IN_EMBED_RMS) {
         v = __ldg(P.embed + (size_t)P.ids[0] * n + e);
@@ -337,19 +401,24 @@ struct Cons {
         v = (__ldcg(ph.in_a + e) + __ldcg(ph.in_b + e)) + __ldg(ph.in_c + e);
         if (blockIdx.x == 0) ph.xout[e] = v;
       } else {
-        v = __ldcg(src + e);
+        v = __ldcg(ph.in_a + e);
       }
-      sm.xin[e] = v;
+      sm.xraw[e] = v;
       ss = fmaf(v, v, ss);
     }
     ss = warp_sum(ss);
     if (lane == 0) sm.red[warp] = ss;
     consumers_sync();
-    float t = 0.0f;
+    float tsum = 0.0f;
 #pragma unroll
-    for (int w = 0; w < kConsumerWarps; w++) t += sm.red[w];
-    const float r = 1.0f / sqrtf(t / (float)n + P.eps);
-    for (int e = tid; e < n; e += 256) sm.xin[e] = sm.xin[e] * r * __ldg(ph.norm_w + e);
+    for (int w = 0; w < kConsumerWarps; w++) tsum += sm.red[w];
+    const float r = 1.0f / sqrtf(tsum / (float)n + P.eps);
+#pragma unroll
+    for (int j = 0; j < kMaxD / 256; j++) {
+      int e = tid + j * 256;
+      if (e >= n) break;
+      sm.xin[e] = sm.xraw[e] * r * wv[j];
+    }
     consumers_sync();
   }
 
@@ -358,8 +427,9 @@ struct Cons {
     // rows ≤ 16.  With fewer than 8 rows, warps split the columns.
     const int seg = rows >= 8 ? 1 : 8 / rows;
     const int span = cols / seg;
+    const int stride = rows >= 8 ? 8 : rows;
     const float4* x4 = reinterpret_cast<const float4*>(sm.xin);
-    for (int r = warp % (rows >= 8 ? 8 : rows); r < rows; r += (rows >= 8 ? 8 : rows)) {
+    for (int r = warp % stride; r < rows; r += stride) {
       const int sgi = rows >= 8 ? 0 : warp / rows;
       if (rows < 8 && sgi >= seg) break;
       const float4* w4 = reinterpret_cast<const float4*>(w + (size_t)r * cols + sgi * span);
@@ -370,7 +440,6 @@ struct Cons {
       a = warp_sum(a);
       if (lane == 0) {
         if (seg == 1) {
-          // row r of the tile → logical output and pair half
           int half = pair_n ? r / n : 0, o = pair_n ? r % n : r;
           sm.acc[half][acc_base + o] = a;
         } else {
@@ -389,10 +458,11 @@ struct Cons {
     }
   }
 
-  __device__ void gemv_phase(const Phase& ph, int item_phase_index) {
+  __device__ void gemv_phase(const Phase& ph) {
     const int G = gridDim.x;
-    bool any = blockIdx.x < ph.items;
-    if (!any) return;
+    // Normalising prologues run everywhere: they also refresh sm.xraw, the
+    // residual of the phases that follow.
+    if (blockIdx.x >= ph.items && ph.in_mode == IN_PLAIN) return;
     prologue(ph);
     const int T = tile_outs(ph);
     const bool pair = is_pair(ph);
@@ -411,18 +481,17 @@ struct Cons {
       epilogue(ph, sg, o0, o1, i);
       consumers_sync();
     }
-    (void)item_phase_index;
   }
 
   __device__ void epilogue(const Phase& ph, const Segment& sg, int o0, int o1, int item) {
     const int n = o1 - o0;
     if (ph.out_mode == OUT_ROPE) {
       const int d = P.d;
+      const size_t slot = (size_t)(pos % ph.cap);
       for (int t = tid; t < n; t += 256) {
         int o = o0 + t;
         int sec = o / (d / 2), rem = o % (d / 2), h = rem / 32, j = rem % 32;
         float a = sm.acc[0][t], b = sm.acc[1][t];
-        size_t slot = (size_t)(pos % ph.cap);
         if (sec < 2) {
           float ang = (float)pos * __ldg(ph.inv_freq + j);
           float sn, cs;
@@ -448,16 +517,16 @@ struct Cons {
       int o = o0 + t;
       float a = sm.acc[0][t];
       if (ph.out_mode == OUT_ADD)
-        sg.out[o] = __ldcg(sg.out + o) + a;
+        sg.out[o] = (ph.res_smem ? sm.xraw[o] : __ldcg(sg.out + o)) + a;
       else if (ph.out_mode == OUT_SILU)
         sg.out[o] = silu_mul(a, sm.acc[1][t]);
       else
         sg.out[o] = a;
     }
-    if (ph.out_mode == OUT_LOGITS) logits_argmax(sg, o0, n, item, ph.items);
+    if (ph.out_mode == OUT_LOGITS) logits_argmax(o0, n, item, ph.items);
   }
 
-  __device__ void logits_argmax(const Segment& sg, int o0, int n, int item, int items) {
+  __device__ void logits_argmax(int o0, int n, int item, int items) {
     unsigned long long best = 0;
     for (int t = tid; t < n; t += 256) {
       float v = sm.acc[0][t];
@@ -559,16 +628,14 @@ struct Cons {
       if (!tile) return;
       const float* Kt = tile;
       const float* Vt = tile + kAttnTile * kDH;
-      // warp w: rows w*8 .. w*8+7; lane group: rows +grp and +4+grp.
 #pragma unroll
-      for (int half = 0; half < 2; half++) {
-        int r = warp * 8 + half * 4 + grp;
+      for (int j = 0; j < kAttnTile / 32; j++) {
+        int r = grp + 4 * warp + 32 * j;
         bool valid = r < n;
         int rr = valid ? r : 0;
         float sc = fold(Kt + rr * kDH);
         if (valid) update(sc, Vt + rr * kDH);
       }
-      consumers_sync();
       release();
     }
     if (s == ph.splits - 1 && warp == 0 && grp == 0) {
@@ -615,18 +682,18 @@ struct Cons {
     }
     consumers_sync();
     float* out = ph.part + (size_t)item * (kDH + 2);
-    if (tid < kDH) {
-      float m0 = sm.wsm[0][kDH], l0 = sm.wsm[0][kDH + 1], a0 = sm.wsm[0][tid];
+    if (tid < kDH + 2) {
+      const int e = tid < kDH ? tid : 0;
+      float m0 = sm.wsm[0][kDH], l0 = sm.wsm[0][kDH + 1], a0 = sm.wsm[0][e];
       for (int w = 1; w < kConsumerWarps; w++) {
         float om = sm.wsm[w][kDH], ol = sm.wsm[w][kDH + 1];
         float M = fmaxf(m0, om);
         float ca = m0 == -INFINITY ? 0.0f : expf(m0 - M), cb = om == -INFINITY ? 0.0f : expf(om - M);
         l0 = l0 * ca + ol * cb;
-        a0 = a0 * ca + sm.wsm[w][tid] * cb;
+        a0 = a0 * ca + sm.wsm[w][e] * cb;
         m0 = M;
       }
-      out[tid] = a0;
-      if (tid == 0) out[kDH] = m0, out[kDH + 1] = l0;
+      out[tid] = tid < kDH ? a0 : (tid == kDH ? m0 : l0);
     }
     consumers_sync();
     if (tid == 0) {
@@ -636,19 +703,22 @@ struct Cons {
     }
     consumers_sync();
     if (sm.flag == 2) {
+      // Last split of head h to arrive: merge all splits, in split order.
       __threadfence();
+      const float* p0 = ph.part + (size_t)h * ph.splits * (kDH + 2);
+      for (int e = tid; e < ph.splits * (kDH + 2); e += 256) sm.cmb[e / (kDH + 2)][e % (kDH + 2)] = __ldcg(p0 + e);
+      consumers_sync();
       if (tid < kDH) {
-        const float* p0 = ph.part + (size_t)h * ph.splits * (kDH + 2);
         float M = -INFINITY;
-        for (int j = 0; j < ph.splits; j++) M = fmaxf(M, __ldcg(p0 + j * (kDH + 2) + kDH));
+        for (int j = 0; j < ph.splits; j++) M = fmaxf(M, sm.cmb[j][kDH]);
         float L = 0.0f, A = 0.0f;
         if (M != -INFINITY)
           for (int j = 0; j < ph.splits; j++) {
-            float mj = __ldcg(p0 + j * (kDH + 2) + kDH);
+            float mj = sm.cmb[j][kDH];
             if (mj == -INFINITY) continue;
             float c = expf(mj - M);
-            L += __ldcg(p0 + j * (kDH + 2) + kDH + 1) * c;
-            A += __ldcg(p0 + j * (kDH + 2) + tid) * c;
+            L += sm.cmb[j][kDH + 1] * c;
+            A += sm.cmb[j][tid] * c;
           }
         ph.y[h * kDH + tid] = L > 0.0f ? A / L : 0.0f;
       }
@@ -670,6 +740,7 @@ struct Cons {
       sm.vec[2][tid] = __ldcg(row + 2 * d + h * kDH + tid);
       sm.vec[3][tid] = __ldcg(row + 3 * d + h * kDH + tid);
     }
+    const float dcy = 1.0f / (1.0f + expf(__ldcg(ph.dec + h) + __ldg(ph.bias + h)));
     consumers_sync();
     if (warp < 2) {  // warp 0: |q|, warp 1: |k|
       float a = sm.vec[warp][lane], b = sm.vec[warp][lane + 32];
@@ -678,9 +749,7 @@ struct Cons {
       sm.vec[warp][lane] = a * r;
       sm.vec[warp][lane + 32] = b * r;
     }
-    const float dcy = 1.0f / (1.0f + expf(__ldcg(ph.dec + h) + __ldg(ph.bias + h)));
-    float* tile = const_cast<float*>(take());
-    consumers_sync();
+    float* tile = const_cast<float*>(take());  // (its barrier also orders the l2norm above)
     if (!tile) return;
     const int b = tid & 63, qa = tid >> 6;
     const float vb = sm.vec[2][b];
@@ -710,19 +779,37 @@ struct Cons {
     release();
   }
 
-  __device__ void run(const Plan& Pl) {
-    for (int p = 0; p < Pl.nphases && ok; p++) {
-      const Phase& ph = Pl.phases[p];
+  __device__ void stamp(int p, int which) {
+    if (P.trace && tid == 0) P.trace[((size_t)p * gridDim.x + blockIdx.x) * 2 + which] = now_ns();
+  }
+
+  __device__ void run() {
+    for (int p = 0; p < P.nphases && ok; p++) {
+      const Phase& ph = P.phases[p];
       if (p > 0) {
+        stamp(p - 1, 1);
         grid_sync();
         if (!ok) return;
       }
+      stamp(p, 0);
       if (ph.kind == PH_GEMV) {
-        gemv_phase(ph, p);
+        gemv_phase(ph);
       } else if (ph.kind == PH_ATTN) {
         for (int i = blockIdx.x; i < ph.items && ok; i += gridDim.x) attn_item(ph, i);
       } else {
         for (int i = blockIdx.x; i < ph.items && ok; i += gridDim.x) gla_item(ph, i);
+      }
+    }
+    consumers_sync();
+    stamp(P.nphases - 1, 1);
+    if (tid == 0 && ok) {
+      // The last CTA to finish resets the barrier count for the next step:
+      // every CTA has passed every barrier by then.
+      __threadfence();
+      unsigned prev = atomicAdd(P.bar + 1, 1u);
+      if (prev == gridDim.x - 1) {
+        atomicExch(P.bar, 0u);
+        atomicExch(P.bar + 1, 0u);
       }
     }
   }
@@ -748,12 +835,14 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_mega(const Plan* __restr
     return;
   }
   Cons c(P, sm, ring, pos);
-  c.run(P);
+  c.run();
 }
 
 }  // namespace
 
 size_t smem_bytes() { return ((sizeof(Smem) + 1023) / 1024) * 1024 + (size_t)kStages * kStageBytes; }
+static_assert(((sizeof(Smem) + 1023) / 1024) * 1024 + (size_t)kStages * kStageBytes <= 227 * 1024,
+              "decode kernel shared memory above the 227 KB an sm_100 CTA may use");
 
 void prepare() {
   SLM_CUDA(cudaFuncSetAttribute(k_decode_mega, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_bytes()));

@@ -13,9 +13,12 @@ constexpr int kThreads = (kConsumerWarps + 1) * 32;  // + one producer warp
 constexpr int kStages = 4;
 constexpr int kStageBytes = 48 * 1024;
 constexpr int kMaxCols = 3072;       // widest GEMV input held on chip
+constexpr int kMaxD = 1024;          // widest normalised (d_model) input
 constexpr int kMaxItemOut = 256;     // logical outputs per GEMV item
 constexpr int kDH = 64;              // head size of the kernel
-constexpr int kAttnTile = 64;        // cache positions per attention tile
+constexpr int kAttnTile = 96;        // cache positions per attention tile (K + V = one stage)
+constexpr int kMaxSplits = 16;       // attention splits per head
+constexpr int kLookahead = 8;        // tiles prefetched into L2 ahead of the ring
 
 enum PhaseKind : int { PH_GEMV = 0, PH_ATTN = 1, PH_GLA = 2 };
 
@@ -49,6 +52,7 @@ struct Phase {
   // GEMV
   int cols;
   int in_mode, out_mode;
+  int res_smem;  // OUT_ADD: the residual is the x of the last normalising prologue (kept on chip)
   const float *in_a, *in_b, *in_c, *norm_w;
   float* xout;
   int nseg;
@@ -87,9 +91,12 @@ struct Plan {
   unsigned* out_index;
   uint32_t* hist;       // optional history array (same index as out + hist_base)
   unsigned long long hist_base;
-  unsigned* bar;        // grid barrier: [0] arrivals, [1] generation
+  unsigned* bar;        // grid barrier: [0] arrivals (monotonic in a step), [1] CTAs done
   int* err;             // error word: 8 = a bounded wait expired
   long long spin_limit;
+  // Optional timeline: trace[(phase·grid + cta)·2 + {0, 1}] = globaltimer (ns)
+  // when the CTA starts the phase's work and when it reaches the barrier.
+  unsigned long long* trace;
 };
 
 }  // namespace mega

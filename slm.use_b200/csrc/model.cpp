@@ -101,6 +101,8 @@ struct slm_session {
   slm::mega::Phase* phases_dev = nullptr;
   float* xc = nullptr;
   int grid = 0;
+  unsigned long long* trace = nullptr;  // per-phase timeline of the last step (SLM_OPT_TRACE)
+  unsigned* attn_count = nullptr;        // per-head arrival counters of the attention phases
 };
 
 namespace slm {
@@ -373,7 +375,7 @@ void advance(slm_session* se, size_t m, bool want_logits) {
 std::string mega_unsupported(const slm_model* md) {
   const Config& c = md->cfg;
   if (c.dh() != (size_t)mega::kDH) return "head size is not 64";
-  if (c.d % 32 != 0 || c.d > (size_t)mega::kMaxCols) return "d_model must be a multiple of 32 and at most 3072";
+  if (c.d % 32 != 0 || c.d > (size_t)mega::kMaxD) return "d_model must be a multiple of 32 and at most 1024";
   if (md->hidden % 32 != 0 || md->hidden > (size_t)mega::kMaxCols) return "FFN width must be a multiple of 32, <= 3072";
   if (c.damp != 1.0f) return "damp != 1";
   if (c.prelude.empty()) return "no prelude block";
@@ -412,11 +414,12 @@ void build_plan(slm_session* se) {
     p.items = s0.items;
     return p;
   };
-  const int splits = std::max(1, G / H);
+  const int splits = std::min(kMaxSplits, std::max(1, G / H));
   const float scale = 1.0f / std::sqrt((float)c.dh());
   // Attention partials (heads × splits × (dh + 2)) and per-head arrival counters.
   float* attn_part = static_cast<float*>(alloc_zero(se, (size_t)H * splits * (kDH + 2) * sizeof(float)));
   auto* attn_count = static_cast<unsigned*>(alloc_zero(se, (size_t)H * sizeof(unsigned)));
+  se->attn_count = attn_count;
   float* X0 = se->xa;
   struct In {
     int mode;
@@ -449,12 +452,16 @@ void build_plan(slm_session* se) {
       g.items = H;
       ph.push_back(g);
     }
+    // The residual of o and down is the x of the phase two back, whose
+    // normalising prologue left it in shared memory on every CTA.
     ph.push_back(gemv(d, IN_PLAIN, se->y, nullptr, nullptr, nullptr, nullptr, OUT_ADD, seg(b.o.w, d, per(d, G, 1), X)));
+    ph.back().res_smem = 1;
     const int F = (int)b.down.cols;
     ph.push_back(gemv(d, IN_RMS, X, nullptr, nullptr, b.norm2, nullptr, OUT_SILU,
                       seg(b.up.w, F, per(F, G, 1), se->mid)));
     ph.push_back(gemv(F, IN_PLAIN, se->mid, nullptr, nullptr, nullptr, nullptr, OUT_ADD,
                       seg(b.down.w, d, per(d, G, 1), X)));
+    ph.back().res_smem = 1;
   };
   for (size_t i = 0; i < md->prelude.size(); i++)
     block(md->prelude[i], se->pre[i], X0, In{i == 0 ? IN_EMBED_RMS : IN_RMS, nullptr, nullptr, nullptr, nullptr});
@@ -568,12 +575,18 @@ void step_device(slm_session* se) {
   se->pos += 1;
 }
 
-void check_device_error(slm_ctx* c) {
+void check_device_error(slm_ctx* c, slm_session* se = nullptr) {
   int h = 0;
   SLM_CUDA(cudaMemcpyAsync(&h, c->err, sizeof(int), cudaMemcpyDeviceToHost, c->stream));
   SLM_CUDA(cudaStreamSynchronize(c->stream));
   if (h) {
     SLM_CUDA(cudaMemsetAsync(c->err, 0, sizeof(int), c->stream));
+    if ((h & 8) && se && se->mega_ok) {
+      // A step that gave up left its barrier and arrival counters mid-way.
+      SLM_CUDA(cudaMemsetAsync(se->plan_host.arg_count, 0, 16 * sizeof(unsigned), c->stream));
+      SLM_CUDA(cudaMemsetAsync(se->attn_count, 0, se->model->cfg.heads * sizeof(unsigned), c->stream));
+      SLM_CUDA(cudaStreamSynchronize(c->stream));
+    }
     std::string why;
     if (h & 1) why += " token id out of range;";
     if (h & 8) why += " a bounded wait in the decode kernel expired (state of this step is undefined);";
@@ -823,6 +836,18 @@ int slm_session_set(slm_session* se, int option, int64_t value) {
       if (!se->use_graph) drop_graph(se);
       return;
     }
+    if (option == SLM_OPT_TRACE) {
+      SLM_REQUIRE(se->mega_ok, "tracing needs the persistent decode kernel");
+      Device dev(se->ctx);
+      if (value && !se->trace) {
+        size_t n = (size_t)se->plan_host.nphases * se->grid * 2;
+        se->trace = static_cast<unsigned long long*>(alloc_zero(se, n * sizeof(unsigned long long)));
+      }
+      se->plan_host.trace = value ? se->trace : nullptr;
+      SLM_CUDA(cudaMemcpyAsync(se->plan_dev, &se->plan_host, sizeof(se->plan_host), cudaMemcpyHostToDevice,
+                               se->ctx->stream));
+      return;
+    }
     if (option == SLM_OPT_MEGA) {
       if (value && !se->mega_ok) fail(SLM_ERR_INVALID, "persistent decode kernel unavailable: " + se->mega_why);
       se->use_mega = value != 0;
@@ -840,6 +865,20 @@ int slm_session_stat(const slm_session* se, int what, int64_t* out) {
     else if (what == SLM_STAT_MEGA) *out = se->use_mega ? 1 : 0;
     else if (what == SLM_STAT_PHASES) *out = se->mega_ok ? se->plan_host.nphases : 0;
     else fail(SLM_ERR_INVALID, "unknown counter");
+  });
+}
+
+int slm_session_trace(slm_session* se, uint64_t* out, size_t cap, size_t* n_out) {
+  return guard([&] {
+    SLM_REQUIRE(se && n_out && (out || cap == 0), "bad arguments");
+    SLM_REQUIRE(se->trace, "tracing is off (SLM_OPT_TRACE)");
+    Device dev(se->ctx);
+    size_t n = (size_t)se->plan_host.nphases * se->grid * 2;
+    *n_out = n;
+    if (cap >= n) {
+      SLM_CUDA(cudaMemcpyAsync(out, se->trace, n * sizeof(uint64_t), cudaMemcpyDeviceToHost, se->ctx->stream));
+      SLM_CUDA(cudaStreamSynchronize(se->ctx->stream));
+    }
   });
 }
 
@@ -886,7 +925,7 @@ int slm_logits(slm_session* se, float* out) {
     Device dev(se->ctx);
     SLM_CUDA(cudaMemcpyAsync(out, se->logits, se->model->cfg.vocab * sizeof(float), cudaMemcpyDeviceToHost,
                              se->ctx->stream));
-    check_device_error(se->ctx);
+    check_device_error(se->ctx, se);
   });
 }
 
@@ -930,7 +969,7 @@ int slm_sample(slm_session* se, const slm_sampling* sp, const uint32_t* recent, 
     uint32_t id = 0;
     SLM_CUDA(cudaMemcpyAsync(&id, se->out_dev, sizeof(id), cudaMemcpyDeviceToHost, s));
     SLM_CUDA(cudaMemcpyAsync(&st, se->rng_dev, sizeof(st), cudaMemcpyDeviceToHost, s));
-    check_device_error(se->ctx);
+    check_device_error(se->ctx, se);
     *out_id = id;
     *rng_state = st;
   });
@@ -1013,7 +1052,7 @@ int slm_decode(slm_session* se, uint32_t first, size_t n, const slm_sampling* sp
     if (fused) plan_outputs(se, false, nullptr, nullptr, 0);
     SLM_CUDA(cudaMemcpyAsync(out, se->outs_dev, n * sizeof(uint32_t), cudaMemcpyDeviceToHost, s));
     SLM_CUDA(cudaMemcpyAsync(&st, se->rng_dev, sizeof(st), cudaMemcpyDeviceToHost, s));
-    check_device_error(se->ctx);
+    check_device_error(se->ctx, se);
     *rng_state = st;
   });
 }

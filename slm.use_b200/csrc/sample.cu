@@ -65,8 +65,8 @@ struct Shared {
   float red[32];
   float wpre[32];
   unsigned long long best, prefix, thresh;
-  uint32_t remaining, count, found, keep, nsorted;
-  float held, enough, s_sum, s_r, top;
+  uint32_t remaining, count, found, nsorted;
+  float s_sum, s_r;
 };
 
 // The c largest composites below `bound` (all when bound == 0): sets
@@ -275,25 +275,17 @@ __global__ void __launch_bounds__(ST) k_sample(SampleArgs a) {
     return;
   }
 
-  // Sorted candidates, in rounds.
+  // Sorted candidates, in rounds.  Without top-k every id is sorted, so the
+  // top-p total is the sequential sum in sorted order, as the reference
+  // computes it (sample.rs:61-73).
   const uint32_t K = use_k ? a.top_k : (uint32_t)V;
   const bool multi = K > (uint32_t)MAXC;
-  if (!use_k) {  // the top-p cut needs Σ over every id
-    float part = 0.0f;
-    for (int i = tid; i < V; i += ST) part += expf((work[i] - top) / invT);
-    float total = block_sum(part, sh.red);
-    if (tid == 0) sh.enough = a.top_p * total;
-  }
-  if (tid == 0) {
-    sh.nsorted = 0;
-    sh.keep = 0;
-    sh.held = 0.0f;
-  }
+  if (tid == 0) sh.nsorted = 0;
   __syncthreads();
   unsigned long long bound = 0;
   while (true) {
     const uint32_t done = sh.nsorted;
-    if (done >= K || sh.keep) break;
+    if (done >= K) break;
     const uint32_t c = min((uint32_t)MAXC, K - done);
     select_round(work, V, bound, c, sh);
     gather_sort(work, V, bound, c, sh);
@@ -307,43 +299,25 @@ __global__ void __launch_bounds__(ST) k_sample(SampleArgs a) {
       }
     }
     __syncthreads();
-    if (tid == 0) {
-      if (!use_k && a.top_p < 1.0f) {
-        float held = sh.held;
-        for (uint32_t i = 0; i < c; i++) {
-          held += sh.wts[i];
-          if (held >= sh.enough) {
-            sh.keep = done + i + 1;
-            break;
-          }
-        }
-        sh.held = held;
-      }
-      sh.nsorted = done + c;
-    }
+    if (tid == 0) sh.nsorted = done + c;
     bound = sh.cand[c - 1];
     __syncthreads();
   }
   if (tid == 0) {
     auto W = [&](uint32_t i) { return multi ? sw[i] : sh.wts[i]; };
     auto ID = [&](uint32_t i) { return multi ? sid[i] : comp_id(sh.cand[i]); };
-    uint32_t keep = sh.keep;
-    if (use_k) {
-      keep = K;
-      if (a.top_p < 1.0f) {
-        float total = 0.0f;
-        for (uint32_t i = 0; i < K; i++) total += W(i);
-        float enough = a.top_p * total, held = 0.0f;
-        for (uint32_t i = 0; i < K; i++) {
-          held += W(i);
-          if (held >= enough) {
-            keep = i + 1;
-            break;
-          }
+    uint32_t keep = K;
+    if (a.top_p < 1.0f) {
+      float total = 0.0f;
+      for (uint32_t i = 0; i < K; i++) total += W(i);
+      float enough = a.top_p * total, held = 0.0f;
+      for (uint32_t i = 0; i < K; i++) {
+        held += W(i);
+        if (held >= enough) {
+          keep = i + 1;
+          break;
         }
       }
-    } else if (keep == 0) {
-      keep = sh.nsorted;
     }
     float total = 0.0f;
     for (uint32_t i = 0; i < keep; i++) total += W(i);
