@@ -224,9 +224,11 @@ int slm_session_set(slm_session* se, int option, int64_t value);
 int slm_session_stat(const slm_session* se, int what, int64_t* out);
 
 /* Timeline of the last persistent step (SLM_OPT_TRACE on): for each phase p
- * and CTA c, out[(p·grid + c)·2] is the globaltimer (ns) when the CTA began
- * the phase's work and out[(p·grid + c)·2 + 1] when it reached the next grid
- * barrier.  *n_out receives the count; nothing is copied when cap < count. */
+ * and CTA c, eight values at out[(p·grid + c)·8]: the globaltimer (ns) when
+ * the CTA began the phase's work and when it reached the next grid barrier;
+ * the ns it spent waiting for tiles, building the phase's input, on tile
+ * arithmetic and in GEMV epilogues; the GEMV tiles it took; 0.
+ * *n_out receives the count; nothing is copied when cap < count. */
 int slm_session_trace(slm_session* se, uint64_t* out, size_t cap, size_t* n_out);
 
 #ifdef __cplusplus

@@ -440,13 +440,14 @@ class Session:
         _check(lib().slm_session_set(self._h, SLM_OPT_TRACE, 1 if on else 0))
 
     def trace(self) -> np.ndarray:
-        """Timeline of the last persistent step: [phase][cta][start, barrier] in ns."""
+        """Timeline of the last persistent step: [phase][cta][8] (start, barrier, waited, prologue,
+        compute, epilogue ns, tiles, 0)."""
         n = _sz(0)
         _check(lib().slm_session_trace(self._h, None, 0, _c.byref(n)))
         out = np.empty(n.value, dtype=np.uint64)
         _check(lib().slm_session_trace(self._h, out.ctypes.data_as(_u64p), n.value, _c.byref(n)))
         phases = self.stat(SLM_STAT_PHASES)
-        return out.reshape(phases, -1, 2)
+        return out.reshape(phases, -1, 8)
 
     @property
     def mega(self) -> bool:

@@ -64,6 +64,10 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, unsigned by
 __device__ __forceinline__ void prefetch_l2(const void* src, unsigned bytes) {
   asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
 }
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(saddr(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 __device__ __forceinline__ unsigned long long now_ns() {
   unsigned long long t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
@@ -269,10 +273,10 @@ struct Walker {
 
 struct Smem {
   uint64_t full[kStages], empty[kStages];
+  Phase ph[2];  // descriptors of this phase and the next, staged with cp.async
   float xin[kMaxCols];
   float xraw[kMaxD];
-  float acc[2][kMaxItemOut];
-  float part[16][8];
+  float acc[2][2][kMaxItemOut];  // [column half][pair half][output]
   float red[32];
   float wsm[kConsumerWarps][kDH + 2];
   float cmb[kMaxSplits][kDH + 2];
@@ -286,12 +290,13 @@ struct Smem {
 // Producer: one thread, two cursors over the same tile sequence.
 // ---------------------------------------------------------------------------
 __device__ void producer(const Plan& P, Smem& sm, char* ring, long long pos) {
+  // The lookahead cursor starts where the ring's first fill ends and is only
+  // advanced after a ring copy has been issued, so prefetches never queue
+  // ahead of data the consumers are about to wait for.
   Walker ring_w(&P, pos), ahead(&P, pos);
-  Tile T;
-  for (int j = 0; j < kLookahead; j++) {
-    if (!ahead.next(T)) break;
-    for (int s = 0; s < T.n; s++) prefetch_l2(T.src[s], T.bytes[s]);
-  }
+  Tile T, A;
+  for (int j = 0; j < kStages; j++)
+    if (!ahead.next(A)) break;
   unsigned k = 0;
   while (ring_w.next(T)) {
     const int s = k % kStages;
@@ -300,9 +305,14 @@ __device__ void producer(const Plan& P, Smem& sm, char* ring, long long pos) {
     char* dst = ring + (size_t)s * kStageBytes;
     for (int j = 0; j < T.n; j++) bulk_g2s(dst + T.off[j], T.src[j], T.bytes[j], &sm.full[s]);
     k++;
-    Tile A;
-    if (ahead.next(A))
-      for (int j = 0; j < A.n; j++) prefetch_l2(A.src[j], A.bytes[j]);
+    if (k >= (unsigned)kStages) {
+      // One more tile of lookahead per tile issued, up to kLookahead beyond the ring.
+      int burst = k == (unsigned)kStages ? kLookahead : 1;
+      for (int b = 0; b < burst; b++) {
+        if (!ahead.next(A)) break;
+        for (int j = 0; j < A.n; j++) prefetch_l2(A.src[j], A.bytes[j]);
+      }
+    }
   }
   // Drain: every copy issued must land before the CTA may exit.
   unsigned first = k > (unsigned)kStages ? k - kStages : 0;
@@ -329,9 +339,25 @@ struct Cons {
     lane = tid & 31;
   }
 
+  // Starts copying phase q's descriptor into sm.ph[q & 1]; it lands by the
+  // next consumers barrier after stage_wait().  Reading descriptors from
+  // shared memory keeps them off the post-barrier critical path (a gpu-scope
+  // acquire leaves L1 cold).
+  __device__ void stage_phase(int q) {
+    constexpr int chunks = sizeof(Phase) / 16;
+    if (q < P.nphases && tid < chunks)
+      cp_async16(reinterpret_cast<char*>(&sm.ph[q & 1]) + tid * 16,
+                 reinterpret_cast<const char*>(P.phases + q) + tid * 16);
+  }
+  __device__ void stage_wait() { cp_async_wait_all(); }
+
+  unsigned long long waited = 0, pro_ns = 0, comp_ns = 0, epi_ns = 0, ntiles = 0;  // for the timeline
+
   __device__ const float* take() {
     int s = k % kStages;
+    unsigned long long t0 = P.trace && tid == 0 ? now_ns() : 0;
     int got = wait_mbar(&sm.full[s], (k / kStages) & 1, P.err) ? 1 : 0;
+    if (t0) waited += now_ns() - t0;
     if (!consumers_and(got)) {
       ok = false;
       return nullptr;
@@ -352,8 +378,7 @@ struct Cons {
     if (tid == 0) {
       unsigned* cnt = P.bar;
       const unsigned target = barriers * gridDim.x;
-      __threadfence();
-      red_release_add(cnt, 1u);
+      red_release_add(cnt, 1u);  // release: covers the CTA's writes ordered by the barrier above
       unsigned long long t0 = 0;
       for (unsigned it = 0; ld_acquire(cnt) < target; it++) {
         if ((it & 15) == 15) {
@@ -376,94 +401,217 @@ struct Cons {
   }
 
   // Input vector of a GEMV phase into sm.xin (and the raw x into sm.xraw).
+  // Every load of a thread is issued before any is used.
   __device__ void prologue(const Phase& ph) {
-    const int n = ph.cols;
+    const int n4 = ph.cols / 4;
+    if (ph.in_mode == IN_ATTN) {
+      attn_merge(ph);
+      return;
+    }
     if (ph.in_mode == IN_PLAIN) {
-      for (int e = tid; e < n; e += 256) sm.xin[e] = __ldcg(ph.in_a + e);
+      constexpr int J = kMaxCols / 4 / 256;
+      float4 v[J];
+      const float4* a4 = reinterpret_cast<const float4*>(ph.in_a);
+#pragma unroll
+      for (int j = 0; j < J; j++)
+        if (tid + j * 256 < n4) v[j] = __ldcg(a4 + tid + j * 256);
+#pragma unroll
+      for (int j = 0; j < J; j++)
+        if (tid + j * 256 < n4) reinterpret_cast<float4*>(sm.xin)[tid + j * 256] = v[j];
       consumers_sync();
       return;
     }
-    float ss = 0.0f;
-    float wv[kMaxD / 256];
-#pragma unroll
-    for (int j = 0; j < kMaxD / 256; j++) {
-      int e = tid + j * 256;
-      if (e >= n) break;
-      wv[j] = __ldg(ph.norm_w + e);
-      float v;
+    // Normalised input: d ≤ kMaxD, at most one float4 per thread.
+    const bool own = tid < n4;
+    float4 x = make_float4(0.f, 0.f, 0.f, 0.f), w = x;
+    if (own) {
+      w = __ldg(reinterpret_cast<const float4*>(ph.norm_w) + tid);
       if (ph.in_mode == IN_EMBED_RMS) {
-        v = __ldg(P.embed + (size_t)P.ids[0] * n + e);
+        x = __ldg(reinterpret_cast<const float4*>(P.embed + (size_t)P.ids[0] * ph.cols) + tid);
         if (blockIdx.x == 0) {
-          P.e0[e] = v;
-          P.x0[e] = v;
+          reinterpret_cast<float4*>(P.e0)[tid] = x;
+          reinterpret_cast<float4*>(P.x0)[tid] = x;
         }
       } else if (ph.in_mode == IN_LOOP_RMS) {
-        v = (__ldcg(ph.in_a + e) + __ldcg(ph.in_b + e)) + __ldg(ph.in_c + e);
-        if (blockIdx.x == 0) ph.xout[e] = v;
+        float4 a = __ldcg(reinterpret_cast<const float4*>(ph.in_a) + tid);
+        float4 b = __ldcg(reinterpret_cast<const float4*>(ph.in_b) + tid);
+        float4 c = __ldg(reinterpret_cast<const float4*>(ph.in_c) + tid);
+        x = make_float4((a.x + b.x) + c.x, (a.y + b.y) + c.y, (a.z + b.z) + c.z, (a.w + b.w) + c.w);
+        if (blockIdx.x == 0) reinterpret_cast<float4*>(ph.xout)[tid] = x;
       } else {
-        v = __ldcg(ph.in_a + e);
+        x = __ldcg(reinterpret_cast<const float4*>(ph.in_a) + tid);
       }
-      sm.xraw[e] = v;
-      ss = fmaf(v, v, ss);
+      reinterpret_cast<float4*>(sm.xraw)[tid] = x;
     }
+    float ss = x.x * x.x;
+    ss = fmaf(x.y, x.y, ss);
+    ss = fmaf(x.z, x.z, ss);
+    ss = fmaf(x.w, x.w, ss);
     ss = warp_sum(ss);
     if (lane == 0) sm.red[warp] = ss;
     consumers_sync();
     float tsum = 0.0f;
 #pragma unroll
-    for (int w = 0; w < kConsumerWarps; w++) tsum += sm.red[w];
-    const float r = 1.0f / sqrtf(tsum / (float)n + P.eps);
+    for (int q = 0; q < kConsumerWarps; q++) tsum += sm.red[q];
+    const float r = 1.0f / sqrtf(tsum / (float)ph.cols + P.eps);
+    if (own)
+      reinterpret_cast<float4*>(sm.xin)[tid] =
+          make_float4(x.x * r * w.x, x.y * r * w.y, x.z * r * w.z, x.w * r * w.w);
+    consumers_sync();
+  }
+
+  // Attention output y = Σ_s e^{m_s−M}·acc_s / Σ_s e^{m_s−M}·l_s per (head, dim)
+  // from the partials of the previous phase ([head][split][dh | m | l]),
+  // merged in split order on every CTA: one round of loads, no last-arriver
+  // step in the attention phase.
+  template <int Q, int S>
+  __device__ void attn_merge_t(const Phase& ph, int d, int s_rt) {
+    const int H = ph.heads, Srt = S > 0 ? S : s_rt;
+    constexpr int QQ = Q > 0 ? Q : 1, SS = S > 0 ? S : 1;
+    float* ml = &sm.cmb[0][0];          // [H·S][2]: m, l; then c = e^{m − M_h}
+    float* Lh = &sm.cmb[kMaxSplits / 2][0];  // [H]: Σ_s c·l (after the H·S·2 ≤ 512 floats above)
+    for (int i = tid; i < H * Srt; i += 256) {
+      ml[2 * i] = __ldcg(ph.in_a + (size_t)i * (kDH + 2) + kDH);
+      ml[2 * i + 1] = __ldcg(ph.in_a + (size_t)i * (kDH + 2) + kDH + 1);
+    }
+    float av[QQ][SS];
+    if (Q > 0 && S > 0) {
 #pragma unroll
-    for (int j = 0; j < kMaxD / 256; j++) {
-      int e = tid + j * 256;
-      if (e >= n) break;
-      sm.xin[e] = sm.xraw[e] * r * wv[j];
+      for (int q = 0; q < QQ; q++) {
+        const int o = tid + 256 * q;
+        if (o >= d) break;
+        const float* src = ph.in_a + (size_t)(o / kDH) * S * (kDH + 2) + (o % kDH);
+#pragma unroll
+        for (int j = 0; j < SS; j++) av[q][j] = __ldcg(src + (size_t)j * (kDH + 2));
+      }
+    }
+    consumers_sync();
+    if (tid < H) {  // per head: the split weights, in split order
+      float* m = ml + 2 * tid * Srt;
+      float M = -INFINITY;
+      for (int j = 0; j < Srt; j++) M = fmaxf(M, m[2 * j]);
+      float L = 0.0f;
+      for (int j = 0; j < Srt; j++) {
+        float c = (M == -INFINITY || m[2 * j] == -INFINITY) ? 0.0f : expf(m[2 * j] - M);
+        L += m[2 * j + 1] * c;
+        m[2 * j] = c;
+      }
+      Lh[tid] = L;
+    }
+    consumers_sync();
+    for (int q = 0; q < (d + 255) / 256; q++) {
+      const int o = tid + 256 * q;
+      if (o >= d) break;
+      const float* c = ml + 2 * (o / kDH) * Srt;
+      const float* src = ph.in_a + (size_t)(o / kDH) * Srt * (kDH + 2) + (o % kDH);
+      float A = 0.0f;
+#pragma unroll
+      for (int j = 0; j < (S > 0 ? S : kMaxSplits); j++) {
+        if (j >= Srt) break;
+        float a;
+        if (Q > 0 && S > 0) {
+          a = 0.0f;
+#pragma unroll
+          for (int qq = 0; qq < QQ; qq++)
+            if (qq == q) a = av[qq][j];
+        } else {
+          a = __ldcg(src + (size_t)j * (kDH + 2));
+        }
+        A = fmaf(a, c[2 * j], A);
+      }
+      const float L = Lh[o / kDH];
+      sm.xin[o] = L > 0.0f ? A / L : 0.0f;
     }
     consumers_sync();
   }
 
-  // Dot products of one tile: `rows` weight rows of `cols` in smem → sm.acc.
-  __device__ void gemv_tile(const float* w, int rows, int cols, int acc_base, int pair_n, int n) {
-    // rows ≤ 16.  With fewer than 8 rows, warps split the columns.
-    const int seg = rows >= 8 ? 1 : 8 / rows;
-    const int span = cols / seg;
-    const int stride = rows >= 8 ? 8 : rows;
-    const float4* x4 = reinterpret_cast<const float4*>(sm.xin);
-    for (int r = warp % stride; r < rows; r += stride) {
-      const int sgi = rows >= 8 ? 0 : warp / rows;
-      if (rows < 8 && sgi >= seg) break;
-      const float4* w4 = reinterpret_cast<const float4*>(w + (size_t)r * cols + sgi * span);
-      const int c0 = sgi * span / 4;
-      float a = 0.0f;
-#pragma unroll 4
-      for (int c = lane; c < span / 4; c += 32) a = dot4(w4[c], x4[c0 + c], a);
-      a = warp_sum(a);
-      if (lane == 0) {
-        if (seg == 1) {
-          int half = pair_n ? r / n : 0, o = pair_n ? r % n : r;
-          sm.acc[half][acc_base + o] = a;
-        } else {
-          sm.part[r][sgi] = a;
+  // Attention output y = Σ_s e^{m_s−M}·acc_s / Σ_s e^{m_s−M}·l_s per (head, dim)
+  // from the partials of the previous phase ([head][split][dh | m | l]),
+  // merged in split order on every CTA: one round of loads, no last-arriver
+  // step in the attention phase.
+  template <int Q, int S>
+  __device__ void attn_merge_t(const Phase& ph, int d, int s_rt) {
+    const int H = ph.heads, Srt = S > 0 ? S : s_rt;
+    constexpr int QQ = Q > 0 ? Q : 1, SS = S > 0 ? S : 1;
+    float* ml = &sm.cmb[0][0];  // 2·H·S floats: m, l
+    for (int i = tid; i < H * Srt; i += 256) {
+      ml[2 * i] = __ldcg(ph.in_a + (size_t)i * (kDH + 2) + kDH);
+      ml[2 * i + 1] = __ldcg(ph.in_a + (size_t)i * (kDH + 2) + kDH + 1);
+    }
+    float av[QQ][SS];
+    if (Q > 0 && S > 0) {
+#pragma unroll
+      for (int q = 0; q < QQ; q++) {
+        const int o = tid + 256 * q;
+        if (o >= d) break;
+        const float* src = ph.in_a + (size_t)(o / kDH) * S * (kDH + 2) + (o % kDH);
+#pragma unroll
+        for (int j = 0; j < SS; j++) av[q][j] = __ldcg(src + (size_t)j * (kDH + 2));
+      }
+    }
+    consumers_sync();
+    for (int q = 0; q < (d + 255) / 256; q++) {
+      const int o = tid + 256 * q;
+      if (o >= d) break;
+      const float* mlh = ml + 2 * (o / kDH) * Srt;
+      const float* src = ph.in_a + (size_t)(o / kDH) * Srt * (kDH + 2) + (o % kDH);
+      float M = -INFINITY;
+      for (int j = 0; j < Srt; j++) M = fmaxf(M, mlh[2 * j]);
+      float L = 0.0f, A = 0.0f;
+      if (M != -INFINITY) {
+#pragma unroll
+        for (int j = 0; j < (S > 0 ? S : kMaxSplits); j++) {
+          if (j >= Srt) break;
+          const float mj = mlh[2 * j];
+          if (mj == -INFINITY) continue;
+          const float c = expf(mj - M);
+          L += mlh[2 * j + 1] * c;
+          float a;
+          if (Q > 0 && S > 0) {
+            a = 0.0f;
+#pragma unroll
+            for (int qq = 0; qq < QQ; qq++)
+              if (qq == q) a = av[qq][j];
+          } else {
+            a = __ldcg(src + (size_t)j * (kDH + 2));
+          }
+          A += a * c;
         }
       }
+      sm.xin[o] = L > 0.0f ? A / L : 0.0f;
     }
-    if (seg > 1) {
-      consumers_sync();
-      if (tid < rows) {
-        float a = 0.0f;
-        for (int g = 0; g < seg; g++) a += sm.part[tid][g];
-        int half = pair_n ? tid / n : 0, o = pair_n ? tid % n : tid;
-        sm.acc[half][acc_base + o] = a;
-      }
-    }
+    consumers_sync();
   }
 
-  __device__ void gemv_phase(const Phase& ph) {
+  // Attention output y = Σ_s e^{m_s−M}·acc_s / Σ_s e^{m_s−M}·l_s per (head, dim)
+  // from the partials of the previous phase ([head][split][dh | m | l]),
+  // merged in split order on every CTA: one round of loads, no last-arriver
+  // step in the attention phase.
+  __device__ void attn_merge(const Phase& ph) {
+    const int d = ph.cols;
+    if (d == 768 && ph.splits == 12)
+      attn_merge_t<3, 12>(ph, d, 12);
+    else
+      attn_merge_t<0, 0>(ph, d, ph.splits);
+  }
+
+  // GEMV phase with K float4 of x per lane held in registers.  A row of
+  // `cols` is split over S = 1 or 2 warps (S = 2 above 1536 columns); each
+  // warp walks the rows of a tile two at a time (two independent chains).
+  // Partial sums land in sm.acc[column half][pair half][output] and are
+  // combined, in a fixed order, in the epilogue.
+  template <int K>
+  __device__ void gemv_phase_k(const Phase& ph) {
     const int G = gridDim.x;
-    // Normalising prologues run everywhere: they also refresh sm.xraw, the
-    // residual of the phases that follow.
-    if (blockIdx.x >= ph.items && ph.in_mode == IN_PLAIN) return;
-    prologue(ph);
+    const int S = ph.cols > 1536 ? 2 : 1;
+    const int span = ph.cols / S;
+    const int sgi = warp % S, rowslot = warp / S, rstride = kConsumerWarps / S;
+    float4 xr[K];
+    {
+      const float4* xin4 = reinterpret_cast<const float4*>(sm.xin) + sgi * span / 4 + lane;
+#pragma unroll
+      for (int k = 0; k < K; k++) xr[k] = xin4[32 * k];
+    }
     const int T = tile_outs(ph);
     const bool pair = is_pair(ph);
     for (int i = blockIdx.x; i < ph.items && ok; i += G) {
@@ -471,15 +619,76 @@ struct Cons {
       gemv_item(ph, i, &s, &o0, &o1);
       const Segment& sg = ph.seg[s];
       for (int t0 = o0; t0 < o1; t0 += T) {
-        int n = min(T, o1 - t0);
+        const int n = min(T, o1 - t0);
+        const int rows = pair ? 2 * n : n;
         const float* w = take();
         if (!w) return;
-        gemv_tile(w, pair ? 2 * n : n, ph.cols, t0 - o0, pair ? 1 : 0, n);
-        consumers_sync();  // every warp done with the stage and sm.acc written
+        unsigned long long c0 = P.trace && tid == 0 ? now_ns() : 0;
+        for (int r = rowslot; r < rows; r += 2 * rstride) {
+          const int r2 = r + rstride;
+          const bool two = r2 < rows;
+          const float4* w0 = reinterpret_cast<const float4*>(w + (size_t)r * ph.cols + sgi * span) + lane;
+          const float4* w1 = reinterpret_cast<const float4*>(w + (size_t)(two ? r2 : r) * ph.cols + sgi * span) + lane;
+          float a0 = 0.0f, b0 = 0.0f, a1 = 0.0f, b1 = 0.0f;
+#pragma unroll
+          for (int k = 0; k < K; k++) {
+            float4 u = w0[32 * k], v = w1[32 * k];
+            if (k & 1) {
+              b0 = dot4(u, xr[k], b0);
+              b1 = dot4(v, xr[k], b1);
+            } else {
+              a0 = dot4(u, xr[k], a0);
+              a1 = dot4(v, xr[k], a1);
+            }
+          }
+          a0 += b0;
+          a1 += b1;
+#pragma unroll
+          for (int o = 16; o > 0; o >>= 1) {
+            a0 += __shfl_xor_sync(0xffffffffu, a0, o);
+            a1 += __shfl_xor_sync(0xffffffffu, a1, o);
+          }
+          if (lane == 0) {
+            const int base = t0 - o0;
+            sm.acc[sgi][pair ? r / n : 0][base + (pair ? r % n : r)] = a0;
+            if (two) sm.acc[sgi][pair ? r2 / n : 0][base + (pair ? r2 % n : r2)] = a1;
+          }
+        }
         release();
+        if (c0) comp_ns += now_ns() - c0, ntiles++;
       }
+      consumers_sync();  // every partial of the item written
+      unsigned long long e0 = P.trace && tid == 0 ? now_ns() : 0;
+      if (S == 2)
+        for (int t = tid; t < o1 - o0; t += 256) {
+          sm.acc[0][0][t] += sm.acc[1][0][t];
+          if (pair) sm.acc[0][1][t] += sm.acc[1][1][t];
+        }
+      if (S == 2) consumers_sync();
       epilogue(ph, sg, o0, o1, i);
       consumers_sync();
+      if (e0) epi_ns += now_ns() - e0;
+    }
+  }
+
+  __device__ void gemv_phase(const Phase& ph) {
+    // Normalising prologues run everywhere: they also refresh sm.xraw, the
+    // residual of the phases that follow.
+    if (blockIdx.x >= ph.items && ph.in_mode == IN_PLAIN) return;
+    unsigned long long t0 = P.trace && tid == 0 ? now_ns() : 0;
+    prologue(ph);
+    if (t0) pro_ns += now_ns() - t0;
+    if (blockIdx.x >= ph.items) return;
+    const int K = ph.cols / (ph.cols > 1536 ? 2 : 1) / 128;
+    switch (K) {
+      case 1: gemv_phase_k<1>(ph); break;
+      case 2: gemv_phase_k<2>(ph); break;
+      case 3: gemv_phase_k<3>(ph); break;
+      case 4: gemv_phase_k<4>(ph); break;
+      case 6: gemv_phase_k<6>(ph); break;
+      case 8: gemv_phase_k<8>(ph); break;
+      case 12: gemv_phase_k<12>(ph); break;
+      default: break;  // excluded when the plan is built
     }
   }
 
@@ -491,7 +700,7 @@ struct Cons {
       for (int t = tid; t < n; t += 256) {
         int o = o0 + t;
         int sec = o / (d / 2), rem = o % (d / 2), h = rem / 32, j = rem % 32;
-        float a = sm.acc[0][t], b = sm.acc[1][t];
+        float a = sm.acc[0][0][t], b = sm.acc[0][1][t];
         if (sec < 2) {
           float ang = (float)pos * __ldg(ph.inv_freq + j);
           float sn, cs;
@@ -515,11 +724,11 @@ struct Cons {
     }
     for (int t = tid; t < n; t += 256) {
       int o = o0 + t;
-      float a = sm.acc[0][t];
+      float a = sm.acc[0][0][t];
       if (ph.out_mode == OUT_ADD)
         sg.out[o] = (ph.res_smem ? sm.xraw[o] : __ldcg(sg.out + o)) + a;
       else if (ph.out_mode == OUT_SILU)
-        sg.out[o] = silu_mul(a, sm.acc[1][t]);
+        sg.out[o] = silu_mul(a, sm.acc[0][1][t]);
       else
         sg.out[o] = a;
     }
@@ -529,7 +738,7 @@ struct Cons {
   __device__ void logits_argmax(int o0, int n, int item, int items) {
     unsigned long long best = 0;
     for (int t = tid; t < n; t += 256) {
-      float v = sm.acc[0][t];
+      float v = sm.acc[0][0][t];
       if (v != v) continue;
       unsigned long long c = ((unsigned long long)total_key(v) << 32) | (0xFFFFFFFFu - (uint32_t)(o0 + t));
       if (c > best) best = c;
@@ -609,34 +818,53 @@ struct Cons {
       sc += __shfl_xor_sync(0xffffffffu, sc, 4);
       return sc * ph.scale;
     };
-    auto update = [&](float sc, const float* vr) {
-      float M = fmaxf(mx, sc);
-      float corr = mx == -INFINITY ? 0.0f : expf(mx - M);
-      float pe = expf(sc - M);
-      l = l * corr + pe;
-      float4 v0 = *reinterpret_cast<const float4*>(vr + d0), v1 = *reinterpret_cast<const float4*>(vr + d1);
-      float vv[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
-#pragma unroll
-      for (int e = 0; e < 8; e++) acc[e] = acc[e] * corr + pe * vv[e];
-      mx = M;
-    };
     long long a, b;
     attn_slice(ph, pos, s, &a, &b);
+    unsigned long long c0 = P.trace && tid == 0 ? now_ns() : 0;
     for (long long t0 = a; t0 < b; t0 += kAttnTile) {
       const int n = (int)min((long long)kAttnTile, b - t0);
       const float* tile = take();
       if (!tile) return;
       const float* Kt = tile;
       const float* Vt = tile + kAttnTile * kDH;
+      constexpr int J = kAttnTile / 32;
+      float sc[J];
 #pragma unroll
-      for (int j = 0; j < kAttnTile / 32; j++) {
+      for (int j = 0; j < J; j++) {
         int r = grp + 4 * warp + 32 * j;
-        bool valid = r < n;
-        int rr = valid ? r : 0;
-        float sc = fold(Kt + rr * kDH);
-        if (valid) update(sc, Vt + rr * kDH);
+        sc[j] = fold(Kt + (r < n ? r : 0) * kDH);
+        if (r >= n) sc[j] = -INFINITY;
+      }
+      float M = mx;
+#pragma unroll
+      for (int j = 0; j < J; j++) M = fmaxf(M, sc[j]);
+      if (M != -INFINITY) {
+        const float corr = mx == -INFINITY ? 0.0f : expf(mx - M);
+        l *= corr;
+#pragma unroll
+        for (int e = 0; e < 8; e++) acc[e] *= corr;
+#pragma unroll
+        for (int j = 0; j < J; j++) {
+          int r = grp + 4 * warp + 32 * j;
+          if (r >= n) continue;
+          const float pe = expf(sc[j] - M);
+          l += pe;
+          const float* vr = Vt + r * kDH;
+          float4 v0 = *reinterpret_cast<const float4*>(vr + d0), v1 = *reinterpret_cast<const float4*>(vr + d1);
+          acc[0] = fmaf(pe, v0.x, acc[0]), acc[1] = fmaf(pe, v0.y, acc[1]);
+          acc[2] = fmaf(pe, v0.z, acc[2]), acc[3] = fmaf(pe, v0.w, acc[3]);
+          acc[4] = fmaf(pe, v1.x, acc[4]), acc[5] = fmaf(pe, v1.y, acc[5]);
+          acc[6] = fmaf(pe, v1.z, acc[6]), acc[7] = fmaf(pe, v1.w, acc[7]);
+        }
+        mx = M;
       }
       release();
+    }
+    unsigned long long e0 = 0;
+    if (c0) {
+      e0 = now_ns();
+      comp_ns += e0 - c0;
+      ntiles++;
     }
     if (s == ph.splits - 1 && warp == 0 && grp == 0) {
       // The step's own position, stored by the qkv phase.
@@ -695,39 +923,8 @@ struct Cons {
       }
       out[tid] = tid < kDH ? a0 : (tid == kDH ? m0 : l0);
     }
-    consumers_sync();
-    if (tid == 0) {
-      __threadfence();
-      unsigned prev = atomicAdd(ph.counters + h, 1u);
-      sm.flag = prev == (unsigned)ph.splits - 1 ? 2 : 0;
-    }
-    consumers_sync();
-    if (sm.flag == 2) {
-      // Last split of head h to arrive: merge all splits, in split order.
-      __threadfence();
-      const float* p0 = ph.part + (size_t)h * ph.splits * (kDH + 2);
-      for (int e = tid; e < ph.splits * (kDH + 2); e += 256) sm.cmb[e / (kDH + 2)][e % (kDH + 2)] = __ldcg(p0 + e);
-      consumers_sync();
-      if (tid < kDH) {
-        float M = -INFINITY;
-        for (int j = 0; j < ph.splits; j++) M = fmaxf(M, sm.cmb[j][kDH]);
-        float L = 0.0f, A = 0.0f;
-        if (M != -INFINITY)
-          for (int j = 0; j < ph.splits; j++) {
-            float mj = sm.cmb[j][kDH];
-            if (mj == -INFINITY) continue;
-            float c = expf(mj - M);
-            L += sm.cmb[j][kDH + 1] * c;
-            A += sm.cmb[j][tid] * c;
-          }
-        ph.y[h * kDH + tid] = L > 0.0f ? A / L : 0.0f;
-      }
-      if (tid == 0) {
-        ph.counters[h] = 0;
-        sm.flag = 0;
-      }
-      consumers_sync();
-    }
+    consumers_sync();  // sm.wsm is free for the next item
+    if (e0) epi_ns += now_ns() - e0;
   }
 
   // GLA for head h: l2norm q, k; S = d·S + kᵀv; y = q·S; head_norm; silu gate.
@@ -780,18 +977,30 @@ struct Cons {
   }
 
   __device__ void stamp(int p, int which) {
-    if (P.trace && tid == 0) P.trace[((size_t)p * gridDim.x + blockIdx.x) * 2 + which] = now_ns();
+    if (P.trace && tid == 0) {
+      unsigned long long* t = P.trace + ((size_t)p * gridDim.x + blockIdx.x) * 8;
+      t[which] = now_ns();
+      if (which == 1) {
+        t[2] = waited, t[3] = pro_ns, t[4] = comp_ns, t[5] = epi_ns, t[6] = ntiles, t[7] = 0;
+        waited = pro_ns = comp_ns = epi_ns = ntiles = 0;
+      }
+    }
   }
 
   __device__ void run() {
+    stage_phase(0);
+    stage_wait();
+    consumers_sync();
     for (int p = 0; p < P.nphases && ok; p++) {
-      const Phase& ph = P.phases[p];
       if (p > 0) {
         stamp(p - 1, 1);
+        stage_wait();  // phase p's descriptor, requested one phase ago
         grid_sync();
         if (!ok) return;
       }
       stamp(p, 0);
+      stage_phase(p + 1);
+      const Phase& ph = sm.ph[p & 1];
       if (ph.kind == PH_GEMV) {
         gemv_phase(ph);
       } else if (ph.kind == PH_ATTN) {
@@ -815,9 +1024,8 @@ struct Cons {
   }
 };
 
-__global__ void __launch_bounds__(kThreads, 1) k_decode_mega(const Plan* __restrict__ plan) {
+__global__ void __launch_bounds__(kThreads, 1) k_decode_mega(const __grid_constant__ Plan P) {
   extern __shared__ __align__(1024) char smem_raw[];
-  const Plan& P = *plan;
   Smem& sm = *reinterpret_cast<Smem*>(smem_raw);
   char* ring = smem_raw + ((sizeof(Smem) + 1023) / 1024) * 1024;
   const long long pos = P.pos[0];
@@ -854,7 +1062,7 @@ int blocks_per_sm() {
   return n;
 }
 
-void launch(const Plan* plan_dev, int grid, cudaStream_t st) {
+void launch(const Plan& plan, int grid, cudaStream_t st) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(kThreads);
@@ -865,7 +1073,7 @@ void launch(const Plan* plan_dev, int grid, cudaStream_t st) {
   attr[0].val.cooperative = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  SLM_CUDA(cudaLaunchKernelEx(&cfg, k_decode_mega, plan_dev));
+  SLM_CUDA(cudaLaunchKernelEx(&cfg, k_decode_mega, plan));
 }
 
 }  // namespace mega

@@ -28,6 +28,7 @@ enum InMode : int {
   IN_RMS = 1,        // v = rms(a)·w
   IN_EMBED_RMS = 2,  // x = embed[ids[0]] (written to a and b), v = rms(x)·w
   IN_LOOP_RMS = 3,   // x = (a + b) + c, written to xout; v = rms(x)·w
+  IN_ATTN = 4,       // v = the attention output, merged from the (head, split) partials in a
 };
 
 // What a GEMV phase does with its dot products.
@@ -47,7 +48,7 @@ struct Segment {
   float* out;       // output (OUT_STORE/ADD/SILU/LOGITS)
 };
 
-struct Phase {
+struct alignas(16) Phase {
   int kind;
   // GEMV
   int cols;
@@ -94,8 +95,11 @@ struct Plan {
   unsigned* bar;        // grid barrier: [0] arrivals (monotonic in a step), [1] CTAs done
   int* err;             // error word: 8 = a bounded wait expired
   long long spin_limit;
-  // Optional timeline: trace[(phase·grid + cta)·2 + {0, 1}] = globaltimer (ns)
-  // when the CTA starts the phase's work and when it reaches the barrier.
+  // Optional timeline, per phase and CTA, eight words at (phase·grid + cta)·8:
+  // globaltimer (ns) when the CTA starts the phase's work and when it reaches
+  // the next barrier, then the ns it spent waiting for tiles, building the
+  // input vector, on tile arithmetic and in GEMV epilogues, the GEMV tiles it
+  // took, and a spare zero.
   unsigned long long* trace;
 };
 

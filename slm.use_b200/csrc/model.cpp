@@ -22,7 +22,7 @@ namespace mega {
 size_t smem_bytes();
 void prepare();
 int blocks_per_sm();
-void launch(const Plan* plan_dev, int grid, cudaStream_t st);
+void launch(const Plan& plan, int grid, cudaStream_t st);
 }  // namespace mega
 }  // namespace slm
 
@@ -97,7 +97,6 @@ struct slm_session {
   bool mega_ok = false, use_mega = false;
   std::string mega_why;                  // why the kernel does not apply, if it does not
   slm::mega::Plan plan_host{};
-  slm::mega::Plan* plan_dev = nullptr;
   slm::mega::Phase* phases_dev = nullptr;
   float* xc = nullptr;
   int grid = 0;
@@ -375,8 +374,14 @@ void advance(slm_session* se, size_t m, bool want_logits) {
 std::string mega_unsupported(const slm_model* md) {
   const Config& c = md->cfg;
   if (c.dh() != (size_t)mega::kDH) return "head size is not 64";
-  if (c.d % 32 != 0 || c.d > (size_t)mega::kMaxD) return "d_model must be a multiple of 32 and at most 1024";
-  if (md->hidden % 32 != 0 || md->hidden > (size_t)mega::kMaxCols) return "FFN width must be a multiple of 32, <= 3072";
+  // A GEMV row is split over one warp (≤ 1536 columns) or two; each warp holds
+  // cols/128 (per split) float4 of the input in registers: 1, 2, 3, 4, 6, 8 or 12.
+  auto cols_ok = [](size_t cols) {
+    size_t k = cols / (cols > 1536 ? 2 : 1) / 128;
+    return cols % (cols > 1536 ? 256 : 128) == 0 && (k <= 4 || k == 6 || k == 8 || k == 12);
+  };
+  if (!cols_ok(c.d) || c.d > (size_t)mega::kMaxD) return "d_model must be 128·{1,2,3,4,6,8} (at most 1024)";
+  if (!cols_ok(md->hidden) || md->hidden > (size_t)mega::kMaxCols) return "FFN width must suit the GEMV split, <= 3072";
   if (c.damp != 1.0f) return "damp != 1";
   if (c.prelude.empty()) return "no prelude block";
   for (const std::string* part : {&c.prelude, &c.core, &c.coda})
@@ -415,6 +420,9 @@ void build_plan(slm_session* se) {
     return p;
   };
   const int splits = std::min(kMaxSplits, std::max(1, G / H));
+  // The merge in the o prologue keeps m, l of every (head, split) on chip.
+  SLM_REQUIRE(2 * H * splits <= (kMaxSplits / 2) * (kDH + 2) && H <= (kMaxSplits / 2) * (kDH + 2),
+              "too many attention partials for the decode kernel");
   const float scale = 1.0f / std::sqrt((float)c.dh());
   // Attention partials (heads × splits × (dh + 2)) and per-head arrival counters.
   float* attn_part = static_cast<float*>(alloc_zero(se, (size_t)H * splits * (kDH + 2) * sizeof(float)));
@@ -453,8 +461,15 @@ void build_plan(slm_session* se) {
       ph.push_back(g);
     }
     // The residual of o and down is the x of the phase two back, whose
-    // normalising prologue left it in shared memory on every CTA.
-    ph.push_back(gemv(d, IN_PLAIN, se->y, nullptr, nullptr, nullptr, nullptr, OUT_ADD, seg(b.o.w, d, per(d, G, 1), X)));
+    // normalising prologue left it in shared memory on every CTA.  After an
+    // S mixer, o's input is merged from the attention partials.
+    if (b.kind == 'S') {
+      Phase o = gemv(d, IN_ATTN, attn_part, nullptr, nullptr, nullptr, nullptr, OUT_ADD, seg(b.o.w, d, per(d, G, 1), X));
+      o.heads = H, o.splits = splits;
+      ph.push_back(o);
+    } else {
+      ph.push_back(gemv(d, IN_PLAIN, se->y, nullptr, nullptr, nullptr, nullptr, OUT_ADD, seg(b.o.w, d, per(d, G, 1), X)));
+    }
     ph.back().res_smem = 1;
     const int F = (int)b.down.cols;
     ph.push_back(gemv(d, IN_RMS, X, nullptr, nullptr, b.norm2, nullptr, OUT_SILU,
@@ -507,8 +522,6 @@ void build_plan(slm_session* se) {
   P.arg_part = static_cast<unsigned long long*>(alloc_zero(se, logit_items * sizeof(unsigned long long)));
   P.next_id = se->ids_dev;
   P.err = se->ctx->err;
-  se->plan_dev = static_cast<Plan*>(alloc_zero(se, sizeof(Plan)));
-  SLM_CUDA(cudaMemcpyAsync(se->plan_dev, &P, sizeof(Plan), cudaMemcpyHostToDevice, se->ctx->stream));
 }
 
 // Points the plan's greedy outputs at `out` (nullptr: logits only).
@@ -517,13 +530,12 @@ void plan_outputs(slm_session* se, bool greedy, uint32_t* out, uint32_t* hist, u
   P.greedy = greedy ? 1 : 0;
   P.out_ids = out;
   P.hist = hist;
-  P.hist_base = hist_base;
-  SLM_CUDA(cudaMemcpyAsync(se->plan_dev, &P, sizeof(P), cudaMemcpyHostToDevice, se->ctx->stream));
+  P.hist_base = hist_base;  // the plan travels by value with each launch
   SLM_CUDA(cudaMemsetAsync(P.out_index, 0, sizeof(unsigned), se->ctx->stream));
 }
 
 void mega_step(slm_session* se) {
-  mega::launch(se->plan_dev, se->grid, se->ctx->stream);
+  mega::launch(se->plan_host, se->grid, se->ctx->stream);
   se->pos += 1;
 }
 
@@ -840,12 +852,10 @@ int slm_session_set(slm_session* se, int option, int64_t value) {
       SLM_REQUIRE(se->mega_ok, "tracing needs the persistent decode kernel");
       Device dev(se->ctx);
       if (value && !se->trace) {
-        size_t n = (size_t)se->plan_host.nphases * se->grid * 2;
+        size_t n = (size_t)se->plan_host.nphases * se->grid * 8;
         se->trace = static_cast<unsigned long long*>(alloc_zero(se, n * sizeof(unsigned long long)));
       }
       se->plan_host.trace = value ? se->trace : nullptr;
-      SLM_CUDA(cudaMemcpyAsync(se->plan_dev, &se->plan_host, sizeof(se->plan_host), cudaMemcpyHostToDevice,
-                               se->ctx->stream));
       return;
     }
     if (option == SLM_OPT_MEGA) {
@@ -873,7 +883,7 @@ int slm_session_trace(slm_session* se, uint64_t* out, size_t cap, size_t* n_out)
     SLM_REQUIRE(se && n_out && (out || cap == 0), "bad arguments");
     SLM_REQUIRE(se->trace, "tracing is off (SLM_OPT_TRACE)");
     Device dev(se->ctx);
-    size_t n = (size_t)se->plan_host.nphases * se->grid * 2;
+    size_t n = (size_t)se->plan_host.nphases * se->grid * 8;
     *n_out = n;
     if (cap >= n) {
       SLM_CUDA(cudaMemcpyAsync(out, se->trace, n * sizeof(uint64_t), cudaMemcpyDeviceToHost, se->ctx->stream));
