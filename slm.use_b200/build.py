@@ -64,4 +64,9 @@ def build(force: bool = False, verbose: bool = False) -> Path:
 
 
 if __name__ == "__main__":
-    build(force="--force" in sys.argv, verbose=True)
+    try:
+        build(force="--force" in sys.argv, verbose=True)
+    except RuntimeError as e:
+        print(e, file=sys.stderr)
+        print("BUILD FAILED", file=sys.stderr)
+        sys.exit(1)

@@ -64,6 +64,13 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, unsigned by
 __device__ __forceinline__ void prefetch_l2(const void* src, unsigned bytes) {
   asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
 }
+// Explicit shared-window load (the ring is reached through pointers the
+// compiler cannot prove to be shared, which would make it emit generic loads).
+__device__ __forceinline__ float4 lds4(uint32_t a) {
+  float4 v;
+  asm volatile("ld.shared.v4.f32 {%0,%1,%2,%3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(a));
+  return v;
+}
 __device__ __forceinline__ void cp_async16(void* dst, const void* src) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(saddr(dst)), "l"(src) : "memory");
 }
@@ -364,6 +371,21 @@ struct Cons {
     }
     return reinterpret_cast<const float*>(ring + (size_t)s * kStageBytes);
   }
+  // Per-warp variant: no CTA barrier, so warps overlap their tile work; a
+  // failed wait only clears `ok`, and items end with a uniform check.
+  __device__ const float* take_warp() {
+    int s = k % kStages;
+    unsigned long long t0 = P.trace && tid == 0 ? now_ns() : 0;
+    if (!wait_mbar(&sm.full[s], (k / kStages) & 1, P.err)) ok = false;
+    if (t0) waited += now_ns() - t0;
+    return reinterpret_cast<const float*>(ring + (size_t)s * kStageBytes);
+  }
+  // Consumers barrier that also makes `ok` uniform; false when any failed.
+  __device__ bool all_ok() {
+    if (!consumers_and(ok ? 1 : 0)) ok = false;
+    return ok;
+  }
+
   __device__ void release() {
     __syncwarp();
     if (lane == 0) mbar_arrive(&sm.empty[k % kStages]);
@@ -460,10 +482,7 @@ struct Cons {
     consumers_sync();
   }
 
-  // Attention output y = Σ_s e^{m_s−M}·acc_s / Σ_s e^{m_s−M}·l_s per (head, dim)
-  // from the partials of the previous phase ([head][split][dh | m | l]),
-  // merged in split order on every CTA: one round of loads, no last-arriver
-  // step in the attention phase.
+  // Merge of the attention partials for one GEMV input (see attn_merge).
   template <int Q, int S>
   __device__ void attn_merge_t(const Phase& ph, int d, int s_rt) {
     const int H = ph.heads, Srt = S > 0 ? S : s_rt;
@@ -529,64 +548,6 @@ struct Cons {
   // from the partials of the previous phase ([head][split][dh | m | l]),
   // merged in split order on every CTA: one round of loads, no last-arriver
   // step in the attention phase.
-  template <int Q, int S>
-  __device__ void attn_merge_t(const Phase& ph, int d, int s_rt) {
-    const int H = ph.heads, Srt = S > 0 ? S : s_rt;
-    constexpr int QQ = Q > 0 ? Q : 1, SS = S > 0 ? S : 1;
-    float* ml = &sm.cmb[0][0];  // 2·H·S floats: m, l
-    for (int i = tid; i < H * Srt; i += 256) {
-      ml[2 * i] = __ldcg(ph.in_a + (size_t)i * (kDH + 2) + kDH);
-      ml[2 * i + 1] = __ldcg(ph.in_a + (size_t)i * (kDH + 2) + kDH + 1);
-    }
-    float av[QQ][SS];
-    if (Q > 0 && S > 0) {
-#pragma unroll
-      for (int q = 0; q < QQ; q++) {
-        const int o = tid + 256 * q;
-        if (o >= d) break;
-        const float* src = ph.in_a + (size_t)(o / kDH) * S * (kDH + 2) + (o % kDH);
-#pragma unroll
-        for (int j = 0; j < SS; j++) av[q][j] = __ldcg(src + (size_t)j * (kDH + 2));
-      }
-    }
-    consumers_sync();
-    for (int q = 0; q < (d + 255) / 256; q++) {
-      const int o = tid + 256 * q;
-      if (o >= d) break;
-      const float* mlh = ml + 2 * (o / kDH) * Srt;
-      const float* src = ph.in_a + (size_t)(o / kDH) * Srt * (kDH + 2) + (o % kDH);
-      float M = -INFINITY;
-      for (int j = 0; j < Srt; j++) M = fmaxf(M, mlh[2 * j]);
-      float L = 0.0f, A = 0.0f;
-      if (M != -INFINITY) {
-#pragma unroll
-        for (int j = 0; j < (S > 0 ? S : kMaxSplits); j++) {
-          if (j >= Srt) break;
-          const float mj = mlh[2 * j];
-          if (mj == -INFINITY) continue;
-          const float c = expf(mj - M);
-          L += mlh[2 * j + 1] * c;
-          float a;
-          if (Q > 0 && S > 0) {
-            a = 0.0f;
-#pragma unroll
-            for (int qq = 0; qq < QQ; qq++)
-              if (qq == q) a = av[qq][j];
-          } else {
-            a = __ldcg(src + (size_t)j * (kDH + 2));
-          }
-          A += a * c;
-        }
-      }
-      sm.xin[o] = L > 0.0f ? A / L : 0.0f;
-    }
-    consumers_sync();
-  }
-
-  // Attention output y = Σ_s e^{m_s−M}·acc_s / Σ_s e^{m_s−M}·l_s per (head, dim)
-  // from the partials of the previous phase ([head][split][dh | m | l]),
-  // merged in split order on every CTA: one round of loads, no last-arriver
-  // step in the attention phase.
   __device__ void attn_merge(const Phase& ph) {
     const int d = ph.cols;
     if (d == 768 && ph.splits == 12)
@@ -621,18 +582,17 @@ struct Cons {
       for (int t0 = o0; t0 < o1; t0 += T) {
         const int n = min(T, o1 - t0);
         const int rows = pair ? 2 * n : n;
-        const float* w = take();
-        if (!w) return;
+        const float* w = take_warp();
         unsigned long long c0 = P.trace && tid == 0 ? now_ns() : 0;
         for (int r = rowslot; r < rows; r += 2 * rstride) {
           const int r2 = r + rstride;
           const bool two = r2 < rows;
-          const float4* w0 = reinterpret_cast<const float4*>(w + (size_t)r * ph.cols + sgi * span) + lane;
-          const float4* w1 = reinterpret_cast<const float4*>(w + (size_t)(two ? r2 : r) * ph.cols + sgi * span) + lane;
+          const uint32_t w0 = saddr(w + (size_t)r * ph.cols + sgi * span) + lane * 16;
+          const uint32_t w1 = saddr(w + (size_t)(two ? r2 : r) * ph.cols + sgi * span) + lane * 16;
           float a0 = 0.0f, b0 = 0.0f, a1 = 0.0f, b1 = 0.0f;
 #pragma unroll
           for (int k = 0; k < K; k++) {
-            float4 u = w0[32 * k], v = w1[32 * k];
+            float4 u = lds4(w0 + 512 * k), v = lds4(w1 + 512 * k);
             if (k & 1) {
               b0 = dot4(u, xr[k], b0);
               b1 = dot4(v, xr[k], b1);
@@ -657,7 +617,7 @@ struct Cons {
         release();
         if (c0) comp_ns += now_ns() - c0, ntiles++;
       }
-      consumers_sync();  // every partial of the item written
+      if (!all_ok()) return;  // every partial of the item written
       unsigned long long e0 = P.trace && tid == 0 ? now_ns() : 0;
       if (S == 2)
         for (int t = tid; t < o1 - o0; t += 256) {
@@ -810,7 +770,8 @@ struct Cons {
 #pragma unroll
     for (int e = 0; e < 8; e++) acc[e] = 0.0f;
     auto fold = [&](const float* kr) {
-      float4 k0 = *reinterpret_cast<const float4*>(kr + d0), k1 = *reinterpret_cast<const float4*>(kr + d1);
+      const uint32_t ka = saddr(kr);
+      float4 k0 = lds4(ka + d0 * 4), k1 = lds4(ka + d1 * 4);
       float sc = qv[0] * k0.x + qv[1] * k0.y + qv[2] * k0.z + qv[3] * k0.w + qv[4] * k1.x + qv[5] * k1.y +
                  qv[6] * k1.z + qv[7] * k1.w;
       sc += __shfl_xor_sync(0xffffffffu, sc, 1);
@@ -823,8 +784,7 @@ struct Cons {
     unsigned long long c0 = P.trace && tid == 0 ? now_ns() : 0;
     for (long long t0 = a; t0 < b; t0 += kAttnTile) {
       const int n = (int)min((long long)kAttnTile, b - t0);
-      const float* tile = take();
-      if (!tile) return;
+      const float* tile = take_warp();
       const float* Kt = tile;
       const float* Vt = tile + kAttnTile * kDH;
       constexpr int J = kAttnTile / 32;
@@ -849,8 +809,8 @@ struct Cons {
           if (r >= n) continue;
           const float pe = expf(sc[j] - M);
           l += pe;
-          const float* vr = Vt + r * kDH;
-          float4 v0 = *reinterpret_cast<const float4*>(vr + d0), v1 = *reinterpret_cast<const float4*>(vr + d1);
+          const uint32_t va = saddr(Vt + r * kDH);
+          float4 v0 = lds4(va + d0 * 4), v1 = lds4(va + d1 * 4);
           acc[0] = fmaf(pe, v0.x, acc[0]), acc[1] = fmaf(pe, v0.y, acc[1]);
           acc[2] = fmaf(pe, v0.z, acc[2]), acc[3] = fmaf(pe, v0.w, acc[3]);
           acc[4] = fmaf(pe, v1.x, acc[4]), acc[5] = fmaf(pe, v1.y, acc[5]);
@@ -908,7 +868,7 @@ struct Cons {
       for (int e = 0; e < 4; e++) sm.wsm[warp][d0 + e] = acc[e], sm.wsm[warp][d1 + e] = acc[4 + e];
       if (sub == 0) sm.wsm[warp][kDH] = mx, sm.wsm[warp][kDH + 1] = l;
     }
-    consumers_sync();
+    if (!all_ok()) return;
     float* out = ph.part + (size_t)item * (kDH + 2);
     if (tid < kDH + 2) {
       const int e = tid < kDH ? tid : 0;
