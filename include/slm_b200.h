@@ -144,6 +144,20 @@ typedef struct slm_attn {
 int slm_op_attend(slm_ctx* ctx, slm_buf* y, slm_buf* scores, const slm_buf* q, size_t qoff,
                   const slm_buf* k, const slm_buf* v, const slm_attn* a);
 
+/* Ops::attend without any device allocation.  No counterpart in the
+ * reference: it exists for callers that cannot call cudaMalloc — code running
+ * between kernels of a latency-critical loop (cudaMalloc/cudaFree may
+ * synchronise the device) or a process whose device memory is reserved up
+ * front by its own allocator.  y, q, k, v are device pointers laid out as for
+ * slm_op_attend (q and y: m × heads × dh; k, v: key_heads × cap × dh).  The
+ * scratch is a fixed 4 MiB __device__ array per device: calls need
+ * m·heads·(dh + 2) ≤ 1,048,512 floats and fail with SLM_ERR_INVALID above
+ * it.  The first call on a device looks up that array's address (set-up, no
+ * allocation); make that first call before any stream capture.  All calls on
+ * a device share the array, so calls that overlap on the GPU race. */
+int slm_op_attend_noalloc(slm_ctx* ctx, float* y, const float* q, const float* k, const float* v,
+                          const slm_attn* a);
+
 /* ---------------------------------------------------------------------- */
 /* Model level (src/model.rs, src/sample.rs).                              */
 /* ---------------------------------------------------------------------- */

@@ -98,6 +98,7 @@ _SIGS = {
     "slm_op_gla": (_c.c_int, [_vp, _vp, _vp, _vp, _sz, _vp, _sz, _vp, _sz, _vp, _vp, _sz, _sz, _sz]),
     "slm_op_store": (_c.c_int, [_vp, _vp, _vp, _sz, _sz, _sz, _sz, _sz, _sz]),
     "slm_op_attend": (_c.c_int, [_vp, _vp, _vp, _vp, _sz, _vp, _vp, _c.POINTER(_Attn)]),
+    "slm_op_attend_noalloc": (_c.c_int, [_vp, _vp, _vp, _vp, _vp, _c.POINTER(_Attn)]),
     "slm_model_load": (_c.c_int, [_vp, _c.c_char_p, _c.POINTER(_vp)]),
     "slm_model_free": (_c.c_int, [_vp]),
     "slm_model_info_get": (_c.c_int, [_vp, _c.POINTER(_Info)]),
@@ -342,6 +343,14 @@ class Ops:
         qb, qo = self._at(q)
         a = _Attn(pos, m, SIZE_MAX if reach is None else reach, gap, cap, heads, key_heads, dh, scale)
         _check(lib().slm_op_attend(self._c, y._h, scores._h, qb._h, qo, k._h, v._h, _c.byref(a)))
+
+
+def attend_noalloc(ctx: Context, y: Buf, q: Buf, k: Buf, v: Buf, *, pos: int, m: int, reach: int | None, gap: int,
+                   cap: int, heads: int, key_heads: int, dh: int, scale: float) -> None:
+    """Ops::attend on caller-owned device buffers with no device allocation
+    (scratch in a fixed per-device array); see slm_op_attend_noalloc."""
+    a = _Attn(pos, m, SIZE_MAX if reach is None else reach, gap, cap, heads, key_heads, dh, scale)
+    _check(lib().slm_op_attend_noalloc(ctx._h, y.ptr, q.ptr, k.ptr, v.ptr, _c.byref(a)))
 
 
 # ---------------------------------------------------------------------------
