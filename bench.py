@@ -17,7 +17,8 @@ Printed on one JSON line (rank 0):
             host id + `slm_sample` returning a host id), host clock;
   prefill   tok/s of the 4096-token prompt (feed + logits read back);
   extra     R = 8 and R = 16 decode with the sampling of configs[2];
-  roofline  the dominant decode kernel (GEMV) against measured HBM bandwidth;
+  roofline  the decode step's kernel (one persistent kernel per token) against
+            measured HBM bandwidth, and the m = 1 GEMV op on its own;
   cpu_baseline  the CPU oracle (a C++ restatement of the reference's CPU
             backend) on a bounded sample, rank 0 only, N = 1 only.
 
@@ -45,6 +46,9 @@ import numpy as np
 
 ROOT = Path(__file__).resolve().parent
 MODEL_BYTES_NOTE = "inputs larger than L2: 640 MB of weights and KV read per token at R=4"
+# DRAM bytes (read + write) of one k_decode_mega launch from an ncu capture of
+# this bench (profiles/k_decode_mega_R4.md), by loop count.
+MEGA_TRAFFIC = {4: 652.9e6}
 
 
 def load_pkg():
@@ -57,6 +61,21 @@ def load_pkg():
     sys.modules["slm_b200"] = mod
     spec.loader.exec_module(mod)
     return mod
+
+
+def prompt_for(rank: int, vocab: int, n: int) -> np.ndarray:
+    """The prompt of rank r: n uniform ids from seed r (each rank decodes its own sequence)."""
+    return np.random.default_rng(rank).integers(0, vocab, n).astype(np.uint32)
+
+
+def max_over_ranks(values, dist=None, device=None):
+    """Element-wise max of per-rank timings (the slowest rank sets the job's time)."""
+    if dist is None or not dist.is_initialized() or dist.get_world_size() == 1:
+        return list(values)
+    import torch
+    t = torch.tensor(list(values), dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return t.tolist()
 
 
 def model_dir(cfg: dict, seed: int) -> Path:
@@ -204,8 +223,7 @@ def run_b200(args, rank: int, world: int, local: int) -> dict | None:
     stream = torch.cuda.ExternalStream(ctx.stream, device=dev)
     V = cfg["vocab_size"]
     greedy = slm.Sampling()
-    rng = np.random.default_rng(rank)
-    prompt = rng.integers(0, V, args.prompt).astype(np.uint32)
+    prompt = prompt_for(rank, V, args.prompt)
 
     def events():
         return torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -316,10 +334,7 @@ def run_b200(args, rank: int, world: int, local: int) -> dict | None:
     res = {"dec_ms": dec_ms, "e2e_s": e2e_s, "prefill_ms": prefill_ms, "prefill_host_s": prefill_host_s,
            "gemv_us": gemv_us, "clocks": clocks.summary(), "extra": extra, "step_kernels": step_kernels,
            "device": ctx.name, "state_bytes": se.state_bytes()}
-    if world > 1:
-        t = torch.tensor([dec_ms, e2e_s, prefill_ms], dtype=torch.float64, device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        res["dec_ms"], res["e2e_s"], res["prefill_ms"] = t.tolist()
+    res["dec_ms"], res["e2e_s"], res["prefill_ms"] = max_over_ranks([dec_ms, e2e_s, prefill_ms], dist, dev)
     se.close()
     model.close()
     ctx.close()
@@ -411,10 +426,15 @@ def main():
                 "how": "per token slm_step(host id) + slm_sample -> host id, host clock"},
         "prefill": {"value": world * args.prompt / (res["prefill_ms"] / 1000.0), "unit": "tok/s",
                     "e2e_value": world * args.prompt / res["prefill_host_s"], "prompt": args.prompt},
-        "roofline": {"bound": "hbm", "kernel": "k_gemv<1,STORE> (32000x768 fp32, m=1)",
-                     "achieved": gemv_gbs, "peak": hbm, "unit": "GB/s", "frac": gemv_gbs / hbm,
-                     "traffic": None, "peak_source": peak_src,
-                     "step": {"bytes_per_token": byts["total"], "achieved": step_gbs, "frac": step_gbs / hbm}},
+        # The m = 1 step is one persistent kernel (k_decode_mega), so its
+        # average launch duration is the decode time per token (CUDA events
+        # over the K launches; inter-launch gaps included).
+        "roofline": {"bound": "hbm", "kernel": "k_decode_mega (one m=1 token step, R=%d)" % args.loops,
+                     "achieved": step_gbs, "peak": hbm, "unit": "GB/s", "frac": step_gbs / hbm,
+                     "bytes_per_launch": byts["total"], "traffic": MEGA_TRAFFIC.get(args.loops),
+                     "peak_source": peak_src,
+                     "gemv": {"kernel": "k_gemv<1,STORE> (32000x768 fp32, m=1)", "achieved": gemv_gbs,
+                              "frac": gemv_gbs / hbm}},
         "clocks": res["clocks"],
         "gpu_launches": K * (res["step_kernels"] + 1),
         "extra": res["extra"],
