@@ -226,6 +226,11 @@ int slm_decode(slm_session* se, uint32_t first, size_t n, const slm_sampling* s,
 #define SLM_OPT_GRAPH 1
 #define SLM_OPT_MEGA 2
 #define SLM_OPT_TRACE 3 /* 1 = record the per-phase timeline of each persistent step */
+/* Test hook: 1 = the persistent step's first grid barrier waits for an arrival
+ * that never comes, so its bounded wait (~2 s) expires and the step reports
+ * SLM_ERR_DEVICE at the next synchronising call.  The session's state is then
+ * undefined; the context stays usable. */
+#define SLM_OPT_TEST_STALL 4
 int slm_session_set(slm_session* se, int option, int64_t value);
 
 /* Counters of a session:

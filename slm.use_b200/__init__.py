@@ -36,6 +36,7 @@ _sz = _c.c_size_t
 SLM_OPT_GRAPH = 1
 SLM_OPT_MEGA = 2
 SLM_OPT_TRACE = 3
+SLM_OPT_TEST_STALL = 4
 SLM_STAT_STEP_KERNELS, SLM_STAT_GRAPHS, SLM_STAT_MEGA, SLM_STAT_PHASES = 1, 2, 3, 4
 SIZE_MAX = (1 << 64) - 1
 
@@ -444,6 +445,10 @@ class Session:
     def set_mega(self, on: bool) -> None:
         """Run m = 1 steps as one persistent kernel (where the model allows it)."""
         _check(lib().slm_session_set(self._h, SLM_OPT_MEGA, 1 if on else 0))
+
+    def set_stall_test(self, on: bool) -> None:
+        """Test hook: the next persistent steps wait for a barrier arrival that never comes."""
+        _check(lib().slm_session_set(self._h, SLM_OPT_TEST_STALL, 1 if on else 0))
 
     def set_trace(self, on: bool) -> None:
         _check(lib().slm_session_set(self._h, SLM_OPT_TRACE, 1 if on else 0))

@@ -399,7 +399,7 @@ struct Cons {
     barriers++;
     if (tid == 0) {
       unsigned* cnt = P.bar;
-      const unsigned target = barriers * gridDim.x;
+      const unsigned target = barriers * gridDim.x + (P.test_stall && barriers == 1 ? 1u : 0u);
       red_release_add(cnt, 1u);  // release: covers the CTA's writes ordered by the barrier above
       unsigned long long t0 = 0;
       for (unsigned it = 0; ld_acquire(cnt) < target; it++) {

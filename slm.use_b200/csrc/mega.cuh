@@ -101,6 +101,9 @@ struct Plan {
   // input vector, on tile arithmetic and in GEMV epilogues, the GEMV tiles it
   // took, and a spare zero.
   unsigned long long* trace;
+  // Test hook: when set, the first grid barrier waits for one arrival more
+  // than the grid has, so its bounded wait runs out (failure-path test).
+  int test_stall;
 };
 
 }  // namespace mega

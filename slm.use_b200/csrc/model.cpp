@@ -858,6 +858,11 @@ int slm_session_set(slm_session* se, int option, int64_t value) {
       se->plan_host.trace = value ? se->trace : nullptr;
       return;
     }
+    if (option == SLM_OPT_TEST_STALL) {
+      SLM_REQUIRE(se->mega_ok, "the stall test needs the persistent decode kernel");
+      se->plan_host.test_stall = value != 0;
+      return;
+    }
     if (option == SLM_OPT_MEGA) {
       if (value && !se->mega_ok) fail(SLM_ERR_INVALID, "persistent decode kernel unavailable: " + se->mega_why);
       se->use_mega = value != 0;
