@@ -17,6 +17,8 @@ struct slm_ctx {
   int* err = nullptr;           // device error word (bad ids, sampler limits)
   void* stage = nullptr;        // staging buffer for host arrays (ids, factors)
   size_t stage_bytes = 0;
+  void* gemm_ws = nullptr;      // tensor-core GEMM workspace (grown on demand, outside captures)
+  size_t gemm_ws_bytes = 0;
 };
 
 struct slm_buf {
@@ -43,6 +45,9 @@ void dev_free(void* p);
 void ensure(slm_buf* y, size_t n);
 const float* view(const slm_buf* b, size_t off, size_t n, const char* what);
 void* stage(slm_ctx* c, const void* host, size_t bytes);
+// Sets a.ws/a.ws_bytes to the context's GEMM workspace, growing it if the
+// tensor-core path needs more (never during a stream capture).
+void gemm_workspace(slm_ctx* c, struct LinearArgs& a, bool capturing);
 
 // Runs f, turning failures into a status code and the thread's error message.
 template <class F>

@@ -200,6 +200,14 @@ __global__ void k_g_post(float* q, size_t d, size_t m, const long long* pos_ptr,
   }
 }
 
+// mid[i][j] = silu(up[i][j])·up[i][F + j]: the MLP gate on a [m][2F] product.
+__global__ void k_silu_pair(float* mid, const float* up, size_t m, size_t F) {
+  GRID_STRIDE(t, m * F) {
+    size_t i = t / F, j = t % F;
+    mid[t] = silu_mul(up[i * 2 * F + j], up[i * 2 * F + F + j]);
+  }
+}
+
 __global__ void k_advance_pos(long long* pos, long long m) {
   if (threadIdx.x == 0 && blockIdx.x == 0) pos[0] += m;
 }
@@ -303,6 +311,11 @@ void ew_g_post(float* q, size_t d, size_t m, const long long* pos_ptr, float inv
   k_g_post<<<ew_grid(m * d), EW, 0, st>>>(q, d, m, pos_ptr, inv_log, logn, keys, ldk, vals, ldv, kd, cap, dh, kc,
                                           vc);
   SLM_LAUNCHED("k_g_post");
+}
+void ew_silu_pair(float* mid, const float* up, size_t m, size_t F, cudaStream_t st) {
+  if (!m) return;
+  k_silu_pair<<<ew_grid(m * F), EW, 0, st>>>(mid, up, m, F);
+  SLM_LAUNCHED("k_silu_pair");
 }
 void ew_advance_pos(long long* pos, long long m, cudaStream_t st) {
   k_advance_pos<<<1, 32, 0, st>>>(pos, m);

@@ -18,8 +18,15 @@ struct LinearArgs {
   const float* res = nullptr;  // EPI_ADD
   int ldres = 0;
   int epi = 0;
+  // Workspace for the tensor-core path (see tc_linear_workspace); may be null.
+  void* ws = nullptr;
+  size_t ws_bytes = 0;
 };
 void linear(const LinearArgs& a, cudaStream_t st);
+// Tensor-core (sm100 FastFP32) path for m > 8, gemm_tc.cu.
+bool tc_linear_ok(const LinearArgs& a);
+size_t tc_linear_workspace(const LinearArgs& a);
+void tc_linear(const LinearArgs& a, void* workspace, cudaStream_t st);
 void linear_prepare();
 
 // Attention geometry (reference Attn, src/ops.rs:31-46).  reach 0 = unbounded.
@@ -91,6 +98,7 @@ void ew_rope_store(const float* mix, size_t ldmix, const float* inv, const long 
 void ew_g_post(float* q, size_t d, size_t m, const long long* pos_ptr, float inv_log, int logn, const float* keys,
                size_t ldk, const float* vals, size_t ldv, size_t kd, size_t cap, size_t dh, float* kc, float* vc,
                cudaStream_t st);
+void ew_silu_pair(float* mid, const float* up, size_t m, size_t F, cudaStream_t st);
 void ew_advance_pos(long long* pos, long long m, cudaStream_t st);
 
 }  // namespace slm

@@ -258,6 +258,13 @@ void linear(const LinearArgs& a, cudaStream_t st) {
     return;
   }
   if (a.epi == EPI_SILU) SLM_REQUIRE(a.rows % 2 == 0, "linear: silu pairing needs an even row count");
+  if (a.m > 8 && tc_linear_ok(a)) {
+    const size_t need = tc_linear_workspace(a);
+    if (need <= a.ws_bytes) {
+      tc_linear(a, a.ws, st);
+      return;
+    }
+  }
   switch (a.epi) {
     case EPI_STORE: dispatch<EPI_STORE>(a, st); break;
     case EPI_ADD: dispatch<EPI_ADD>(a, st); break;

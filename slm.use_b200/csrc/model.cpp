@@ -79,7 +79,7 @@ struct slm_session {
   std::vector<float*> owned;  // device allocations of this session
   float *xa = nullptr, *xb = nullptr, *e0 = nullptr, *e_proj = nullptr, *n = nullptr, *mix = nullptr, *q = nullptr,
         *kb = nullptr, *kin = nullptr, *kvs = nullptr, *y = nullptr, *mid = nullptr, *dec = nullptr, *part = nullptr,
-        *logits = nullptr, *work = nullptr, *nlast = nullptr;
+        *logits = nullptr, *work = nullptr, *nlast = nullptr, *upbuf = nullptr;
   long long* pos_dev = nullptr;
   uint32_t* ids_dev = nullptr;
   unsigned long long* rng_dev = nullptr;
@@ -253,6 +253,9 @@ void ensure_caps(slm_session* se, size_t m) {
   for (auto& st : se->coda) one(st);
 }
 
+thread_local slm_ctx* g_ctx_for_linear = nullptr;  // set by the driver around each advance
+thread_local bool g_capturing = false;
+
 void run_linear(cudaStream_t s, const Mat& w, const float* x, int ldx, int m, float* y, int ldy, int epi,
                 const float* res = nullptr, int ldres = 0, size_t rows = 0) {
   LinearArgs a;
@@ -267,6 +270,7 @@ void run_linear(cudaStream_t s, const Mat& w, const float* x, int ldx, int m, fl
   a.res = res;
   a.ldres = ldres;
   a.epi = epi;
+  if (g_ctx_for_linear) gemm_workspace(g_ctx_for_linear, a, g_capturing);
   linear(a, s);
 }
 
@@ -332,12 +336,20 @@ void block(slm_session* se, const Block& b, LState& st, float* x, size_t m) {
   if (has_h) run_linear(s, b.o, se->y, id, im, x, id, EPI_ADD, x, id);  // x += o·y
   ew_rms(se->n, x, b.norm2, m, d, c.eps, nullptr, s);
   const size_t hidden = b.down.cols;
-  run_linear(s, b.up, se->n, id, im, se->mid, (int)hidden, EPI_SILU);          // silu(gate)·amp
+  if (m > 8 && hidden % 4 == 0) {
+    // Chunks: the [m][2F] product on the tensor cores, then the gate.
+    run_linear(s, b.up, se->n, id, im, se->upbuf, (int)(2 * hidden), EPI_STORE);
+    ew_silu_pair(se->mid, se->upbuf, m, hidden, s);
+  } else {
+    run_linear(s, b.up, se->n, id, im, se->mid, (int)hidden, EPI_SILU);  // silu(gate)·amp
+  }
   run_linear(s, b.down, se->mid, (int)hidden, im, x, id, EPI_ADD, x, id);       // x += down·mid
 }
 
 // Model::advance (src/model.rs:563-640).  Ids are already in se->ids_dev.
 void advance(slm_session* se, size_t m, bool want_logits) {
+  g_ctx_for_linear = se->ctx;
+  g_capturing = se->capturing;
   slm_model* md = se->model;
   const Config& c = md->cfg;
   cudaStream_t s = se->ctx->stream;
@@ -756,6 +768,7 @@ int slm_session_new(slm_model* md, size_t loops, slm_session** out) {
       se->kvs = f(CHUNK * kd);
       se->y = f(CHUNK * d);
       se->mid = f(CHUNK * std::max<size_t>(md->hidden, 1));
+      se->upbuf = f(CHUNK * 2 * std::max<size_t>(md->hidden, 1));
       se->dec = f(CHUNK * c.heads);
       se->nlast = f(d);
       se->logits = f(c.vocab);

@@ -75,6 +75,22 @@ void* stage(slm_ctx* c, const void* host, size_t bytes) {
   return c->stage;
 }
 
+void gemm_workspace(slm_ctx* c, LinearArgs& a, bool capturing) {
+  if (a.m > 8 && tc_linear_ok(a)) {
+    const size_t need = tc_linear_workspace(a);
+    if (need > c->gemm_ws_bytes && !capturing) {
+      SLM_CUDA(cudaStreamSynchronize(c->stream));
+      dev_free(c->gemm_ws);
+      c->gemm_ws = nullptr;
+      c->gemm_ws_bytes = 0;
+      c->gemm_ws = dev_alloc(need);
+      c->gemm_ws_bytes = need;
+    }
+  }
+  a.ws = c->gemm_ws;
+  a.ws_bytes = c->gemm_ws_bytes;
+}
+
 }  // namespace slm
 
 using namespace slm;
@@ -131,6 +147,7 @@ int slm_ctx_free(slm_ctx* c) {
       Device dev(c);
       cudaStreamSynchronize(c->stream);
       dev_free(c->stage);
+      dev_free(c->gemm_ws);
       dev_free(c->err);
       cudaStreamDestroy(c->stream);
     }
@@ -286,6 +303,7 @@ int slm_op_linear(slm_ctx* c, slm_buf* y, const slm_buf* w, size_t rows, size_t 
     LinearArgs a;
     a.w = ws, a.rows = (int)rows, a.cols = (int)cols, a.x = xs, a.ldx = (int)cols, a.m = (int)m;
     a.y = y->ptr, a.ldy = (int)rows, a.epi = EPI_STORE;
+    gemm_workspace(c, a, false);
     linear(a, c->stream);
   });
 }
