@@ -187,11 +187,15 @@ class Context:
         h = _vp()
         _check(lib().slm_ctx_new(device, _c.byref(h)))
         self._h = h
+        self._free = lib().slm_ctx_free
         self.device = device
 
     def close(self):
+        # The free function is looked up while the module is intact: at
+        # interpreter exit its globals may already be gone.
         if getattr(self, "_h", None):
-            lib().slm_ctx_free(self._h)
+            free = getattr(self, "_free", None) or lib().slm_ctx_free
+            free(self._h)
             self._h = None
 
     __del__ = close
@@ -218,10 +222,14 @@ class Buf:
     def __init__(self, ctx: Context, handle):
         self.ctx = ctx
         self._h = handle
+        self._free = lib().slm_buf_free
 
     def close(self):
+        # The free function is looked up while the module is intact: at
+        # interpreter exit its globals may already be gone.
         if getattr(self, "_h", None):
-            lib().slm_buf_free(self._h)
+            free = getattr(self, "_free", None) or lib().slm_buf_free
+            free(self._h)
             self._h = None
 
     __del__ = close
@@ -379,6 +387,7 @@ class Model:
         h = _vp()
         _check(lib().slm_model_load(ctx._h, str(folder).encode(), _c.byref(h)))
         self._h = h
+        self._free = lib().slm_model_free
         info = _Info()
         _check(lib().slm_model_info_get(h, _c.byref(info)))
         self.info = {f: getattr(info, f) for f, _ in _Info._fields_}
@@ -387,8 +396,11 @@ class Model:
         self.vocab = info.vocab
 
     def close(self):
+        # The free function is looked up while the module is intact: at
+        # interpreter exit its globals may already be gone.
         if getattr(self, "_h", None):
-            lib().slm_model_free(self._h)
+            free = getattr(self, "_free", None) or lib().slm_model_free
+            free(self._h)
             self._h = None
 
     __del__ = close
@@ -408,11 +420,15 @@ class Session:
         h = _vp()
         _check(lib().slm_session_new(model._h, loops or 0, _c.byref(h)))
         self._h = h
+        self._free = lib().slm_session_free
         self.vocab = model.vocab
 
     def close(self):
+        # The free function is looked up while the module is intact: at
+        # interpreter exit its globals may already be gone.
         if getattr(self, "_h", None):
-            lib().slm_session_free(self._h)
+            free = getattr(self, "_free", None) or lib().slm_session_free
+            free(self._h)
             self._h = None
 
     __del__ = close

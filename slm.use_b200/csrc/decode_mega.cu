@@ -289,6 +289,7 @@ struct Smem {
   float cmb[kMaxSplits][kDH + 2];
   float vec[4][kDH];
   float yp[4][kDH];
+  float inv_freq[kDH / 2];
   unsigned long long best;
   int flag;
 };
@@ -312,7 +313,7 @@ __device__ void producer(const Plan& P, Smem& sm, char* ring, long long pos) {
     char* dst = ring + (size_t)s * kStageBytes;
     for (int j = 0; j < T.n; j++) bulk_g2s(dst + T.off[j], T.src[j], T.bytes[j], &sm.full[s]);
     k++;
-    if (k >= (unsigned)kStages) {
+    if (kLookahead > 0 && k >= (unsigned)kStages) {
       // One more tile of lookahead per tile issued, up to kLookahead beyond the ring.
       int burst = k == (unsigned)kStages ? kLookahead : 1;
       for (int b = 0; b < burst; b++) {
@@ -662,7 +663,7 @@ struct Cons {
         int sec = o / (d / 2), rem = o % (d / 2), h = rem / 32, j = rem % 32;
         float a = sm.acc[0][0][t], b = sm.acc[0][1][t];
         if (sec < 2) {
-          float ang = (float)pos * __ldg(ph.inv_freq + j);
+          float ang = (float)pos * sm.inv_freq[j];
           float sn, cs;
           sincosf(ang, &sn, &cs);
           float u = a * cs - b * sn, v = a * sn + b * cs;
@@ -948,6 +949,7 @@ struct Cons {
   }
 
   __device__ void run() {
+    if (tid < kDH / 2 && P.inv_freq) sm.inv_freq[tid] = __ldg(P.inv_freq + tid);
     stage_phase(0);
     stage_wait();
     consumers_sync();

@@ -18,7 +18,10 @@ constexpr int kMaxItemOut = 256;     // logical outputs per GEMV item
 constexpr int kDH = 64;              // head size of the kernel
 constexpr int kAttnTile = 96;        // cache positions per attention tile (K + V = one stage)
 constexpr int kMaxSplits = 16;       // attention splits per head
-constexpr int kLookahead = 8;        // tiles prefetched into L2 ahead of the ring
+#ifndef SLM_LOOKAHEAD
+#define SLM_LOOKAHEAD 2
+#endif
+constexpr int kLookahead = SLM_LOOKAHEAD;  // tiles prefetched into L2 ahead of the ring
 
 enum PhaseKind : int { PH_GEMV = 0, PH_ATTN = 1, PH_GLA = 2 };
 
@@ -81,6 +84,7 @@ struct Plan {
   int d, heads, vocab;
   float eps;
   const float* embed;
+  const float* inv_freq;  // rope frequencies (dh/2), staged in shared memory at entry
   const uint32_t* ids;  // ids[0]: the token of this step
   float *e0, *x0;       // embedding outputs
   long long* pos;       // position of this step (advanced at the end)

@@ -525,6 +525,7 @@ void build_plan(slm_session* se) {
   P.phases = se->phases_dev;
   P.d = d, P.heads = H, P.vocab = (int)c.vocab, P.eps = c.eps;
   P.embed = md->embed.w;
+  P.inv_freq = md->inv_freq;
   P.ids = se->ids_dev;
   P.e0 = se->e0, P.x0 = X0;
   P.pos = se->pos_dev;
