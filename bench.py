@@ -21,6 +21,10 @@ Printed on one JSON line (rank 0):
             measured HBM bandwidth, and the m = 1 GEMV op on its own;
   cpu_baseline  the CPU oracle (a C++ restatement of the reference's CPU
             backend) on a bounded sample, rank 0 only, N = 1 only.
+  ref_cuda_baseline  the reference's own CUDA kernels (kernels/slm.cu built
+            from source) under a C++ restatement of its host side, on the same
+            GPU with its own bench protocol; 32 decode steps per loop count
+            after the same 4096-id prompt; rank 0, N = 1 only.
 
 --impl reference runs only the CPU oracle on the host cores (rank 0), since
 the reference itself (Rust) cannot be built on this image.
@@ -200,6 +204,63 @@ def cpu_measure(folder: Path, loops: int, steps: int, warmup: int, budget_s: flo
 
 
 # ---------------------------------------------------------------------------
+# The reference CUDA backend on the same GPU — baseline only
+# ---------------------------------------------------------------------------
+
+def ref_cuda_measure(folder: Path, prompt: np.ndarray, loops_list, decode_steps: int, device: int) -> dict | None:
+    """The reference's own kernels (kernels/slm.cu from source, JIT-compiled
+    compute_60 PTX) under the C++ restatement of its host side, with its bench
+    protocol (src/main.rs:200-223): prefill = feed + logits read, decode =
+    logits read + host pick + step per token, host clock."""
+    sys.path.insert(0, str(ROOT))
+    from oracle import oracle as O
+    from oracle import ref_cuda as RC
+
+    if not RC.available():
+        return None
+    backend = RC.Backend(device)
+    model = RC.Model(backend, folder)
+    out = {}
+    for loops in loops_list:
+        se = model.session(loops)
+        t0 = time.perf_counter()
+        se.feed(prompt, 256)
+        logits = se.logits()
+        pre_s = time.perf_counter() - t0
+        greedy = loops == loops_list[0]
+        st = [O.rng_new(0)]
+        hist = [int(t) for t in prompt[-256:]]
+
+        def pick(lg):
+            if greedy:
+                return int(np.argmax(lg))
+            return O.pick(lg, np.array(hist[-256:], dtype=np.uint32), 0.8, 40, 1.0, 1.1, 256, st)
+
+        tok = pick(logits)
+        for _ in range(2):
+            se.step(tok)
+            tok = pick(se.logits())
+        l0, s0 = backend.counts()
+        t0 = time.perf_counter()
+        for _ in range(decode_steps):
+            se.step(tok)
+            tok = pick(se.logits())
+            hist.append(tok)
+        dec_s = time.perf_counter() - t0
+        l1, s1 = backend.counts()
+        out[f"R{loops}"] = {"decode_tok_s": decode_steps / dec_s, "prefill_tok_s": len(prompt) / pre_s,
+                            "decode_steps": decode_steps,
+                            "launches_per_token": (l1 - l0) / decode_steps,
+                            "host_syncs_per_token": (s1 - s0) / decode_steps,
+                            "sampling": "greedy" if greedy else
+                            "T=0.8 top-k 40 repeat-penalty 1.1 (window 256) seed 0, host pick"}
+        se.close()
+    model.close()
+    backend.close()
+    return out
+
+
+# ---------------------------------------------------------------------------
 # The B200 arm
 # ---------------------------------------------------------------------------
 
@@ -351,6 +412,7 @@ def main():
     ap.add_argument("--prompt", type=int, default=4096)
     ap.add_argument("--quick", action="store_true", help="skip the R=8/16 lines")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
+    ap.add_argument("--no-ref-cuda", action="store_true", help="skip the reference CUDA baseline")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -395,9 +457,13 @@ def main():
         torch.cuda.set_device(local)
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
     res = run_b200(args, rank, world, local)
-    cpu = None
+    cpu = refc = None
     if rank == 0 and world == 1 and not args.no_cpu:
         cpu = cpu_measure(model_dir(cfg, 0), args.loops, 64, 2, budget_s=20.0)
+    if rank == 0 and world == 1 and not args.no_ref_cuda:
+        loops_list = [args.loops] + ([] if args.quick else [8, 16])
+        refc = ref_cuda_measure(model_dir(cfg, 0), prompt_for(0, cfg["vocab_size"], args.prompt), loops_list,
+                                32, local)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -444,6 +510,13 @@ def main():
     if cpu:
         line["cpu_baseline"] = {"value": cpu["decode_tok_s"], "unit": "tok/s", "cores": cpu["cores"], "kind": "port",
                                 "sample": cpu["sample"], "prefill_tok_s": cpu["prefill_tok_s"]}
+    if refc:
+        line["ref_cuda_baseline"] = {
+            "value": refc[f"R{args.loops}"]["decode_tok_s"], "unit": "tok/s", "same_gpu": True,
+            "what": "the reference's kernels/slm.cu built from source (compute_60 PTX, JIT) under a C++ "
+                    "restatement of src/cuda.rs + src/model.rs, its own bench protocol (host clock, logits "
+                    "read back and host pick every token)",
+            "by_loops": refc}
     print(json.dumps(line), flush=True)
 
 
