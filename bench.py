@@ -16,7 +16,8 @@ Printed on one JSON line (rank 0):
   e2e       the same decode through the per-token C ABI (`slm_step` with a
             host id + `slm_sample` returning a host id), host clock;
   prefill   tok/s of the 4096-token prompt (feed + logits read back);
-  extra     R = 8 and R = 16 decode with the sampling of configs[2];
+  extra     R = 8 and R = 16 decode with the sampling of configs[2]; C4,
+            the G-layer variant (S | LS | SG) after a 16384-id prompt;
   roofline  the decode step's kernel (one persistent kernel per token) against
             measured HBM bandwidth, and the m = 1 GEMV op on its own;
   cpu_baseline  the CPU oracle (a C++ restatement of the reference's CPU
@@ -24,7 +25,8 @@ Printed on one JSON line (rank 0):
   ref_cuda_baseline  the reference's own CUDA kernels (kernels/slm.cu built
             from source) under a C++ restatement of its host side, on the same
             GPU with its own bench protocol; 32 decode steps per loop count
-            after the same 4096-id prompt; rank 0, N = 1 only.
+            after the same 4096-id prompt, and C4 (16384-id prompt, 16
+            decode steps); rank 0, N = 1 only.
 
 --impl reference runs only the CPU oracle on the host cores (rank 0), since
 the reference itself (Rust) cannot be built on this image.
@@ -207,11 +209,13 @@ def cpu_measure(folder: Path, loops: int, steps: int, warmup: int, budget_s: flo
 # The reference CUDA backend on the same GPU — baseline only
 # ---------------------------------------------------------------------------
 
-def ref_cuda_measure(folder: Path, prompt: np.ndarray, loops_list, decode_steps: int, device: int) -> dict | None:
+def ref_cuda_measure(cases, device: int) -> dict | None:
     """The reference's own kernels (kernels/slm.cu from source, JIT-compiled
     compute_60 PTX) under the C++ restatement of its host side, with its bench
     protocol (src/main.rs:200-223): prefill = feed + logits read, decode =
-    logits read + host pick + step per token, host clock."""
+    logits read + host pick + step per token, host clock.
+
+    cases: (name, model folder, prompt ids, loops, greedy, decode steps)."""
     sys.path.insert(0, str(ROOT))
     from oracle import oracle as O
     from oracle import ref_cuda as RC
@@ -219,15 +223,22 @@ def ref_cuda_measure(folder: Path, prompt: np.ndarray, loops_list, decode_steps:
     if not RC.available():
         return None
     backend = RC.Backend(device)
-    model = RC.Model(backend, folder)
     out = {}
-    for loops in loops_list:
-        se = model.session(loops)
+    models = {}
+    for name, folder, prompt, loops, greedy, steps in cases:
+        if folder not in models:
+            models[folder] = RC.Model(backend, folder)
+            # Warm-up, as the library's arm has: first launches and pool growth.
+            w = models[folder].session(loops)
+            w.feed(prompt[:512], 256)
+            w.step(int(np.argmax(w.logits())))
+            w.logits()
+            w.close()
+        se = models[folder].session(loops)
         t0 = time.perf_counter()
         se.feed(prompt, 256)
         logits = se.logits()
         pre_s = time.perf_counter() - t0
-        greedy = loops == loops_list[0]
         st = [O.rng_new(0)]
         hist = [int(t) for t in prompt[-256:]]
 
@@ -242,20 +253,20 @@ def ref_cuda_measure(folder: Path, prompt: np.ndarray, loops_list, decode_steps:
             tok = pick(se.logits())
         l0, s0 = backend.counts()
         t0 = time.perf_counter()
-        for _ in range(decode_steps):
+        for _ in range(steps):
             se.step(tok)
             tok = pick(se.logits())
             hist.append(tok)
         dec_s = time.perf_counter() - t0
         l1, s1 = backend.counts()
-        out[f"R{loops}"] = {"decode_tok_s": decode_steps / dec_s, "prefill_tok_s": len(prompt) / pre_s,
-                            "decode_steps": decode_steps,
-                            "launches_per_token": (l1 - l0) / decode_steps,
-                            "host_syncs_per_token": (s1 - s0) / decode_steps,
-                            "sampling": "greedy" if greedy else
-                            "T=0.8 top-k 40 repeat-penalty 1.1 (window 256) seed 0, host pick"}
+        out[name] = {"decode_tok_s": steps / dec_s, "prefill_tok_s": len(prompt) / pre_s, "decode_steps": steps,
+                     "prompt": len(prompt), "launches_per_token": (l1 - l0) / steps,
+                     "host_syncs_per_token": (s1 - s0) / steps,
+                     "sampling": "greedy" if greedy else
+                     "T=0.8 top-k 40 repeat-penalty 1.1 (window 256) seed 0, host pick"}
         se.close()
-    model.close()
+    for m in models.values():
+        m.close()
     backend.close()
     return out
 
@@ -391,6 +402,38 @@ def run_b200(args, rank: int, world: int, local: int) -> dict | None:
                                   "sampling": "T=0.8 top-k 40 repeat-penalty 1.1 (window 256) seed 0"}
             s2.close()
 
+    if not args.quick:
+        # configs[3] ("C4"): the G-layer variant (S | LS | SG, the fixture's
+        # global options), 16384-id prompt, then 256 greedy decodes.
+        gcfg = syn.GLOBAL
+        gfolder = model_dir(gcfg, 0)
+        gmodel = model.__class__(ctx, gfolder)
+        gprompt = prompt_for(rank, V, 16384)
+        s3 = gmodel.session(args.loops)
+        torch.cuda.synchronize(dev)
+        a, b = events()
+        a.record(stream)
+        s3.feed(gprompt, 256)
+        lg = s3.logits()
+        b.record(stream)
+        torch.cuda.synchronize(dev)
+        pre_ms = a.elapsed_time(b)
+        first = int(np.argmax(lg))
+        s3.decode(first, 8, greedy)
+        first = int(s3.sample(greedy))
+        n3 = 256
+        a, b = events()
+        a.record(stream)
+        s3.decode(first, n3, greedy)
+        b.record(stream)
+        torch.cuda.synchronize(dev)
+        extra["C4"] = {"decode_tok_s": n3 / (a.elapsed_time(b) / 1000.0), "prefill_tok_s": 16384 / (pre_ms / 1000.0),
+                       "decode_steps": n3, "prompt": 16384, "layout": "S|LS|SG", "loops": args.loops,
+                       "decode_path": "persistent kernel" if s3.mega else "captured graph",
+                       "sampling": "greedy"}
+        s3.close()
+        gmodel.close()
+
     step_kernels = se.step_kernels
     res = {"dec_ms": dec_ms, "e2e_s": e2e_s, "prefill_ms": prefill_ms, "prefill_host_s": prefill_host_s,
            "gemv_us": gemv_us, "clocks": clocks.summary(), "extra": extra, "step_kernels": step_kernels,
@@ -461,9 +504,13 @@ def main():
     if rank == 0 and world == 1 and not args.no_cpu:
         cpu = cpu_measure(model_dir(cfg, 0), args.loops, 64, 2, budget_s=20.0)
     if rank == 0 and world == 1 and not args.no_ref_cuda:
-        loops_list = [args.loops] + ([] if args.quick else [8, 16])
-        refc = ref_cuda_measure(model_dir(cfg, 0), prompt_for(0, cfg["vocab_size"], args.prompt), loops_list,
-                                32, local)
+        prompt = prompt_for(0, cfg["vocab_size"], args.prompt)
+        cases = [(f"R{args.loops}", model_dir(cfg, 0), prompt, args.loops, True, 32)]
+        if not args.quick:
+            cases += [(f"R{r}", model_dir(cfg, 0), prompt, r, False, 32) for r in (8, 16)]
+            cases.append(("C4", model_dir(syn.GLOBAL, 0), prompt_for(0, cfg["vocab_size"], 16384), args.loops,
+                          True, 16))
+        refc = ref_cuda_measure(cases, local)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -516,7 +563,7 @@ def main():
             "what": "the reference's kernels/slm.cu built from source (compute_60 PTX, JIT) under a C++ "
                     "restatement of src/cuda.rs + src/model.rs, its own bench protocol (host clock, logits "
                     "read back and host pick every token)",
-            "by_loops": refc}
+            "cases": refc}
     print(json.dumps(line), flush=True)
 
 
