@@ -93,6 +93,160 @@ __global__ void __launch_bounds__(GlaShape<DH>::T)
   for (int j = 0; j < R; j++) Sh_[(size_t)(a0 + j) * DH + b] = col[j];
 }
 
+// ---------------------------------------------------------------------------
+// Many tokens (prefill chunks): column-parallel recurrence + a norm/gate pass.
+//
+// A CTA owns CG = 8 columns of one head's state (grid heads × DH/CG), one warp:
+// each column is split over RQ = 4 lanes holding DH/4 of its rows in
+// registers.  Lane rq owns the float4 chunks rq, rq + 4, … of a row of q or k,
+// so the four lanes of a column read consecutive 16-byte words (no bank
+// conflicts).  Tokens are staged TC at a time with cp.async, double-buffered,
+// so the next stage loads while this one runs.  The bare y goes to `out`; the
+// head_norm + gate (which need a whole head) follow in k_gla_norm.
+// ---------------------------------------------------------------------------
+
+template <int DH>
+struct GlaCols {
+  static constexpr int CG = 8, RQ = 4, R = DH / RQ, C4 = R / 4, T = CG * RQ;
+  static constexpr int TC = 2048 / DH;  // tokens per stage (32 for DH 64)
+};
+
+__device__ __forceinline__ void cp16(void* dst, const void* src) {
+  unsigned d = (unsigned)__cvta_generic_to_shared(dst);
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(d), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+template <int DH>
+__global__ void __launch_bounds__(GlaCols<DH>::T)
+    k_gla_cols(float* __restrict__ S, const float* __restrict__ q, int ldq, const float* __restrict__ k, int ldk,
+               const float* __restrict__ v, int ldv, const float* __restrict__ dec, int lddec,
+               const float* __restrict__ bias, int m, float* __restrict__ out, int ldo) {
+  using G = GlaCols<DH>;
+  constexpr int CG = G::CG, RQ = G::RQ, C4 = G::C4, T = G::T, TC = G::TC;
+  __shared__ __align__(16) float qs[2][TC][DH], ks[2][TC][DH], vs[2][TC][CG];
+  __shared__ float ds[2][TC], ys[TC][CG];
+  const int h = blockIdx.x, cg = blockIdx.y, t = threadIdx.x;
+  const int b = t / RQ, rq = t % RQ;
+  const int col0 = h * DH + cg * CG;
+  float* Sh = S + (size_t)h * DH * DH;
+  float col[C4][4];
+#pragma unroll
+  for (int c = 0; c < C4; c++)
+#pragma unroll
+    for (int e = 0; e < 4; e++) col[c][e] = Sh[(size_t)(4 * (rq + RQ * c) + e) * DH + cg * CG + b];
+  const float bh = bias[h];
+
+  auto stage = [&](int s) {
+    const int c0 = s * TC, n = min(TC, m - c0), buf = s & 1;
+    for (int e = t; e < n * (DH / 4); e += T) {
+      const int i = e / (DH / 4), x = (e % (DH / 4)) * 4;
+      const size_t row = (size_t)(c0 + i);
+      cp16(&qs[buf][i][x], q + row * ldq + (size_t)h * DH + x);
+      cp16(&ks[buf][i][x], k + row * ldk + (size_t)h * DH + x);
+    }
+    for (int e = t; e < n * (CG / 4); e += T) {
+      const int i = e / (CG / 4), x = (e % (CG / 4)) * 4;
+      cp16(&vs[buf][i][x], v + (size_t)(c0 + i) * ldv + col0 + x);
+    }
+    cp_commit();
+    for (int i = t; i < n; i += T) ds[buf][i] = 1.0f / (1.0f + expf(dec[(size_t)(c0 + i) * lddec + h] + bh));
+  };
+
+  const int stages = (m + TC - 1) / TC;
+  stage(0);
+  for (int s = 0; s < stages; s++) {
+    const int c0 = s * TC, n = min(TC, m - c0), buf = s & 1;
+    if (s + 1 < stages) {
+      stage(s + 1);
+      cp_wait<1>();
+    } else {
+      cp_wait<0>();
+    }
+    __syncthreads();
+    for (int i = 0; i < n; i++) {
+      const float d = ds[buf][i], vb = vs[buf][i][b];
+      const float4* q4 = reinterpret_cast<const float4*>(qs[buf][i]);
+      const float4* k4 = reinterpret_cast<const float4*>(ks[buf][i]);
+      float y0 = 0.0f, y1 = 0.0f;
+#pragma unroll
+      for (int c = 0; c < C4; c++) {
+        const float4 kk = k4[rq + RQ * c], qq = q4[rq + RQ * c];
+        const float s0 = d * col[c][0] + kk.x * vb, s1 = d * col[c][1] + kk.y * vb;
+        const float s2 = d * col[c][2] + kk.z * vb, s3 = d * col[c][3] + kk.w * vb;
+        col[c][0] = s0, col[c][1] = s1, col[c][2] = s2, col[c][3] = s3;
+        y0 = fmaf(qq.x, s0, y0);
+        y1 = fmaf(qq.y, s1, y1);
+        y0 = fmaf(qq.z, s2, y0);
+        y1 = fmaf(qq.w, s3, y1);
+      }
+      float y = y0 + y1;
+#pragma unroll
+      for (int o = 1; o < RQ; o <<= 1) y += __shfl_xor_sync(0xffffffffu, y, o);
+      if (rq == 0) ys[i][b] = y;
+    }
+    __syncthreads();
+    for (int e = t; e < n * CG; e += T) {
+      const int i = e / CG, x = e % CG;
+      out[(size_t)(c0 + i) * ldo + col0 + x] = ys[i][x];
+    }
+    __syncthreads();  // ys and this buffer are reused
+  }
+#pragma unroll
+  for (int c = 0; c < C4; c++)
+#pragma unroll
+    for (int e = 0; e < 4; e++) Sh[(size_t)(4 * (rq + RQ * c) + e) * DH + cg * CG + b] = col[c][e];
+}
+
+// out[i][h] = silu(g[i][h]) · head_norm(y[i][h]) in place, one warp per (token, head).
+template <int DH>
+__global__ void __launch_bounds__(256)
+    k_gla_norm(float* __restrict__ out, int ldo, const float* __restrict__ gt, int ldg, const float* __restrict__ hnw,
+               float eps, int m, int heads) {
+  constexpr int P = (DH + 31) / 32;
+  const int w = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  if (w >= m * heads) return;
+  const int i = w / heads, h = w % heads;
+  float* o = out + (size_t)i * ldo + (size_t)h * DH;
+  const float* g = gt + (size_t)i * ldg + (size_t)h * DH;
+  float y[P];
+  float ss = 0.0f;
+#pragma unroll
+  for (int p = 0; p < P; p++) {
+    const int x = lane + 32 * p;
+    y[p] = x < DH ? o[x] : 0.0f;
+    ss = fmaf(y[p], y[p], ss);
+  }
+  ss = warp_sum(ss);
+  const float r = 1.0f / sqrtf(ss / (float)DH + eps);
+#pragma unroll
+  for (int p = 0; p < P; p++) {
+    const int x = lane + 32 * p;
+    if (x < DH) o[x] = silu_mul(g[x], y[p] * r * hnw[x]);
+  }
+}
+
+template <int DH>
+bool cols_ok(const GlaArgs& g) {
+  auto al = [](const void* p) { return ((uintptr_t)p & 15) == 0; };
+  return g.m >= 8 && g.ldq % 4 == 0 && g.ldk % 4 == 0 && g.ldv % 4 == 0 && al(g.q) && al(g.k) && al(g.v);
+}
+
+template <int DH>
+void launch_cols(const GlaArgs& g, cudaStream_t st) {
+  using G = GlaCols<DH>;
+  k_gla_cols<DH><<<dim3(g.heads, DH / G::CG), G::T, 0, st>>>(g.S, g.q, g.ldq, g.k, g.ldk, g.v, g.ldv, g.dec,
+                                                             g.lddec, g.bias, g.m, g.out, g.ldo);
+  SLM_LAUNCHED("k_gla_cols");
+  if (g.fuse) {
+    const int warps = g.m * g.heads;
+    k_gla_norm<DH><<<(warps + 7) / 8, 256, 0, st>>>(g.out, g.ldo, g.g, g.ldg, g.hnw, g.eps, g.m, g.heads);
+    SLM_LAUNCHED("k_gla_norm");
+  }
+}
+
 template <int DH>
 void launch(const GlaArgs& g, cudaStream_t st) {
   k_gla<DH><<<g.heads, GlaShape<DH>::T, 0, st>>>(g.S, g.q, g.ldq, g.k, g.ldk, g.v, g.ldv, g.g, g.ldg, g.dec, g.lddec,
@@ -107,9 +261,9 @@ void gla(const GlaArgs& g, cudaStream_t st) {
   switch (g.dh) {
     case 8: launch<8>(g, st); break;
     case 16: launch<16>(g, st); break;
-    case 32: launch<32>(g, st); break;
-    case 64: launch<64>(g, st); break;
-    case 128: launch<128>(g, st); break;
+    case 32: cols_ok<32>(g) ? launch_cols<32>(g, st) : launch<32>(g, st); break;
+    case 64: cols_ok<64>(g) ? launch_cols<64>(g, st) : launch<64>(g, st); break;
+    case 128: cols_ok<128>(g) ? launch_cols<128>(g, st) : launch<128>(g, st); break;
     default: fail(SLM_ERR_INVALID, "gla: head size must be one of 8, 16, 32, 64, 128");
   }
 }

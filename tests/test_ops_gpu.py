@@ -80,7 +80,10 @@ def test_l2norm(ops, oracle):
     close(y.read(37 * 64), oracle.l2norm(x, 37, 64))
 
 
-@pytest.mark.parametrize("m,heads,dh", [(1, 12, 64), (37, 4, 8), (256, 12, 64), (5, 2, 128)])
+# m >= 8 with head size 32/64/128 takes the column-parallel kernel (ragged last
+# stages included); the rest the per-head kernel.
+@pytest.mark.parametrize("m,heads,dh", [(1, 12, 64), (37, 4, 8), (256, 12, 64), (5, 2, 128), (100, 12, 64),
+                                        (40, 3, 32), (33, 2, 128), (8, 1, 64)])
 def test_gla(ops, oracle, m, heads, dh):
     n = m * heads * dh
     q, k, v = rand(n, scale=0.2), rand(n, scale=0.2), rand(n)
