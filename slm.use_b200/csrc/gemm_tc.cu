@@ -52,8 +52,11 @@ using CollectiveMainloop = typename cutlass::gemm::collective::CollectiveBuilder
         sizeof(typename CollectiveEpilogue::SharedStorage))>,
     cutlass::gemm::KernelTmaWarpSpecialized1SmFastFP32Sm100>::CollectiveOp;
 
-using GemmKernel =
-    cutlass::gemm::kernel::GemmUniversal<Shape<int, int, int, int>, CollectiveMainloop, CollectiveEpilogue, void>;
+// Stream-K tile scheduling: the 768-wide outputs of a 256-token chunk make only
+// 2 × 12 output tiles, so the K loop is shared out over the idle SMs (with the
+// deterministic reduction of the partial tiles).
+using GemmKernel = cutlass::gemm::kernel::GemmUniversal<Shape<int, int, int, int>, CollectiveMainloop,
+                                                        CollectiveEpilogue, cutlass::gemm::StreamKScheduler>;
 using Gemm = cutlass::gemm::device::GemmUniversalAdapter<GemmKernel>;
 
 using StrideA = typename Gemm::GemmKernel::StrideA;
