@@ -39,7 +39,13 @@ constexpr int kAlign = 4;  // 16 bytes of fp32
 
 using ArchTag = cutlass::arch::Sm100;
 using OpClass = cutlass::arch::OpClassTensorOp;
-using TileShape = Shape<_128, _64, _32>;
+#ifndef SLM_TC_TILE_N
+#define SLM_TC_TILE_N 64
+#endif
+#ifndef SLM_TC_TILE_K
+#define SLM_TC_TILE_K 32
+#endif
+using TileShape = Shape<_128, Int<SLM_TC_TILE_N>, Int<SLM_TC_TILE_K>>;
 using ClusterShape = Shape<_1, _1, _1>;
 
 using CollectiveEpilogue = typename cutlass::epilogue::collective::CollectiveBuilder<
