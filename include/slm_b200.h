@@ -45,6 +45,7 @@ typedef struct slm_ctx slm_ctx;
 typedef struct slm_buf slm_buf;
 typedef struct slm_model slm_model;
 typedef struct slm_session slm_session;
+typedef struct slm_batch slm_batch;
 
 /* Message of the last failed call on this thread ("" if none). */
 const char* slm_last_error(void);
@@ -249,6 +250,35 @@ int slm_session_stat(const slm_session* se, int what, int64_t* out);
  * arithmetic and in GEMV epilogues; the GEMV tiles it took; 0.
  * *n_out receives the count; nothing is copied when cap < count. */
 int slm_session_trace(slm_session* se, uint64_t* out, size_t cap, size_t* n_out);
+
+/* ---- Batched decode --------------------------------------------------------
+ * No counterpart in the reference: its server runs one request at a time
+ * (src/serve.rs:1-3) and Model::step advances one session.  A batch steps n
+ * sessions of the same model together, one token each, reading the weights
+ * once per step for all of them; each session keeps its own caches, GLA state
+ * and position, so row i computes what slm_step would on session i (up to the
+ * rounding of the linears, which run as one n-row product).  This serves many
+ * independent sequences per GPU.
+ *
+ * The sessions must share the model and the loop count, appear once each,
+ * have no global-attention layers, and outlive the batch (slm_session_free
+ * fails while a session belongs to a batch).  Stepping a session on its own
+ * between batch steps is allowed.  After batch steps a session's own logits
+ * (slm_logits) are those of its last own step; read the batch's with
+ * slm_batch_logits. */
+int slm_batch_new(slm_session* const* sessions, size_t n, slm_batch** out);
+int slm_batch_free(slm_batch* b);
+int slm_batch_size(const slm_batch* b, size_t* out);
+/* One step: feeds ids[i] (host, n ids) to session i.  Logits of every row are
+ * kept in the batch. */
+int slm_batch_step(slm_batch* b, const uint32_t* ids);
+/* The last step's logits, out[i·vocab + j] (host, n·vocab floats).  Synchronises. */
+int slm_batch_logits(slm_batch* b, float* out);
+/* `steps` greedy decode steps of every session without leaving the device:
+ * feeds first[i] to session i, then each picked id (first maximum, as pick
+ * with temperature 0).  out[t·n + i] (host) receives session i's id of step t.
+ * Synchronises once at the end. */
+int slm_batch_decode(slm_batch* b, const uint32_t* first, size_t steps, uint32_t* out);
 
 #ifdef __cplusplus
 }

@@ -118,6 +118,12 @@ _SIGS = {
     "slm_sample": (_c.c_int, [_vp, _c.POINTER(_Sampling), _u32p, _sz, _u64p, _u32p]),
     "slm_pick": (_c.c_int, [_vp, _vp, _sz, _c.POINTER(_Sampling), _u32p, _sz, _u64p, _u32p]),
     "slm_decode": (_c.c_int, [_vp, _c.c_uint32, _sz, _c.POINTER(_Sampling), _u32p, _sz, _u64p, _u32p]),
+    "slm_batch_new": (_c.c_int, [_c.POINTER(_vp), _sz, _c.POINTER(_vp)]),
+    "slm_batch_free": (_c.c_int, [_vp]),
+    "slm_batch_size": (_c.c_int, [_vp, _c.POINTER(_sz)]),
+    "slm_batch_step": (_c.c_int, [_vp, _u32p]),
+    "slm_batch_logits": (_c.c_int, [_vp, _f32p]),
+    "slm_batch_decode": (_c.c_int, [_vp, _u32p, _sz, _u32p]),
 }
 
 
@@ -428,10 +434,16 @@ class Session:
         # interpreter exit its globals may already be gone.
         if getattr(self, "_h", None):
             free = getattr(self, "_free", None) or lib().slm_session_free
-            free(self._h)
+            code = free(self._h)
+            if code != 0:  # e.g. still in a batch: the session stays open
+                raise SlmError(code, lib().slm_last_error().decode())
             self._h = None
 
-    __del__ = close
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
     @property
     def pos(self) -> int:
@@ -522,4 +534,52 @@ class Session:
                                 _c.byref(st), out.ctypes.data_as(_u32p)))
         if rng_state is not None:
             rng_state[0] = st.value
+        return out
+
+
+class Batch:
+    """Several sessions of one model stepped together, one token each per step
+    (slm_batch_*; no counterpart in the reference, whose server runs one
+    request at a time).  The sessions must outlive the batch."""
+
+    def __init__(self, sessions):
+        self.sessions = list(sessions)
+        n = len(self.sessions)
+        hs = (_vp * n)(*[se._h for se in self.sessions])
+        h = _vp()
+        _check(lib().slm_batch_new(hs, n, _c.byref(h)))
+        self._h = h
+        self._free = lib().slm_batch_free
+        self.n = n
+        self.vocab = self.sessions[0].vocab
+
+    def close(self):
+        # The free function is looked up while the module is intact: at
+        # interpreter exit its globals may already be gone.
+        if getattr(self, "_h", None):
+            self._free(self._h)
+            self._h = None
+
+    __del__ = close
+
+    def step(self, ids) -> None:
+        """Feeds ids[i] to session i."""
+        ids = _u32(ids)
+        if ids.size != self.n:
+            raise ValueError(f"expected {self.n} ids")
+        _check(lib().slm_batch_step(self._h, ids.ctypes.data_as(_u32p)))
+
+    def logits(self) -> np.ndarray:
+        """[n][vocab] logits of the last step."""
+        out = np.empty((self.n, self.vocab), dtype=np.float32)
+        _check(lib().slm_batch_logits(self._h, out.ctypes.data_as(_f32p)))
+        return out
+
+    def decode(self, first, steps: int) -> np.ndarray:
+        """`steps` greedy steps of every session: [steps][n] picked ids."""
+        first = _u32(first)
+        if first.size != self.n:
+            raise ValueError(f"expected {self.n} ids")
+        out = np.empty((steps, self.n), dtype=np.uint32)
+        _check(lib().slm_batch_decode(self._h, first.ctypes.data_as(_u32p), steps, out.ctypes.data_as(_u32p)))
         return out

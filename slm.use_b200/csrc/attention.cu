@@ -48,17 +48,25 @@ __device__ __forceinline__ void merge(float& m, float& l, float* acc, float om, 
 // ---------------------------------------------------------------------------
 // Slice pass for a few queries.  grid (nsplit, heads, m), 128 threads.
 // ---------------------------------------------------------------------------
+// With `rows` set, query i belongs to its own sequence: its cache is
+// rows->k[i] / rows->v[i] and its position *rows->pos[i] (batched decode of
+// independent sessions, one token each).
 template <int DH>
 __global__ void __launch_bounds__(128)
     k_attn_split(const float* __restrict__ q, int ldq, const float* __restrict__ K, const float* __restrict__ V,
-                 AttnGeom g, const long long* __restrict__ pos_ptr, int nsplit, float* __restrict__ part) {
+                 AttnGeom g, const long long* __restrict__ pos_ptr, int nsplit, float* __restrict__ part,
+                 AttnRows rows) {
   constexpr int G = DH / 8;        // lanes per cache row
   constexpr int PPW = 32 / G;      // rows per warp step
   constexpr int WARPS = 4;
   const int s = blockIdx.x, h = blockIdx.y, i = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int sub = lane % G, grp = lane / G;
-  const long long p = pos_ptr[0] + i;
+  if (rows.pos) {
+    K = rows.k[i];
+    V = rows.v[i];
+  }
+  const long long p = rows.pos ? *rows.pos[i] : pos_ptr[0] + i;
   Range r = visible(p, g.reach, g.gap);
   long long count = r.hi - r.lo;
   long long chunk = (count + nsplit - 1) / nsplit;
@@ -309,7 +317,8 @@ template <int DH>
 void launch_dh(const float* q, int ldq, const float* K, const float* V, const AttnGeom& g, const long long* pos_ptr,
                int nsplit, float* part, cudaStream_t st) {
   if (g.m <= 8 || DH > 128) {
-    k_attn_split<DH><<<dim3(nsplit, g.heads, g.m), 128, 0, st>>>(q, ldq, K, V, g, pos_ptr, nsplit, part);
+    k_attn_split<DH><<<dim3(nsplit, g.heads, g.m), 128, 0, st>>>(q, ldq, K, V, g, pos_ptr, nsplit, part,
+                                                                 AttnRows{});
     SLM_LAUNCHED("k_attn_split");
   } else {
     launch_tile<DH>(q, ldq, K, V, g, pos_ptr, nsplit, part, st);
@@ -344,6 +353,25 @@ void attention(const float* q, int ldq, const float* K, const float* V, const At
     case 256: launch_dh<256>(q, ldq, K, V, g, pos_ptr, nsplit, part, st); break;
     default: fail(SLM_ERR_INVALID, "attend: head size must be one of 8, 16, 32, 64, 128, 256");
   }
+  k_attn_combine<<<g.m * g.heads, 32 * cdiv(g.dh, 32), 0, st>>>(part, nsplit, g.m, g.heads, g.dh, y, ldy);
+  SLM_LAUNCHED("k_attn_combine");
+}
+
+void attention_rows(const float* q, int ldq, const AttnRows& rows, const AttnGeom& g, int nsplit, float* part,
+                    float* y, int ldy, cudaStream_t st) {
+  if (g.m == 0) return;
+  SLM_REQUIRE(g.key_heads > 0 && g.heads % g.key_heads == 0, "attend: heads must be a multiple of key_heads");
+  const dim3 grid(nsplit, g.heads, g.m);
+  switch (g.dh) {
+    case 8: k_attn_split<8><<<grid, 128, 0, st>>>(q, ldq, nullptr, nullptr, g, nullptr, nsplit, part, rows); break;
+    case 16: k_attn_split<16><<<grid, 128, 0, st>>>(q, ldq, nullptr, nullptr, g, nullptr, nsplit, part, rows); break;
+    case 32: k_attn_split<32><<<grid, 128, 0, st>>>(q, ldq, nullptr, nullptr, g, nullptr, nsplit, part, rows); break;
+    case 64: k_attn_split<64><<<grid, 128, 0, st>>>(q, ldq, nullptr, nullptr, g, nullptr, nsplit, part, rows); break;
+    case 128: k_attn_split<128><<<grid, 128, 0, st>>>(q, ldq, nullptr, nullptr, g, nullptr, nsplit, part, rows); break;
+    case 256: k_attn_split<256><<<grid, 128, 0, st>>>(q, ldq, nullptr, nullptr, g, nullptr, nsplit, part, rows); break;
+    default: fail(SLM_ERR_INVALID, "attend: head size must be one of 8, 16, 32, 64, 128, 256");
+  }
+  SLM_LAUNCHED("k_attn_split");
   k_attn_combine<<<g.m * g.heads, 32 * cdiv(g.dh, 32), 0, st>>>(part, nsplit, g.m, g.heads, g.dh, y, ldy);
   SLM_LAUNCHED("k_attn_combine");
 }

@@ -212,6 +212,39 @@ __global__ void k_advance_pos(long long* pos, long long m) {
   if (threadIdx.x == 0 && blockIdx.x == 0) pos[0] += m;
 }
 
+// Batched decode: row i is one token of its own sequence, at *pos[i], with
+// its own ring caches k[i] / v[i] (same arithmetic as k_rope_store).
+__global__ void k_rope_store_rows(const float* mix, size_t ldmix, const float* inv, long long* const* posr, size_t m,
+                                  size_t heads, size_t dh, size_t cap, float* qout, float* const* kr,
+                                  float* const* vr) {
+  const size_t half = dh / 2, d = heads * dh;
+  GRID_STRIDE(t, m * heads * half) {
+    size_t i = t / (heads * half), hh = (t / half) % heads, j = t % half;
+    const long long pos = *posr[i];
+    float a = (float)pos * inv[j];
+    float sn, cs;
+    sincosf(a, &sn, &cs);
+    const float* row = mix + i * ldmix;
+    size_t slot = (size_t)(pos % (long long)cap);
+    float qa = row[hh * dh + j], qb = row[hh * dh + half + j];
+    float* qo = qout + i * d + hh * dh;
+    qo[j] = qa * cs - qb * sn;
+    qo[half + j] = qa * sn + qb * cs;
+    float ka = row[d + hh * dh + j], kb = row[d + hh * dh + half + j];
+    float* ko = kr[i] + (hh * cap + slot) * dh;
+    ko[j] = ka * cs - kb * sn;
+    ko[half + j] = ka * sn + kb * cs;
+    float* vo = vr[i] + (hh * cap + slot) * dh;
+    vo[j] = row[2 * d + hh * dh + j];
+    vo[half + j] = row[2 * d + hh * dh + half + j];
+  }
+}
+
+__global__ void k_advance_rows(long long* const* posr, size_t m, unsigned* counter) {
+  for (size_t i = threadIdx.x; i < m; i += blockDim.x) *posr[i] += 1;
+  if (counter && threadIdx.x == 0) *counter += 1;
+}
+
 }  // namespace
 
 void ew_gather(float* y, const float* w, const uint32_t* ids, size_t m, size_t d, size_t vocab, int* err,
@@ -320,6 +353,18 @@ void ew_silu_pair(float* mid, const float* up, size_t m, size_t F, cudaStream_t 
 void ew_advance_pos(long long* pos, long long m, cudaStream_t st) {
   k_advance_pos<<<1, 32, 0, st>>>(pos, m);
   SLM_LAUNCHED("k_advance_pos");
+}
+void ew_rope_store_rows(const float* mix, size_t ldmix, const float* inv, long long* const* posr, size_t m,
+                        size_t heads, size_t dh, size_t cap, float* qout, float* const* kr, float* const* vr,
+                        cudaStream_t st) {
+  if (!m) return;
+  k_rope_store_rows<<<ew_grid(m * heads * (dh / 2)), EW, 0, st>>>(mix, ldmix, inv, posr, m, heads, dh, cap, qout,
+                                                                  kr, vr);
+  SLM_LAUNCHED("k_rope_store_rows");
+}
+void ew_advance_rows(long long* const* posr, size_t m, unsigned* counter, cudaStream_t st) {
+  k_advance_rows<<<1, 256, 0, st>>>(posr, m, counter);
+  SLM_LAUNCHED("k_advance_rows");
 }
 
 }  // namespace slm

@@ -36,11 +36,18 @@ __global__ void __launch_bounds__(GlaShape<DH>::T)
     k_gla(float* __restrict__ S, const float* __restrict__ q, int ldq, const float* __restrict__ k, int ldk,
           const float* __restrict__ v, int ldv, const float* __restrict__ gt, int ldg, const float* __restrict__ dec,
           int lddec, const float* __restrict__ bias, const float* __restrict__ hnw, float eps, int m, int heads,
-          float* __restrict__ out, int ldo, int fuse) {
+          float* __restrict__ out, int ldo, int fuse, float* const* __restrict__ S_rows) {
   using Sh = GlaShape<DH>;
   constexpr int RQ = Sh::RQ, R = Sh::R, T = Sh::T, TC = Sh::TC;
   __shared__ float qs[TC][DH], ks[TC][DH], vs[TC][DH], ys[TC][DH], ds[TC];
   const int h = blockIdx.x, t = threadIdx.x;
+  if (S_rows) {  // batched decode: sequence blockIdx.y, one token
+    const int r = blockIdx.y;
+    S = S_rows[r];
+    q += (size_t)r * ldq, k += (size_t)r * ldk, v += (size_t)r * ldv, gt += (size_t)r * ldg;
+    dec += (size_t)r * lddec, out += (size_t)r * ldo;
+    m = 1;
+  }
   const int b = t / RQ, rq = t % RQ, a0 = rq * R;
   const int lane = t & 31, warp = t >> 5;
   float col[R];
@@ -250,7 +257,15 @@ void launch_cols(const GlaArgs& g, cudaStream_t st) {
 template <int DH>
 void launch(const GlaArgs& g, cudaStream_t st) {
   k_gla<DH><<<g.heads, GlaShape<DH>::T, 0, st>>>(g.S, g.q, g.ldq, g.k, g.ldk, g.v, g.ldv, g.g, g.ldg, g.dec, g.lddec,
-                                                 g.bias, g.hnw, g.eps, g.m, g.heads, g.out, g.ldo, g.fuse);
+                                                 g.bias, g.hnw, g.eps, g.m, g.heads, g.out, g.ldo, g.fuse, nullptr);
+  SLM_LAUNCHED("k_gla");
+}
+
+template <int DH>
+void launch_rows(const GlaArgs& g, float* const* S_rows, cudaStream_t st) {
+  k_gla<DH><<<dim3(g.heads, g.m), GlaShape<DH>::T, 0, st>>>(nullptr, g.q, g.ldq, g.k, g.ldk, g.v, g.ldv, g.g, g.ldg,
+                                                           g.dec, g.lddec, g.bias, g.hnw, g.eps, 1, g.heads, g.out,
+                                                           g.ldo, g.fuse, S_rows);
   SLM_LAUNCHED("k_gla");
 }
 
@@ -264,6 +279,18 @@ void gla(const GlaArgs& g, cudaStream_t st) {
     case 32: cols_ok<32>(g) ? launch_cols<32>(g, st) : launch<32>(g, st); break;
     case 64: cols_ok<64>(g) ? launch_cols<64>(g, st) : launch<64>(g, st); break;
     case 128: cols_ok<128>(g) ? launch_cols<128>(g, st) : launch<128>(g, st); break;
+    default: fail(SLM_ERR_INVALID, "gla: head size must be one of 8, 16, 32, 64, 128");
+  }
+}
+
+void gla_rows(const GlaArgs& g, float* const* S_rows, cudaStream_t st) {
+  if (g.m == 0) return;
+  switch (g.dh) {
+    case 8: launch_rows<8>(g, S_rows, st); break;
+    case 16: launch_rows<16>(g, S_rows, st); break;
+    case 32: launch_rows<32>(g, S_rows, st); break;
+    case 64: launch_rows<64>(g, S_rows, st); break;
+    case 128: launch_rows<128>(g, S_rows, st); break;
     default: fail(SLM_ERR_INVALID, "gla: head size must be one of 8, 16, 32, 64, 128");
   }
 }

@@ -36,6 +36,12 @@ struct AttnGeom {
   int heads, key_heads, dh;
   float scale;
 };
+// Per-row sequences of a batched decode step (device arrays of g.m entries).
+struct AttnRows {
+  float* const* k = nullptr;
+  float* const* v = nullptr;
+  long long* const* pos = nullptr;
+};
 int attn_splits(const AttnGeom& g, long long max_span);
 size_t attn_part_floats(const AttnGeom& g, int nsplit);
 // y[i][h·dh + e]; part holds attn_part_floats(g, nsplit) floats.
@@ -53,6 +59,12 @@ struct GlaArgs {
   int fuse;  // 1: out = silu(g)·head_norm(y); 0: out = y (the bare Ops::gla)
 };
 void gla(const GlaArgs& a, cudaStream_t st);
+// One token for each of a.m independent sequences: row i's state is S_rows[i]
+// (a.S unused), its q/k/v/g/dec/out rows at i·ld.
+void gla_rows(const GlaArgs& a, float* const* S_rows, cudaStream_t st);
+// Attention of g.m single-token queries, each over its own cache and position.
+void attention_rows(const float* q, int ldq, const AttnRows& rows, const AttnGeom& g, int nsplit, float* part,
+                    float* y, int ldy, cudaStream_t st);
 
 struct SampleArgs {
   const float* logits;
@@ -100,5 +112,15 @@ void ew_g_post(float* q, size_t d, size_t m, const long long* pos_ptr, float inv
                cudaStream_t st);
 void ew_silu_pair(float* mid, const float* up, size_t m, size_t F, cudaStream_t st);
 void ew_advance_pos(long long* pos, long long m, cudaStream_t st);
+// Batched decode of m independent sequences (one token each; arrays of m).
+void ew_rope_store_rows(const float* mix, size_t ldmix, const float* inv, long long* const* posr, size_t m,
+                        size_t heads, size_t dh, size_t cap, float* qout, float* const* kr, float* const* vr,
+                        cudaStream_t st);
+// *posr[i] += 1 for every row; *counter += 1 when counter is set.
+void ew_advance_rows(long long* const* posr, size_t m, unsigned* counter, cudaStream_t st);
+// Greedy pick per row of logits [m][vocab] (first maximum, NaN never wins):
+// next[i] = id; outs[(*out_index)·m + i] = id when outs is set.
+void argmax_rows(const float* logits, size_t vocab, size_t m, uint32_t* next, uint32_t* outs,
+                 const unsigned* out_index, cudaStream_t st);
 
 }  // namespace slm

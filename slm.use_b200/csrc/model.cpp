@@ -102,6 +102,30 @@ struct slm_session {
   int grid = 0;
   unsigned long long* trace = nullptr;  // per-phase timeline of the last step (SLM_OPT_TRACE)
   unsigned* attn_count = nullptr;        // per-head arrival counters of the attention phases
+  int in_batches = 0;                    // batches holding this session
+};
+
+// Several sessions of one model stepped together (one token each per step):
+// the weights are read once per step for all of them, each row keeps its own
+// caches, GLA state and position (decode_batch below).
+struct slm_batch {
+  slm_model* model = nullptr;
+  slm_ctx* ctx = nullptr;
+  std::vector<slm_session*> ses;
+  size_t n = 0;
+  std::vector<void*> owned;
+  float *xa = nullptr, *xb = nullptr, *e0 = nullptr, *e_proj = nullptr, *nb = nullptr, *mix = nullptr, *q = nullptr,
+        *kb = nullptr, *y = nullptr, *mid = nullptr, *dec = nullptr, *part = nullptr, *logits = nullptr,
+        *upbuf = nullptr;
+  uint32_t* ids = nullptr;           // [n] this step's tokens (the arg-max writes the next ones)
+  long long** posr = nullptr;        // [n] the sessions' device positions
+  std::vector<float**> tab;          // per layer instance, in step order: [3][n] k, v, s pointers
+  unsigned* out_index = nullptr;     // steps taken since the last reset
+  uint32_t* outs = nullptr;          // [outs_cap][n] picked ids
+  size_t outs_cap = 0;
+  int nsplit = 1;
+  cudaGraphExec_t graph = nullptr;
+  bool capturing = false;
 };
 
 namespace slm {
@@ -619,6 +643,149 @@ void check_device_error(slm_ctx* c, slm_session* se = nullptr) {
   }
 }
 
+// ---------------------------------------------------------------------------
+// Batched decode: n sessions, one token each per step.  No counterpart in the
+// reference (its server runs one request at a time, src/serve.rs:1-3); the
+// arithmetic of each row is Model::block / Model::advance (src/model.rs:
+// 400-640) for m = 1, on that session's state.
+// ---------------------------------------------------------------------------
+
+void* balloc(slm_batch* bt, size_t bytes) {
+  void* p = dev_alloc(bytes);
+  bt->owned.push_back(p);
+  SLM_CUDA(cudaMemsetAsync(p, 0, bytes, bt->ctx->stream));
+  return p;
+}
+
+void batch_block(slm_batch* bt, const Block& b, size_t li, float* x) {
+  slm_model* md = bt->model;
+  const Config& c = md->cfg;
+  cudaStream_t s = bt->ctx->stream;
+  const size_t d = c.d, heads = c.heads, dh = c.dh(), m = bt->n;
+  const float scale = 1.0f / std::sqrt((float)dh);
+  const int im = (int)m, id = (int)d;
+  float* const* K = bt->tab[li];
+  float* const* V = bt->tab[li] + m;
+  float* const* S = bt->tab[li] + 2 * m;
+  ew_rms(bt->nb, x, b.norm1, m, d, c.eps, nullptr, s);
+  if (b.kind == 'S') {
+    run_linear(s, b.qkv, bt->nb, id, im, bt->mix, (int)(3 * d), EPI_STORE);
+    const size_t cap = c.window + CHUNK;
+    ew_rope_store_rows(bt->mix, 3 * d, md->inv_freq, bt->posr, m, heads, dh, cap, bt->q, K, V, s);
+    AttnGeom g{im, (long long)c.window, 0, (long long)cap, (int)heads, (int)heads, (int)dh, scale};
+    AttnRows rows;
+    rows.k = K, rows.v = V, rows.pos = bt->posr;
+    attention_rows(bt->q, id, rows, g, bt->nsplit, bt->part, bt->y, id, s);
+  } else {  // 'L' (global layers are refused when the batch is made)
+    run_linear(s, b.qkvg, bt->nb, id, im, bt->mix, (int)(4 * d), EPI_STORE);
+    run_linear(s, b.decay, bt->nb, id, im, bt->dec, (int)heads, EPI_STORE);
+    ew_l2norm(bt->q, d, bt->mix, 4 * d, m, heads, dh, s);
+    ew_l2norm(bt->kb, d, bt->mix + d, 4 * d, m, heads, dh, s);
+    GlaArgs a{};
+    a.q = bt->q, a.ldq = id;
+    a.k = bt->kb, a.ldk = id;
+    a.v = bt->mix + 2 * d, a.ldv = (int)(4 * d);
+    a.g = bt->mix + 3 * d, a.ldg = (int)(4 * d);
+    a.dec = bt->dec, a.lddec = (int)heads;
+    a.bias = b.bias, a.hnw = b.head_norm, a.eps = c.eps;
+    a.m = im, a.heads = (int)heads, a.dh = (int)dh;
+    a.out = bt->y, a.ldo = id, a.fuse = 1;
+    gla_rows(a, S, s);
+  }
+  run_linear(s, b.o, bt->y, id, im, x, id, EPI_ADD, x, id);  // x += o·y
+  ew_rms(bt->nb, x, b.norm2, m, d, c.eps, nullptr, s);
+  const size_t hidden = b.down.cols;
+  if (m > 8 && hidden % 4 == 0) {
+    run_linear(s, b.up, bt->nb, id, im, bt->upbuf, (int)(2 * hidden), EPI_STORE);
+    ew_silu_pair(bt->mid, bt->upbuf, m, hidden, s);
+  } else {
+    run_linear(s, b.up, bt->nb, id, im, bt->mid, (int)hidden, EPI_SILU);
+  }
+  run_linear(s, b.down, bt->mid, (int)hidden, im, x, id, EPI_ADD, x, id);
+}
+
+// One step of every session: tokens in bt->ids; the greedy ids of the next
+// step go back to bt->ids and to outs[*out_index]; positions advance.
+void batch_advance(slm_batch* bt) {
+  g_ctx_for_linear = bt->ctx;
+  g_capturing = bt->capturing;
+  slm_model* md = bt->model;
+  const Config& c = md->cfg;
+  cudaStream_t s = bt->ctx->stream;
+  const size_t d = c.d, m = bt->n;
+  const size_t loops = bt->ses[0]->loops;
+  float* x = bt->xa;
+  ew_embed(bt->e0, x, md->embed.w, bt->ids, m, d, c.vocab, bt->ctx->err, s);
+  size_t li = 0;
+  for (size_t i = 0; i < md->prelude.size(); i++) batch_block(bt, md->prelude[i], li++, x);
+  if (md->looped) {
+    run_linear(s, md->inject, x, (int)d, (int)m, bt->e_proj, (int)d, EPI_STORE);
+    float* sbuf = x;
+    for (size_t r = 0; r < loops; r++) {
+      float* xr = (sbuf == bt->xa) ? bt->xb : bt->xa;
+      ew_loop_in(xr, sbuf, bt->e_proj, md->loop_embed.w + r * d, m, d, s);
+      for (size_t j = 0; j < md->core.size(); j++) batch_block(bt, md->core[j], li++, xr);
+      if (c.damp == 1.0f)
+        sbuf = xr;
+      else
+        ew_mix(sbuf, sbuf, xr, m * d, c.damp, s);
+    }
+    x = sbuf;
+  }
+  for (size_t i = 0; i < md->coda.size(); i++) batch_block(bt, md->coda[i], li++, x);
+  ew_rms(bt->nb, x, md->norm_f, m, d, c.eps, nullptr, s);
+  run_linear(s, md->embed, bt->nb, (int)d, (int)m, bt->logits, (int)c.vocab, EPI_STORE);  // tied head, every row
+  argmax_rows(bt->logits, c.vocab, m, bt->ids, bt->outs, bt->out_index, s);
+  ew_advance_rows(bt->posr, m, bt->out_index, s);
+}
+
+void batch_drop_graph(slm_batch* bt) {
+  if (bt->graph) {
+    cudaGraphExecDestroy(bt->graph);
+    bt->graph = nullptr;
+  }
+}
+
+// One step, replayed from a CUDA graph captured on first use.
+void batch_step_device(slm_batch* bt) {
+  cudaStream_t s = bt->ctx->stream;
+  if (!bt->graph) {
+    cudaGraph_t g = nullptr;
+    SLM_CUDA(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
+    bt->capturing = true;
+    try {
+      batch_advance(bt);
+    } catch (...) {
+      bt->capturing = false;
+      cudaStreamEndCapture(s, &g);
+      if (g) cudaGraphDestroy(g);
+      throw;
+    }
+    bt->capturing = false;
+    SLM_CUDA(cudaStreamEndCapture(s, &g));
+    cudaError_t e = cudaGraphInstantiate(&bt->graph, g, 0);
+    cudaGraphDestroy(g);
+    SLM_CUDA(e);
+  }
+  SLM_CUDA(cudaGraphLaunch(bt->graph, s));
+  for (auto* se : bt->ses) se->pos += 1;
+}
+
+void batch_outs(slm_batch* bt, size_t steps) {
+  if (steps <= bt->outs_cap) return;
+  size_t cap = std::max<size_t>(steps, 2 * bt->outs_cap);
+  SLM_CUDA(cudaStreamSynchronize(bt->ctx->stream));
+  auto* p = static_cast<uint32_t*>(dev_alloc(cap * bt->n * sizeof(uint32_t)));
+  for (auto& o : bt->owned)
+    if (o == bt->outs) {
+      dev_free(o);
+      o = p;
+    }
+  bt->outs = p;
+  bt->outs_cap = cap;
+  batch_drop_graph(bt);  // the graph holds the old pointer
+}
+
 void ensure_u32(slm_session* se, uint32_t** p, size_t* cap, size_t n) {
   if (*cap >= n) return;
   SLM_CUDA(cudaStreamSynchronize(se->ctx->stream));
@@ -822,6 +989,7 @@ int slm_session_new(slm_model* md, size_t loops, slm_session** out) {
 int slm_session_free(slm_session* se) {
   return guard([&] {
     if (!se) return;
+    SLM_REQUIRE(se->in_batches == 0, "the session belongs to a batch: free the batch first");
     Device dev(se->ctx);
     cudaStreamSynchronize(se->ctx->stream);
     drop_graph(se);
@@ -1083,6 +1251,134 @@ int slm_decode(slm_session* se, uint32_t first, size_t n, const slm_sampling* sp
     SLM_CUDA(cudaMemcpyAsync(&st, se->rng_dev, sizeof(st), cudaMemcpyDeviceToHost, s));
     check_device_error(se->ctx, se);
     *rng_state = st;
+  });
+}
+
+int slm_batch_new(slm_session* const* sessions, size_t n, slm_batch** out) {
+  return guard([&] {
+    SLM_REQUIRE(sessions && out && n >= 1, "bad arguments");
+    slm_model* md = sessions[0] ? sessions[0]->model : nullptr;
+    SLM_REQUIRE(md, "bad arguments");
+    const Config& c = md->cfg;
+    for (size_t i = 0; i < n; i++) {
+      SLM_REQUIRE(sessions[i] && sessions[i]->model == md, "every session of a batch must use the same model");
+      SLM_REQUIRE(sessions[i]->loops == sessions[0]->loops, "every session of a batch must run the same loops");
+      for (size_t j = 0; j < i; j++) SLM_REQUIRE(sessions[j] != sessions[i], "a session appears twice in the batch");
+    }
+    for (const std::string* part : {&c.prelude, &c.core, &c.coda})
+      SLM_REQUIRE(part->find('G') == std::string::npos, "batched decode does not support global-attention layers");
+    Device dev(md->ctx);
+    auto bt = std::make_unique<slm_batch>();
+    bt->model = md, bt->ctx = md->ctx, bt->n = n;
+    bt->ses.assign(sessions, sessions + n);
+    cudaStream_t s = md->ctx->stream;
+    try {
+      const size_t d = c.d;
+      auto f = [&](size_t k) { return static_cast<float*>(balloc(bt.get(), k * sizeof(float))); };
+      bt->xa = f(n * d), bt->xb = f(n * d), bt->e0 = f(n * d), bt->e_proj = f(n * d), bt->nb = f(n * d);
+      bt->mix = f(n * md->mix_cols), bt->q = f(n * d), bt->kb = f(n * d), bt->y = f(n * d);
+      bt->mid = f(n * std::max<size_t>(md->hidden, 1)), bt->upbuf = f(n * 2 * std::max<size_t>(md->hidden, 1));
+      bt->dec = f(n * c.heads), bt->logits = f(n * c.vocab);
+      // Attention splits: about two CTAs per SM over heads × n rows, at least
+      // 128 positions per slice.
+      const long long ctas = (long long)c.heads * (long long)n;
+      long long want = (2 * bt->ctx->sms + ctas - 1) / ctas, most = ((long long)c.window + 127) / 128;
+      bt->nsplit = (int)std::max<long long>(1, std::min<long long>(std::min(want, most), 256));
+      AttnGeom g{(int)n, 0, 0, 1, (int)c.heads, 1, (int)c.dh(), 1.0f};
+      bt->part = f(attn_part_floats(g, bt->nsplit));
+      bt->ids = static_cast<uint32_t*>(balloc(bt.get(), n * sizeof(uint32_t)));
+      bt->out_index = static_cast<unsigned*>(balloc(bt.get(), 4 * sizeof(unsigned)));
+      bt->outs = static_cast<uint32_t*>(balloc(bt.get(), n * sizeof(uint32_t)));
+      bt->outs_cap = 1;
+      std::vector<long long*> pos(n);
+      for (size_t i = 0; i < n; i++) pos[i] = sessions[i]->pos_dev;
+      bt->posr = static_cast<long long**>(balloc(bt.get(), n * sizeof(long long*)));
+      SLM_CUDA(cudaMemcpyAsync(bt->posr, pos.data(), n * sizeof(long long*), cudaMemcpyHostToDevice, s));
+      // Layer instances in step order: prelude, each loop's core, coda.
+      std::vector<std::vector<const LState*>> inst;  // [instance][session]
+      auto add = [&](auto get) {
+        std::vector<const LState*> row(n);
+        for (size_t i = 0; i < n; i++) row[i] = get(sessions[i]);
+        inst.push_back(row);
+      };
+      for (size_t k = 0; k < md->prelude.size(); k++) add([&](slm_session* se) { return &se->pre[k]; });
+      for (size_t r = 0; r < sessions[0]->loops; r++)
+        for (size_t j = 0; j < md->core.size(); j++) add([&](slm_session* se) { return &se->core[r][j]; });
+      for (size_t k = 0; k < md->coda.size(); k++) add([&](slm_session* se) { return &se->coda[k]; });
+      std::vector<float*> host(3 * n);
+      for (auto& row : inst) {
+        for (size_t i = 0; i < n; i++) host[i] = row[i]->k, host[n + i] = row[i]->v, host[2 * n + i] = row[i]->s;
+        auto* t = static_cast<float**>(balloc(bt.get(), 3 * n * sizeof(float*)));
+        SLM_CUDA(cudaMemcpyAsync(t, host.data(), 3 * n * sizeof(float*), cudaMemcpyHostToDevice, s));
+        bt->tab.push_back(t);
+      }
+      SLM_CUDA(cudaStreamSynchronize(s));
+    } catch (...) {
+      cudaStreamSynchronize(s);
+      for (void* p : bt->owned) dev_free(p);
+      throw;
+    }
+    for (auto* se : bt->ses) se->in_batches++;
+    *out = bt.release();
+  });
+}
+
+int slm_batch_free(slm_batch* bt) {
+  return guard([&] {
+    if (!bt) return;
+    Device dev(bt->ctx);
+    cudaStreamSynchronize(bt->ctx->stream);
+    batch_drop_graph(bt);
+    for (void* p : bt->owned) dev_free(p);
+    for (auto* se : bt->ses) se->in_batches--;
+    delete bt;
+  });
+}
+
+int slm_batch_size(const slm_batch* bt, size_t* out) {
+  return guard([&] {
+    SLM_REQUIRE(bt && out, "bad arguments");
+    *out = bt->n;
+  });
+}
+
+int slm_batch_step(slm_batch* bt, const uint32_t* ids) {
+  return guard([&] {
+    SLM_REQUIRE(bt && ids, "bad arguments");
+    for (size_t i = 0; i < bt->n; i++) SLM_REQUIRE(ids[i] < bt->model->cfg.vocab, "token id out of range");
+    Device dev(bt->ctx);
+    cudaStream_t s = bt->ctx->stream;
+    SLM_CUDA(cudaMemcpyAsync(bt->ids, ids, bt->n * sizeof(uint32_t), cudaMemcpyHostToDevice, s));
+    SLM_CUDA(cudaMemsetAsync(bt->out_index, 0, sizeof(unsigned), s));
+    batch_step_device(bt);
+    check_device_error(bt->ctx);
+  });
+}
+
+int slm_batch_logits(slm_batch* bt, float* out) {
+  return guard([&] {
+    SLM_REQUIRE(bt && out, "bad arguments");
+    Device dev(bt->ctx);
+    cudaStream_t s = bt->ctx->stream;
+    SLM_CUDA(cudaMemcpyAsync(out, bt->logits, bt->n * bt->model->cfg.vocab * sizeof(float), cudaMemcpyDeviceToHost,
+                             s));
+    SLM_CUDA(cudaStreamSynchronize(s));
+  });
+}
+
+int slm_batch_decode(slm_batch* bt, const uint32_t* first, size_t steps, uint32_t* out) {
+  return guard([&] {
+    SLM_REQUIRE(bt && first && (out || steps == 0), "bad arguments");
+    for (size_t i = 0; i < bt->n; i++) SLM_REQUIRE(first[i] < bt->model->cfg.vocab, "token id out of range");
+    if (steps == 0) return;
+    Device dev(bt->ctx);
+    cudaStream_t s = bt->ctx->stream;
+    batch_outs(bt, steps);
+    SLM_CUDA(cudaMemcpyAsync(bt->ids, first, bt->n * sizeof(uint32_t), cudaMemcpyHostToDevice, s));
+    SLM_CUDA(cudaMemsetAsync(bt->out_index, 0, sizeof(unsigned), s));
+    for (size_t t = 0; t < steps; t++) batch_step_device(bt);
+    SLM_CUDA(cudaMemcpyAsync(out, bt->outs, steps * bt->n * sizeof(uint32_t), cudaMemcpyDeviceToHost, s));
+    check_device_error(bt->ctx);
   });
 }
 

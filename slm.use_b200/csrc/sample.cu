@@ -338,6 +338,48 @@ __global__ void __launch_bounds__(ST) k_sample(SampleArgs a) {
 
 }  // namespace
 
+namespace {
+
+// One CTA per row: the largest composite key (logit, then the smaller id);
+// -0.0 and +0.0 share a key, so the first of them wins, as under `>`.
+__global__ void __launch_bounds__(256)
+    k_argmax_rows(const float* __restrict__ logits, size_t V, uint32_t* next, uint32_t* outs,
+                  const unsigned* out_index, size_t m) {
+  __shared__ unsigned long long best_w[8];
+  const size_t row = blockIdx.x;
+  const float* l = logits + row * V;
+  unsigned long long best = 0;
+  for (size_t i = threadIdx.x; i < V; i += blockDim.x) {
+    const float v = l[i];
+    if (v != v) continue;
+    const unsigned long long c = composite(v + 0.0f, (uint32_t)i);
+    if (c > best) best = c;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    unsigned long long other = __shfl_xor_sync(0xffffffffu, best, o);
+    if (other > best) best = other;
+  }
+  if ((threadIdx.x & 31) == 0) best_w[threadIdx.x >> 5] = best;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int w = 1; w < 8; w++)
+      if (best_w[w] > best_w[0]) best_w[0] = best_w[w];
+    const uint32_t id = best_w[0] ? comp_id(best_w[0]) : 0u;
+    next[row] = id;
+    if (outs) outs[(size_t)(*out_index) * m + row] = id;
+  }
+}
+
+}  // namespace
+
+void argmax_rows(const float* logits, size_t vocab, size_t m, uint32_t* next, uint32_t* outs,
+                 const unsigned* out_index, cudaStream_t st) {
+  if (!m) return;
+  k_argmax_rows<<<(unsigned)m, 256, 0, st>>>(logits, vocab, next, outs, out_index, m);
+  SLM_LAUNCHED("k_argmax_rows");
+}
+
 void sample(const SampleArgs& a, cudaStream_t st) {
   k_sample<<<1, ST, 0, st>>>(a);
   SLM_LAUNCHED("k_sample");
