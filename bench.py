@@ -17,7 +17,9 @@ Printed on one JSON line (rank 0):
             host id + `slm_sample` returning a host id), host clock;
   prefill   tok/s of the 4096-token prompt (feed + logits read back);
   extra     R = 8 and R = 16 decode with the sampling of configs[2]; C4,
-            the G-layer variant (S | LS | SG) after a 16384-id prompt;
+            the G-layer variant (S | LS | SG) after a 16384-id prompt; C5,
+            64 sequences (2048-id prompts) split over the ranks and decoded
+            as one batch per GPU (aggregate tok/s, max over ranks);
   roofline  the decode step's kernel (one persistent kernel per token) against
             measured HBM bandwidth, and the m = 1 GEMV op on its own;
   cpu_baseline  the CPU oracle (a C++ restatement of the reference's CPU
@@ -433,6 +435,40 @@ def run_b200(args, rank: int, world: int, local: int) -> dict | None:
                        "sampling": "greedy"}
         s3.close()
         gmodel.close()
+
+    if not args.quick:
+        # configs[4] ("C5"): 64 independent sequences (2048-id prompts, seeds
+        # 0..63) partitioned over the ranks, each rank's share decoded as one
+        # batch (weights read once per step), 256 greedy steps; the total is
+        # fixed, so this part scales strongly.
+        mine = [q for q in range(64) if q % world == rank]
+        sessions = []
+        firsts = []
+        for q in mine:
+            sq = model.session(args.loops)
+            sq.feed(prompt_for(q, V, 2048), 256)
+            firsts.append(int(np.argmax(sq.logits())))
+            sessions.append(sq)
+        bt = slm.Batch(sessions)
+        warm = bt.decode(firsts, 4)
+        nxt = warm[-1]
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+        a, b = events()
+        a.record(stream)
+        bt.decode(nxt, 256)
+        b.record(stream)
+        torch.cuda.synchronize(dev)
+        c5_ms = a.elapsed_time(b)
+        c5_ms = max_over_ranks([c5_ms], dist, dev)[0]
+        extra["C5"] = {"value": 64 * 256 / (c5_ms / 1000.0), "unit": "tok/s (all ranks)", "sequences": 64,
+                       "per_rank": len(mine), "prompt": 2048, "decode_steps": 256, "loops": args.loops,
+                       "scaling": "strong", "ms_per_step": c5_ms / 256, "sampling": "greedy",
+                       "path": "slm_batch_decode (one graph-replayed step for the rank's sequences)"}
+        bt.close()
+        for sq in sessions:
+            sq.close()
 
     step_kernels = se.step_kernels
     res = {"dec_ms": dec_ms, "e2e_s": e2e_s, "prefill_ms": prefill_ms, "prefill_host_s": prefill_host_s,
