@@ -86,38 +86,60 @@ __global__ void __launch_bounds__(128)
 #pragma unroll
   for (int e = 0; e < 8; e++) acc[e] = 0.0f;
 
+  // U cache rows per lane group per round: all their loads are issued before
+  // any is used, and the running max / rescale is applied once per round.
+  constexpr int U = 4;
   const long long slot0 = start < end ? start % g.cap : 0;
-  for (long long base = start + warp * PPW; base < end; base += (long long)WARPS * PPW) {
-    long long pp = base + grp;
-    bool ok = pp < end;
-    float sc = 0.0f;
-    float4 v0 = make_float4(0.f, 0.f, 0.f, 0.f), v1 = v0;
-    if (ok) {
-      long long sl = slot0 + (pp - start);
-      if (sl >= g.cap) sl -= g.cap;
-      if (sl >= g.cap) sl %= g.cap;
-      size_t slot = (size_t)sl;
-      const float4* kr = reinterpret_cast<const float4*>(Kb + slot * DH);
-      const float4* vr = reinterpret_cast<const float4*>(Vb + slot * DH);
-      float4 k0 = ld_stream(kr), k1 = ld_stream(kr + 1);
-      v0 = ld_stream(vr);
-      v1 = ld_stream(vr + 1);
-      sc = qv[0] * k0.x + qv[1] * k0.y + qv[2] * k0.z + qv[3] * k0.w + qv[4] * k1.x + qv[5] * k1.y +
-           qv[6] * k1.z + qv[7] * k1.w;
-    }
+  for (long long base = start + warp * PPW * U; base < end; base += (long long)WARPS * PPW * U) {
+    float4 k0[U], k1[U], v0[U], v1[U];
+    bool okk[U];
 #pragma unroll
-    for (int o = 1; o < G; o <<= 1) sc += __shfl_xor_sync(0xffffffffu, sc, o);
-    if (ok) {
-      sc *= g.scale;
-      float M = fmaxf(mx, sc);
-      float corr = mx == -INFINITY ? 0.0f : expf(mx - M);
-      float pe = expf(sc - M);
-      l = l * corr + pe;
-      float vv[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
-#pragma unroll
-      for (int e = 0; e < 8; e++) acc[e] = acc[e] * corr + pe * vv[e];
-      mx = M;
+    for (int u = 0; u < U; u++) {
+      const long long pp = base + u * PPW + grp;
+      okk[u] = pp < end;
+      k0[u] = k1[u] = v0[u] = v1[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (okk[u]) {
+        long long sl = slot0 + (pp - start);
+        if (sl >= g.cap) sl -= g.cap;
+        if (sl >= g.cap) sl %= g.cap;
+        const size_t slot = (size_t)sl;
+        const float4* kr = reinterpret_cast<const float4*>(Kb + slot * DH);
+        const float4* vr = reinterpret_cast<const float4*>(Vb + slot * DH);
+        k0[u] = ld_stream(kr);
+        k1[u] = ld_stream(kr + 1);
+        v0[u] = ld_stream(vr);
+        v1[u] = ld_stream(vr + 1);
+      }
     }
+    float sc[U];
+#pragma unroll
+    for (int u = 0; u < U; u++)
+      sc[u] = qv[0] * k0[u].x + qv[1] * k0[u].y + qv[2] * k0[u].z + qv[3] * k0[u].w + qv[4] * k1[u].x +
+              qv[5] * k1[u].y + qv[6] * k1[u].z + qv[7] * k1[u].w;
+#pragma unroll
+    for (int o = 1; o < G; o <<= 1)
+#pragma unroll
+      for (int u = 0; u < U; u++) sc[u] += __shfl_xor_sync(0xffffffffu, sc[u], o);
+    float M = mx;
+#pragma unroll
+    for (int u = 0; u < U; u++) {
+      sc[u] *= g.scale;
+      if (okk[u]) M = fmaxf(M, sc[u]);
+    }
+    if (M == -INFINITY) continue;  // nothing visible in this round for this group
+    const float corr = mx == -INFINITY ? 0.0f : expf(mx - M);
+    l *= corr;
+#pragma unroll
+    for (int e = 0; e < 8; e++) acc[e] *= corr;
+#pragma unroll
+    for (int u = 0; u < U; u++) {
+      if (!okk[u]) continue;
+      const float pe = expf(sc[u] - M);
+      l += pe;
+      acc[0] += pe * v0[u].x, acc[1] += pe * v0[u].y, acc[2] += pe * v0[u].z, acc[3] += pe * v0[u].w;
+      acc[4] += pe * v1[u].x, acc[5] += pe * v1[u].y, acc[6] += pe * v1[u].z, acc[7] += pe * v1[u].w;
+    }
+    mx = M;
   }
   // Merge the lane groups of the warp (they hold the same `sub` slices).
 #pragma unroll

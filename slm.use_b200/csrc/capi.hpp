@@ -19,6 +19,7 @@ struct slm_ctx {
   size_t stage_bytes = 0;
   void* gemm_ws = nullptr;      // tensor-core GEMM workspace (grown on demand, outside captures)
   size_t gemm_ws_bytes = 0;
+  unsigned long long gemm_ws_gen = 0;  // bumped whenever gemm_ws moves (graphs holding it must be re-captured)
 };
 
 struct slm_buf {

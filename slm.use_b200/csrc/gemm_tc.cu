@@ -45,7 +45,10 @@ using OpClass = cutlass::arch::OpClassTensorOp;
 #ifndef SLM_TC_TILE_K
 #define SLM_TC_TILE_K 32
 #endif
-using TileShape = Shape<_128, Int<SLM_TC_TILE_N>, Int<SLM_TC_TILE_K>>;
+#ifndef SLM_TC_TILE_M
+#define SLM_TC_TILE_M 128
+#endif
+using TileShape = Shape<Int<SLM_TC_TILE_M>, Int<SLM_TC_TILE_N>, Int<SLM_TC_TILE_K>>;
 using ClusterShape = Shape<_1, _1, _1>;
 
 using CollectiveEpilogue = typename cutlass::epilogue::collective::CollectiveBuilder<

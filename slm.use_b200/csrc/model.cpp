@@ -125,6 +125,7 @@ struct slm_batch {
   size_t outs_cap = 0;
   int nsplit = 1;
   cudaGraphExec_t graph = nullptr;
+  unsigned long long graph_ws_gen = 0;  // the context's GEMM workspace generation the graph holds
   bool capturing = false;
 };
 
@@ -746,10 +747,41 @@ void batch_drop_graph(slm_batch* bt) {
   }
 }
 
-// One step, replayed from a CUDA graph captured on first use.
+// Grows the context's GEMM workspace for every linear of a batch step, so
+// the capture (which cannot allocate) gets the tensor-core path.
+void batch_workspace(slm_batch* bt) {
+  slm_model* md = bt->model;
+  const Config& c = md->cfg;
+  const int m = (int)bt->n, d = (int)c.d;
+  auto one = [&](const Mat& w, int ldx, int ldy, int epi, size_t rows = 0) {
+    LinearArgs a;
+    a.w = w.w, a.rows = (int)(rows ? rows : w.rows), a.cols = (int)w.cols, a.m = m;
+    a.x = bt->nb, a.ldx = ldx, a.y = bt->upbuf, a.ldy = ldy, a.epi = epi;
+    a.res = epi == EPI_ADD ? bt->upbuf : nullptr, a.ldres = epi == EPI_ADD ? ldy : 0;
+    gemm_workspace(bt->ctx, a, false);
+  };
+  auto block = [&](const Block& b) {
+    if (b.kind == 'S') one(b.qkv, d, 3 * d, EPI_STORE);
+    if (b.kind == 'L') one(b.qkvg, d, 4 * d, EPI_STORE), one(b.decay, d, (int)c.heads, EPI_STORE);
+    one(b.o, d, d, EPI_ADD);
+    one(b.up, d, (int)(2 * b.down.cols), EPI_STORE);
+    one(b.down, (int)b.down.cols, d, EPI_ADD);
+  };
+  for (auto& b : md->prelude) block(b);
+  for (auto& b : md->core) block(b);
+  for (auto& b : md->coda) block(b);
+  if (md->looped) one(md->inject, d, d, EPI_STORE);
+  one(md->embed, d, (int)c.vocab, EPI_STORE);
+}
+
+// One step, replayed from a CUDA graph captured on first use (and again
+// after the context's GEMM workspace has moved).
 void batch_step_device(slm_batch* bt) {
   cudaStream_t s = bt->ctx->stream;
+  if (bt->graph && bt->graph_ws_gen != bt->ctx->gemm_ws_gen) batch_drop_graph(bt);
   if (!bt->graph) {
+    batch_workspace(bt);
+    bt->graph_ws_gen = bt->ctx->gemm_ws_gen;
     cudaGraph_t g = nullptr;
     SLM_CUDA(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
     bt->capturing = true;
@@ -1279,10 +1311,11 @@ int slm_batch_new(slm_session* const* sessions, size_t n, slm_batch** out) {
       bt->mix = f(n * md->mix_cols), bt->q = f(n * d), bt->kb = f(n * d), bt->y = f(n * d);
       bt->mid = f(n * std::max<size_t>(md->hidden, 1)), bt->upbuf = f(n * 2 * std::max<size_t>(md->hidden, 1));
       bt->dec = f(n * c.heads), bt->logits = f(n * c.vocab);
-      // Attention splits: about two CTAs per SM over heads × n rows, at least
+      // Attention splits: about 16 resident 128-thread CTAs per SM over
+      // heads × n rows (enough loads in flight to stream the rings), at least
       // 128 positions per slice.
       const long long ctas = (long long)c.heads * (long long)n;
-      long long want = (2 * bt->ctx->sms + ctas - 1) / ctas, most = ((long long)c.window + 127) / 128;
+      long long want = (16 * bt->ctx->sms + ctas - 1) / ctas, most = ((long long)c.window + 127) / 128;
       bt->nsplit = (int)std::max<long long>(1, std::min<long long>(std::min(want, most), 256));
       AttnGeom g{(int)n, 0, 0, 1, (int)c.heads, 1, (int)c.dh(), 1.0f};
       bt->part = f(attn_part_floats(g, bt->nsplit));

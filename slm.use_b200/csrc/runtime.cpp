@@ -85,6 +85,7 @@ void gemm_workspace(slm_ctx* c, LinearArgs& a, bool capturing) {
       c->gemm_ws_bytes = 0;
       c->gemm_ws = dev_alloc(need);
       c->gemm_ws_bytes = need;
+      c->gemm_ws_gen++;
     }
   }
   a.ws = c->gemm_ws;

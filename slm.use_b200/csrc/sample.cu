@@ -342,18 +342,30 @@ namespace {
 
 // One CTA per row: the largest composite key (logit, then the smaller id);
 // -0.0 and +0.0 share a key, so the first of them wins, as under `>`.
-__global__ void __launch_bounds__(256)
+__device__ __forceinline__ void argmax_take(unsigned long long& best, float v, uint32_t i) {
+  if (v != v) return;  // NaN never wins a `>` comparison
+  const unsigned long long c = composite(v + 0.0f, i);
+  if (c > best) best = c;
+}
+
+__global__ void __launch_bounds__(1024)
     k_argmax_rows(const float* __restrict__ logits, size_t V, uint32_t* next, uint32_t* outs,
                   const unsigned* out_index, size_t m) {
-  __shared__ unsigned long long best_w[8];
+  __shared__ unsigned long long best_w[32];
   const size_t row = blockIdx.x;
   const float* l = logits + row * V;
   unsigned long long best = 0;
-  for (size_t i = threadIdx.x; i < V; i += blockDim.x) {
-    const float v = l[i];
-    if (v != v) continue;
-    const unsigned long long c = composite(v + 0.0f, (uint32_t)i);
-    if (c > best) best = c;
+  if (V % 4 == 0 && ((uintptr_t)l & 15) == 0) {
+    const float4* l4 = reinterpret_cast<const float4*>(l);
+    for (size_t i = threadIdx.x; i < V / 4; i += blockDim.x) {
+      const float4 v = l4[i];
+      argmax_take(best, v.x, (uint32_t)(4 * i));
+      argmax_take(best, v.y, (uint32_t)(4 * i + 1));
+      argmax_take(best, v.z, (uint32_t)(4 * i + 2));
+      argmax_take(best, v.w, (uint32_t)(4 * i + 3));
+    }
+  } else {
+    for (size_t i = threadIdx.x; i < V; i += blockDim.x) argmax_take(best, l[i], (uint32_t)i);
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
@@ -363,7 +375,7 @@ __global__ void __launch_bounds__(256)
   if ((threadIdx.x & 31) == 0) best_w[threadIdx.x >> 5] = best;
   __syncthreads();
   if (threadIdx.x == 0) {
-    for (int w = 1; w < 8; w++)
+    for (int w = 1; w < (int)(blockDim.x >> 5); w++)
       if (best_w[w] > best_w[0]) best_w[0] = best_w[w];
     const uint32_t id = best_w[0] ? comp_id(best_w[0]) : 0u;
     next[row] = id;
@@ -376,7 +388,7 @@ __global__ void __launch_bounds__(256)
 void argmax_rows(const float* logits, size_t vocab, size_t m, uint32_t* next, uint32_t* outs,
                  const unsigned* out_index, cudaStream_t st) {
   if (!m) return;
-  k_argmax_rows<<<(unsigned)m, 256, 0, st>>>(logits, vocab, next, outs, out_index, m);
+  k_argmax_rows<<<(unsigned)m, 1024, 0, st>>>(logits, vocab, next, outs, out_index, m);
   SLM_LAUNCHED("k_argmax_rows");
 }
 
