@@ -23,6 +23,12 @@ struct LinearArgs {
   size_t ws_bytes = 0;
 };
 void linear(const LinearArgs& a, cudaStream_t st);
+// SIMT path for 8 < m ≤ 64 tokens (skinny.cu): STORE/ADD epilogues, cols % 32
+// == 0; needs skinny_workspace(a) bytes of a.ws (0 when K is not split).
+void skinny_prepare();
+bool skinny_ok(const LinearArgs& a);
+size_t skinny_workspace(const LinearArgs& a);
+void skinny_linear(const LinearArgs& a, void* ws, cudaStream_t st);
 // Tensor-core (sm100 FastFP32) path for m > 8, gemm_tc.cu.
 bool tc_linear_ok(const LinearArgs& a);
 size_t tc_linear_workspace(const LinearArgs& a);

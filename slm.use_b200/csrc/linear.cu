@@ -244,6 +244,7 @@ void linear_prepare() {
   prepare_m<2>();
   prepare_m<4>();
   prepare_m<8>();
+  skinny_prepare();
 }
 
 void linear(const LinearArgs& a, cudaStream_t st) {
@@ -258,7 +259,11 @@ void linear(const LinearArgs& a, cudaStream_t st) {
     return;
   }
   if (a.epi == EPI_SILU) SLM_REQUIRE(a.rows % 2 == 0, "linear: silu pairing needs an even row count");
-  if (a.m > 8 && tc_linear_ok(a)) {
+  if (skinny_ok(a) && skinny_workspace(a) <= a.ws_bytes) {
+    skinny_linear(a, a.ws, st);
+    return;
+  }
+  if (a.m > 64 && tc_linear_ok(a)) {
     const size_t need = tc_linear_workspace(a);
     if (need <= a.ws_bytes) {
       tc_linear(a, a.ws, st);

@@ -26,7 +26,8 @@ def close(got, want, atol=2e-5, rtol=1e-4):
 
 @pytest.mark.parametrize("rows,cols,m", [(96, 32, 1), (2304, 768, 1), (768, 3072, 3), (6144, 768, 8),
                                          (2304, 768, 17), (768, 768, 256), (5, 7, 3), (32000, 768, 1),
-                                         (12, 768, 1), (130, 36, 70)])
+                                         (12, 768, 1), (130, 36, 70), (768, 3072, 64), (32000, 768, 40),
+                                         (100, 64, 33), (2048, 768, 9)])
 def test_linear(ops, oracle, rows, cols, m):
     w, x = rand(rows, cols, scale=0.02), rand(m, cols)
     y = ops.zeros(1)
