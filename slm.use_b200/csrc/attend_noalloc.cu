@@ -63,6 +63,9 @@ extern "C" int slm_op_attend_noalloc(slm_ctx* c, float* y, const float* q, const
     SLM_REQUIRE(at->key_heads > 0 && at->heads % at->key_heads == 0 && at->cap > 0 && at->reach > 0,
                 "attend_noalloc: bad geometry");
     SLM_REQUIRE(at->m < (1u << 31) && at->heads < (1u << 31), "attend_noalloc: shape too large");
+    // The kernels read q, k and v in 16-byte vectors.
+    SLM_REQUIRE((((uintptr_t)q | (uintptr_t)k | (uintptr_t)v) & 15) == 0,
+                "attend_noalloc: q, k and v must be 16-byte aligned");
     if (!at->m) return;
     AttnGeom g;
     g.m = (int)at->m;

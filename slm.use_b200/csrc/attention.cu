@@ -303,6 +303,176 @@ __global__ void __launch_bounds__(128)
   }
 }
 
+// ---------------------------------------------------------------------------
+// Slice pass for query tiles, head size 64 (prefill chunks).  grid (nsplit,
+// ceil(m/64), heads), 256 threads.  64 queries × 64-key tiles, register-tiled:
+// thread (ty, tx) = (t/16, t%16) scores queries 4ty..4ty+3 against keys tx,
+// tx+16, tx+32, tx+48 (so a warp's K reads hit distinct banks) and accumulates
+// outputs of queries 4ty.. × dims 4tx..4tx+3; rows are padded to 68 floats.
+// K/V tiles are gathered from the ring with cp.async, double-buffered; the
+// probabilities of a tile pass through shared memory for P·V.
+// ---------------------------------------------------------------------------
+
+constexpr int FQ = 64, FKT = 64, FLD = 68;
+constexpr size_t kFlashSmem = (size_t)(FQ + 4 * FKT + FQ) * FLD * sizeof(float);
+
+__device__ __forceinline__ void cp16z(void* dst, const void* src, bool ok) {
+  unsigned d = (unsigned)__cvta_generic_to_shared(dst);
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(d), "l"(src), "r"(ok ? 16 : 0) : "memory");
+}
+
+__global__ void __launch_bounds__(256, 2)
+    k_attn_flash(const float* __restrict__ q, int ldq, const float* __restrict__ K, const float* __restrict__ V,
+                 AttnGeom g, const long long* __restrict__ pos_ptr, int nsplit, float* __restrict__ part) {
+  constexpr int DH = 64;
+  extern __shared__ __align__(16) float fsm[];
+  float(*Qs)[FLD] = reinterpret_cast<float(*)[FLD]>(fsm);
+  float(*Ks)[FKT][FLD] = reinterpret_cast<float(*)[FKT][FLD]>(fsm + FQ * FLD);
+  float(*Vs)[FKT][FLD] = reinterpret_cast<float(*)[FKT][FLD]>(fsm + (FQ + 2 * FKT) * FLD);
+  float(*Ps)[FLD] = reinterpret_cast<float(*)[FLD]>(fsm + (FQ + 4 * FKT) * FLD);
+  const int s = blockIdx.x, i0 = blockIdx.y * FQ, h = blockIdx.z;
+  const int t = threadIdx.x, ty = t >> 4, tx = t & 15;
+  const long long pos = pos_ptr[0];
+  const int kvh = h / (g.heads / g.key_heads);
+  const float* Kb = K + (size_t)kvh * g.cap * DH;
+  const float* Vb = V + (size_t)kvh * g.cap * DH;
+
+  const int ilast = min(i0 + FQ, g.m) - 1;
+  const Range r0 = visible(pos + i0, g.reach, g.gap), r1 = visible(pos + ilast, g.reach, g.gap);
+  const long long ulo = r0.lo, uhi = max(r1.hi, r0.hi);
+  const long long count = uhi - ulo, chunk = (count + nsplit - 1) / nsplit;
+  const long long start = ulo + (long long)s * chunk, end = min(uhi, start + chunk);
+
+  long long qlo[4], qhi[4];
+#pragma unroll
+  for (int j = 0; j < 4; j++) {
+    const int i = i0 + 4 * ty + j;
+    const Range rr = visible(pos + i, g.reach, g.gap);
+    qlo[j] = i < g.m ? rr.lo : 0;
+    qhi[j] = i < g.m ? rr.hi : 0;
+  }
+  for (int e = t; e < FQ * (DH / 4); e += 256) {
+    const int row = e / (DH / 4), c = (e % (DH / 4)) * 4;
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (i0 + row < g.m) v = *reinterpret_cast<const float4*>(q + (size_t)(i0 + row) * ldq + (size_t)h * DH + c);
+    *reinterpret_cast<float4*>(&Qs[row][c]) = v;
+  }
+
+  auto load = [&](int tile, int buf) {
+    const long long base = start + (long long)tile * FKT;
+    for (int e = t; e < FKT * (DH / 4); e += 256) {
+      const int row = e / (DH / 4), c = (e % (DH / 4)) * 4;
+      const long long pp = base + row;
+      const bool ok = pp < end;
+      const size_t slot = ok ? (size_t)(pp % g.cap) : 0;
+      cp16z(&Ks[buf][row][c], Kb + slot * DH + c, ok);
+      cp16z(&Vs[buf][row][c], Vb + slot * DH + c, ok);
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  };
+
+  float o[4][4], mx[4], l[4];
+#pragma unroll
+  for (int j = 0; j < 4; j++) {
+    mx[j] = -INFINITY;
+    l[j] = 0.0f;
+#pragma unroll
+    for (int e = 0; e < 4; e++) o[j][e] = 0.0f;
+  }
+  const int ntiles = start < end ? (int)((end - start + FKT - 1) / FKT) : 0;
+  if (ntiles > 0) load(0, 0);
+  for (int tile = 0; tile < ntiles; tile++) {
+    const int buf = tile & 1;
+    if (tile + 1 < ntiles) {
+      load(tile + 1, buf ^ 1);
+      asm volatile("cp.async.wait_group 1;" ::: "memory");
+    } else {
+      asm volatile("cp.async.wait_group 0;" ::: "memory");
+    }
+    __syncthreads();
+    float sc[4][4];
+#pragma unroll
+    for (int j = 0; j < 4; j++)
+#pragma unroll
+      for (int k = 0; k < 4; k++) sc[j][k] = 0.0f;
+#pragma unroll 4
+    for (int d = 0; d < DH; d += 4) {
+      float4 qv[4], kv[4];
+#pragma unroll
+      for (int j = 0; j < 4; j++) qv[j] = *reinterpret_cast<const float4*>(&Qs[4 * ty + j][d]);
+#pragma unroll
+      for (int k = 0; k < 4; k++) kv[k] = *reinterpret_cast<const float4*>(&Ks[buf][tx + 16 * k][d]);
+#pragma unroll
+      for (int j = 0; j < 4; j++)
+#pragma unroll
+        for (int k = 0; k < 4; k++) sc[j][k] = dot4(qv[j], kv[k], sc[j][k]);
+    }
+    const long long base = start + (long long)tile * FKT;
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      float tmax = -INFINITY;
+#pragma unroll
+      for (int k = 0; k < 4; k++) {
+        const long long kp = base + tx + 16 * k;
+        const bool vis = kp < end && kp >= qlo[j] && kp < qhi[j];
+        sc[j][k] = vis ? sc[j][k] * g.scale : -INFINITY;
+        tmax = fmaxf(tmax, sc[j][k]);
+      }
+#pragma unroll
+      for (int o2 = 1; o2 < 16; o2 <<= 1) tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, o2));
+      const float M = fmaxf(mx[j], tmax);
+      float rs = 0.0f;
+#pragma unroll
+      for (int k = 0; k < 4; k++) {
+        const float p = sc[j][k] == -INFINITY ? 0.0f : expf(sc[j][k] - M);
+        Ps[4 * ty + j][tx + 16 * k] = p;
+        rs += p;
+      }
+#pragma unroll
+      for (int o2 = 1; o2 < 16; o2 <<= 1) rs += __shfl_xor_sync(0xffffffffu, rs, o2);
+      const float corr = mx[j] == -INFINITY ? 0.0f : expf(mx[j] - M);
+      l[j] = l[j] * corr + rs;
+#pragma unroll
+      for (int e = 0; e < 4; e++) o[j][e] *= corr;
+      mx[j] = M;
+    }
+    __syncthreads();
+#pragma unroll 4
+    for (int k = 0; k < FKT; k += 4) {
+      float4 pv[4], vv[4];
+#pragma unroll
+      for (int j = 0; j < 4; j++) pv[j] = *reinterpret_cast<const float4*>(&Ps[4 * ty + j][k]);
+#pragma unroll
+      for (int kk = 0; kk < 4; kk++) vv[kk] = *reinterpret_cast<const float4*>(&Vs[buf][k + kk][4 * tx]);
+#pragma unroll
+      for (int j = 0; j < 4; j++) {
+        const float p4[4] = {pv[j].x, pv[j].y, pv[j].z, pv[j].w};
+#pragma unroll
+        for (int kk = 0; kk < 4; kk++) {
+          o[j][0] = fmaf(p4[kk], vv[kk].x, o[j][0]);
+          o[j][1] = fmaf(p4[kk], vv[kk].y, o[j][1]);
+          o[j][2] = fmaf(p4[kk], vv[kk].z, o[j][2]);
+          o[j][3] = fmaf(p4[kk], vv[kk].w, o[j][3]);
+        }
+      }
+    }
+    __syncthreads();  // Ps and this K/V buffer are rewritten next
+  }
+#pragma unroll
+  for (int j = 0; j < 4; j++) {
+    const int i = i0 + 4 * ty + j;
+    if (i >= g.m) continue;
+    float* out = part + (((size_t)s * g.m + i) * g.heads + h) * (DH + 2);
+    // Rows of dh + 2 floats are only 8-byte aligned: scalar stores.
+#pragma unroll
+    for (int e = 0; e < 4; e++) out[4 * tx + e] = o[j][e];
+    if (tx == 0) {
+      out[DH] = mx[j];
+      out[DH + 1] = l[j];
+    }
+  }
+}
+
 // Merge the slices: y[i][h] = Σ_s e^{m_s - M} acc_s / Σ_s e^{m_s - M} l_s.
 // grid m·heads, block 32·ceil(dh/32).
 __global__ void k_attn_combine(const float* __restrict__ part, int nsplit, int m, int heads, int dh,
@@ -329,7 +499,16 @@ __global__ void k_attn_combine(const float* __restrict__ part, int nsplit, int m
 template <int DH>
 void launch_tile(const float* q, int ldq, const float* K, const float* V, const AttnGeom& g, const long long* pos_ptr,
                  int nsplit, float* part, cudaStream_t st) {
-  if constexpr (DH <= 128) {
+  if constexpr (DH == 64) {
+    static bool attr = [] {
+      SLM_CUDA(cudaFuncSetAttribute(k_attn_flash, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kFlashSmem));
+      return true;
+    }();
+    (void)attr;
+    k_attn_flash<<<dim3(nsplit, cdiv(g.m, FQ), g.heads), 256, kFlashSmem, st>>>(q, ldq, K, V, g, pos_ptr, nsplit,
+                                                                                part);
+    SLM_LAUNCHED("k_attn_flash");
+  } else if constexpr (DH <= 128) {
     k_attn_tile<DH><<<dim3(nsplit, cdiv(g.m, 16), g.heads), 128, 0, st>>>(q, ldq, K, V, g, pos_ptr, nsplit, part);
     SLM_LAUNCHED("k_attn_tile");
   }
@@ -351,7 +530,9 @@ void launch_dh(const float* q, int ldq, const float* K, const float* V, const At
 
 int attn_splits(const AttnGeom& g, long long max_span) {
   if (max_span < 1) max_span = 1;
-  long long ctas = (g.m <= 8 || g.dh > 128) ? (long long)g.heads * g.m : (long long)g.heads * ((g.m + 15) / 16);
+  long long ctas = (g.m <= 8 || g.dh > 128) ? (long long)g.heads * g.m
+                  : g.dh == 64               ? (long long)g.heads * ((g.m + FQ - 1) / FQ)
+                                             : (long long)g.heads * ((g.m + 15) / 16);
   long long want = (2 * 148 + ctas - 1) / ctas;             // two CTAs per SM
   long long most = (max_span + 127) / 128;                 // at least 128 positions per slice
   long long n = want < most ? want : most;

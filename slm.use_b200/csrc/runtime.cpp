@@ -474,9 +474,18 @@ int slm_op_attend(slm_ctx* c, slm_buf* y, slm_buf* scores, const slm_buf* q, siz
     long long span = (long long)(at->pos + at->m) - g.gap - base;
     int nsplit = attn_splits(g, span < 1 ? 1 : span);
     long long pos = (long long)at->pos;
-    ensure(scores, attn_part_floats(g, nsplit) + 2);
+    // Scratch: the position (8 bytes), the partials, and room for q when the
+    // view is not 16-byte aligned (the kernels read q in 16-byte vectors).
+    const size_t parts = attn_part_floats(g, nsplit), nq = at->m * at->heads * at->dh;
+    const bool copy_q = ((uintptr_t)qs & 15) != 0;
+    const size_t qat = (2 + parts + 3) / 4 * 4;  // 16-byte aligned float offset
+    ensure(scores, copy_q ? qat + nq : parts + 2);
     auto* pd = reinterpret_cast<long long*>(scores->ptr);  // first 8 bytes hold the position
     SLM_CUDA(cudaMemcpyAsync(pd, &pos, sizeof(pos), cudaMemcpyHostToDevice, c->stream));
+    if (copy_q) {
+      SLM_CUDA(cudaMemcpyAsync(scores->ptr + qat, qs, nq * sizeof(float), cudaMemcpyDeviceToDevice, c->stream));
+      qs = scores->ptr + qat;
+    }
     attention(qs, (int)(at->heads * at->dh), k->ptr, v->ptr, g, pd, nsplit, scores->ptr + 2, y->ptr,
               (int)(at->heads * at->dh), c->stream);
   });

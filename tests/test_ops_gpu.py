@@ -122,6 +122,10 @@ ATTN_CASES = [
     (20, 40, None, 8, 64, 8, 4, 16),       # some queries see nothing
     (9000, 1, None, 4096, 16384, 12, 4, 64),
     (50, 3, 40, 0, 300, 2, 1, 256),        # the largest head size
+    (4200, 256, 4096, 0, 4352, 12, 12, 64),  # 64-query tiles over a wrapped ring
+    (9000, 256, None, 4096, 16384, 12, 4, 64),  # global, far gap, GQA
+    (3, 100, None, 8, 300, 4, 2, 64),      # the first queries see nothing; ragged last tile
+    (500, 70, 48, 0, 304, 3, 3, 64),       # short window inside one tile
 ]
 
 
@@ -134,6 +138,18 @@ def test_attend(ops, oracle, pos, m, reach, gap, cap, heads, kh, dh):
     ops.attend(y, scores, ops.upload(q), ops.upload(k), ops.upload(v), pos=pos, m=m, reach=reach, gap=gap, cap=cap,
                heads=heads, key_heads=kh, dh=dh, scale=scale)
     want = oracle.attend(q, k, v, pos, m, reach, gap, cap, heads, kh, dh, scale)
+    close(y.read(m * heads * dh), want, atol=2e-5)
+
+
+def test_attend_reads_q_at_an_odd_offset(ops, oracle):
+    # q at a view offset that is not a multiple of 4 floats: staged, not faulted.
+    pos, m, reach, gap, cap, heads, kh, dh = 300, 20, 64, 0, 320, 4, 4, 64
+    q = rand(m * heads * dh + 3)
+    k, v = rand(kh * cap * dh), rand(kh * cap * dh)
+    y, scores = ops.zeros(1), ops.zeros(1)
+    ops.attend(y, scores, (ops.upload(q), 3), ops.upload(k), ops.upload(v), pos=pos, m=m, reach=reach, gap=gap,
+               cap=cap, heads=heads, key_heads=kh, dh=dh, scale=0.125)
+    want = oracle.attend(q[3:], k, v, pos, m, reach, gap, cap, heads, kh, dh, 0.125)
     close(y.read(m * heads * dh), want, atol=2e-5)
 
 
