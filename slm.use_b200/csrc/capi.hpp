@@ -15,6 +15,7 @@ struct slm_ctx {
   std::string name;
   cudaStream_t stream = nullptr;
   int* err = nullptr;           // device error word (bad ids, sampler limits)
+  int* err_host = nullptr;      // pinned copy of it (read after a synchronisation)
   void* stage = nullptr;        // staging buffer for host arrays (ids, factors)
   size_t stage_bytes = 0;
   void* gemm_ws = nullptr;      // tensor-core GEMM workspace (grown on demand, outside captures)

@@ -739,6 +739,7 @@ struct Cons {
       consumers_sync();
       if (tid == 0) {
         uint32_t id = sm.best ? 0xFFFFFFFFu - (uint32_t)(sm.best & 0xFFFFFFFFu) : 0;
+        *P.argmax = id;
         if (P.greedy) {
           P.next_id[0] = id;
           unsigned at = *P.out_index;

@@ -94,6 +94,7 @@ struct Plan {
   uint32_t* next_id;
   uint32_t* out_ids;    // out_ids[*out_index] = id, then ++*out_index
   unsigned* out_index;
+  uint32_t* argmax;     // every step: the arg-max of its logits (first maximum; NaN never wins)
   uint32_t* hist;       // optional history array (same index as out + hist_base)
   unsigned long long hist_base;
   unsigned* bar;        // grid barrier: [0] arrivals (monotonic in a step), [1] CTAs done

@@ -103,6 +103,15 @@ struct slm_session {
   unsigned long long* trace = nullptr;  // per-phase timeline of the last step (SLM_OPT_TRACE)
   unsigned* attn_count = nullptr;        // per-head arrival counters of the attention phases
   int in_batches = 0;                    // batches holding this session
+  uint32_t* argmax_dev = nullptr;        // the persistent step's arg-max of its logits
+  bool argmax_valid = false;             // the logits come from a persistent step
+  // Pinned host words for the per-token transfers (ids in and out, RNG state).
+  struct HostIO {
+    uint32_t id_in, id_out;
+    unsigned long long rng_in, rng_out;
+  }* io = nullptr;
+  cudaEvent_t io_event = nullptr;  // after the last copy that reads io
+  bool io_busy = false;
 };
 
 // Several sessions of one model stepped together (one token each per step):
@@ -373,6 +382,7 @@ void block(slm_session* se, const Block& b, LState& st, float* x, size_t m) {
 
 // Model::advance (src/model.rs:563-640).  Ids are already in se->ids_dev.
 void advance(slm_session* se, size_t m, bool want_logits) {
+  se->argmax_valid = false;
   g_ctx_for_linear = se->ctx;
   g_capturing = se->capturing;
   slm_model* md = se->model;
@@ -557,6 +567,8 @@ void build_plan(slm_session* se) {
   P.arg_count = words;
   P.bar = words + 4;
   P.out_index = words + 8;
+  se->argmax_dev = words + 12;
+  P.argmax = se->argmax_dev;
   P.arg_part = static_cast<unsigned long long*>(alloc_zero(se, logit_items * sizeof(unsigned long long)));
   P.next_id = se->ids_dev;
   P.err = se->ctx->err;
@@ -575,6 +587,7 @@ void plan_outputs(slm_session* se, bool greedy, uint32_t* out, uint32_t* hist, u
 void mega_step(slm_session* se) {
   mega::launch(se->plan_host, se->grid, se->ctx->stream);
   se->pos += 1;
+  se->argmax_valid = true;
 }
 
 // One decode step for the id already in ids_dev[0]: graph replay when enabled.
@@ -585,6 +598,7 @@ void step_device(slm_session* se) {
     mega_step(se);
     return;
   }
+  se->argmax_valid = false;  // graph replays do not write the arg-max word
   if (!se->use_graph) {
     advance(se, 1, true);
     return;
@@ -626,9 +640,9 @@ void step_device(slm_session* se) {
 }
 
 void check_device_error(slm_ctx* c, slm_session* se = nullptr) {
-  int h = 0;
-  SLM_CUDA(cudaMemcpyAsync(&h, c->err, sizeof(int), cudaMemcpyDeviceToHost, c->stream));
+  SLM_CUDA(cudaMemcpyAsync(c->err_host, c->err, sizeof(int), cudaMemcpyDeviceToHost, c->stream));
   SLM_CUDA(cudaStreamSynchronize(c->stream));
+  const int h = *c->err_host;
   if (h) {
     SLM_CUDA(cudaMemsetAsync(c->err, 0, sizeof(int), c->stream));
     if ((h & 8) && se && se->mega_ok) {
@@ -984,6 +998,8 @@ int slm_session_new(slm_model* md, size_t loops, slm_session** out) {
       se->ids_dev = reinterpret_cast<uint32_t*>(alloc_zero(se.get(), CHUNK * sizeof(uint32_t)));
       se->rng_dev = reinterpret_cast<unsigned long long*>(alloc_zero(se.get(), sizeof(unsigned long long)));
       se->out_dev = reinterpret_cast<uint32_t*>(alloc_zero(se.get(), sizeof(uint32_t) * 4));
+      SLM_CUDA(cudaHostAlloc(reinterpret_cast<void**>(&se->io), sizeof(slm_session::HostIO), cudaHostAllocDefault));
+      SLM_CUDA(cudaEventCreateWithFlags(&se->io_event, cudaEventDisableTiming));
       se->mega_why = mega_unsupported(md);
       if (se->mega_why.empty()) {
         int coop = 0;
@@ -1005,6 +1021,8 @@ int slm_session_new(slm_model* md, size_t loops, slm_session** out) {
       SLM_CUDA(cudaStreamSynchronize(se->ctx->stream));
     } catch (...) {
       cudaStreamSynchronize(se->ctx->stream);
+      if (se->io) cudaFreeHost(se->io);
+      if (se->io_event) cudaEventDestroy(se->io_event);
       for (float* p : se->owned) dev_free(p);
       for (auto* v : {&se->pre, &se->coda})
         for (auto& st : *v)
@@ -1035,6 +1053,8 @@ int slm_session_free(slm_session* se) {
     for (auto& st : se->coda) g(st);
     dev_free(se->hist_dev);
     dev_free(se->outs_dev);
+    if (se->io) cudaFreeHost(se->io);
+    if (se->io_event) cudaEventDestroy(se->io_event);
     delete se;
   });
 }
@@ -1143,7 +1163,13 @@ int slm_step(slm_session* se, uint32_t id) {
     SLM_REQUIRE(se, "session is null");
     SLM_REQUIRE(id < se->model->cfg.vocab, "token id out of range");
     Device dev(se->ctx);
-    SLM_CUDA(cudaMemcpyAsync(se->ids_dev, &id, sizeof(uint32_t), cudaMemcpyHostToDevice, se->ctx->stream));
+    // The pinned word is read by the copy engine in stream order; wait for an
+    // earlier step's copy of it before overwriting.
+    if (se->io_busy) SLM_CUDA(cudaEventSynchronize(se->io_event));
+    se->io->id_in = id;
+    SLM_CUDA(cudaMemcpyAsync(se->ids_dev, &se->io->id_in, sizeof(uint32_t), cudaMemcpyHostToDevice, se->ctx->stream));
+    SLM_CUDA(cudaEventRecord(se->io_event, se->ctx->stream));
+    se->io_busy = true;
     step_device(se);
   });
 }
@@ -1185,22 +1211,34 @@ int slm_sample(slm_session* se, const slm_sampling* sp, const uint32_t* recent, 
     check_sampling(sp);
     Device dev(se->ctx);
     cudaStream_t s = se->ctx->stream;
+    // Greedy without a penalty on logits of a persistent step: that step
+    // already computed the arg-max (same order: first maximum, NaN never
+    // wins) and pick draws nothing from the RNG (src/sample.rs:33-45).
+    const bool fast = se->argmax_valid && sp->temperature <= 0.0f && (sp->repeat_penalty == 1.0f || n_recent == 0);
+    if (fast) {
+      SLM_CUDA(cudaMemcpyAsync(&se->io->id_out, se->argmax_dev, sizeof(uint32_t), cudaMemcpyDeviceToHost, s));
+      check_device_error(se->ctx, se);
+      se->io_busy = false;  // the stream is idle
+      *out_id = se->io->id_out;
+      return;
+    }
     ensure_u32(se, &se->hist_dev, &se->hist_cap, n_recent + 1);
     if (n_recent)
       SLM_CUDA(cudaMemcpyAsync(se->hist_dev, recent, n_recent * sizeof(uint32_t), cudaMemcpyHostToDevice, s));
-    unsigned long long st = *rng_state;
-    SLM_CUDA(cudaMemcpyAsync(se->rng_dev, &st, sizeof(st), cudaMemcpyHostToDevice, s));
+    if (se->io_busy) SLM_CUDA(cudaEventSynchronize(se->io_event));
+    se->io->rng_in = *rng_state;
+    SLM_CUDA(cudaMemcpyAsync(se->rng_dev, &se->io->rng_in, sizeof(unsigned long long), cudaMemcpyHostToDevice, s));
     SampleArgs a = sample_args(se, sp);
     a.recent = se->hist_dev;
     a.nrecent = (long long)n_recent;
     a.out = se->out_dev;
     sample(a, s);
-    uint32_t id = 0;
-    SLM_CUDA(cudaMemcpyAsync(&id, se->out_dev, sizeof(id), cudaMemcpyDeviceToHost, s));
-    SLM_CUDA(cudaMemcpyAsync(&st, se->rng_dev, sizeof(st), cudaMemcpyDeviceToHost, s));
+    SLM_CUDA(cudaMemcpyAsync(&se->io->id_out, se->out_dev, sizeof(uint32_t), cudaMemcpyDeviceToHost, s));
+    SLM_CUDA(cudaMemcpyAsync(&se->io->rng_out, se->rng_dev, sizeof(unsigned long long), cudaMemcpyDeviceToHost, s));
     check_device_error(se->ctx, se);
-    *out_id = id;
-    *rng_state = st;
+    se->io_busy = false;
+    *out_id = se->io->id_out;
+    *rng_state = se->io->rng_out;
   });
 }
 

@@ -134,6 +134,7 @@ int slm_ctx_new(int device, slm_ctx** out) {
       linear_prepare();
       c->err = static_cast<int*>(dev_alloc(sizeof(int) * 4));
       SLM_CUDA(cudaMemsetAsync(c->err, 0, sizeof(int) * 4, c->stream));
+      SLM_CUDA(cudaHostAlloc(reinterpret_cast<void**>(&c->err_host), sizeof(int) * 4, cudaHostAllocDefault));
     } catch (...) {
       delete c;
       throw;
@@ -151,6 +152,7 @@ int slm_ctx_free(slm_ctx* c) {
       dev_free(c->stage);
       dev_free(c->gemm_ws);
       dev_free(c->err);
+      if (c->err_host) cudaFreeHost(c->err_host);
       cudaStreamDestroy(c->stream);
     }
     delete c;

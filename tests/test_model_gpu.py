@@ -174,6 +174,31 @@ def test_persistent_kernel_sampling_path(slm, ctx, small):
     np.testing.assert_array_equal(a.decode(first, 40, s, hist, sa), b.decode(first, 40, s, hist, sb))
 
 
+def test_greedy_sample_after_persistent_steps(slm, ctx, oracle, small):
+    # slm_sample with greedy settings reads the arg-max the persistent step
+    # computed; with a penalty, after a feed, or after graph steps it runs the
+    # sampler.  Every case must equal pick on the logits read back.
+    model = slm.Model(ctx, small)
+    se = model.session()
+    prompt = np.random.default_rng(8).integers(0, 1000, 40)
+    se.feed(prompt)
+    greedy = slm.Sampling()
+    st = [slm.rng_seed(1)]
+    tok = se.sample(greedy, [], st)
+    assert tok == int(np.argmax(se.logits()))
+    for step in range(12):
+        if step == 6:
+            se.set_mega(False)
+        se.step(tok)
+        lg = se.logits()
+        assert se.sample(greedy, [], st) == int(np.argmax(lg))
+        pen = slm.Sampling(repeat_penalty=1.3, repeat_window=16)
+        recent = [int(t) for t in prompt[-16:]]
+        want = oracle.pick(lg, np.array(recent, dtype=np.uint32), repeat_penalty=1.3, repeat_window=16)
+        tok = se.sample(pen, recent, st)
+        assert tok == want
+
+
 def test_persistent_kernel_is_refused_where_it_does_not_apply(slm, tiny):
     se = tiny.session()
     assert not se.mega  # head size 8 and a global layer
