@@ -169,15 +169,17 @@ __device__ __forceinline__ void gemv_item(const Phase& ph, int i, int* seg, int*
   *o1 = min(sg.rows, *o0 + sg.per_item);
 }
 
-// The step's query sees positions lo..pos; split s takes a slice of the old
-// positions lo..pos-1 (the last split also takes `pos` itself, from the ring
-// the qkv phase just wrote).
+// The step's query sees positions lo .. pos - gap (lo = 0 for an unbounded
+// window).  With gap 0, split s takes a slice of the old positions lo..pos-1
+// and the last split also takes `pos` itself, from the cache the projection
+// phase just wrote; with gap ≥ 1 the slices cover lo..pos-gap.
 __device__ __forceinline__ void attn_slice(const Phase& ph, long long pos, int s, long long* a, long long* b) {
   long long lo = ph.window > 0 && pos > ph.window - 1 ? pos - (ph.window - 1) : 0;
-  long long count = pos - lo;
+  long long hi = ph.gap > 0 ? pos + 1 - ph.gap : pos;  // exclusive
+  long long count = hi > lo ? hi - lo : 0;
   long long chunk = (count + ph.splits - 1) / ph.splits;
   *a = lo + (long long)s * chunk;
-  *b = min(pos, *a + chunk);
+  *b = min(hi, *a + chunk);
   if (*b < *a) *b = *a;
 }
 
@@ -444,6 +446,42 @@ struct Cons {
       consumers_sync();
       return;
     }
+    if (ph.in_mode == IN_RMS_E) {
+      // G: v = rms(x)·w (+ rms(e0)·w_e), as two normalisations and one add.
+      const bool own = tid < n4;
+      float4 x = make_float4(0.f, 0.f, 0.f, 0.f), e = x, w = x, we = x;
+      if (own) {
+        w = __ldg(reinterpret_cast<const float4*>(ph.norm_w) + tid);
+        x = __ldcg(reinterpret_cast<const float4*>(ph.in_a) + tid);
+        if (ph.in_c) {
+          we = __ldg(reinterpret_cast<const float4*>(ph.in_c) + tid);
+          e = __ldcg(reinterpret_cast<const float4*>(P.e0) + tid);
+        }
+        reinterpret_cast<float4*>(sm.xraw)[tid] = x;
+      }
+      float s1 = x.x * x.x, s2 = e.x * e.x;
+      s1 = fmaf(x.y, x.y, s1), s2 = fmaf(e.y, e.y, s2);
+      s1 = fmaf(x.z, x.z, s1), s2 = fmaf(e.z, e.z, s2);
+      s1 = fmaf(x.w, x.w, s1), s2 = fmaf(e.w, e.w, s2);
+      s1 = warp_sum(s1), s2 = warp_sum(s2);
+      if (lane == 0) sm.red[warp] = s1, sm.red[kConsumerWarps + warp] = s2;
+      consumers_sync();
+      float t1 = 0.0f, t2 = 0.0f;
+#pragma unroll
+      for (int q = 0; q < kConsumerWarps; q++) t1 += sm.red[q], t2 += sm.red[kConsumerWarps + q];
+      const float r1 = 1.0f / sqrtf(t1 / (float)ph.cols + P.eps), r2 = 1.0f / sqrtf(t2 / (float)ph.cols + P.eps);
+      if (own) {
+        float4 v = make_float4(x.x * r1 * w.x, x.y * r1 * w.y, x.z * r1 * w.z, x.w * r1 * w.w);
+        if (ph.in_c) {
+          v.x = v.x + e.x * r2 * we.x, v.y = v.y + e.y * r2 * we.y;
+          v.z = v.z + e.z * r2 * we.z, v.w = v.w + e.w * r2 * we.w;
+        }
+        reinterpret_cast<float4*>(sm.xin)[tid] = v;
+        if (blockIdx.x == 0 && ph.xout) reinterpret_cast<float4*>(ph.xout)[tid] = v;
+      }
+      consumers_sync();
+      return;
+    }
     // Normalised input: d ≤ kMaxD, at most one float4 per thread.
     const bool own = tid < n4;
     float4 x = make_float4(0.f, 0.f, 0.f, 0.f), w = x;
@@ -655,6 +693,29 @@ struct Cons {
 
   __device__ void epilogue(const Phase& ph, const Segment& sg, int o0, int o1, int item) {
     const int n = o1 - o0;
+    if (ph.out_mode == OUT_G) {
+      if (&sg == &ph.seg[0]) {  // q rows, scaled as the graph path does (k_g_post)
+        const float f = ph.inv_log > 0.0f ? log1pf((float)pos) * ph.inv_log : 1.0f;
+        for (int t = tid; t < n; t += 256) {
+          const float a = sm.acc[0][0][t];
+          sg.out[o0 + t] = ph.inv_log > 0.0f ? a * f : a;
+        }
+      } else {  // kv rows: [keys (heads · dh) | values (heads · dh)]
+        const int kd = ph.heads * kDH;
+        for (int t = tid; t < n; t += 256) {
+          const int o = o0 + t;
+          const float a = sm.acc[0][0][t];
+          if (o < kd) {
+            const long long slot = ph.kshift ? pos + 1 : pos;
+            ph.kc[((size_t)(o / kDH) * ph.cap + (size_t)slot) * kDH + o % kDH] = a;
+          } else {
+            const int u = o - kd;
+            ph.vc[((size_t)(u / kDH) * ph.cap + (size_t)pos) * kDH + u % kDH] = a;
+          }
+        }
+      }
+      return;
+    }
     if (ph.out_mode == OUT_ROPE) {
       const int d = P.d;
       const size_t slot = (size_t)(pos % ph.cap);
@@ -755,32 +816,26 @@ struct Cons {
     }
   }
 
-  // Window attention for head h, split s (one query at `pos`).
-  __device__ void attn_item(const Phase& ph, int item) {
-    const int h = item / ph.splits, s = item % ph.splits;
+  // Attention of the step's query for cache head c, split s: the QG query
+  // heads c·QG … that share the head (GQA) walk the same K/V tiles (one HBM
+  // read); each writes its (head, split) partial (acc, m, l).
+  template <int QG>
+  __device__ void attn_item_t(const Phase& ph, int item) {
+    const int c = item / ph.splits, s = item % ph.splits;
     const int sub = lane & 7, grp = lane >> 3;
     // Lane `sub` of a group owns dims sub*4 .. sub*4+3 and 32+sub*4 .. 32+sub*4+3,
     // so a group reads each cached row as two contiguous 128-byte runs.
     const int d0 = sub * 4, d1 = 32 + sub * 4;
-    float qv[8];
-    {
-      const float* qp = ph.q + h * kDH;
+    float qv[QG][8], mx[QG], l[QG], acc[QG][8];
 #pragma unroll
-      for (int e = 0; e < 4; e++) qv[e] = __ldcg(qp + d0 + e), qv[4 + e] = __ldcg(qp + d1 + e);
+    for (int g = 0; g < QG; g++) {
+      const float* qp = ph.q + (c * QG + g) * kDH;
+#pragma unroll
+      for (int e = 0; e < 4; e++) qv[g][e] = __ldcg(qp + d0 + e), qv[g][4 + e] = __ldcg(qp + d1 + e);
+      mx[g] = -INFINITY, l[g] = 0.0f;
+#pragma unroll
+      for (int e = 0; e < 8; e++) acc[g][e] = 0.0f;
     }
-    float mx = -INFINITY, l = 0.0f, acc[8];
-#pragma unroll
-    for (int e = 0; e < 8; e++) acc[e] = 0.0f;
-    auto fold = [&](const float* kr) {
-      const uint32_t ka = saddr(kr);
-      float4 k0 = lds4(ka + d0 * 4), k1 = lds4(ka + d1 * 4);
-      float sc = qv[0] * k0.x + qv[1] * k0.y + qv[2] * k0.z + qv[3] * k0.w + qv[4] * k1.x + qv[5] * k1.y +
-                 qv[6] * k1.z + qv[7] * k1.w;
-      sc += __shfl_xor_sync(0xffffffffu, sc, 1);
-      sc += __shfl_xor_sync(0xffffffffu, sc, 2);
-      sc += __shfl_xor_sync(0xffffffffu, sc, 4);
-      return sc * ph.scale;
-    };
     long long a, b;
     attn_slice(ph, pos, s, &a, &b);
     unsigned long long c0 = P.trace && tid == 0 ? now_ns() : 0;
@@ -790,35 +845,44 @@ struct Cons {
       const float* Kt = tile;
       const float* Vt = tile + kAttnTile * kDH;
       constexpr int J = kAttnTile / 32;
-      float sc[J];
 #pragma unroll
-      for (int j = 0; j < J; j++) {
-        int r = grp + 4 * warp + 32 * j;
-        sc[j] = fold(Kt + (r < n ? r : 0) * kDH);
-        if (r >= n) sc[j] = -INFINITY;
-      }
-      float M = mx;
-#pragma unroll
-      for (int j = 0; j < J; j++) M = fmaxf(M, sc[j]);
-      if (M != -INFINITY) {
-        const float corr = mx == -INFINITY ? 0.0f : expf(mx - M);
-        l *= corr;
-#pragma unroll
-        for (int e = 0; e < 8; e++) acc[e] *= corr;
+      for (int g = 0; g < QG; g++) {
+        float sc[J];
 #pragma unroll
         for (int j = 0; j < J; j++) {
-          int r = grp + 4 * warp + 32 * j;
-          if (r >= n) continue;
-          const float pe = expf(sc[j] - M);
-          l += pe;
-          const uint32_t va = saddr(Vt + r * kDH);
-          float4 v0 = lds4(va + d0 * 4), v1 = lds4(va + d1 * 4);
-          acc[0] = fmaf(pe, v0.x, acc[0]), acc[1] = fmaf(pe, v0.y, acc[1]);
-          acc[2] = fmaf(pe, v0.z, acc[2]), acc[3] = fmaf(pe, v0.w, acc[3]);
-          acc[4] = fmaf(pe, v1.x, acc[4]), acc[5] = fmaf(pe, v1.y, acc[5]);
-          acc[6] = fmaf(pe, v1.z, acc[6]), acc[7] = fmaf(pe, v1.w, acc[7]);
+          const int r = grp + 4 * warp + 32 * j;
+          const uint32_t ka = saddr(Kt + (r < n ? r : 0) * kDH);
+          float4 k0 = lds4(ka + d0 * 4), k1 = lds4(ka + d1 * 4);
+          float x = qv[g][0] * k0.x + qv[g][1] * k0.y + qv[g][2] * k0.z + qv[g][3] * k0.w + qv[g][4] * k1.x +
+                    qv[g][5] * k1.y + qv[g][6] * k1.z + qv[g][7] * k1.w;
+          x += __shfl_xor_sync(0xffffffffu, x, 1);
+          x += __shfl_xor_sync(0xffffffffu, x, 2);
+          x += __shfl_xor_sync(0xffffffffu, x, 4);
+          sc[j] = r < n ? x * ph.scale : -INFINITY;
         }
-        mx = M;
+        float M = mx[g];
+#pragma unroll
+        for (int j = 0; j < J; j++) M = fmaxf(M, sc[j]);
+        if (M != -INFINITY) {
+          const float corr = mx[g] == -INFINITY ? 0.0f : expf(mx[g] - M);
+          l[g] *= corr;
+#pragma unroll
+          for (int e = 0; e < 8; e++) acc[g][e] *= corr;
+#pragma unroll
+          for (int j = 0; j < J; j++) {
+            const int r = grp + 4 * warp + 32 * j;
+            if (r >= n) continue;
+            const float pe = expf(sc[j] - M);
+            l[g] += pe;
+            const uint32_t va = saddr(Vt + r * kDH);
+            float4 v0 = lds4(va + d0 * 4), v1 = lds4(va + d1 * 4);
+            acc[g][0] = fmaf(pe, v0.x, acc[g][0]), acc[g][1] = fmaf(pe, v0.y, acc[g][1]);
+            acc[g][2] = fmaf(pe, v0.z, acc[g][2]), acc[g][3] = fmaf(pe, v0.w, acc[g][3]);
+            acc[g][4] = fmaf(pe, v1.x, acc[g][4]), acc[g][5] = fmaf(pe, v1.y, acc[g][5]);
+            acc[g][6] = fmaf(pe, v1.z, acc[g][6]), acc[g][7] = fmaf(pe, v1.w, acc[g][7]);
+          }
+          mx[g] = M;
+        }
       }
       release();
     }
@@ -828,65 +892,79 @@ struct Cons {
       comp_ns += e0 - c0;
       ntiles++;
     }
-    if (s == ph.splits - 1 && warp == 0 && grp == 0) {
-      // The step's own position, stored by the qkv phase.
-      size_t slot = (size_t)(pos % ph.cap);
-      const float* kr = ph.kc + ((size_t)h * ph.cap + slot) * kDH;
-      const float* vr = ph.vc + ((size_t)h * ph.cap + slot) * kDH;
+    if (ph.gap == 0 && s == ph.splits - 1 && warp == 0 && grp == 0) {
+      // The step's own position, stored by the projection phase.
+      const size_t slot = (size_t)(pos % ph.cap);
+      const float* kr = ph.kc + ((size_t)c * ph.cap + slot) * kDH;
+      const float* vr = ph.vc + ((size_t)c * ph.cap + slot) * kDH;
       float kk[8], vv[8];
 #pragma unroll
       for (int e = 0; e < 4; e++) {
         kk[e] = __ldcg(kr + d0 + e), kk[4 + e] = __ldcg(kr + d1 + e);
         vv[e] = __ldcg(vr + d0 + e), vv[4 + e] = __ldcg(vr + d1 + e);
       }
-      float sc = 0.0f;
 #pragma unroll
-      for (int e = 0; e < 8; e++) sc += qv[e] * kk[e];
-      sc += __shfl_xor_sync(0x000000ffu, sc, 1);
-      sc += __shfl_xor_sync(0x000000ffu, sc, 2);
-      sc += __shfl_xor_sync(0x000000ffu, sc, 4);
-      sc *= ph.scale;
-      float M = fmaxf(mx, sc);
-      float corr = mx == -INFINITY ? 0.0f : expf(mx - M);
-      float pe = expf(sc - M);
-      l = l * corr + pe;
+      for (int g = 0; g < QG; g++) {
+        float sc = 0.0f;
 #pragma unroll
-      for (int e = 0; e < 8; e++) acc[e] = acc[e] * corr + pe * vv[e];
-      mx = M;
-    }
-    // Merge the four lane groups of each warp, then the warps.
+        for (int e = 0; e < 8; e++) sc += qv[g][e] * kk[e];
+        sc += __shfl_xor_sync(0x000000ffu, sc, 1);
+        sc += __shfl_xor_sync(0x000000ffu, sc, 2);
+        sc += __shfl_xor_sync(0x000000ffu, sc, 4);
+        sc *= ph.scale;
+        const float M = fmaxf(mx[g], sc);
+        const float corr = mx[g] == -INFINITY ? 0.0f : expf(mx[g] - M);
+        const float pe = expf(sc - M);
+        l[g] = l[g] * corr + pe;
 #pragma unroll
-    for (int o = 8; o < 32; o <<= 1) {
-      float om = __shfl_xor_sync(0xffffffffu, mx, o), ol = __shfl_xor_sync(0xffffffffu, l, o);
-      float M = fmaxf(mx, om);
-      float ca = mx == -INFINITY ? 0.0f : expf(mx - M), cb = om == -INFINITY ? 0.0f : expf(om - M);
-      l = l * ca + ol * cb;
-#pragma unroll
-      for (int e = 0; e < 8; e++) acc[e] = acc[e] * ca + __shfl_xor_sync(0xffffffffu, acc[e], o) * cb;
-      mx = M;
-    }
-    if (grp == 0) {
-#pragma unroll
-      for (int e = 0; e < 4; e++) sm.wsm[warp][d0 + e] = acc[e], sm.wsm[warp][d1 + e] = acc[4 + e];
-      if (sub == 0) sm.wsm[warp][kDH] = mx, sm.wsm[warp][kDH + 1] = l;
-    }
-    if (!all_ok()) return;
-    float* out = ph.part + (size_t)item * (kDH + 2);
-    if (tid < kDH + 2) {
-      const int e = tid < kDH ? tid : 0;
-      float m0 = sm.wsm[0][kDH], l0 = sm.wsm[0][kDH + 1], a0 = sm.wsm[0][e];
-      for (int w = 1; w < kConsumerWarps; w++) {
-        float om = sm.wsm[w][kDH], ol = sm.wsm[w][kDH + 1];
-        float M = fmaxf(m0, om);
-        float ca = m0 == -INFINITY ? 0.0f : expf(m0 - M), cb = om == -INFINITY ? 0.0f : expf(om - M);
-        l0 = l0 * ca + ol * cb;
-        a0 = a0 * ca + sm.wsm[w][e] * cb;
-        m0 = M;
+        for (int e = 0; e < 8; e++) acc[g][e] = acc[g][e] * corr + pe * vv[e];
+        mx[g] = M;
       }
-      out[tid] = tid < kDH ? a0 : (tid == kDH ? m0 : l0);
     }
-    consumers_sync();  // sm.wsm is free for the next item
+#pragma unroll
+    for (int g = 0; g < QG; g++) {
+      // Merge the four lane groups of each warp, then the warps.
+#pragma unroll
+      for (int o = 8; o < 32; o <<= 1) {
+        float om = __shfl_xor_sync(0xffffffffu, mx[g], o), ol = __shfl_xor_sync(0xffffffffu, l[g], o);
+        float M = fmaxf(mx[g], om);
+        float ca = mx[g] == -INFINITY ? 0.0f : expf(mx[g] - M), cb = om == -INFINITY ? 0.0f : expf(om - M);
+        l[g] = l[g] * ca + ol * cb;
+#pragma unroll
+        for (int e = 0; e < 8; e++) acc[g][e] = acc[g][e] * ca + __shfl_xor_sync(0xffffffffu, acc[g][e], o) * cb;
+        mx[g] = M;
+      }
+      if (grp == 0) {
+#pragma unroll
+        for (int e = 0; e < 4; e++) sm.wsm[warp][d0 + e] = acc[g][e], sm.wsm[warp][d1 + e] = acc[g][4 + e];
+        if (sub == 0) sm.wsm[warp][kDH] = mx[g], sm.wsm[warp][kDH + 1] = l[g];
+      }
+      if (!all_ok()) return;
+      float* out = ph.part + ((size_t)(c * QG + g) * ph.splits + s) * (kDH + 2);
+      if (tid < kDH + 2) {
+        const int e = tid < kDH ? tid : 0;
+        float m0 = sm.wsm[0][kDH], l0 = sm.wsm[0][kDH + 1], a0 = sm.wsm[0][e];
+        for (int w = 1; w < kConsumerWarps; w++) {
+          float om = sm.wsm[w][kDH], ol = sm.wsm[w][kDH + 1];
+          float M = fmaxf(m0, om);
+          float ca = m0 == -INFINITY ? 0.0f : expf(m0 - M), cb = om == -INFINITY ? 0.0f : expf(om - M);
+          l0 = l0 * ca + ol * cb;
+          a0 = a0 * ca + sm.wsm[w][e] * cb;
+          m0 = M;
+        }
+        out[tid] = tid < kDH ? a0 : (tid == kDH ? m0 : l0);
+      }
+      consumers_sync();  // sm.wsm is free for the next head / item
+    }
     if (e0) epi_ns += now_ns() - e0;
+  }
+
+  __device__ void attn_item(const Phase& ph, int item) {
+    switch (ph.qg) {
+      case 2: attn_item_t<2>(ph, item); break;
+      case 3: attn_item_t<3>(ph, item); break;
+      default: attn_item_t<1>(ph, item); break;  // the plan allows 1..3
+    }
   }
 
   // GLA for head h: l2norm q, k; S = d·S + kᵀv; y = q·S; head_norm; silu gate.

@@ -208,6 +208,16 @@ __global__ void k_silu_pair(float* mid, const float* up, size_t m, size_t F) {
   }
 }
 
+// kc[h][pos + off][:] = src[h·dh …] for every cache head (one row per head).
+__global__ void k_store_next(float* kc, const float* src, const long long* pos_ptr, long long off, size_t kh,
+                             size_t dh, size_t cap) {
+  const size_t slot = (size_t)(pos_ptr[0] + off);
+  GRID_STRIDE(t, kh * dh) {
+    const size_t h = t / dh, e = t % dh;
+    if (slot < cap) kc[(h * cap + slot) * dh + e] = src[t];
+  }
+}
+
 __global__ void k_advance_pos(long long* pos, long long m) {
   if (threadIdx.x == 0 && blockIdx.x == 0) pos[0] += m;
 }
@@ -349,6 +359,11 @@ void ew_silu_pair(float* mid, const float* up, size_t m, size_t F, cudaStream_t 
   if (!m) return;
   k_silu_pair<<<ew_grid(m * F), EW, 0, st>>>(mid, up, m, F);
   SLM_LAUNCHED("k_silu_pair");
+}
+void ew_store_next(float* kc, const float* src, const long long* pos_ptr, long long off, size_t kh, size_t dh,
+                   size_t cap, cudaStream_t st) {
+  k_store_next<<<ew_grid(kh * dh), EW, 0, st>>>(kc, src, pos_ptr, off, kh, dh, cap);
+  SLM_LAUNCHED("k_store_next");
 }
 void ew_advance_pos(long long* pos, long long m, cudaStream_t st) {
   k_advance_pos<<<1, 32, 0, st>>>(pos, m);

@@ -118,6 +118,9 @@ void ew_g_post(float* q, size_t d, size_t m, const long long* pos_ptr, float inv
                cudaStream_t st);
 void ew_silu_pair(float* mid, const float* up, size_t m, size_t F, cudaStream_t st);
 void ew_advance_pos(long long* pos, long long m, cudaStream_t st);
+// kc[h][*pos_ptr + off] = src[h·dh …] (h < kh), skipped past the capacity.
+void ew_store_next(float* kc, const float* src, const long long* pos_ptr, long long off, size_t kh, size_t dh,
+                   size_t cap, cudaStream_t st);
 // Batched decode of m independent sequences (one token each; arrays of m).
 void ew_rope_store_rows(const float* mix, size_t ldmix, const float* inv, long long* const* posr, size_t m,
                         size_t heads, size_t dh, size_t cap, float* qout, float* const* kr, float* const* vr,

@@ -32,6 +32,7 @@ enum InMode : int {
   IN_EMBED_RMS = 2,  // x = embed[ids[0]] (written to a and b), v = rms(x)·w
   IN_LOOP_RMS = 3,   // x = (a + b) + c, written to xout; v = rms(x)·w
   IN_ATTN = 4,       // v = the attention output, merged from the (head, split) partials in a
+  IN_RMS_E = 5,      // G: v = rms(a)·w (+ rms(e0)·c when c is set); v written to xout (the next shift input)
 };
 
 // What a GEMV phase does with its dot products.
@@ -41,6 +42,8 @@ enum OutMode : int {
   OUT_SILU = 2,    // pairs (j, j + n): y[j] = silu(acc_j)·acc_{j+n}
   OUT_ROPE = 3,    // S qkv: rotate q, k pairs (j, j+32) of each head, write q, store k, v in the ring
   OUT_LOGITS = 4,  // y[r] = acc and a per-item arg-max partial
+  OUT_G = 5,       // G: segment 0 = q rows (× the logn factor) into q; segment 1 = kv rows: keys into
+                   // the cache at pos (pos + 1 with kshift: the next position's shifted key), values at pos
 };
 
 struct Segment {
@@ -61,9 +64,13 @@ struct alignas(16) Phase {
   float* xout;
   int nseg;
   Segment seg[2];
-  // OUT_ROPE / ATTN / GLA
-  float *q, *kc, *vc;  // q buffer and the layer's ring (ATTN, ROPE)
-  long long cap, window;
+  // OUT_ROPE / OUT_G / ATTN / GLA
+  float *q, *kc, *vc;  // q buffer and the layer's cache (ATTN, ROPE, G)
+  long long cap, window;  // window 0: unbounded reach (G)
+  long long gap;          // ATTN: the query at p sees positions up to p - gap
+  int qg;                 // ATTN: query heads per cache head (items are cache heads × splits)
+  int kshift;             // OUT_G
+  float inv_log;          // OUT_G: 1/ln(logn), 0 for no logn scaling
   const float* inv_freq;
   // ATTN: heads × splits items; partials and per-head arrival counters
   int heads, splits;

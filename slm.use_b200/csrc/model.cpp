@@ -102,6 +102,8 @@ struct slm_session {
   int grid = 0;
   unsigned long long* trace = nullptr;  // per-phase timeline of the last step (SLM_OPT_TRACE)
   unsigned* attn_count = nullptr;        // per-head arrival counters of the attention phases
+  float* attn_part = nullptr;            // attention partials of the persistent step
+  bool plan_stale = false;               // a global cache moved: the phase descriptors need refreshing
   int in_batches = 0;                    // batches holding this session
   uint32_t* argmax_dev = nullptr;        // the persistent step's arg-max of its logits
   bool argmax_valid = false;             // the logits come from a persistent step
@@ -274,12 +276,16 @@ void grow(slm_session* se, LState& st) {
   }
   st.cap = nw;
   drop_graph(se);
+  se->plan_stale = true;  // the persistent step's descriptors hold the old cache
 }
 
 void ensure_caps(slm_session* se, size_t m) {
+  // With kshift a step also stores the next position's key (W_k · n of its
+  // last token), so a global cache keeps one slot beyond the step.
+  const size_t extra = se->model->cfg.kshift ? 1 : 0;
   auto one = [&](LState& st) {
     if (st.kind == 'G')
-      while (se->pos + m > st.cap) grow(se, st);
+      while (se->pos + m + extra > st.cap) grow(se, st);
   };
   for (auto& st : se->pre) one(st);
   for (auto& l : se->core)
@@ -357,6 +363,13 @@ void block(slm_session* se, const Block& b, LState& st, float* x, size_t m) {
     float inv_log = c.logn ? 1.0f / std::log((float)c.logn) : 0.0f;
     ew_g_post(se->q, d, m, se->pos_dev, inv_log, c.logn ? 1 : 0, keys, ldk, se->mix + kd, 2 * kd, kd, st.cap, dh,
               st.k, st.v, s);
+    if (c.kshift) {
+      // The next position's key, W_k · n of this chunk's last token (now in
+      // prev): the persistent step relies on it being in the cache already,
+      // and the next chunk overwrites it with the same value.
+      run_linear(s, b.kv, st.prev, id, 1, se->kvs, (int)kd, EPI_STORE, nullptr, 0, kd);
+      ew_store_next(st.k, se->kvs, se->pos_dev, (long long)m, kh, dh, st.cap, s);
+    }
     size_t far = c.far ? c.window : 0;
     if (se->capturing || se->pos + m > far) {
       AttnGeom g{im, 0, (long long)far, (long long)st.cap, (int)heads, (int)kh, (int)dh, scale};
@@ -431,13 +444,22 @@ std::string mega_unsupported(const slm_model* md) {
   if (!cols_ok(md->hidden) || md->hidden > (size_t)mega::kMaxCols) return "FFN width must suit the GEMV split, <= 3072";
   if (c.damp != 1.0f) return "damp != 1";
   if (c.prelude.empty()) return "no prelude block";
-  for (const std::string* part : {&c.prelude, &c.core, &c.coda})
-    if (part->find('G') != std::string::npos) return "global-attention layers";
+  const bool has_g = (c.prelude + c.core + c.coda).find('G') != std::string::npos;
+  if (has_g) {
+    // A global block forms its own input (x, and e0 for global_emb): it cannot
+    // be the first block of the prelude or of the loop.
+    if (c.prelude[0] == 'G' || (!c.core.empty() && c.core[0] == 'G'))
+      return "a global-attention layer opens the prelude or the loop";
+    if (c.kv_heads == 0 || c.heads % c.kv_heads != 0 || c.heads / c.kv_heads > 3)
+      return "global layers need heads / kv_heads in 1..3";
+  }
   return "";
 }
 
 // The m = 1 step as phases (decode_mega.cu), for this session's buffers.
-void build_plan(slm_session* se) {
+// refresh: only regenerate the phase descriptors (a global cache moved or
+// grew); counters, outputs and the rest of the plan stay.
+void build_plan(slm_session* se, bool refresh = false) {
   using namespace mega;
   slm_model* md = se->model;
   const Config& c = md->cfg;
@@ -471,10 +493,18 @@ void build_plan(slm_session* se) {
   SLM_REQUIRE(2 * H * splits <= (kMaxSplits / 2) * (kDH + 2) && H <= (kMaxSplits / 2) * (kDH + 2),
               "too many attention partials for the decode kernel");
   const float scale = 1.0f / std::sqrt((float)c.dh());
+  // Global layers: items are cache heads × splits (each serving heads / kv_heads queries).
+  const int kh = (int)c.kv_heads;
+  const int gsplits = std::min(kMaxSplits, std::max(1, G / kh));
+  SLM_REQUIRE(2 * H * gsplits <= (kMaxSplits / 2) * (kDH + 2), "too many attention partials for the decode kernel");
   // Attention partials (heads × splits × (dh + 2)) and per-head arrival counters.
-  float* attn_part = static_cast<float*>(alloc_zero(se, (size_t)H * splits * (kDH + 2) * sizeof(float)));
-  auto* attn_count = static_cast<unsigned*>(alloc_zero(se, (size_t)H * sizeof(unsigned)));
-  se->attn_count = attn_count;
+  if (!refresh) {
+    se->attn_part = static_cast<float*>(
+        alloc_zero(se, (size_t)H * std::max(splits, gsplits) * (kDH + 2) * sizeof(float)));
+    se->attn_count = static_cast<unsigned*>(alloc_zero(se, (size_t)H * sizeof(unsigned)));
+  }
+  float* attn_part = se->attn_part;
+  unsigned* attn_count = se->attn_count;
   float* X0 = se->xa;
   struct In {
     int mode;
@@ -494,6 +524,26 @@ void build_plan(slm_session* se) {
       a.heads = H, a.splits = splits, a.part = attn_part, a.counters = attn_count;
       a.y = se->y, a.scale = scale, a.items = H * splits;
       ph.push_back(a);
+    } else if (b.kind == 'G') {
+      // q and kv from n = rms(x)·w (+ rms(e0)·w_e); n becomes the next shift
+      // input; items split between the two products by rows.
+      const int kd = kh * kDH;
+      const int qi = std::max(1, G * d / (d + 2 * kd)), ki = std::max(1, G - qi);
+      Phase p = gemv(d, IN_RMS_E, X, nullptr, b.norm_e, b.norm1, c.kshift ? st.prev : nullptr, OUT_G,
+                     seg(b.q.w, d, per(d, qi, 1), se->q));
+      p.nseg = 2;
+      p.seg[1] = seg(b.kv.w, 2 * kd, per(2 * kd, ki, 1), nullptr);
+      p.items = p.seg[0].items + p.seg[1].items;
+      p.kc = st.k, p.vc = st.v, p.cap = (long long)st.cap, p.heads = kh, p.kshift = c.kshift ? 1 : 0;
+      p.inv_log = c.logn ? 1.0f / std::log((float)c.logn) : 0.0f;
+      ph.push_back(p);
+      Phase a{};
+      a.kind = PH_ATTN;
+      a.kc = st.k, a.vc = st.v, a.q = se->q, a.cap = (long long)st.cap, a.window = 0;
+      a.gap = c.far ? (long long)c.window : 0;
+      a.heads = H, a.qg = H / kh, a.splits = gsplits, a.part = attn_part, a.counters = attn_count;
+      a.y = se->y, a.scale = scale, a.items = kh * gsplits;
+      ph.push_back(a);
     } else {
       Phase p = gemv(d, in.mode, ia, in.b, in.c, b.norm1, in.xout, OUT_STORE,
                      seg(b.qkvg.w, 4 * d, per(4 * d, std::max(1, G - 1), 1), se->mix));
@@ -510,9 +560,9 @@ void build_plan(slm_session* se) {
     // The residual of o and down is the x of the phase two back, whose
     // normalising prologue left it in shared memory on every CTA.  After an
     // S mixer, o's input is merged from the attention partials.
-    if (b.kind == 'S') {
+    if (b.kind == 'S' || b.kind == 'G') {
       Phase o = gemv(d, IN_ATTN, attn_part, nullptr, nullptr, nullptr, nullptr, OUT_ADD, seg(b.o.w, d, per(d, G, 1), X));
-      o.heads = H, o.splits = splits;
+      o.heads = H, o.splits = b.kind == 'G' ? gsplits : splits;
       ph.push_back(o);
     } else {
       ph.push_back(gemv(d, IN_PLAIN, se->y, nullptr, nullptr, nullptr, nullptr, OUT_ADD, seg(b.o.w, d, per(d, G, 1), X)));
@@ -549,6 +599,13 @@ void build_plan(slm_session* se) {
                     seg(md->embed.w, (int)c.vocab, per((int)c.vocab, G, 1), se->logits)));
   const int logit_items = ph.back().items;
 
+  if (refresh) {
+    SLM_REQUIRE((int)ph.size() == se->plan_host.nphases, "decode plan changed shape");
+    SLM_CUDA(cudaMemcpyAsync(se->phases_dev, ph.data(), ph.size() * sizeof(Phase), cudaMemcpyHostToDevice,
+                             se->ctx->stream));
+    se->plan_stale = false;
+    return;
+  }
   // Device memory of the plan: phases, arg-max partials, counters, barrier words.
   se->phases_dev = static_cast<Phase*>(alloc_zero(se, ph.size() * sizeof(Phase)));
   SLM_CUDA(cudaMemcpyAsync(se->phases_dev, ph.data(), ph.size() * sizeof(Phase), cudaMemcpyHostToDevice,
@@ -585,6 +642,7 @@ void plan_outputs(slm_session* se, bool greedy, uint32_t* out, uint32_t* hist, u
 }
 
 void mega_step(slm_session* se) {
+  if (se->plan_stale) build_plan(se, true);
   mega::launch(se->plan_host, se->grid, se->ctx->stream);
   se->pos += 1;
   se->argmax_valid = true;

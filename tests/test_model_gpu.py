@@ -199,6 +199,73 @@ def test_greedy_sample_after_persistent_steps(slm, ctx, oracle, small):
         assert tok == want
 
 
+@pytest.fixture(scope="module")
+def g64(tmp_path_factory):
+    load_pkg()
+    # Global variant with head size 64 and GQA (6 heads over 2 cache heads), a
+    # short window so the far gap opens after 32 positions.
+    return _synthetic(tmp_path_factory, "g64", "GLOBAL", vocab_size=1000, d_model=384, n_heads=6, hidden=768,
+                      window=32, max_loops=3, default_loops=2, global_kv_heads=2)
+
+
+def _lockstep(a, b, tok, steps, atol):
+    worst = 0.0
+    for _ in range(steps):
+        a.step(tok)
+        b.step(tok)
+        la, lb = a.logits(), b.logits()
+        worst = max(worst, float(np.abs(la - lb).max()))
+        assert int(np.argmax(la)) == int(np.argmax(lb))
+        tok = int(np.argmax(lb))
+    assert worst < atol, worst
+    return tok
+
+
+def test_persistent_kernel_runs_global_layers(slm, ctx, oracle, g64):
+    # Persistent steps of a model with a global layer (norm_e, logn, kshift,
+    # far gap, GQA) against the graph path, from before the far gap opens to
+    # well after, and against the oracle.
+    model = slm.Model(ctx, g64)
+    a, b = model.session(), model.session()
+    assert a.mega, a.stat(3)
+    b.set_mega(False)
+    ids = np.random.default_rng(11).integers(0, 1000, 20)
+    a.feed(ids)
+    b.feed(ids)
+    tok = _lockstep(a, b, int(np.argmax(b.logits())), 50, 2e-5)
+    ref = oracle.Model(g64).session()
+    ref.feed(ids)
+    # Replay the same tokens on the oracle: a's history is ids + the 50 stepped ones.
+    c = model.session()
+    c.feed(ids)
+    t = int(np.argmax(c.logits()))
+    worst = 0.0
+    for _ in range(50):
+        c.step(t)
+        ref.step(t)
+        worst = max(worst, float(np.abs(c.logits() - ref.logits()).max()))
+        t = int(np.argmax(ref.logits()))
+    assert worst < 2e-4, worst
+    assert a.state_bytes() == b.state_bytes()
+
+
+def test_persistent_kernel_follows_global_cache_growth(slm, ctx, g64):
+    # The first global cache holds 8192 positions; stepping across it moves the
+    # cache and the persistent step must follow (its plan is refreshed).
+    model = slm.Model(ctx, g64)
+    a, b = model.session(1), model.session(1)
+    b.set_mega(False)
+    ids = np.random.default_rng(12).integers(0, 1000, 8180)
+    a.feed(ids)
+    b.feed(ids)
+    _lockstep(a, b, int(np.argmax(b.logits())), 24, 2e-5)
+    assert a.pos == b.pos == 8204
+    greedy = slm.Sampling()
+    first = a.sample(greedy)
+    assert first == b.sample(greedy)
+    np.testing.assert_array_equal(a.decode(first, 16, greedy), b.decode(first, 16, greedy))
+
+
 def test_persistent_kernel_is_refused_where_it_does_not_apply(slm, tiny):
     se = tiny.session()
     assert not se.mega  # head size 8 and a global layer
