@@ -104,6 +104,7 @@ __device__ __forceinline__ int consumers_and(int v) {
 
 constexpr unsigned long long kWaitNs = 2000000000ull;  // 2 s per wait
 
+
 // Bounded wait on an mbarrier phase; false (and the error bit) on expiry or
 // when another CTA has already failed.
 __device__ bool wait_mbar(uint64_t* b, unsigned parity, int* err) {
@@ -173,9 +174,10 @@ __device__ __forceinline__ void gemv_item(const Phase& ph, int i, int* seg, int*
 // window).  With gap 0, split s takes a slice of the old positions lo..pos-1
 // and the last split also takes `pos` itself, from the cache the projection
 // phase just wrote; with gap ≥ 1 the slices cover lo..pos-gap.
+template <bool GL = true>
 __device__ __forceinline__ void attn_slice(const Phase& ph, long long pos, int s, long long* a, long long* b) {
   long long lo = ph.window > 0 && pos > ph.window - 1 ? pos - (ph.window - 1) : 0;
-  long long hi = ph.gap > 0 ? pos + 1 - ph.gap : pos;  // exclusive
+  long long hi = GL && ph.gap > 0 ? pos + 1 - ph.gap : pos;  // exclusive
   long long count = hi > lo ? hi - lo : 0;
   long long chunk = (count + ph.splits - 1) / ph.splits;
   *a = lo + (long long)s * chunk;
@@ -333,6 +335,9 @@ __device__ void producer(const Plan& P, Smem& sm, char* ring, long long pos) {
 // Consumers
 // ---------------------------------------------------------------------------
 
+// GL: the plan has global-attention layers (G projection, GQA items, gap);
+// the kernel without them keeps the smaller code of the S/L path.
+template <bool GL>
 struct Cons {
   const Plan& P;
   Smem& sm;
@@ -446,7 +451,7 @@ struct Cons {
       consumers_sync();
       return;
     }
-    if (ph.in_mode == IN_RMS_E) {
+    if (GL && ph.in_mode == IN_RMS_E) {
       // G: v = rms(x)·w (+ rms(e0)·w_e), as two normalisations and one add.
       const bool own = tid < n4;
       float4 x = make_float4(0.f, 0.f, 0.f, 0.f), e = x, w = x, we = x;
@@ -693,7 +698,7 @@ struct Cons {
 
   __device__ void epilogue(const Phase& ph, const Segment& sg, int o0, int o1, int item) {
     const int n = o1 - o0;
-    if (ph.out_mode == OUT_G) {
+    if (GL && ph.out_mode == OUT_G) {
       if (&sg == &ph.seg[0]) {  // q rows, scaled as the graph path does (k_g_post)
         const float f = ph.inv_log > 0.0f ? log1pf((float)pos) * ph.inv_log : 1.0f;
         for (int t = tid; t < n; t += 256) {
@@ -837,7 +842,7 @@ struct Cons {
       for (int e = 0; e < 8; e++) acc[g][e] = 0.0f;
     }
     long long a, b;
-    attn_slice(ph, pos, s, &a, &b);
+    attn_slice<GL>(ph, pos, s, &a, &b);
     unsigned long long c0 = P.trace && tid == 0 ? now_ns() : 0;
     for (long long t0 = a; t0 < b; t0 += kAttnTile) {
       const int n = (int)min((long long)kAttnTile, b - t0);
@@ -892,7 +897,7 @@ struct Cons {
       comp_ns += e0 - c0;
       ntiles++;
     }
-    if (ph.gap == 0 && s == ph.splits - 1 && warp == 0 && grp == 0) {
+    if ((!GL || ph.gap == 0) && s == ph.splits - 1 && warp == 0 && grp == 0) {
       // The step's own position, stored by the projection phase.
       const size_t slot = (size_t)(pos % ph.cap);
       const float* kr = ph.kc + ((size_t)c * ph.cap + slot) * kDH;
@@ -960,6 +965,10 @@ struct Cons {
   }
 
   __device__ void attn_item(const Phase& ph, int item) {
+    if (!GL) {
+      attn_item_t<1>(ph, item);
+      return;
+    }
     switch (ph.qg) {
       case 2: attn_item_t<2>(ph, item); break;
       case 3: attn_item_t<3>(ph, item); break;
@@ -1065,6 +1074,7 @@ struct Cons {
   }
 };
 
+template <bool GL>
 __global__ void __launch_bounds__(kThreads, 1) k_decode_mega(const __grid_constant__ Plan P) {
   extern __shared__ __align__(1024) char smem_raw[];
   Smem& sm = *reinterpret_cast<Smem*>(smem_raw);
@@ -1083,7 +1093,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_mega(const __grid_consta
     if (threadIdx.x == kConsumerWarps * 32) producer(P, sm, ring, pos);
     return;
   }
-  Cons c(P, sm, ring, pos);
+  Cons<GL> c(P, sm, ring, pos);
   c.run();
 }
 
@@ -1094,13 +1104,17 @@ static_assert(((sizeof(Smem) + 1023) / 1024) * 1024 + (size_t)kStages * kStageBy
               "decode kernel shared memory above the 227 KB an sm_100 CTA may use");
 
 void prepare() {
-  SLM_CUDA(cudaFuncSetAttribute(k_decode_mega, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_bytes()));
+  SLM_CUDA(
+      cudaFuncSetAttribute(k_decode_mega<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_bytes()));
+  SLM_CUDA(
+      cudaFuncSetAttribute(k_decode_mega<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_bytes()));
 }
 
 int blocks_per_sm() {
-  int n = 0;
-  SLM_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k_decode_mega, kThreads, smem_bytes()));
-  return n;
+  int a = 0, b = 0;
+  SLM_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&a, k_decode_mega<false>, kThreads, smem_bytes()));
+  SLM_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, k_decode_mega<true>, kThreads, smem_bytes()));
+  return a < b ? a : b;
 }
 
 void launch(const Plan& plan, int grid, cudaStream_t st) {
@@ -1114,7 +1128,10 @@ void launch(const Plan& plan, int grid, cudaStream_t st) {
   attr[0].val.cooperative = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  SLM_CUDA(cudaLaunchKernelEx(&cfg, k_decode_mega, plan));
+  if (plan.global)
+    SLM_CUDA(cudaLaunchKernelEx(&cfg, k_decode_mega<true>, plan));
+  else
+    SLM_CUDA(cudaLaunchKernelEx(&cfg, k_decode_mega<false>, plan));
 }
 
 }  // namespace mega

@@ -116,6 +116,7 @@ struct Plan {
   // Test hook: when set, the first grid barrier waits for one arrival more
   // than the grid has, so its bounded wait runs out (failure-path test).
   int test_stall;
+  int global;  // the plan has global-attention layers (selects the kernel built for them)
 };
 
 }  // namespace mega

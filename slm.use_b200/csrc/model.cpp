@@ -626,6 +626,7 @@ void build_plan(slm_session* se, bool refresh = false) {
   P.out_index = words + 8;
   se->argmax_dev = words + 12;
   P.argmax = se->argmax_dev;
+  P.global = (c.prelude + c.core + c.coda).find('G') != std::string::npos ? 1 : 0;
   P.arg_part = static_cast<unsigned long long*>(alloc_zero(se, logit_items * sizeof(unsigned long long)));
   P.next_id = se->ids_dev;
   P.err = se->ctx->err;
