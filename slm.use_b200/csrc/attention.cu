@@ -16,6 +16,8 @@
 //    tiles staged in shared memory.
 // The position of the first query comes from device memory, so the same
 // launch (and a CUDA graph holding it) serves every decode step.
+#include <algorithm>
+
 #include "common.cuh"
 #include "kernels.cuh"
 
@@ -533,7 +535,9 @@ int attn_splits(const AttnGeom& g, long long max_span) {
   long long ctas = (g.m <= 8 || g.dh > 128) ? (long long)g.heads * g.m
                   : g.dh == 64               ? (long long)g.heads * ((g.m + FQ - 1) / FQ)
                                              : (long long)g.heads * ((g.m + 15) / 16);
-  long long want = (2 * 148 + ctas - 1) / ctas;             // two CTAs per SM
+  // Two CTAs per SM.  The flash tiles hold exactly two per SM, so their
+  // count rounds down to one full wave instead of spilling into a second.
+  long long want = (g.m > 8 && g.dh == 64) ? std::max(1ll, (2 * 148) / ctas) : (2 * 148 + ctas - 1) / ctas;
   long long most = (max_span + 127) / 128;                 // at least 128 positions per slice
   long long n = want < most ? want : most;
   if (n < 1) n = 1;
