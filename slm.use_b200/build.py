@@ -23,13 +23,13 @@ NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 
 
 def _cutlass_includes() -> list[str]:
-    """CUTLASS/CuTe headers vendored in the image (flashinfer's copy), for gemm_tc.cu."""
+    """CUTLASS/CuTe headers vendored in the image (flashinfer's copy), for the gemm_*.cu kernels."""
     import site
     roots = [Path(p) / "flashinfer" / "data" / "cutlass" for p in site.getsitepackages()]
     for r in roots:
         if (r / "include" / "cutlass" / "cutlass.h").exists():
             return ["-I", str(r / "include"), "-I", str(r / "tools" / "util" / "include")]
-    raise RuntimeError("CUTLASS headers not found (flashinfer/data/cutlass); gemm_tc.cu needs them")
+    raise RuntimeError("CUTLASS headers not found (flashinfer/data/cutlass); the gemm_*.cu kernels need them")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC,-O3", "--expt-relaxed-constexpr",
          "-I", str(INCLUDE)]
@@ -49,7 +49,7 @@ def _compile(src: Path, force: bool, hdr: float) -> Path:
     if not force and obj.exists() and obj.stat().st_mtime >= max(src.stat().st_mtime, hdr):
         return obj
     lang = ["-x", "cu"]
-    extra = _cutlass_includes() if src.name == "gemm_tc.cu" else []
+    extra = _cutlass_includes() if src.name.startswith("gemm_") else []
     cmd = [NVCC, *ARCH, *FLAGS, *extra, *lang, "-c", str(src), "-o", str(obj)]
     r = subprocess.run(cmd, capture_output=True, text=True)
     if r.returncode != 0:

@@ -18,9 +18,11 @@ struct LinearArgs {
   const float* res = nullptr;  // EPI_ADD
   int ldres = 0;
   int epi = 0;
-  // Workspace for the tensor-core path (see tc_linear_workspace); may be null.
+  // Workspace for the tensor-core paths (see tc_linear_workspace); may be null.
   void* ws = nullptr;
   size_t ws_bytes = 0;
+  // The weights split into bf16 parts for the bf16x3 GEMM (gemm_bf16x3.cu), or null.
+  const void* wplanes = nullptr;
 };
 void linear(const LinearArgs& a, cudaStream_t st);
 // SIMT path for 8 < m ≤ 64 tokens (skinny.cu): STORE/ADD epilogues, cols % 32
@@ -29,6 +31,12 @@ void skinny_prepare();
 bool skinny_ok(const LinearArgs& a);
 size_t skinny_workspace(const LinearArgs& a);
 void skinny_linear(const LinearArgs& a, void* ws, cudaStream_t st);
+// bf16x3 tensor-core path for m > 64 with split weights (gemm_bf16x3.cu).
+size_t b3_planes_bytes(size_t rows, size_t cols);
+void b3_split_weights(const float* w, size_t rows, size_t cols, void* planes, cudaStream_t st);
+bool b3_linear_ok(const LinearArgs& a);
+size_t b3_linear_workspace(const LinearArgs& a);
+void b3_linear(const LinearArgs& a, void* ws, cudaStream_t st);
 // Tensor-core (sm100 FastFP32) path for m > 8, gemm_tc.cu.
 bool tc_linear_ok(const LinearArgs& a);
 size_t tc_linear_workspace(const LinearArgs& a);

@@ -263,6 +263,10 @@ void linear(const LinearArgs& a, cudaStream_t st) {
     skinny_linear(a, a.ws, st);
     return;
   }
+  if (b3_linear_ok(a) && b3_linear_workspace(a) <= a.ws_bytes) {
+    b3_linear(a, a.ws, st);
+    return;
+  }
   if (a.m > 64 && tc_linear_ok(a)) {
     const size_t need = tc_linear_workspace(a);
     if (need <= a.ws_bytes) {

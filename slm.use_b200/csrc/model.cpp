@@ -35,6 +35,7 @@ constexpr size_t G_CAP0 = 1u << 13;      // first global cache capacity, src/mod
 struct Mat {
   const float* w = nullptr;
   size_t rows = 0, cols = 0;
+  const void* planes = nullptr;  // bf16 parts for chunk linears (gemm_bf16x3.cu), in the model's plane arena
 };
 
 struct Block {
@@ -62,6 +63,7 @@ struct slm_model {
   slm_ctx* ctx = nullptr;
   Config cfg;
   float* arena = nullptr;
+  void* planes = nullptr;  // bf16x3 parts of the block and inject matrices
   std::vector<Block> prelude, core, coda;
   Mat embed, inject, loop_embed;
   bool looped = false;
@@ -310,6 +312,7 @@ void run_linear(cudaStream_t s, const Mat& w, const float* x, int ldx, int m, fl
   a.res = res;
   a.ldres = ldres;
   a.epi = epi;
+  a.wplanes = w.planes;
   if (g_ctx_for_linear) gemm_workspace(g_ctx_for_linear, a, g_capturing);
   linear(a, s);
 }
@@ -828,7 +831,7 @@ void batch_workspace(slm_batch* bt) {
   const int m = (int)bt->n, d = (int)c.d;
   auto one = [&](const Mat& w, int ldx, int ldy, int epi, size_t rows = 0) {
     LinearArgs a;
-    a.w = w.w, a.rows = (int)(rows ? rows : w.rows), a.cols = (int)w.cols, a.m = m;
+    a.w = w.w, a.rows = (int)(rows ? rows : w.rows), a.cols = (int)w.cols, a.m = m, a.wplanes = w.planes;
     a.x = bt->nb, a.ldx = ldx, a.y = bt->upbuf, a.ldy = ldy, a.epi = epi;
     a.res = epi == EPI_ADD ? bt->upbuf : nullptr, a.ldres = epi == EPI_ADD ? ldy : 0;
     gemm_workspace(bt->ctx, a, false);
@@ -977,6 +980,26 @@ int slm_model_load(slm_ctx* ctx, const char* dir, slm_model** out) {
     p += mat_params(md->embed) + c.d + mat_params(md->inject) + mat_params(md->loop_embed);
     md->params = p;
     md->mix_cols = std::max({3 * c.d, 4 * c.d, 2 * c.kv_heads * dh});
+    // bf16x3 parts of every matrix a prefill chunk multiplies (all but the
+    // tied head, which only ever sees the last token).
+    std::vector<Mat*> mats;
+    for (auto* bs : {&md->prelude, &md->core, &md->coda})
+      for (auto& b : *bs)
+        for (Mat* m : {&b.qkv, &b.o, &b.up, &b.down, &b.qkvg, &b.decay, &b.q, &b.kv})
+          if (m->w) mats.push_back(m);
+    if (md->inject.w) mats.push_back(&md->inject);
+    size_t total = 0;
+    for (Mat* m : mats) total += (b3_planes_bytes(m->rows, m->cols) + 255) / 256 * 256;
+    if (total) {
+      md->planes = dev_alloc(total);
+      char* at = static_cast<char*>(md->planes);
+      for (Mat* m : mats) {
+        b3_split_weights(m->w, m->rows, m->cols, at, ctx->stream);
+        m->planes = at;
+        at += (b3_planes_bytes(m->rows, m->cols) + 255) / 256 * 256;
+      }
+      SLM_CUDA(cudaStreamSynchronize(ctx->stream));
+    }
     *out = md.release();
   });
 }
@@ -987,6 +1010,7 @@ int slm_model_free(slm_model* md) {
     Device dev(md->ctx);
     cudaStreamSynchronize(md->ctx->stream);
     dev_free(md->arena);
+    dev_free(md->planes);
     delete md;
   });
 }
