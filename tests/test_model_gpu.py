@@ -125,6 +125,16 @@ def test_86m_shapes_match_oracle(slm, ctx, oracle, tmp_path_factory):
     compare(dev, ref, ids, 64, 4, 1e-3)
 
 
+def test_86m_shapes_full_chunks_match_oracle(slm, ctx, oracle, tmp_path_factory):
+    # 256-token chunks: the wide linears (qkv, qkvg, up) run as the bf16x3
+    # tensor-core GEMM, the 768-wide ones as the FastFP32 kernel.
+    folder = _synthetic(tmp_path_factory, "m86c", "BASE", window=128)
+    ids = np.random.default_rng(6).integers(0, 32000, 300)
+    dev = slm.Model(ctx, folder).session(2)
+    ref = oracle.Model(folder).session(2)
+    compare(dev, ref, ids, 256, 2, 1e-3)
+
+
 def test_errors_are_statuses(slm, ctx, tiny):
     se = tiny.session()
     with pytest.raises(slm.SlmError):
