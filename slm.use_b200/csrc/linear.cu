@@ -259,12 +259,12 @@ void linear(const LinearArgs& a, cudaStream_t st) {
     return;
   }
   if (a.epi == EPI_SILU) SLM_REQUIRE(a.rows % 2 == 0, "linear: silu pairing needs an even row count");
-  if (skinny_ok(a) && skinny_workspace(a) <= a.ws_bytes) {
-    skinny_linear(a, a.ws, st);
-    return;
-  }
   if (b3_linear_ok(a) && b3_linear_workspace(a) <= a.ws_bytes) {
     b3_linear(a, a.ws, st);
+    return;
+  }
+  if (skinny_ok(a) && skinny_workspace(a) <= a.ws_bytes) {
+    skinny_linear(a, a.ws, st);
     return;
   }
   if (a.m > 64 && tc_linear_ok(a)) {

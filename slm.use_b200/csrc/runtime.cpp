@@ -76,7 +76,7 @@ void* stage(slm_ctx* c, const void* host, size_t bytes) {
 }
 
 void gemm_workspace(slm_ctx* c, LinearArgs& a, bool capturing) {
-  const bool skinny = skinny_ok(a), b3 = !skinny && b3_linear_ok(a), tc = !skinny && !b3 && a.m > 64 && tc_linear_ok(a);
+  const bool b3 = b3_linear_ok(a), skinny = !b3 && skinny_ok(a), tc = !skinny && !b3 && a.m > 64 && tc_linear_ok(a);
   if (skinny || b3 || tc) {
     const size_t need = skinny ? skinny_workspace(a) : b3 ? b3_linear_workspace(a) : tc_linear_workspace(a);
     if (need > c->gemm_ws_bytes && !capturing) {
