@@ -56,7 +56,7 @@ ROOT = Path(__file__).resolve().parent
 MODEL_BYTES_NOTE = "inputs larger than L2: 640 MB of weights and KV read per token at R=4"
 # DRAM bytes (read + write) of one k_decode_mega launch from an ncu capture of
 # this bench (profiles/k_decode_mega_R4.md), by loop count.
-MEGA_TRAFFIC = {4: 652.9e6}
+MEGA_TRAFFIC = {4: 584.4e6}
 
 
 def load_pkg():
