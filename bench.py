@@ -274,6 +274,57 @@ def ref_cuda_measure(cases, device: int) -> dict | None:
 
 
 # ---------------------------------------------------------------------------
+# Device timeline of the persistent decode step (--trace)
+# ---------------------------------------------------------------------------
+
+def phase_kinds(cfg: dict, loops: int) -> list[str]:
+    """Phase names of the persistent step, in plan order (model.cpp build_plan)."""
+    names = {"S": ["S1", "attn", "o", "up", "down"], "L": ["L1", "gla", "o", "up", "down"],
+             "G": ["G1", "gattn", "o", "up", "down"]}
+    out = [n for k in cfg["prelude"] for n in names[k]]
+    if cfg["core"]:
+        out.append("inject")
+        out += [n for _ in range(loops) for k in cfg["core"] for n in names[k]]
+    out += [n for k in cfg["coda"] for n in names[k]]
+    return out + ["logits"]
+
+
+def write_trace(se, greedy, cfg: dict, loops: int, path: str) -> None:
+    """Three traced persistent steps; the last one's per-phase sums, grouped by
+    phase kind, as a markdown table (critical span = first CTA start to last
+    CTA arrival; gap = last arrival to the next phase's first start)."""
+    se.set_trace(True)
+    tok = int(se.sample(greedy))
+    for _ in range(3):
+        tok = int(se.decode(tok, 1, greedy)[0])
+    se.set_trace(False)
+    tr = se.trace().astype(np.int64)
+    kinds = phase_kinds(cfg, loops)
+    if len(kinds) != tr.shape[0]:
+        return
+    t0 = tr[0, :, 0].min()
+    st, en = tr[:, :, 0] - t0, tr[:, :, 1] - t0
+    rows: dict = {}
+    for p in range(tr.shape[0]):
+        gap = st[p + 1].min() - en[p].max() if p + 1 < tr.shape[0] else 0
+        r = rows.setdefault(kinds[p], [0, 0.0, 0.0, 0.0, 0.0, 0.0])
+        r[0] += 1
+        r[1] += en[p].max() - st[p].min()
+        r[2] += gap
+        r[3] += float(np.median(tr[p, :, 3]))
+        r[4] += float(np.median(tr[p, :, 4]))
+        r[5] += float(np.median(tr[p, :, 2]))
+    lines = [f"Total step (trace run): {en[-1].max() / 1000:.1f} us over {tr.shape[0]} phases", "",
+             "| phase kind | count | critical span µs (sum) | barrier gap µs (sum) | input prologue µs (median, sum)"
+             " | tile work µs (median, sum) | tile waits µs (median, sum) |", "|---|---|---|---|---|---|---|"]
+    for k, r in sorted(rows.items(), key=lambda kv: -kv[1][1]):
+        lines.append(f"| {k} | {r[0]} | {r[1] / 1000:.1f} | {r[2] / 1000:.1f} | {r[3] / 1000:.1f} | "
+                     f"{r[4] / 1000:.1f} | {r[5] / 1000:.1f} |")
+    Path(path).parent.mkdir(parents=True, exist_ok=True)
+    Path(path).write_text("\n".join(lines) + "\n")
+
+
+# ---------------------------------------------------------------------------
 # The B200 arm
 # ---------------------------------------------------------------------------
 
@@ -470,6 +521,9 @@ def run_b200(args, rank: int, world: int, local: int) -> dict | None:
         for sq in sessions:
             sq.close()
 
+    if args.trace and se.mega:
+        write_trace(se, greedy, cfg, args.loops, args.trace)
+
     step_kernels = se.step_kernels
     res = {"dec_ms": dec_ms, "e2e_s": e2e_s, "prefill_ms": prefill_ms, "prefill_host_s": prefill_host_s,
            "gemv_us": gemv_us, "clocks": clocks.summary(), "extra": extra, "step_kernels": step_kernels,
@@ -492,6 +546,7 @@ def main():
     ap.add_argument("--quick", action="store_true", help="skip the R=8/16 lines")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
     ap.add_argument("--no-ref-cuda", action="store_true", help="skip the reference CUDA baseline")
+    ap.add_argument("--trace", default="", help="write the persistent step's phase timeline (markdown) here")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 

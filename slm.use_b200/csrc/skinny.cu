@@ -1,6 +1,8 @@
 // Linears with a few token rows (8 < m ≤ 64: a batched decode step of
-// independent sessions, short prompt chunks): y[i] = W·x[i] (+ residual),
-// the reference's Ops::linear (src/ops.rs:118, src/cpu.rs:111-130) in fp32.
+// independent sessions, short prompt chunks) and the narrow outputs of full
+// prefill chunks (m ≤ 256, tiled 64 tokens at a time): y[i] = W·x[i]
+// (+ residual), the reference's Ops::linear (src/ops.rs:118,
+// src/cpu.rs:111-130) in fp32.
 //
 // At these sizes the weights (one read per call) and the launch dominate,
 // and a tensor-core tile pipeline sits mostly idle, so this is a SIMT kernel
@@ -28,6 +30,9 @@ constexpr int LD = KT + 4;
 #define SLM_SKINNY_STAGES 4
 #endif
 constexpr int STAGES = SLM_SKINNY_STAGES;
+#ifndef SLM_SKINNY_MAX_M
+#define SLM_SKINNY_MAX_M 64  // token rows (above 64 in tiles of 64; 256-token chunks measured faster on FastFP32)
+#endif
 
 template <int TT>
 constexpr size_t smem_bytes() {
@@ -44,8 +49,8 @@ __device__ __forceinline__ void wait_group() {
   asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
-// grid (ceil(rows/64), slices); 128 threads.  Thread t: rows 4·(t%16) …,
-// tokens (TT/8)·(t/16) ….
+// grid (ceil(rows/64), slices, ceil(m/TT)); 128 threads.  Thread t: rows
+// 4·(t%16) …, tokens z·TT + (TT/8)·(t/16) ….
 template <int TT, int EPI>
 __global__ void __launch_bounds__(128)
     k_skinny(const float* __restrict__ w, int rows, int cols, const float* __restrict__ x, int ldx, int m, int kper,
@@ -55,7 +60,7 @@ __global__ void __launch_bounds__(128)
   float (*Ws)[RT][LD] = reinterpret_cast<float (*)[RT][LD]>(smem);
   float (*Xs)[TT][LD] = reinterpret_cast<float (*)[TT][LD]>(smem + (size_t)STAGES * RT * LD);
   const int t = threadIdx.x, tr = t % 16, tt = t / 16;
-  const int r0 = blockIdx.x * RT, s = blockIdx.y;
+  const int r0 = blockIdx.x * RT, s = blockIdx.y, i0 = blockIdx.z * TT;
   const int k0 = s * kper, k1 = min(cols, k0 + kper);
   const int stages = (k1 - k0) / KT;
 
@@ -68,8 +73,8 @@ __global__ void __launch_bounds__(128)
     }
     for (int e = t; e < TT * (KT / 4); e += 128) {
       const int i = e / (KT / 4), c = (e % (KT / 4)) * 4;
-      const bool ok = i < m;
-      cp16z(&Xs[buf][i][c], x + (size_t)(ok ? i : 0) * ldx + kb + c, ok);
+      const bool ok = i0 + i < m;
+      cp16z(&Xs[buf][i][c], x + (size_t)(ok ? i0 + i : 0) * ldx + kb + c, ok);
     }
   };
 
@@ -116,7 +121,7 @@ __global__ void __launch_bounds__(128)
   if (!part) {
 #pragma unroll
     for (int u = 0; u < TPT; u++) {
-      const int i = TPT * tt + u;
+      const int i = i0 + TPT * tt + u;
 #pragma unroll
       for (int j = 0; j < 4; j++) {
         const int r = r0 + 4 * tr + j;
@@ -127,7 +132,7 @@ __global__ void __launch_bounds__(128)
   }
 #pragma unroll
   for (int u = 0; u < TPT; u++) {
-    const int i = TPT * tt + u;
+    const int i = i0 + TPT * tt + u;
 #pragma unroll
     for (int j = 0; j < 4; j++) {
       const int r = r0 + 4 * tr + j;
@@ -161,7 +166,7 @@ int sm_count() {
 
 // K per slice (a multiple of KT) and the slice count.
 void plan(const LinearArgs& a, int* kper, int* slices) {
-  const int tiles = (a.rows + RT - 1) / RT, kt = a.cols / KT;
+  const int tiles = (a.rows + RT - 1) / RT * ((a.m + 63) / 64), kt = a.cols / KT;
   int want = (2 * sm_count() + tiles - 1) / tiles;
   want = std::max(1, std::min(want, kt));
   const int per = (kt + want - 1) / want;
@@ -171,7 +176,7 @@ void plan(const LinearArgs& a, int* kper, int* slices) {
 
 template <int TT, int EPI>
 void launch(const LinearArgs& a, int kper, int slices, float* part, cudaStream_t st) {
-  dim3 grid((a.rows + RT - 1) / RT, slices);
+  dim3 grid((a.rows + RT - 1) / RT, slices, (a.m + TT - 1) / TT);
   k_skinny<TT, EPI><<<grid, 128, smem_bytes<TT>(), st>>>(a.w, a.rows, a.cols, a.x, a.ldx, a.m, kper, a.y, a.ldy,
                                                           a.res, a.ldres, part);
   SLM_LAUNCHED("k_skinny");
@@ -194,7 +199,8 @@ void skinny_prepare() {
 
 bool skinny_ok(const LinearArgs& a) {
   auto al = [](const void* p) { return ((uintptr_t)p & 15) == 0; };
-  return a.m > 8 && a.m <= 64 && (a.epi == EPI_STORE || a.epi == EPI_ADD) && a.cols % KT == 0 && a.ldx % 4 == 0 &&
+  return a.m > 8 && a.m <= SLM_SKINNY_MAX_M && (a.epi == EPI_STORE || a.epi == EPI_ADD) && a.cols % KT == 0 &&
+         a.ldx % 4 == 0 &&
          al(a.w) && al(a.x);
 }
 
