@@ -43,6 +43,7 @@ import argparse
 import hashlib
 import importlib.util
 import json
+import math
 import os
 import statistics
 import subprocess
@@ -113,6 +114,21 @@ def decode_bytes(cfg: dict, loops: int) -> dict:
     kv = n_s * 2 * h * w * dh * 4
     gla = n_l * 2 * h * dh * dh * 4
     return {"weights": weights, "kv": kv, "gla_state": gla, "total": weights + kv + gla}
+
+
+def prefill_flops(cfg: dict, loops: int, n: int) -> float:
+    """Algorithmic fp32 flops of reading an n-token prompt (S | LS | S layouts):
+    the linears of every token, attention over each token's window, the GLA
+    recurrence, and the logits of the last token."""
+    d, h, f, v, w = cfg["d_model"], cfg["n_heads"], cfg["hidden"], cfg["vocab_size"], cfg["window"]
+    dh = d // h
+    s_lin = 3 * d * d + d * d + 2 * f * d + f * d
+    l_lin = 4 * d * d + h * d + d * d + 2 * f * d + f * d
+    n_s = cfg["prelude"].count("S") + cfg["coda"].count("S") + loops * cfg["core"].count("S")
+    n_l = loops * cfg["core"].count("L")
+    lin = n_s * s_lin + n_l * l_lin + (d * d if cfg["core"] else 0)
+    spans = sum(min(p + 1, w) for p in range(n))
+    return 2.0 * lin * n + n_s * 4.0 * d * spans + n_l * 4.0 * h * dh * dh * n + 2.0 * v * d
 
 
 # ---------------------------------------------------------------------------
@@ -426,6 +442,33 @@ def run_b200(args, rank: int, world: int, local: int) -> dict | None:
         for mbuf in mats:
             mbuf.close()
 
+        # Decode attention on its own (the m = 1 op, k_attn_split + combine):
+        # one query per head over a full window of a 4352-slot ring; six
+        # caches rotate (160 MB) so each call streams its K/V from HBM.
+        H, dh = cfg["n_heads"], cfg["d_model"] // cfg["n_heads"]
+        W, cap = cfg["window"], cfg["window"] + 256
+        rng = np.random.default_rng(5)
+        caches = [(ops.upload(rng.standard_normal(H * cap * dh, dtype=np.float32)),
+                   ops.upload(rng.standard_normal(H * cap * dh, dtype=np.float32))) for _ in range(6)]
+        qa, ya, sa = ops.upload(np.ones(H * dh, dtype=np.float32)), ops.zeros(H * dh), ops.zeros(1)
+
+        def attend(i):
+            ops.attend(ya, sa, qa, caches[i % 6][0], caches[i % 6][1], pos=cap + 100, m=1, reach=W, gap=0, cap=cap,
+                       heads=H, key_heads=H, dh=dh, scale=1.0 / math.sqrt(dh))
+
+        for i in range(6):
+            attend(i)
+        a, b = events()
+        a.record(stream)
+        for i in range(36):
+            attend(i)
+        b.record(stream)
+        torch.cuda.synchronize(dev)
+        attn_us = a.elapsed_time(b) * 1000.0 / 36
+        for kb, vb in caches:
+            kb.close()
+            vb.close()
+
     extra = {}
     if not args.quick:
         c3 = slm.Sampling(temperature=0.8, top_k=40, repeat_penalty=1.1, repeat_window=256)
@@ -526,7 +569,7 @@ def run_b200(args, rank: int, world: int, local: int) -> dict | None:
 
     step_kernels = se.step_kernels
     res = {"dec_ms": dec_ms, "e2e_s": e2e_s, "prefill_ms": prefill_ms, "prefill_host_s": prefill_host_s,
-           "gemv_us": gemv_us, "clocks": clocks.summary(), "extra": extra, "step_kernels": step_kernels,
+           "gemv_us": gemv_us, "attn_us": attn_us, "clocks": clocks.summary(), "extra": extra, "step_kernels": step_kernels,
            "device": ctx.name, "state_bytes": se.state_bytes()}
     res["dec_ms"], res["e2e_s"], res["prefill_ms"] = max_over_ranks([dec_ms, e2e_s, prefill_ms], dist, dev)
     se.close()
@@ -620,6 +663,9 @@ def main():
     gemv_bytes = (cfg["vocab_size"] * cfg["d_model"] + cfg["d_model"] + cfg["vocab_size"]) * 4
     gemv_gbs = gemv_bytes / (res["gemv_us"] * 1e-6) / 1e9
     step_gbs = byts["total"] / (res["dec_ms"] / 1000.0 / K) / 1e9
+    H, dh = cfg["n_heads"], cfg["d_model"] // cfg["n_heads"]
+    attn_gbs = (2 * H * cfg["window"] * dh * 4 + 2 * H * dh * 4) / (res["attn_us"] * 1e-6) / 1e9
+    pre_flops = prefill_flops(cfg, args.loops, args.prompt)
     line = {
         "metric": f"decode tok/s, R={args.loops}, 4096 ctx full", "value": value, "unit": "tok/s",
         "n_gpus": world, "steps": K, "warmup": args.warmup, "ms_per_step": res["dec_ms"] / K,
@@ -629,7 +675,9 @@ def main():
                 "d2h_bytes_per_step": 16,
                 "how": "per token slm_step(host id) + slm_sample -> host id, host clock"},
         "prefill": {"value": world * args.prompt / (res["prefill_ms"] / 1000.0), "unit": "tok/s",
-                    "e2e_value": world * args.prompt / res["prefill_host_s"], "prompt": args.prompt},
+                    "e2e_value": world * args.prompt / res["prefill_host_s"], "prompt": args.prompt,
+                    "tflops_fp32": pre_flops / (res["prefill_ms"] / 1000.0) / 1e12,
+                    "flops_per_token": pre_flops / args.prompt},
         # The m = 1 step is one persistent kernel (k_decode_mega), so its
         # average launch duration is the decode time per token (CUDA events
         # over the K launches; inter-launch gaps included).
@@ -638,7 +686,10 @@ def main():
                      "bytes_per_launch": byts["total"], "traffic": MEGA_TRAFFIC.get(args.loops),
                      "peak_source": peak_src,
                      "gemv": {"kernel": "k_gemv<1,STORE> (32000x768 fp32, m=1)", "achieved": gemv_gbs,
-                              "frac": gemv_gbs / hbm}},
+                              "frac": gemv_gbs / hbm},
+                     "attention": {"kernel": "k_attn_split + k_attn_combine (m=1, 12 heads x 4096 positions of a "
+                                             "4352-slot ring, K and V from HBM)",
+                                   "achieved": attn_gbs, "frac": attn_gbs / hbm}},
         "clocks": res["clocks"],
         "gpu_launches": K * (res["step_kernels"] + 1),
         "extra": res["extra"],
