@@ -305,16 +305,33 @@ def phase_kinds(cfg: dict, loops: int) -> list[str]:
     return out + ["logits"]
 
 
-def write_trace(se, greedy, cfg: dict, loops: int, path: str) -> None:
-    """Three traced persistent steps; the last one's per-phase sums, grouped by
-    phase kind, as a markdown table (critical span = first CTA start to last
-    CTA arrival; gap = last arrival to the next phase's first start)."""
+def traced_step(se, greedy) -> np.ndarray:
+    """Three traced persistent steps; the last one's timeline [phase][cta][8]."""
     se.set_trace(True)
     tok = int(se.sample(greedy))
     for _ in range(3):
         tok = int(se.decode(tok, 1, greedy)[0])
     se.set_trace(False)
-    tr = se.trace().astype(np.int64)
+    return se.trace().astype(np.int64)
+
+
+def attention_phases(tr: np.ndarray, cfg: dict, loops: int) -> dict | None:
+    """The persistent step's window-attention phases at a full window: their
+    K/V bytes over their critical spans (first CTA start to last arrival)."""
+    kinds = phase_kinds(cfg, loops)
+    if len(kinds) != tr.shape[0]:
+        return None
+    spans = [int(tr[p, :, 1].max() - tr[p, :, 0].min()) for p in range(tr.shape[0]) if kinds[p] == "attn"]
+    h, dh = cfg["n_heads"], cfg["d_model"] // cfg["n_heads"]
+    per = 2 * h * cfg["window"] * dh * 4
+    return {"phases": len(spans), "bytes_per_phase": per, "us_per_phase": sum(spans) / len(spans) / 1000.0,
+            "achieved": per * len(spans) / (sum(spans) * 1e-9) / 1e9}
+
+
+def write_trace(tr: np.ndarray, cfg: dict, loops: int, path: str) -> None:
+    """Per-phase sums of a traced step, grouped by phase kind, as a markdown
+    table (critical span = first CTA start to last CTA arrival; gap = last
+    arrival to the next phase's first start)."""
     kinds = phase_kinds(cfg, loops)
     if len(kinds) != tr.shape[0]:
         return
@@ -564,12 +581,16 @@ def run_b200(args, rank: int, world: int, local: int) -> dict | None:
         for sq in sessions:
             sq.close()
 
-    if args.trace and se.mega:
-        write_trace(se, greedy, cfg, args.loops, args.trace)
+    attn_phase = None
+    if se.mega:
+        tr = traced_step(se, greedy)
+        attn_phase = attention_phases(tr, cfg, args.loops)
+        if args.trace:
+            write_trace(tr, cfg, args.loops, args.trace)
 
     step_kernels = se.step_kernels
     res = {"dec_ms": dec_ms, "e2e_s": e2e_s, "prefill_ms": prefill_ms, "prefill_host_s": prefill_host_s,
-           "gemv_us": gemv_us, "attn_us": attn_us, "clocks": clocks.summary(), "extra": extra, "step_kernels": step_kernels,
+           "gemv_us": gemv_us, "attn_us": attn_us, "attn_phase": attn_phase, "clocks": clocks.summary(), "extra": extra, "step_kernels": step_kernels,
            "device": ctx.name, "state_bytes": se.state_bytes()}
     res["dec_ms"], res["e2e_s"], res["prefill_ms"] = max_over_ranks([dec_ms, e2e_s, prefill_ms], dist, dev)
     se.close()
@@ -696,6 +717,13 @@ def main():
         "device": res["device"],
         "state_mib": res["state_bytes"] / 2**20,
     }
+    if res.get("attn_phase"):
+        ap = res["attn_phase"]
+        line["roofline"]["attention_in_step"] = {
+            "kernel": "k_decode_mega window-attention phases (12 heads x 4096 positions, 12 splits per head)",
+            "achieved": ap["achieved"], "frac": ap["achieved"] / hbm, "us_per_phase": ap["us_per_phase"],
+            "bytes_per_phase": ap["bytes_per_phase"], "how": "globaltimer trace of one step (first start to last "
+            "arrival of each attention phase)"}
     if cpu:
         line["cpu_baseline"] = {"value": cpu["decode_tok_s"], "unit": "tok/s", "cores": cpu["cores"], "kind": "port",
                                 "sample": cpu["sample"], "prefill_tok_s": cpu["prefill_tok_s"]}

@@ -476,26 +476,58 @@ __global__ void __launch_bounds__(256, 2)
 }
 
 // Merge the slices: y[i][h] = Σ_s e^{m_s - M} acc_s / Σ_s e^{m_s - M} l_s.
-// grid m·heads, block 32·ceil(dh/32).
-__global__ void k_attn_combine(const float* __restrict__ part, int nsplit, int m, int heads, int dh,
-                               float* __restrict__ y, int ldy) {
-  int pair = blockIdx.x, i = pair / heads, h = pair % heads, e = threadIdx.x;
-  size_t stride = (size_t)m * heads * (dh + 2);
+// grid m·heads, 256 threads: the slices are spread over the threads (max and
+// weighted sums as block reductions), so the merge costs a few L2 round trips
+// whatever the split count.  Slices combine in a fixed order per thread and
+// a fixed tree across threads.
+__global__ void __launch_bounds__(256) k_attn_combine(const float* __restrict__ part, int nsplit, int m, int heads,
+                                                      int dh, float* __restrict__ y, int ldy) {
+  __shared__ float red[8], cw[256];
+  __shared__ float acc_sh[4][256 + 4];
+  const int pair = blockIdx.x, i = pair / heads, h = pair % heads, t = threadIdx.x;
+  const int lane = t & 31, warp = t >> 5;
+  const size_t stride = (size_t)m * heads * (dh + 2);
   const float* p0 = part + ((size_t)i * heads + h) * (dh + 2);
-  float M = -INFINITY;
-  for (int s = 0; s < nsplit; s++) M = fmaxf(M, p0[s * stride + dh]);
-  float L = 0.0f, a = 0.0f;
-  if (M != -INFINITY) {
-    for (int s = 0; s < nsplit; s++) {
-      const float* ps = p0 + s * stride;
-      float ms = ps[dh];
-      if (ms == -INFINITY) continue;
-      float c = expf(ms - M);
-      L += ps[dh + 1] * c;
-      if (e < dh) a += ps[e] * c;
-    }
+  // 1. M = max_s m_s.
+  float mx = -INFINITY;
+  for (int s = t; s < nsplit; s += 256) mx = fmaxf(mx, p0[s * stride + dh]);
+  mx = warp_max(mx);
+  if (lane == 0) red[warp] = mx;
+  __syncthreads();
+  float M = red[0];
+  for (int w = 1; w < 8; w++) M = fmaxf(M, red[w]);
+  __syncthreads();
+  // 2. c_s = e^{m_s - M} (kept per split), L = Σ c_s l_s.
+  float lsum = 0.0f;
+  for (int s = t; s < nsplit; s += 256) {
+    const float ms = p0[s * stride + dh];
+    const float c = (M == -INFINITY || ms == -INFINITY) ? 0.0f : expf(ms - M);
+    if (s < 256) cw[s] = c;
+    lsum += p0[s * stride + dh + 1] * c;
   }
-  if (e < dh) y[(size_t)i * ldy + (size_t)h * dh + e] = L > 0.0f ? a / L : 0.0f;
+  lsum = warp_sum(lsum);
+  if (lane == 0) red[warp] = lsum;
+  __syncthreads();
+  float L = 0.0f;
+  for (int w = 0; w < 8; w++) L += red[w];
+  // 3. Σ_s c_s acc_s[e]: thread (q, e) takes the splits q, q + Q, … for dim e.
+  const int Q = 256 / dh >= 1 ? (256 / dh > 4 ? 4 : 256 / dh) : 1;
+  const int q = t / dh, e = t % dh;
+  float a = 0.0f;
+  if (q < Q && dh <= 256)
+    for (int s = q; s < nsplit; s += Q) {
+      const float c = s < 256 ? cw[s] : ((M == -INFINITY || p0[s * stride + dh] == -INFINITY)
+                                             ? 0.0f
+                                             : expf(p0[s * stride + dh] - M));
+      a = fmaf(p0[s * stride + e], c, a);
+    }
+  if (q < Q) acc_sh[q][e] = a;
+  __syncthreads();
+  for (int d = t; d < dh; d += 256) {
+    float v = 0.0f;
+    for (int qq = 0; qq < Q; qq++) v += acc_sh[qq][d];
+    y[(size_t)i * ldy + (size_t)h * dh + d] = L > 0.0f ? v / L : 0.0f;
+  }
 }
 
 template <int DH>
@@ -535,10 +567,11 @@ int attn_splits(const AttnGeom& g, long long max_span) {
   long long ctas = (g.m <= 8 || g.dh > 128) ? (long long)g.heads * g.m
                   : g.dh == 64               ? (long long)g.heads * ((g.m + FQ - 1) / FQ)
                                              : (long long)g.heads * ((g.m + 15) / 16);
-  // Two CTAs per SM.  The flash tiles hold exactly two per SM, so their
-  // count rounds down to one full wave instead of spilling into a second.
+  // Two CTAs per SM (more splits measured slower: per-slice set-up and the
+  // merge outweigh the extra loads in flight).  The flash tiles hold exactly
+  // two per SM, so their count rounds down to one full wave.
   long long want = (g.m > 8 && g.dh == 64) ? std::max(1ll, (2 * 148) / ctas) : (2 * 148 + ctas - 1) / ctas;
-  long long most = (max_span + 127) / 128;                 // at least 128 positions per slice
+  long long most = (max_span + 127) / 128;  // at least 128 positions per slice
   long long n = want < most ? want : most;
   if (n < 1) n = 1;
   if (n > 256) n = 256;
@@ -560,7 +593,7 @@ void attention(const float* q, int ldq, const float* K, const float* V, const At
     case 256: launch_dh<256>(q, ldq, K, V, g, pos_ptr, nsplit, part, st); break;
     default: fail(SLM_ERR_INVALID, "attend: head size must be one of 8, 16, 32, 64, 128, 256");
   }
-  k_attn_combine<<<g.m * g.heads, 32 * cdiv(g.dh, 32), 0, st>>>(part, nsplit, g.m, g.heads, g.dh, y, ldy);
+  k_attn_combine<<<g.m * g.heads, 256, 0, st>>>(part, nsplit, g.m, g.heads, g.dh, y, ldy);
   SLM_LAUNCHED("k_attn_combine");
 }
 
@@ -579,7 +612,7 @@ void attention_rows(const float* q, int ldq, const AttnRows& rows, const AttnGeo
     default: fail(SLM_ERR_INVALID, "attend: head size must be one of 8, 16, 32, 64, 128, 256");
   }
   SLM_LAUNCHED("k_attn_split");
-  k_attn_combine<<<g.m * g.heads, 32 * cdiv(g.dh, 32), 0, st>>>(part, nsplit, g.m, g.heads, g.dh, y, ldy);
+  k_attn_combine<<<g.m * g.heads, 256, 0, st>>>(part, nsplit, g.m, g.heads, g.dh, y, ldy);
   SLM_LAUNCHED("k_attn_combine");
 }
 
