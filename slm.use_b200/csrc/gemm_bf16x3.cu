@@ -10,7 +10,7 @@
 //   A = [x0 | x1 | x2 | x0 | x1 | x0]   (m × 6K, split per call, bf16)
 //   B = [w0 | w0 | w0 | w1 | w1 | w2]   (N × 6K, split once at model load)
 // so one plain bf16 GEMM with fp32 accumulation computes the sum: a CUTLASS
-// sm100 kernel (TMA loads, tcgen05.mma into TMEM, stream-K) whose epilogue
+// sm100 kernel (TMA loads, tcgen05.mma into TMEM, 128 × 64 tiles, stream-K) whose epilogue
 // adds the residual (β = 1) for the block's x += h.
 #include "cutlass/cutlass.h"
 #include "cute/tensor.hpp"
@@ -47,7 +47,7 @@ constexpr int kAlignCD = 4;  // 16 bytes of fp32
 using ArchTag = cutlass::arch::Sm100;
 using OpClass = cutlass::arch::OpClassTensorOp;
 #ifndef SLM_B3_TILE_N
-#define SLM_B3_TILE_N 128
+#define SLM_B3_TILE_N 64  // 128 × 64 output tiles: twice the CTAs of 128 × 128, measured 4% faster on prefill
 #endif
 using TileShape = Shape<_128, Int<SLM_B3_TILE_N>, _64>;
 using ClusterShape = Shape<_1, _1, _1>;  // no cluster: plain (non-multicast) TMA loads
