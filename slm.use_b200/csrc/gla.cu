@@ -112,6 +112,11 @@ __global__ void __launch_bounds__(GlaShape<DH>::T)
 // head_norm + gate (which need a whole head) follow in k_gla_norm.
 // ---------------------------------------------------------------------------
 
+#ifndef SLM_GLA_UNROLL
+#define SLM_GLA_UNROLL 4
+#endif
+constexpr int kGlaUnroll = SLM_GLA_UNROLL;
+
 template <int DH>
 struct GlaCols {
   static constexpr int CG = 8, RQ = 4, R = DH / RQ, C4 = R / 4, T = CG * RQ;
@@ -173,6 +178,9 @@ __global__ void __launch_bounds__(GlaCols<DH>::T)
       cp_wait<0>();
     }
     __syncthreads();
+    // Only col[] carries from token to token: unrolled, the next tokens'
+    // loads and y sums overlap this one's update.
+#pragma unroll kGlaUnroll
     for (int i = 0; i < n; i++) {
       const float d = ds[buf][i], vb = vs[buf][i][b];
       const float4* q4 = reinterpret_cast<const float4*>(qs[buf][i]);
