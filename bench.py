@@ -88,12 +88,24 @@ def max_over_ranks(values, dist=None, device=None):
 
 
 def model_dir(cfg: dict, seed: int) -> Path:
+    """The synthetic model for (cfg, seed), written once.  Each process writes
+    into its own temporary folder and publishes it with an atomic rename, so
+    ranks that start together never read a half-written file."""
+    import shutil
+
     import slm_b200.synthetic as syn  # noqa: F401  (package registered by load_pkg)
     tag = hashlib.sha1(json.dumps([cfg, seed], sort_keys=True).encode()).hexdigest()[:12]
-    folder = Path(os.environ.get("SLM_BENCH_DIR", "/tmp/slm_b200_bench")) / tag
-    if not (folder / "done").exists():
-        syn.write_model(folder, cfg, seed)
-        (folder / "done").write_text("ok")
+    root = Path(os.environ.get("SLM_BENCH_DIR", str(ROOT / "_bench_models")))
+    folder = root / tag
+    if (folder / "done").exists():
+        return folder
+    tmp = root / f".{tag}.{os.getpid()}"
+    syn.write_model(tmp, cfg, seed)
+    (tmp / "done").write_text("ok")
+    try:
+        os.rename(tmp, folder)
+    except OSError:  # another process published it first
+        shutil.rmtree(tmp, ignore_errors=True)
     return folder
 
 
