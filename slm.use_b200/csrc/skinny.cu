@@ -199,7 +199,10 @@ void skinny_prepare() {
 
 bool skinny_ok(const LinearArgs& a) {
   auto al = [](const void* p) { return ((uintptr_t)p & 15) == 0; };
-  return a.m > 8 && a.m <= SLM_SKINNY_MAX_M && (a.epi == EPI_STORE || a.epi == EPI_ADD) && a.cols % KT == 0 &&
+  // Outputs of at most 128 rows (the GLA decay) take it for whole chunks too:
+  // a tensor-core GEMM launch costs ~20 µs for almost no work there.
+  const int max_m = a.rows <= 128 ? 256 : SLM_SKINNY_MAX_M;
+  return a.m > 8 && a.m <= max_m && (a.epi == EPI_STORE || a.epi == EPI_ADD) && a.cols % KT == 0 &&
          a.ldx % 4 == 0 &&
          al(a.w) && al(a.x);
 }
