@@ -103,6 +103,28 @@ __global__ void k_split_x(const float* __restrict__ x, int ldx, size_t m, size_t
   }
 }
 
+// RMSNorm of each group (src/cpu.rs:187-207, as k_rms) that also writes the
+// bf16x3 planes of its output, the A operand of the wide linears that read it.
+__global__ void k_rms_split(float* __restrict__ y, __nv_bfloat16* __restrict__ planes, const float* __restrict__ x,
+                            const float* __restrict__ w, size_t size, float eps) {
+  __shared__ float red[32];
+  const float* in = x + (size_t)blockIdx.x * size;
+  float s = 0.0f;
+  for (size_t e = threadIdx.x; e < size; e += blockDim.x) s = fmaf(in[e], in[e], s);
+  s = block_sum(s, red);
+  const float r = 1.0f / sqrtf(s / (float)size + eps);
+  float* out = y + (size_t)blockIdx.x * size;
+  __nv_bfloat16* o = planes + (size_t)blockIdx.x * 6 * size;
+  for (size_t e = threadIdx.x; e < size; e += blockDim.x) {
+    const float v = in[e] * r * w[e];
+    out[e] = v;
+    __nv_bfloat16 p[3];
+    split3(v, p);
+    o[e] = p[0], o[size + e] = p[1], o[2 * size + e] = p[2], o[3 * size + e] = p[0], o[4 * size + e] = p[1],
+    o[5 * size + e] = p[0];
+  }
+}
+
 typename Gemm::Arguments make_args(const LinearArgs& a, const void* aplanes) {
   const int K6 = 6 * a.cols;
   const float beta = a.epi == EPI_ADD ? 1.0f : 0.0f;
@@ -151,12 +173,23 @@ size_t b3_linear_workspace(const LinearArgs& a) {
   return planes + Gemm::get_workspace_size(make_args(a, nullptr));
 }
 
+void b3_rms_split(float* y, void* planes, const float* x, const float* w, size_t groups, size_t size, float eps,
+                  cudaStream_t st) {
+  if (!groups) return;
+  k_rms_split<<<(unsigned)groups, 256, 0, st>>>(y, static_cast<__nv_bfloat16*>(planes), x, w, size, eps);
+  SLM_LAUNCHED("k_rms_split");
+}
+
 void b3_linear(const LinearArgs& a, void* ws, cudaStream_t st) {
-  auto* planes = static_cast<__nv_bfloat16*>(ws);
   const size_t pb = ((size_t)a.m * 6 * a.cols * sizeof(__nv_bfloat16) + 255) / 256 * 256;
-  const size_t n = (size_t)a.m * a.cols;
-  k_split_x<<<(unsigned)std::min<size_t>((n + 255) / 256, 148 * 16), 256, 0, st>>>(a.x, a.ldx, a.m, a.cols, planes);
-  SLM_LAUNCHED("k_split_x");
+  const void* planes = a.xplanes;
+  if (!planes) {  // split the activations here
+    const size_t n = (size_t)a.m * a.cols;
+    k_split_x<<<(unsigned)std::min<size_t>((n + 255) / 256, 148 * 16), 256, 0, st>>>(
+        a.x, a.ldx, a.m, a.cols, static_cast<__nv_bfloat16*>(ws));
+    SLM_LAUNCHED("k_split_x");
+    planes = ws;
+  }
   auto args = make_args(a, planes);
   Gemm gemm;
   cutlass::Status s = gemm.can_implement(args);

@@ -23,6 +23,8 @@ struct LinearArgs {
   size_t ws_bytes = 0;
   // The weights split into bf16 parts for the bf16x3 GEMM (gemm_bf16x3.cu), or null.
   const void* wplanes = nullptr;
+  // x already split the same way (written by b3_rms_split), or null.
+  const void* xplanes = nullptr;
 };
 void linear(const LinearArgs& a, cudaStream_t st);
 // SIMT path for 8 < m ≤ 64 tokens (skinny.cu): STORE/ADD epilogues, cols % 32
@@ -37,6 +39,9 @@ void b3_split_weights(const float* w, size_t rows, size_t cols, void* planes, cu
 bool b3_linear_ok(const LinearArgs& a);
 size_t b3_linear_workspace(const LinearArgs& a);
 void b3_linear(const LinearArgs& a, void* ws, cudaStream_t st);
+// ew_rms without a base, also writing x's bf16x3 planes ([groups][6·size] bf16).
+void b3_rms_split(float* y, void* planes, const float* x, const float* w, size_t groups, size_t size, float eps,
+                  cudaStream_t st);
 // Tensor-core (sm100 FastFP32) path for m > 8, gemm_tc.cu.
 bool tc_linear_ok(const LinearArgs& a);
 size_t tc_linear_workspace(const LinearArgs& a);

@@ -82,6 +82,7 @@ struct slm_session {
   float *xa = nullptr, *xb = nullptr, *e0 = nullptr, *e_proj = nullptr, *n = nullptr, *mix = nullptr, *q = nullptr,
         *kb = nullptr, *kin = nullptr, *kvs = nullptr, *y = nullptr, *mid = nullptr, *dec = nullptr, *part = nullptr,
         *logits = nullptr, *work = nullptr, *nlast = nullptr, *upbuf = nullptr;
+  void* nplanes = nullptr;  // bf16x3 planes of `n` for the wide chunk linears (when the model has split weights)
   long long* pos_dev = nullptr;
   uint32_t* ids_dev = nullptr;
   unsigned long long* rng_dev = nullptr;
@@ -299,7 +300,7 @@ thread_local slm_ctx* g_ctx_for_linear = nullptr;  // set by the driver around e
 thread_local bool g_capturing = false;
 
 void run_linear(cudaStream_t s, const Mat& w, const float* x, int ldx, int m, float* y, int ldy, int epi,
-                const float* res = nullptr, int ldres = 0, size_t rows = 0) {
+                const float* res = nullptr, int ldres = 0, size_t rows = 0, const void* xplanes = nullptr) {
   LinearArgs a;
   a.w = w.w;
   a.rows = (int)(rows ? rows : w.rows);
@@ -313,6 +314,7 @@ void run_linear(cudaStream_t s, const Mat& w, const float* x, int ldx, int m, fl
   a.ldres = ldres;
   a.epi = epi;
   a.wplanes = w.planes;
+  a.xplanes = xplanes;
   if (g_ctx_for_linear) gemm_workspace(g_ctx_for_linear, a, g_capturing);
   linear(a, s);
 }
@@ -325,16 +327,23 @@ void block(slm_session* se, const Block& b, LState& st, float* x, size_t m) {
   const size_t d = c.d, heads = c.heads, dh = c.dh();
   const float scale = 1.0f / std::sqrt((float)dh);
   const int im = (int)m, id = (int)d;
-  ew_rms(se->n, x, b.norm1, m, d, c.eps, nullptr, s);
+  // Chunks: the normalised input also gets its bf16x3 planes for the wide
+  // linears that read it (qkv, qkvg, up), in the same kernel.
+  const bool split = m > 64 && se->nplanes && b.kind != 'G';
+  if (split)
+    b3_rms_split(se->n, se->nplanes, x, b.norm1, m, d, c.eps, s);
+  else
+    ew_rms(se->n, x, b.norm1, m, d, c.eps, nullptr, s);
+  const void* np = split ? se->nplanes : nullptr;
   bool has_h = true;
   if (b.kind == 'S') {
-    run_linear(s, b.qkv, se->n, id, im, se->mix, (int)(3 * d), EPI_STORE);
+    run_linear(s, b.qkv, se->n, id, im, se->mix, (int)(3 * d), EPI_STORE, nullptr, 0, 0, np);
     ew_rope_store(se->mix, 3 * d, md->inv_freq, se->pos_dev, m, heads, dh, st.cap, se->q, st.k, st.v, s);
     AttnGeom g{im, (long long)c.window, 0, (long long)st.cap, (int)heads, (int)heads, (int)dh, scale};
     int ns = attn_splits(g, (long long)(c.window + m - 1));
     attention(se->q, id, st.k, st.v, g, se->pos_dev, ns, se->part, se->y, id, s);
   } else if (b.kind == 'L') {
-    run_linear(s, b.qkvg, se->n, id, im, se->mix, (int)(4 * d), EPI_STORE);
+    run_linear(s, b.qkvg, se->n, id, im, se->mix, (int)(4 * d), EPI_STORE, nullptr, 0, 0, np);
     run_linear(s, b.decay, se->n, id, im, se->dec, (int)heads, EPI_STORE);
     ew_l2norm(se->q, d, se->mix, 4 * d, m, heads, dh, s);
     ew_l2norm(se->kb, d, se->mix + d, 4 * d, m, heads, dh, s);
@@ -384,11 +393,16 @@ void block(slm_session* se, const Block& b, LState& st, float* x, size_t m) {
     }
   }
   if (has_h) run_linear(s, b.o, se->y, id, im, x, id, EPI_ADD, x, id);  // x += o·y
-  ew_rms(se->n, x, b.norm2, m, d, c.eps, nullptr, s);
+  const bool split2 = m > 64 && se->nplanes;
+  if (split2)
+    b3_rms_split(se->n, se->nplanes, x, b.norm2, m, d, c.eps, s);
+  else
+    ew_rms(se->n, x, b.norm2, m, d, c.eps, nullptr, s);
   const size_t hidden = b.down.cols;
   if (m > 8 && hidden % 4 == 0) {
     // Chunks: the [m][2F] product on the tensor cores, then the gate.
-    run_linear(s, b.up, se->n, id, im, se->upbuf, (int)(2 * hidden), EPI_STORE);
+    run_linear(s, b.up, se->n, id, im, se->upbuf, (int)(2 * hidden), EPI_STORE, nullptr, 0, 0,
+               split2 ? se->nplanes : nullptr);
     ew_silu_pair(se->mid, se->upbuf, m, hidden, s);
   } else {
     run_linear(s, b.up, se->n, id, im, se->mid, (int)hidden, EPI_SILU);  // silu(gate)·amp
@@ -1066,6 +1080,7 @@ int slm_session_new(slm_model* md, size_t loops, slm_session** out) {
       se->y = f(CHUNK * d);
       se->mid = f(CHUNK * std::max<size_t>(md->hidden, 1));
       se->upbuf = f(CHUNK * 2 * std::max<size_t>(md->hidden, 1));
+      if (md->planes) se->nplanes = alloc_zero(se.get(), CHUNK * 6 * c.d * 2);
       se->dec = f(CHUNK * c.heads);
       se->nlast = f(d);
       se->logits = f(c.vocab);
