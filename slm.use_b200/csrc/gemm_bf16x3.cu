@@ -155,13 +155,17 @@ void b3_split_weights(const float* w, size_t rows, size_t cols, void* planes, cu
 #ifndef SLM_B3_MIN_ROWS
 #define SLM_B3_MIN_ROWS 2048  // narrower outputs stay on the FastFP32 kernel
 #endif
+#ifndef SLM_B3_MIN_COLS
+#define SLM_B3_MIN_COLS 1000000000  // deep inputs (the down projection) stay on FastFP32 unless set
+#endif
 #ifndef SLM_B3_MIN_M
 #define SLM_B3_MIN_M 65  // fewer token rows go to the skinny SIMT kernel
 #endif
 
 bool b3_linear_ok(const LinearArgs& a) {
   auto al = [](const void* p) { return ((uintptr_t)p & 15) == 0; };
-  return a.wplanes && a.m >= SLM_B3_MIN_M && a.rows >= SLM_B3_MIN_ROWS && a.epi != EPI_SILU && a.cols % 8 == 0 &&
+  return a.wplanes && a.m >= SLM_B3_MIN_M && (a.rows >= SLM_B3_MIN_ROWS || a.cols >= SLM_B3_MIN_COLS) &&
+         a.epi != EPI_SILU && a.cols % 8 == 0 &&
          a.rows % 4 == 0 && a.ldy == a.rows &&
          (a.epi != EPI_ADD || a.ldres == a.rows) && al(a.wplanes) && al(a.y) && (a.epi != EPI_ADD || al(a.res));
 }

@@ -103,10 +103,10 @@ __global__ void __launch_bounds__(GlaShape<DH>::T)
 // ---------------------------------------------------------------------------
 // Many tokens (prefill chunks): column-parallel recurrence + a norm/gate pass.
 //
-// A CTA owns CG = 8 columns of one head's state (grid heads × DH/CG), one warp:
-// each column is split over RQ = 4 lanes holding DH/4 of its rows in
-// registers.  Lane rq owns the float4 chunks rq, rq + 4, … of a row of q or k,
-// so the four lanes of a column read consecutive 16-byte words (no bank
+// A CTA owns CG = 32/RQ columns of one head's state (grid heads × DH/CG), one
+// warp: each column is split over RQ = 8 lanes holding DH/8 of its rows in
+// registers.  Lane rq owns the float4 chunks rq, rq + RQ, … of a row of q or
+// k, so the lanes of a column read consecutive 16-byte words (no bank
 // conflicts).  Tokens are staged TC at a time with cp.async, double-buffered,
 // so the next stage loads while this one runs.  The bare y goes to `out`; the
 // head_norm + gate (which need a whole head) follow in k_gla_norm.
@@ -116,10 +116,15 @@ __global__ void __launch_bounds__(GlaShape<DH>::T)
 #define SLM_GLA_UNROLL 4
 #endif
 constexpr int kGlaUnroll = SLM_GLA_UNROLL;
+#ifndef SLM_GLA_RQ
+#define SLM_GLA_RQ 8  // lanes per state column
+#endif
 
 template <int DH>
 struct GlaCols {
-  static constexpr int CG = 8, RQ = 4, R = DH / RQ, C4 = R / 4, T = CG * RQ;
+  // 8 lanes per column, 4 columns per one-warp CTA: heads × DH/4 CTAs (192
+  // for 12 heads of 64), DH/8 rows of a column per lane.
+  static constexpr int RQ = SLM_GLA_RQ, CG = 32 / RQ, R = DH / RQ, C4 = R / 4, T = CG * RQ;
   static constexpr int TC = 2048 / DH;  // tokens per stage (32 for DH 64)
 };
 
