@@ -305,16 +305,26 @@ def ref_cuda_measure(cases, device: int) -> dict | None:
 # Device timeline of the persistent decode step (--trace)
 # ---------------------------------------------------------------------------
 
-def phase_kinds(cfg: dict, loops: int) -> list[str]:
-    """Phase names of the persistent step, in plan order (model.cpp build_plan)."""
-    names = {"S": ["S1", "attn", "o", "up", "down"], "L": ["L1", "gla", "o", "up", "down"],
-             "G": ["G1", "gattn", "o", "up", "down"]}
+def phase_kinds(cfg: dict, loops: int, fused: bool = True) -> list[str]:
+    """Phase names of the persistent step, in plan order (model.cpp build_plan).
+    fused: each MLP is one phase ("mlp"); else gate/up ("up") and down."""
+    mlp = ["mlp"] if fused else ["up", "down"]
+    names = {"S": ["S1", "attn", "o"] + mlp, "L": ["L1", "gla", "o"] + mlp, "G": ["G1", "gattn", "o"] + mlp}
     out = [n for k in cfg["prelude"] for n in names[k]]
     if cfg["core"]:
         out.append("inject")
         out += [n for _ in range(loops) for k in cfg["core"] for n in names[k]]
     out += [n for k in cfg["coda"] for n in names[k]]
     return out + ["logits"]
+
+
+def trace_kinds(tr: np.ndarray, cfg: dict, loops: int) -> list[str] | None:
+    """Phase names for a traced step of either plan shape (None if neither fits)."""
+    for fused in (True, False):
+        kinds = phase_kinds(cfg, loops, fused)
+        if len(kinds) == tr.shape[0]:
+            return kinds
+    return None
 
 
 def traced_step(se, greedy) -> np.ndarray:
@@ -330,8 +340,8 @@ def traced_step(se, greedy) -> np.ndarray:
 def attention_phases(tr: np.ndarray, cfg: dict, loops: int) -> dict | None:
     """The persistent step's window-attention phases at a full window: their
     K/V bytes over their critical spans (first CTA start to last arrival)."""
-    kinds = phase_kinds(cfg, loops)
-    if len(kinds) != tr.shape[0]:
+    kinds = trace_kinds(tr, cfg, loops)
+    if kinds is None:
         return None
     spans = [int(tr[p, :, 1].max() - tr[p, :, 0].min()) for p in range(tr.shape[0]) if kinds[p] == "attn"]
     h, dh = cfg["n_heads"], cfg["d_model"] // cfg["n_heads"]
@@ -344,8 +354,8 @@ def write_trace(tr: np.ndarray, cfg: dict, loops: int, path: str) -> None:
     """Per-phase sums of a traced step, grouped by phase kind, as a markdown
     table (critical span = first CTA start to last CTA arrival; gap = last
     arrival to the next phase's first start)."""
-    kinds = phase_kinds(cfg, loops)
-    if len(kinds) != tr.shape[0]:
+    kinds = trace_kinds(tr, cfg, loops)
+    if kinds is None:
         return
     t0 = tr[0, :, 0].min()
     st, en = tr[:, :, 0] - t0, tr[:, :, 1] - t0

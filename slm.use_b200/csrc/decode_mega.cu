@@ -71,6 +71,14 @@ __device__ __forceinline__ float4 lds4(uint32_t a) {
   asm volatile("ld.shared.v4.f32 {%0,%1,%2,%3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(a));
   return v;
 }
+__device__ __forceinline__ float lds1(uint32_t a) {
+  float v;
+  asm volatile("ld.shared.f32 %0, [%1];" : "=f"(v) : "r"(a));
+  return v;
+}
+__device__ __forceinline__ void red_add_u64(long long* p, long long v) {
+  asm volatile("red.relaxed.gpu.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
 __device__ __forceinline__ void cp_async16(void* dst, const void* src) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(saddr(dst)), "l"(src) : "memory");
 }
@@ -127,18 +135,30 @@ __device__ __forceinline__ uint32_t total_key(float f) {
   return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
 }
 
+// Four consecutive values of a fused MLP's fixed-point slot (d wide) as floats:
+// one rounding of the exact sum; NaN everywhere when a part was out of range.
+__device__ __forceinline__ float4 fx_load4(const long long* fx, int i4, int d) {
+  const longlong2* f = reinterpret_cast<const longlong2*>(fx) + 2 * i4;
+  const longlong2 a = __ldcg(f), b = __ldcg(f + 1);
+  if (__ldcg(fx + d) != 0) return make_float4(NAN, NAN, NAN, NAN);
+  return make_float4(__ll2float_rn(a.x) * kFxInv, __ll2float_rn(a.y) * kFxInv, __ll2float_rn(b.x) * kFxInv,
+                     __ll2float_rn(b.y) * kFxInv);
+}
+
 // ---------------------------------------------------------------------------
 // Tile geometry shared by the producer and the consumers
 // ---------------------------------------------------------------------------
 
 __device__ __forceinline__ bool is_pair(const Phase& ph) {
-  return ph.out_mode == OUT_SILU || ph.out_mode == OUT_ROPE;
+  return ph.out_mode == OUT_SILU || ph.out_mode == OUT_ROPE || ph.out_mode == OUT_MLP;
 }
 
-// Logical outputs per tile of a GEMV phase.
+// Logical outputs per tile of a GEMV phase (a fused MLP unit takes three rows:
+// gate, up and downᵀ).
 __device__ __forceinline__ int tile_outs(const Phase& ph) {
   int rows = kStageBytes / (ph.cols * 4);
   if (rows > 16) rows = 16;
+  if (ph.out_mode == OUT_MLP) return rows / 3;
   return is_pair(ph) ? rows / 2 : rows;
 }
 
@@ -148,7 +168,7 @@ __device__ __forceinline__ void out_rows(const Phase& ph, const Segment& sg, int
     int sec = o / (d / 2), rem = o % (d / 2), h = rem / 32, j = rem % 32;
     *r0 = sec * d + h * kDH + j;
     *r1 = *r0 + 32;
-  } else if (ph.out_mode == OUT_SILU) {
+  } else if (ph.out_mode == OUT_SILU || ph.out_mode == OUT_MLP) {
     *r0 = o;
     *r1 = o + sg.rows;
   } else {
@@ -255,6 +275,8 @@ struct Walker {
       const unsigned rowb = (unsigned)ph.cols * 4;
       T.src[0] = sg.w + (size_t)r0 * ph.cols, T.bytes[0] = n * rowb, T.off[0] = 0, T.n = 1;
       if (is_pair(ph)) T.src[1] = sg.w + (size_t)r1 * ph.cols, T.bytes[1] = n * rowb, T.off[1] = n * rowb, T.n = 2;
+      if (ph.out_mode == OUT_MLP)  // [gate n][up n][downᵀ n]
+        T.src[2] = ph.wt + (size_t)t * ph.cols, T.bytes[2] = n * rowb, T.off[2] = 2 * n * rowb, T.n = 3;
       t += n;
     } else if (ph.kind == PH_ATTN) {
       const int h = i / ph.splits;
@@ -430,6 +452,13 @@ struct Cons {
     if (sm.flag == 1) ok = false;
   }
 
+  // Float4 i4 of a phase's `a` input: the float buffer, or the fixed-point slot
+  // of the fused MLP phase that produced it.
+  __device__ __forceinline__ float4 in4(const Phase& ph, int i4) {
+    if (ph.fx_in) return fx_load4(ph.fx_in, i4, P.d);
+    return __ldcg(reinterpret_cast<const float4*>(ph.in_a) + i4);
+  }
+
   // Input vector of a GEMV phase into sm.xin (and the raw x into sm.xraw).
   // Every load of a thread is issued before any is used.
   __device__ void prologue(const Phase& ph) {
@@ -444,7 +473,8 @@ struct Cons {
       const float4* a4 = reinterpret_cast<const float4*>(ph.in_a);
 #pragma unroll
       for (int j = 0; j < J; j++)
-        if (tid + j * 256 < n4) v[j] = __ldcg(a4 + tid + j * 256);
+        if (tid + j * 256 < n4)
+          v[j] = ph.fx_in ? fx_load4(ph.fx_in, tid + j * 256, P.d) : __ldcg(a4 + tid + j * 256);
 #pragma unroll
       for (int j = 0; j < J; j++)
         if (tid + j * 256 < n4) reinterpret_cast<float4*>(sm.xin)[tid + j * 256] = v[j];
@@ -457,7 +487,7 @@ struct Cons {
       float4 x = make_float4(0.f, 0.f, 0.f, 0.f), e = x, w = x, we = x;
       if (own) {
         w = __ldg(reinterpret_cast<const float4*>(ph.norm_w) + tid);
-        x = __ldcg(reinterpret_cast<const float4*>(ph.in_a) + tid);
+        x = in4(ph, tid);
         if (ph.in_c) {
           we = __ldg(reinterpret_cast<const float4*>(ph.in_c) + tid);
           e = __ldcg(reinterpret_cast<const float4*>(P.e0) + tid);
@@ -487,7 +517,13 @@ struct Cons {
       consumers_sync();
       return;
     }
-    // Normalised input: d ≤ kMaxD, at most one float4 per thread.
+    rms_prologue(ph);
+  }
+
+  // Normalised input (IN_RMS, IN_EMBED_RMS, IN_LOOP_RMS): d ≤ kMaxD, at most
+  // one float4 per thread.
+  __device__ __forceinline__ void rms_prologue(const Phase& ph) {
+    const int n4 = ph.cols / 4;
     const bool own = tid < n4;
     float4 x = make_float4(0.f, 0.f, 0.f, 0.f), w = x;
     if (own) {
@@ -499,13 +535,13 @@ struct Cons {
           reinterpret_cast<float4*>(P.x0)[tid] = x;
         }
       } else if (ph.in_mode == IN_LOOP_RMS) {
-        float4 a = __ldcg(reinterpret_cast<const float4*>(ph.in_a) + tid);
+        float4 a = in4(ph, tid);
         float4 b = __ldcg(reinterpret_cast<const float4*>(ph.in_b) + tid);
         float4 c = __ldg(reinterpret_cast<const float4*>(ph.in_c) + tid);
         x = make_float4((a.x + b.x) + c.x, (a.y + b.y) + c.y, (a.z + b.z) + c.z, (a.w + b.w) + c.w);
         if (blockIdx.x == 0) reinterpret_cast<float4*>(ph.xout)[tid] = x;
       } else {
-        x = __ldcg(reinterpret_cast<const float4*>(ph.in_a) + tid);
+        x = in4(ph, tid);
       }
       reinterpret_cast<float4*>(sm.xraw)[tid] = x;
     }
@@ -675,7 +711,223 @@ struct Cons {
     }
   }
 
+  // Fused MLP items: hidden units j in tiles of n = tile_outs units, laid out
+  // [gate rows n][up rows n][downᵀ rows n].  The 2n dot products of a tile go
+  // to sm.acc[tile parity] (a warp may start the next tile's products while
+  // another still reads this tile's), then every thread adds h_j·downᵀ[j][c]
+  // for its columns c = tid + 256·q into y, in unit order.
+  template <int K>
+  __device__ __forceinline__ void mlp_items(const Phase& ph, float (&y)[kMaxD / 256]) {
+    const int G = gridDim.x, d = ph.cols;
+    float4 xr[K];
+    {
+      const float4* xin4 = reinterpret_cast<const float4*>(sm.xin) + lane;
+#pragma unroll
+      for (int k = 0; k < K; k++) xr[k] = xin4[32 * k];
+    }
+    const int T = tile_outs(ph);
+    unsigned tile = 0;
+    for (int i = blockIdx.x; i < ph.items && ok; i += G) {
+      int s, o0, o1;
+      gemv_item(ph, i, &s, &o0, &o1);
+      for (int t0 = o0; t0 < o1; t0 += T, tile++) {
+        const int n = min(T, o1 - t0), rows = 2 * n;
+        const float* w = take_warp();
+        unsigned long long c0 = P.trace && tid == 0 ? now_ns() : 0;
+        float(*acc)[kMaxItemOut] = sm.acc[tile & 1];
+        for (int r = warp; r < rows; r += 2 * kConsumerWarps) {
+          const int r2 = r + kConsumerWarps;
+          const bool two = r2 < rows;
+          const uint32_t w0 = saddr(w + (size_t)r * d) + lane * 16;
+          const uint32_t w1 = saddr(w + (size_t)(two ? r2 : r) * d) + lane * 16;
+          float a0 = 0.0f, b0 = 0.0f, a1 = 0.0f, b1 = 0.0f;
+#pragma unroll
+          for (int k = 0; k < K; k++) {
+            float4 u = lds4(w0 + 512 * k), v = lds4(w1 + 512 * k);
+            if (k & 1) {
+              b0 = dot4(u, xr[k], b0);
+              b1 = dot4(v, xr[k], b1);
+            } else {
+              a0 = dot4(u, xr[k], a0);
+              a1 = dot4(v, xr[k], a1);
+            }
+          }
+          a0 += b0;
+          a1 += b1;
+#pragma unroll
+          for (int o = 16; o > 0; o >>= 1) {
+            a0 += __shfl_xor_sync(0xffffffffu, a0, o);
+            a1 += __shfl_xor_sync(0xffffffffu, a1, o);
+          }
+          if (lane == 0) {
+            acc[r / n][r % n] = a0;
+            if (two) acc[r2 / n][r2 % n] = a1;
+          }
+        }
+        consumers_sync();  // every gate and up product of the tile
+        const uint32_t dt = saddr(w + (size_t)2 * n * d) + tid * 4;
+        for (int j = 0; j < n; j++) {
+          const float h = silu_mul(acc[0][j], acc[1][j]);
+#pragma unroll
+          for (int q = 0; q < kMaxD / 256; q++)
+            if (tid + 256 * q < d) y[q] = fmaf(h, lds1(dt + (uint32_t)(j * d + 256 * q) * 4), y[q]);
+        }
+        release();
+        if (c0) comp_ns += now_ns() - c0, ntiles++;
+      }
+      if (!all_ok()) return;
+    }
+  }
+
+  // Fused MLP items, a warp per hidden unit: unit u of this CTA (counted over
+  // its tiles) belongs to warp u mod 8, which forms gate·n and up·n (two
+  // chains), h = silu(gate)·up, and adds h·downᵀ[u] into its own partial
+  // (columns 4·lane + 128·k).  No CTA barrier per tile; the eight partials are
+  // summed once at the end, in a fixed order (needs 4·d ≤ kMaxCols floats of
+  // sm.xin).
+  template <int K>
+  __device__ __forceinline__ void mlp_items_w(const Phase& ph, float (&y)[kMaxD / 256]) {
+    const int G = gridDim.x, d = ph.cols;
+    float4 xr[K], yv[K];
+    {
+      const float4* xin4 = reinterpret_cast<const float4*>(sm.xin) + lane;
+      const float4* xraw4 = reinterpret_cast<const float4*>(sm.xraw) + lane;
+      const bool res = blockIdx.x == 0 && warp == 0;  // the residual, once per slot
+#pragma unroll
+      for (int k = 0; k < K; k++) {
+        xr[k] = xin4[32 * k];
+        yv[k] = res ? xraw4[32 * k] : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+    }
+    const int T = tile_outs(ph);
+    int u = 0;  // units of this CTA before the current tile
+    for (int i = blockIdx.x; i < ph.items && ok; i += G) {
+      int s, o0, o1;
+      gemv_item(ph, i, &s, &o0, &o1);
+      for (int t0 = o0; t0 < o1; t0 += T) {
+        const int n = min(T, o1 - t0);
+        const float* w = take_warp();
+        unsigned long long c0 = P.trace && tid == 0 ? now_ns() : 0;
+        for (int j = (warp - u % kConsumerWarps + kConsumerWarps) % kConsumerWarps; j < n; j += kConsumerWarps) {
+          const uint32_t g0 = saddr(w + (size_t)j * d) + lane * 16;
+          const uint32_t u0 = saddr(w + (size_t)(n + j) * d) + lane * 16;
+          const uint32_t r0 = saddr(w + (size_t)(2 * n + j) * d) + lane * 16;
+          float a0 = 0.0f, b0 = 0.0f, a1 = 0.0f, b1 = 0.0f;
+#pragma unroll
+          for (int k = 0; k < K; k++) {
+            float4 gq = lds4(g0 + 512 * k), uq = lds4(u0 + 512 * k);
+            if (k & 1) {
+              b0 = dot4(gq, xr[k], b0);
+              b1 = dot4(uq, xr[k], b1);
+            } else {
+              a0 = dot4(gq, xr[k], a0);
+              a1 = dot4(uq, xr[k], a1);
+            }
+          }
+          a0 += b0;
+          a1 += b1;
+#pragma unroll
+          for (int o = 16; o > 0; o >>= 1) {
+            a0 += __shfl_xor_sync(0xffffffffu, a0, o);
+            a1 += __shfl_xor_sync(0xffffffffu, a1, o);
+          }
+          const float h = silu_mul(a0, a1);
+#pragma unroll
+          for (int k = 0; k < K; k++) {
+            const float4 dq = lds4(r0 + 512 * k);
+            yv[k].x = fmaf(h, dq.x, yv[k].x), yv[k].y = fmaf(h, dq.y, yv[k].y);
+            yv[k].z = fmaf(h, dq.z, yv[k].z), yv[k].w = fmaf(h, dq.w, yv[k].w);
+          }
+        }
+        release();
+        u += n;
+        if (c0) comp_ns += now_ns() - c0, ntiles++;
+      }
+      if (!all_ok()) return;
+    }
+    // ((w0 + w4) + (w1 + w5)) + ((w2 + w6) + (w3 + w7)) per column, through sm.xin.
+    float4* buf = reinterpret_cast<float4*>(sm.xin);  // [4][d / 4]
+    const int d4 = d / 4;
+    consumers_sync();  // every warp has read its x from sm.xin
+    if (warp >= 4)
+#pragma unroll
+      for (int k = 0; k < K; k++) buf[(warp - 4) * d4 + lane + 32 * k] = yv[k];
+    consumers_sync();
+    if (warp < 4)
+#pragma unroll
+      for (int k = 0; k < K; k++) {
+        float4& o = buf[warp * d4 + lane + 32 * k];
+        const float4 v = o;
+        o = make_float4(yv[k].x + v.x, yv[k].y + v.y, yv[k].z + v.z, yv[k].w + v.w);
+      }
+    consumers_sync();
+    const float* b = sm.xin;
+#pragma unroll
+    for (int q = 0; q < kMaxD / 256; q++) {
+      const int c = tid + 256 * q;
+      if (c < d) y[q] = (b[c] + b[d + c]) + (b[2 * d + c] + b[3 * d + c]);
+    }
+  }
+
+  // The whole MLP of a block as one phase: x' = x + down·(silu(gate·n)·(up·n))
+  // with n = rms(x)·w.  Each CTA sums its hidden units' down columns on chip
+  // and adds them, as int64 fixed point, into the phase's slot; CTA 0 also adds
+  // the residual x.  The next phase reads x' from the slot.
+  __device__ __noinline__ void mlp_phase(const Phase& ph) {
+    unsigned long long t0 = P.trace && tid == 0 ? now_ns() : 0;
+    rms_prologue(ph);  // the plan gives fused MLPs IN_RMS inputs
+    if (t0) pro_ns += now_ns() - t0;
+    if (blockIdx.x >= ph.items) return;
+    const int d = ph.cols;
+    float y[kMaxD / 256];
+#pragma unroll
+    for (int q = 0; q < kMaxD / 256; q++) y[q] = 0.0f;
+    if (!P.mlp_cta) {
+      switch (d / 128) {
+        case 1: mlp_items_w<1>(ph, y); break;
+        case 2: mlp_items_w<2>(ph, y); break;
+        case 3: mlp_items_w<3>(ph, y); break;
+        case 4: mlp_items_w<4>(ph, y); break;
+        case 6: mlp_items_w<6>(ph, y); break;
+        default: break;  // d > 768 takes the per-tile CTA split (mlp_cta set by the plan)
+      }
+    } else {
+#pragma unroll
+      for (int q = 0; q < kMaxD / 256; q++) {
+        const int c = tid + 256 * q;
+        y[q] = blockIdx.x == 0 && c < d ? sm.xraw[c] : 0.0f;
+      }
+      switch (d / 128) {
+        case 1: mlp_items<1>(ph, y); break;
+        case 2: mlp_items<2>(ph, y); break;
+        case 3: mlp_items<3>(ph, y); break;
+        case 4: mlp_items<4>(ph, y); break;
+        case 6: mlp_items<6>(ph, y); break;
+        case 8: mlp_items<8>(ph, y); break;
+        default: break;  // excluded when the plan is built
+      }
+    }
+    if (!ok) return;
+    unsigned long long e0 = P.trace && tid == 0 ? now_ns() : 0;
+    bool bad = false;
+#pragma unroll
+    for (int q = 0; q < kMaxD / 256; q++) {
+      const int c = tid + 256 * q;
+      if (c < d) {
+        const float v = y[q];
+        if (!(fabsf(v) < kFxMax)) bad = true;  // NaN included
+        red_add_u64(ph.fx_out + c, __float2ll_rn(v * kFxScale));
+      }
+    }
+    if (bad) atomicOr(reinterpret_cast<unsigned long long*>(ph.fx_out + d), 1ull);
+    if (e0) epi_ns += now_ns() - e0;
+  }
+
   __device__ void gemv_phase(const Phase& ph) {
+    if (ph.out_mode == OUT_MLP) {
+      mlp_phase(ph);
+      return;
+    }
     // Normalising prologues run everywhere: they also refresh sm.xraw, the
     // residual of the phases that follow.
     if (blockIdx.x >= ph.items && ph.in_mode == IN_PLAIN) return;
@@ -1038,6 +1290,9 @@ struct Cons {
 
   __device__ void run() {
     if (tid < kDH / 2 && P.inv_freq) sm.inv_freq[tid] = __ldg(P.inv_freq + tid);
+    // The fused MLP slots start the step at zero (the previous step's readers
+    // ended with its launch; the first MLP comes after at least one barrier).
+    for (int e = blockIdx.x * 256 + tid; e < P.fx_words; e += gridDim.x * 256) P.fx[e] = 0;
     stage_phase(0);
     stage_wait();
     consumers_sync();

@@ -297,6 +297,29 @@ void ew_scale_rows(float* y, const float* x, const float* f, size_t m, size_t d,
   k_scale_rows<<<ew_grid(m * d), EW, 0, st>>>(y, x, f, m, d);
   SLM_LAUNCHED("k_scale_rows");
 }
+// dst[c][r] = src[r][c] through a 32 × 33 shared tile (coalesced both ways).
+__global__ void k_transpose(float* __restrict__ dst, const float* __restrict__ src, int rows, int cols) {
+  __shared__ float t[32][33];
+  const int c0 = blockIdx.x * 32, r0 = blockIdx.y * 32;
+  for (int j = threadIdx.y; j < 32; j += 8) {
+    const int r = r0 + j, c = c0 + threadIdx.x;
+    if (r < rows && c < cols) t[j][threadIdx.x] = src[(size_t)r * cols + c];
+  }
+  __syncthreads();
+  for (int j = threadIdx.y; j < 32; j += 8) {
+    const int c = c0 + j, r = r0 + threadIdx.x;
+    if (c < cols && r < rows) dst[(size_t)c * rows + r] = t[threadIdx.x][j];
+  }
+}
+
+void ew_transpose(float* dst, const float* src, size_t rows, size_t cols, cudaStream_t st) {
+  if (!rows || !cols) return;
+  SLM_REQUIRE(rows <= (size_t)65535 * 32 && cols < (size_t)1 << 31, "matrix too large to transpose");
+  k_transpose<<<dim3((unsigned)((cols + 31) / 32), (unsigned)((rows + 31) / 32)), dim3(32, 8), 0, st>>>(
+      dst, src, (int)rows, (int)cols);
+  SLM_LAUNCHED("k_transpose");
+}
+
 void ew_mix(float* y, const float* a, const float* b, size_t n, float t, cudaStream_t st) {
   if (!n) return;
   k_mix<<<ew_grid(n), EW, 0, st>>>(y, a, b, n, t);

@@ -44,7 +44,17 @@ enum OutMode : int {
   OUT_LOGITS = 4,  // y[r] = acc and a per-item arg-max partial
   OUT_G = 5,       // G: segment 0 = q rows (× the logn factor) into q; segment 1 = kv rows: keys into
                    // the cache at pos (pos + 1 with kshift: the next position's shifted key), values at pos
+  OUT_MLP = 6,     // the whole MLP: items are hidden units j; h_j = silu(gate_j)·up_j, then
+                   // Σ_j h_j·downᵀ[j] (+ the residual on CTA 0) added into the fixed-point sum fx_out
 };
+
+// Fixed-point residual sums of fused MLP phases: int64 in units of 2^-32, one
+// slot of d + 2 words per MLP of the step ([d] sums, [d] a flag set when a part
+// was non-finite or beyond ±2^23, [d + 1] padding).  Integer adds are exact, so
+// the sum does not depend on the order in which CTAs arrive.
+constexpr float kFxScale = 4294967296.0f;       // 2^32
+constexpr float kFxInv = 1.0f / 4294967296.0f;  // 2^-32
+constexpr float kFxMax = 8388608.0f;            // 2^23: 255 parts of this size stay below 2^31
 
 struct Segment {
   const float* w;   // weight rows, row-major, `cols` wide
@@ -72,6 +82,11 @@ struct alignas(16) Phase {
   int kshift;             // OUT_G
   float inv_log;          // OUT_G: 1/ln(logn), 0 for no logn scaling
   const float* inv_freq;
+  // OUT_MLP: downᵀ ([F][d], row j = column j of down) and the slot its sums go to
+  const float* wt;
+  long long* fx_out;
+  // Inputs: when set, the `a` input is this fixed-point slot instead of in_a
+  const long long* fx_in;
   // ATTN: heads × splits items; partials and per-head arrival counters
   int heads, splits;
   float* part;
@@ -117,6 +132,9 @@ struct Plan {
   // than the grid has, so its bounded wait runs out (failure-path test).
   int test_stall;
   int global;  // the plan has global-attention layers (selects the kernel built for them)
+  long long* fx;  // fixed-point slots of the fused MLP phases, zeroed at the start of each step
+  int fx_words;
+  int mlp_cta;    // 1: fused MLP tiles split by rows with a CTA barrier per tile (always for d > 768)
 };
 
 }  // namespace mega

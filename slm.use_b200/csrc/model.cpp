@@ -6,6 +6,7 @@
 // device slot that the on-device sampler writes.
 #include <algorithm>
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <memory>
 #include <string>
@@ -36,6 +37,7 @@ struct Mat {
   const float* w = nullptr;
   size_t rows = 0, cols = 0;
   const void* planes = nullptr;  // bf16 parts for chunk linears (gemm_bf16x3.cu), in the model's plane arena
+  const float* t = nullptr;      // down only: the transpose ([cols][rows]) read by the fused decode MLP
 };
 
 struct Block {
@@ -64,6 +66,7 @@ struct slm_model {
   Config cfg;
   float* arena = nullptr;
   void* planes = nullptr;  // bf16x3 parts of the block and inject matrices
+  float* tarena = nullptr;  // transposed down matrices (Mat::t)
   std::vector<Block> prelude, core, coda;
   Mat embed, inject, loop_embed;
   bool looped = false;
@@ -106,6 +109,8 @@ struct slm_session {
   unsigned long long* trace = nullptr;  // per-phase timeline of the last step (SLM_OPT_TRACE)
   unsigned* attn_count = nullptr;        // per-head arrival counters of the attention phases
   float* attn_part = nullptr;            // attention partials of the persistent step
+  bool fuse_mlp = false;                 // the persistent step runs each MLP as one phase
+  long long* fx = nullptr;               // fixed-point slots of those phases
   bool plan_stale = false;               // a global cache moved: the phase descriptors need refreshing
   int in_batches = 0;                    // batches holding this session
   uint32_t* argmax_dev = nullptr;        // the persistent step's arg-max of its logits
@@ -447,6 +452,20 @@ void advance(slm_session* se, size_t m, bool want_logits) {
   se->pos += m;
 }
 
+// SLM_MEGA_FUSE_MLP=0 keeps the MLP of the persistent step as two phases
+// (gate/up, then down) with float residual adds; the default fuses them.
+bool fuse_mlp_enabled() {
+  const char* e = std::getenv("SLM_MEGA_FUSE_MLP");
+  return !(e && e[0] == '0');
+}
+
+// SLM_MEGA_MLP_CTA=1 splits each fused MLP tile's rows over the CTA's warps
+// (a CTA barrier per tile) instead of giving each warp whole hidden units.
+bool mlp_cta_setting() {
+  const char* e = std::getenv("SLM_MEGA_MLP_CTA");
+  return e && e[0] == '1';
+}
+
 // Why the persistent decode kernel cannot run this model ("" if it can).
 std::string mega_unsupported(const slm_model* md) {
   const Config& c = md->cfg;
@@ -523,6 +542,28 @@ void build_plan(slm_session* se, bool refresh = false) {
   float* attn_part = se->attn_part;
   unsigned* attn_count = se->attn_count;
   float* X0 = se->xa;
+  // Fused MLP phases: one fixed-point slot each, in plan order.  fx_of(buf)
+  // is the slot holding buffer buf's current value when a fused MLP wrote it
+  // last (its readers take the slot; the float buffer is stale).
+  const size_t nmlp = md->prelude.size() + se->loops * md->core.size() + md->coda.size();
+  const size_t slot_words = (size_t)d + 2;
+  if (!refresh && se->fuse_mlp)
+    se->fx = static_cast<long long*>(alloc_zero(se, nmlp * slot_words * sizeof(long long)));
+  size_t next_slot = 0;
+  std::vector<std::pair<const float*, long long*>> fxw;
+  auto fx_of = [&](const float* buf) -> const long long* {
+    for (auto& e : fxw)
+      if (e.first == buf) return e.second;
+    return nullptr;
+  };
+  auto fx_set = [&](const float* buf, long long* slot) {
+    for (auto& e : fxw)
+      if (e.first == buf) {
+        e.second = slot;
+        return;
+      }
+    fxw.emplace_back(buf, slot);
+  };
   struct In {
     int mode;
     const float *a, *b, *c;
@@ -534,6 +575,7 @@ void build_plan(slm_session* se, bool refresh = false) {
       Phase p = gemv(d, in.mode, ia, in.b, in.c, b.norm1, in.xout, OUT_ROPE,
                      seg(b.qkv.w, 3 * d / 2, per(3 * d / 2, G, 8), nullptr));
       p.q = se->q, p.kc = st.k, p.vc = st.v, p.cap = (long long)st.cap, p.inv_freq = md->inv_freq;
+      p.fx_in = fx_of(ia);
       ph.push_back(p);
       Phase a{};
       a.kind = PH_ATTN;
@@ -553,6 +595,7 @@ void build_plan(slm_session* se, bool refresh = false) {
       p.items = p.seg[0].items + p.seg[1].items;
       p.kc = st.k, p.vc = st.v, p.cap = (long long)st.cap, p.heads = kh, p.kshift = c.kshift ? 1 : 0;
       p.inv_log = c.logn ? 1.0f / std::log((float)c.logn) : 0.0f;
+      p.fx_in = fx_of(X);
       ph.push_back(p);
       Phase a{};
       a.kind = PH_ATTN;
@@ -567,6 +610,7 @@ void build_plan(slm_session* se, bool refresh = false) {
       p.nseg = 2;
       p.seg[1] = seg(b.decay.w, H, per(H, 1, 1), se->dec);
       p.items = p.seg[0].items + p.seg[1].items;
+      p.fx_in = fx_of(ia);
       ph.push_back(p);
       Phase g{};
       g.kind = PH_GLA;
@@ -585,7 +629,16 @@ void build_plan(slm_session* se, bool refresh = false) {
       ph.push_back(gemv(d, IN_PLAIN, se->y, nullptr, nullptr, nullptr, nullptr, OUT_ADD, seg(b.o.w, d, per(d, G, 1), X)));
     }
     ph.back().res_smem = 1;
+    fx_set(X, nullptr);  // o wrote the float x
     const int F = (int)b.down.cols;
+    if (se->fuse_mlp) {
+      Phase u = gemv(d, IN_RMS, X, nullptr, nullptr, b.norm2, nullptr, OUT_MLP, seg(b.up.w, F, per(F, G, 1), nullptr));
+      u.wt = b.down.t;
+      u.fx_out = se->fx + slot_words * next_slot++;
+      ph.push_back(u);
+      fx_set(X, u.fx_out);
+      return;
+    }
     ph.push_back(gemv(d, IN_RMS, X, nullptr, nullptr, b.norm2, nullptr, OUT_SILU,
                       seg(b.up.w, F, per(F, G, 1), se->mid)));
     ph.push_back(gemv(F, IN_PLAIN, se->mid, nullptr, nullptr, nullptr, nullptr, OUT_ADD,
@@ -598,6 +651,7 @@ void build_plan(slm_session* se, bool refresh = false) {
   if (md->looped) {
     ph.push_back(gemv(d, IN_PLAIN, X0, nullptr, nullptr, nullptr, nullptr, OUT_STORE,
                       seg(md->inject.w, d, per(d, G, 1), se->e_proj)));
+    ph.back().fx_in = fx_of(X0);
     const float* sbuf = X0;
     for (size_t r = 0; r < se->loops; r++) {
       float* xr = (r % 2 == 0) ? se->xb : se->xc;
@@ -614,7 +668,9 @@ void build_plan(slm_session* se, bool refresh = false) {
     block(md->coda[i], se->coda[i], X, In{IN_RMS, nullptr, nullptr, nullptr, nullptr});
   ph.push_back(gemv(d, IN_RMS, X, nullptr, nullptr, md->norm_f, nullptr, OUT_LOGITS,
                     seg(md->embed.w, (int)c.vocab, per((int)c.vocab, G, 1), se->logits)));
+  ph.back().fx_in = fx_of(X);
   const int logit_items = ph.back().items;
+  SLM_REQUIRE(next_slot == (se->fuse_mlp ? nmlp : 0), "fused MLP slots out of step");
 
   if (refresh) {
     SLM_REQUIRE((int)ph.size() == se->plan_host.nphases, "decode plan changed shape");
@@ -645,6 +701,9 @@ void build_plan(slm_session* se, bool refresh = false) {
   P.argmax = se->argmax_dev;
   P.global = (c.prelude + c.core + c.coda).find('G') != std::string::npos ? 1 : 0;
   P.arg_part = static_cast<unsigned long long*>(alloc_zero(se, logit_items * sizeof(unsigned long long)));
+  P.fx = se->fx;
+  P.fx_words = se->fuse_mlp ? (int)(nmlp * slot_words) : 0;
+  P.mlp_cta = d > kMaxCols / 4 || mlp_cta_setting() ? 1 : 0;
   P.next_id = se->ids_dev;
   P.err = se->ctx->err;
 }
@@ -1014,6 +1073,23 @@ int slm_model_load(slm_ctx* ctx, const char* dir, slm_model** out) {
       }
       SLM_CUDA(cudaStreamSynchronize(ctx->stream));
     }
+    // The fused MLP phase of the persistent step reads down by columns: keep
+    // a transposed copy of each down matrix when that kernel can run.
+    if (mega_unsupported(md.get()).empty() && fuse_mlp_enabled()) {
+      std::vector<Mat*> downs;
+      for (auto* bs : {&md->prelude, &md->core, &md->coda})
+        for (auto& b : *bs) downs.push_back(&b.down);
+      size_t tot = 0;
+      for (Mat* m : downs) tot += (m->rows * m->cols + 63) / 64 * 64;
+      md->tarena = static_cast<float*>(dev_alloc(tot * sizeof(float)));
+      float* at = md->tarena;
+      for (Mat* m : downs) {
+        ew_transpose(at, m->w, m->rows, m->cols, ctx->stream);
+        m->t = at;
+        at += (m->rows * m->cols + 63) / 64 * 64;
+      }
+      SLM_CUDA(cudaStreamSynchronize(ctx->stream));
+    }
     *out = md.release();
   });
 }
@@ -1025,6 +1101,7 @@ int slm_model_free(slm_model* md) {
     cudaStreamSynchronize(md->ctx->stream);
     dev_free(md->arena);
     dev_free(md->planes);
+    dev_free(md->tarena);
     delete md;
   });
 }
@@ -1106,6 +1183,8 @@ int slm_session_new(slm_model* md, size_t loops, slm_session** out) {
           mega::prepare();
           if (mega::blocks_per_sm() >= 1) {
             se->grid = se->ctx->sms;  // one CTA per SM, all resident (cooperative launch)
+            // At most 255 CTAs add into a fused MLP slot, each part below 2^23.
+            se->fuse_mlp = md->tarena != nullptr && se->grid <= 255 && fuse_mlp_enabled();
             build_plan(se.get());
             se->mega_ok = true;
             se->use_mega = true;

@@ -1,9 +1,12 @@
 """bench.py's bookkeeping on CPU: algorithmic bytes and flops of the C2
-workload (SURVEY-style arithmetic restated from the model shapes) and the
-phase list of the persistent step (52 phases at R = 4 for S | LS | S)."""
+workload (restated from the model shapes) and the phase list of the
+persistent step (42 phases at R = 4 for S | LS | S with fused MLPs, 52 with
+two-phase MLPs)."""
 from __future__ import annotations
 
 import sys
+
+import numpy as np
 
 from conftest import ROOT, load_pkg
 
@@ -36,7 +39,14 @@ def test_prefill_flops_of_the_86m_config():
 
 def test_phase_kinds_match_the_plan_shape():
     b, syn = _bench(), _syn()
+    two = b.phase_kinds(syn.BASE, 4, fused=False)
+    assert len(two) == 52 and two[0] == "S1" and two[5] == "inject" and two[-1] == "logits"
+    assert len(b.phase_kinds(syn.GLOBAL, 4, fused=False)) == 57
+    assert two.count("attn") == 6 and two.count("gla") == 4
+    # Fused MLPs: one phase per block fewer (10 blocks at R = 4).
     kinds = b.phase_kinds(syn.BASE, 4)
-    assert len(kinds) == 52 and kinds[0] == "S1" and kinds[5] == "inject" and kinds[-1] == "logits"
-    assert len(b.phase_kinds(syn.GLOBAL, 4)) == 57
-    assert kinds.count("attn") == 6 and kinds.count("gla") == 4
+    assert len(kinds) == 42 and kinds[4] == "inject" and kinds.count("mlp") == 10
+    tr = np.zeros((42, 3, 8), dtype=np.int64)
+    assert b.trace_kinds(tr, syn.BASE, 4) == kinds
+    assert b.trace_kinds(np.zeros((52, 3, 8), dtype=np.int64), syn.BASE, 4) == two
+    assert b.trace_kinds(np.zeros((7, 3, 8), dtype=np.int64), syn.BASE, 4) is None

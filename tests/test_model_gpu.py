@@ -153,7 +153,7 @@ def test_persistent_kernel_matches_graph_path(slm, ctx, small):
     a, b = model.session(), model.session()
     b.set_mega(False)
     assert a.mega and not b.mega
-    assert a.stat(slm.SLM_STAT_PHASES) == 5 * (2 + 3 * 2) + 2  # 8 blocks of 5 phases + inject + logits
+    assert a.stat(slm.SLM_STAT_PHASES) == 4 * (2 + 3 * 2) + 2  # 8 blocks of 4 phases + inject + logits
     a.feed(ids[:300])
     b.feed(ids[:300])
     worst = 0.0
@@ -167,6 +167,46 @@ def test_persistent_kernel_matches_graph_path(slm, ctx, small):
     assert first == b.sample(greedy)
     np.testing.assert_array_equal(a.decode(first, 64, greedy), b.decode(first, 64, greedy))
     assert a.pos == b.pos
+
+
+@pytest.mark.parametrize("which", ["small", "g64"])
+def test_fused_mlp_matches_two_phase_mlp(slm, ctx, request, monkeypatch, which):
+    # The persistent step runs each MLP as one phase whose residual sum is
+    # int64 fixed point; SLM_MEGA_FUSE_MLP=0 keeps gate/up and down as two
+    # phases with float adds.  Same tokens, logits within fp32 noise; two fused
+    # sessions give bit-identical logits (integer sums do not depend on the
+    # order in which CTAs add).
+    model = slm.Model(ctx, request.getfixturevalue(which))
+    a = model.session()
+    monkeypatch.setenv("SLM_MEGA_FUSE_MLP", "0")
+    b = model.session()
+    monkeypatch.delenv("SLM_MEGA_FUSE_MLP")
+    c = model.session()
+    monkeypatch.setenv("SLM_MEGA_MLP_CTA", "1")  # tiles split by rows, a CTA barrier per tile
+    e = model.session()
+    monkeypatch.delenv("SLM_MEGA_MLP_CTA")
+    assert a.mega and b.mega and c.mega and e.mega
+    blocks = b.stat(slm.SLM_STAT_PHASES) - a.stat(slm.SLM_STAT_PHASES)
+    assert blocks > 0 and c.stat(slm.SLM_STAT_PHASES) == a.stat(slm.SLM_STAT_PHASES) == e.stat(slm.SLM_STAT_PHASES)
+    if which == "small":
+        assert blocks == 2 + 3 * 2
+    ids = np.random.default_rng(13).integers(0, 1000, 90)
+    for se in (a, b, c, e):
+        se.feed(ids)
+    tok = int(np.argmax(b.logits()))
+    worst = 0.0
+    for _ in range(40):
+        for se in (a, b, c, e):
+            se.step(tok)
+        la, lb, lc, le = a.logits(), b.logits(), c.logits(), e.logits()
+        worst = max(worst, float(np.abs(la - lb).max()), float(np.abs(le - lb).max()))
+        np.testing.assert_array_equal(la, lc)
+        tok = int(np.argmax(lb))
+    assert worst < 2e-5, worst
+    greedy = slm.Sampling()
+    first = a.sample(greedy)
+    assert first == b.sample(greedy) == c.sample(greedy)
+    np.testing.assert_array_equal(a.decode(first, 32, greedy), b.decode(first, 32, greedy))
 
 
 def test_persistent_kernel_sampling_path(slm, ctx, small):
