@@ -182,6 +182,27 @@ def rng_seed(seed: int) -> int:
     return int(lib().slm_rng_seed(seed))
 
 
+_SEED0: int | None = None
+_NO_RECENT = None
+
+
+def _seed0() -> int:
+    """rng_seed(0), computed once (the state a sample() call without one starts from)."""
+    global _SEED0
+    if _SEED0 is None:
+        _SEED0 = rng_seed(0)
+    return _SEED0
+
+
+def _no_recent():
+    """Pointer to a one-word buffer for calls with no recent ids (n = 0)."""
+    global _NO_RECENT
+    if _NO_RECENT is None:
+        arr = np.zeros(1, dtype=np.uint32)
+        _NO_RECENT = (arr, arr.ctypes.data_as(_u32p))
+    return _NO_RECENT[1]
+
+
 # ---------------------------------------------------------------------------
 # Context and buffers
 # ---------------------------------------------------------------------------
@@ -384,6 +405,16 @@ class Sampling:
     def _c(self) -> _Sampling:
         return _Sampling(self.temperature, self.top_k, self.top_p, self.repeat_penalty, self.repeat_window)
 
+    def _ref(self):
+        """byref of the C struct, rebuilt only when a field changed (per-token calls reuse it)."""
+        key = (self.temperature, self.top_k, self.top_p, self.repeat_penalty, self.repeat_window)
+        c = self.__dict__.get("_cache")
+        if c is None or c[0] != key:
+            sc = self._c()
+            c = (key, sc, _c.byref(sc))
+            self.__dict__["_cache"] = c
+        return c[2]
+
 
 class Model:
     """Model::load (src/model.rs:226-269) on a context."""
@@ -428,6 +459,9 @@ class Session:
         self._h = h
         self._free = lib().slm_session_free
         self.vocab = model.vocab
+        # Per-token sample() arguments, reused across calls.
+        self._st, self._out = _c.c_uint64(0), _c.c_uint32(0)
+        self._st_ref, self._out_ref = _c.byref(self._st), _c.byref(self._out)
 
     def close(self):
         # The free function is looked up while the module is intact: at
@@ -514,15 +548,17 @@ class Session:
 
     def sample(self, s: Sampling, recent=(), rng_state: list | None = None) -> int:
         """pick (src/sample.rs:33-93) on the device; rng_state is a one-element list."""
-        rec = _u32(recent if len(recent) else [0])
-        st = _c.c_uint64(rng_state[0] if rng_state is not None else rng_seed(0))
-        out = _c.c_uint32(0)
-        sc = s._c()
-        _check(lib().slm_sample(self._h, _c.byref(sc), rec.ctypes.data_as(_u32p), len(recent), _c.byref(st),
-                                _c.byref(out)))
+        if len(recent):
+            rec = _u32(recent)
+            rp, n = rec.ctypes.data_as(_u32p), rec.size
+        else:
+            rp, n = _no_recent(), 0
+        st = self._st
+        st.value = rng_state[0] if rng_state is not None else _seed0()
+        _check(lib().slm_sample(self._h, s._ref(), rp, n, self._st_ref, self._out_ref))
         if rng_state is not None:
             rng_state[0] = st.value
-        return out.value
+        return self._out.value
 
     def decode(self, first: int, n: int, s: Sampling, recent=(), rng_state: list | None = None) -> np.ndarray:
         """n steps on the device: feed `first`, then each sampled id."""

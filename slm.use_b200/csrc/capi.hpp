@@ -14,8 +14,10 @@ struct slm_ctx {
   int sms = 0;
   std::string name;
   cudaStream_t stream = nullptr;
-  int* err = nullptr;           // device error word (bad ids, sampler limits)
+  int* err = nullptr;           // device error word (bad ids, sampler limits); err[1]: the arg-max of
+                                // the last persistent step on this context (that of `argmax_owner`)
   int* err_host = nullptr;      // pinned copy of it (read after a synchronisation)
+  const void* argmax_owner = nullptr;  // session whose persistent step wrote err[1] last
   void* stage = nullptr;        // staging buffer for host arrays (ids, factors)
   size_t stage_bytes = 0;
   void* gemm_ws = nullptr;      // tensor-core GEMM workspace (grown on demand, outside captures)

@@ -529,7 +529,8 @@ struct Cons {
     if (own) {
       w = __ldg(reinterpret_cast<const float4*>(ph.norm_w) + tid);
       if (ph.in_mode == IN_EMBED_RMS) {
-        x = __ldg(reinterpret_cast<const float4*>(P.embed + (size_t)P.ids[0] * ph.cols) + tid);
+        const uint32_t id = P.host_id >= 0 ? (uint32_t)P.host_id : P.ids[0];
+        x = __ldg(reinterpret_cast<const float4*>(P.embed + (size_t)id * ph.cols) + tid);
         if (blockIdx.x == 0) {
           reinterpret_cast<float4*>(P.e0)[tid] = x;
           reinterpret_cast<float4*>(P.x0)[tid] = x;
@@ -1058,6 +1059,7 @@ struct Cons {
       if (tid == 0) {
         uint32_t id = sm.best ? 0xFFFFFFFFu - (uint32_t)(sm.best & 0xFFFFFFFFu) : 0;
         *P.argmax = id;
+        if (P.argmax2) *P.argmax2 = id;
         if (P.greedy) {
           P.next_id[0] = id;
           unsigned at = *P.out_index;

@@ -117,6 +117,7 @@ struct Plan {
   uint32_t* out_ids;    // out_ids[*out_index] = id, then ++*out_index
   unsigned* out_index;
   uint32_t* argmax;     // every step: the arg-max of its logits (first maximum; NaN never wins)
+  uint32_t* argmax2;    // the same id, beside the context's error word (one copy reads both)
   uint32_t* hist;       // optional history array (same index as out + hist_base)
   unsigned long long hist_base;
   unsigned* bar;        // grid barrier: [0] arrivals (monotonic in a step), [1] CTAs done
@@ -132,6 +133,7 @@ struct Plan {
   // than the grid has, so its bounded wait runs out (failure-path test).
   int test_stall;
   int global;  // the plan has global-attention layers (selects the kernel built for them)
+  long long host_id;  // ≥ 0: this step's token, passed with the launch; < 0: read ids[0]
   long long* fx;  // fixed-point slots of the fused MLP phases, zeroed at the start of each step
   int fx_words;
   int mlp_cta;    // 1: fused MLP tiles split by rows with a CTA barrier per tile (always for d > 768)

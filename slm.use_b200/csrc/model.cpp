@@ -699,6 +699,8 @@ void build_plan(slm_session* se, bool refresh = false) {
   P.out_index = words + 8;
   se->argmax_dev = words + 12;
   P.argmax = se->argmax_dev;
+  P.argmax2 = reinterpret_cast<uint32_t*>(se->ctx->err + 1);
+  P.host_id = -1;
   P.global = (c.prelude + c.core + c.coda).find('G') != std::string::npos ? 1 : 0;
   P.arg_part = static_cast<unsigned long long*>(alloc_zero(se, logit_items * sizeof(unsigned long long)));
   P.fx = se->fx;
@@ -718,11 +720,20 @@ void plan_outputs(slm_session* se, bool greedy, uint32_t* out, uint32_t* hist, u
   SLM_CUDA(cudaMemsetAsync(P.out_index, 0, sizeof(unsigned), se->ctx->stream));
 }
 
-void mega_step(slm_session* se) {
+// host_id ≥ 0: the step's token, passed in the launch parameters (no copy);
+// else the kernel reads ids_dev[0].
+void mega_step(slm_session* se, long long host_id = -1) {
   if (se->plan_stale) build_plan(se, true);
-  mega::launch(se->plan_host, se->grid, se->ctx->stream);
+  if (host_id >= 0) {
+    mega::Plan p = se->plan_host;
+    p.host_id = host_id;
+    mega::launch(p, se->grid, se->ctx->stream);
+  } else {
+    mega::launch(se->plan_host, se->grid, se->ctx->stream);
+  }
   se->pos += 1;
   se->argmax_valid = true;
+  se->ctx->argmax_owner = se;
 }
 
 // One decode step for the id already in ids_dev[0]: graph replay when enabled.
@@ -1232,6 +1243,7 @@ int slm_session_free(slm_session* se) {
     dev_free(se->outs_dev);
     if (se->io) cudaFreeHost(se->io);
     if (se->io_event) cudaEventDestroy(se->io_event);
+    if (se->ctx->argmax_owner == se) se->ctx->argmax_owner = nullptr;
     delete se;
   });
 }
@@ -1342,6 +1354,11 @@ int slm_step(slm_session* se, uint32_t id) {
     Device dev(se->ctx);
     // The pinned word is read by the copy engine in stream order; wait for an
     // earlier step's copy of it before overwriting.
+    if (se->use_mega) {  // the id travels with the launch
+      ensure_caps(se, 1);
+      mega_step(se, id);
+      return;
+    }
     if (se->io_busy) SLM_CUDA(cudaEventSynchronize(se->io_event));
     se->io->id_in = id;
     SLM_CUDA(cudaMemcpyAsync(se->ids_dev, &se->io->id_in, sizeof(uint32_t), cudaMemcpyHostToDevice, se->ctx->stream));
@@ -1393,8 +1410,17 @@ int slm_sample(slm_session* se, const slm_sampling* sp, const uint32_t* recent, 
     // wins) and pick draws nothing from the RNG (src/sample.rs:33-45).
     const bool fast = se->argmax_valid && sp->temperature <= 0.0f && (sp->repeat_penalty == 1.0f || n_recent == 0);
     if (fast) {
+      slm_ctx* c = se->ctx;
+      if (c->argmax_owner == se) {  // one copy: the error word and this step's arg-max beside it
+        SLM_CUDA(cudaMemcpyAsync(c->err_host, c->err, 2 * sizeof(int), cudaMemcpyDeviceToHost, s));
+        SLM_CUDA(cudaStreamSynchronize(s));
+        if (c->err_host[0]) check_device_error(c, se);  // reports it
+        se->io_busy = false;
+        *out_id = static_cast<uint32_t>(c->err_host[1]);
+        return;
+      }
       SLM_CUDA(cudaMemcpyAsync(&se->io->id_out, se->argmax_dev, sizeof(uint32_t), cudaMemcpyDeviceToHost, s));
-      check_device_error(se->ctx, se);
+      check_device_error(c, se);
       se->io_busy = false;  // the stream is idle
       *out_id = se->io->id_out;
       return;

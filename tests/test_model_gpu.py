@@ -249,6 +249,31 @@ def test_greedy_sample_after_persistent_steps(slm, ctx, oracle, small):
         assert tok == want
 
 
+def test_greedy_sample_with_interleaved_sessions(slm, ctx, small):
+    # Persistent steps pass the id in the launch and greedy sampling reads the
+    # arg-max beside the context's error word when this session stepped last;
+    # sessions stepped in turn on one context must each get their own.
+    model = slm.Model(ctx, small)
+    a, b = model.session(), model.session()
+    rng = np.random.default_rng(14)
+    a.feed(rng.integers(0, 1000, 30))
+    b.feed(rng.integers(0, 1000, 50))
+    greedy = slm.Sampling()
+    ta, tb = a.sample(greedy), b.sample(greedy)
+    for i in range(10):
+        a.step(ta)
+        b.step(tb)
+        if i % 3 == 2:
+            a.step(ta)  # two steps of a in a row: the later one counts
+        la, lb = a.logits(), b.logits()
+        ta, tb = a.sample(greedy), b.sample(greedy)
+        assert ta == int(np.argmax(la)) and tb == int(np.argmax(lb))
+        assert a.sample(greedy) == ta  # sampling again reads the same step
+    b.close()
+    a.step(ta)
+    assert a.sample(greedy) == int(np.argmax(a.logits()))
+
+
 @pytest.fixture(scope="module")
 def g64(tmp_path_factory):
     load_pkg()
