@@ -714,9 +714,11 @@ def main():
         "n_gpus": world, "steps": K, "warmup": args.warmup, "ms_per_step": res["dec_ms"] / K,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (N(0,0.02) random init, uniform random ids, seed 0 / rank)", "config": config,
-        "e2e": {"value": world * K / res["e2e_s"], "unit": "tok/s", "h2d_bytes_per_step": 12,
-                "d2h_bytes_per_step": 16,
-                "how": "per token slm_step(host id) + slm_sample -> host id, host clock"},
+        "e2e": {"value": world * K / res["e2e_s"], "unit": "tok/s", "h2d_bytes_per_step": 4,
+                "d2h_bytes_per_step": 8,
+                "how": "per token slm_step(host id) + slm_sample -> host id, host clock; the id goes in the "
+                       "persistent kernel's launch parameters, the picked id and the error word come back in "
+                       "one 8-byte copy"},
         "prefill": {"value": world * args.prompt / (res["prefill_ms"] / 1000.0), "unit": "tok/s",
                     "e2e_value": world * args.prompt / res["prefill_host_s"], "prompt": args.prompt,
                     "tflops_fp32": pre_flops / (res["prefill_ms"] / 1000.0) / 1e12,
