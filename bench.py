@@ -305,11 +305,14 @@ def ref_cuda_measure(cases, device: int) -> dict | None:
 # Device timeline of the persistent decode step (--trace)
 # ---------------------------------------------------------------------------
 
-def phase_kinds(cfg: dict, loops: int, fused: bool = True) -> list[str]:
+def phase_kinds(cfg: dict, loops: int, fused: bool = True, attn_o: bool | None = None) -> list[str]:
     """Phase names of the persistent step, in plan order (model.cpp build_plan).
-    fused: each MLP is one phase ("mlp"); else gate/up ("up") and down."""
+    fused: each MLP is one phase ("mlp"); else gate/up ("up") and down.
+    attn_o (default: fused): S blocks run o in their attention phase ("attn")."""
+    attn_o = fused if attn_o is None else attn_o
     mlp = ["mlp"] if fused else ["up", "down"]
-    names = {"S": ["S1", "attn", "o"] + mlp, "L": ["L1", "gla", "o"] + mlp, "G": ["G1", "gattn", "o"] + mlp}
+    s_mix = ["S1", "attn"] if attn_o else ["S1", "attn", "o"]
+    names = {"S": s_mix + mlp, "L": ["L1", "gla", "o"] + mlp, "G": ["G1", "gattn", "o"] + mlp}
     out = [n for k in cfg["prelude"] for n in names[k]]
     if cfg["core"]:
         out.append("inject")
@@ -320,8 +323,8 @@ def phase_kinds(cfg: dict, loops: int, fused: bool = True) -> list[str]:
 
 def trace_kinds(tr: np.ndarray, cfg: dict, loops: int) -> list[str] | None:
     """Phase names for a traced step of either plan shape (None if neither fits)."""
-    for fused in (True, False):
-        kinds = phase_kinds(cfg, loops, fused)
+    for fused, attn_o in ((True, True), (True, False), (False, False)):
+        kinds = phase_kinds(cfg, loops, fused, attn_o)
         if len(kinds) == tr.shape[0]:
             return kinds
     return None

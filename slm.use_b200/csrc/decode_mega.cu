@@ -76,6 +76,14 @@ __device__ __forceinline__ float lds1(uint32_t a) {
   asm volatile("ld.shared.f32 %0, [%1];" : "=f"(v) : "r"(a));
   return v;
 }
+__device__ __forceinline__ void red_release_add_u64(unsigned long long* p, unsigned long long v) {
+  asm volatile("red.release.gpu.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_acquire_u64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
 __device__ __forceinline__ void red_add_u64(long long* p, long long v) {
   asm volatile("red.relaxed.gpu.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
@@ -143,6 +151,13 @@ __device__ __forceinline__ float4 fx_load4(const long long* fx, int i4, int d) {
   if (__ldcg(fx + d) != 0) return make_float4(NAN, NAN, NAN, NAN);
   return make_float4(__ll2float_rn(a.x) * kFxInv, __ll2float_rn(a.y) * kFxInv, __ll2float_rn(b.x) * kFxInv,
                      __ll2float_rn(b.y) * kFxInv);
+}
+
+// Value i of a fixed-point slot (d wide) as a float (NaN when the slot is flagged).
+__device__ __forceinline__ float fx_load1(const long long* fx, int i, int d) {
+  const long long a = __ldcg(fx + i);
+  if (__ldcg(fx + d) != 0) return NAN;
+  return __ll2float_rn(a) * kFxInv;
 }
 
 // ---------------------------------------------------------------------------
@@ -221,6 +236,7 @@ struct Walker {
   int me, G;
   int p = 0, i = -1, seg = 0;
   long long t = 0, tend = 0;
+  int extra = 0;  // ATTN with o: the o tile follows the item's K/V tiles
 
   __device__ Walker(const Plan* pl, long long ps) : P(pl), pos(ps) {
     me = blockIdx.x;
@@ -237,6 +253,7 @@ struct Walker {
     } else {
       t = 0, tend = 1;
     }
+    extra = ph.kind == PH_ATTN && ph.wo ? 1 : 0;
   }
 
   __device__ bool next(Tile& T) {
@@ -252,6 +269,15 @@ struct Walker {
       }
       if (t < tend) {
         make(ph, T);
+        return true;
+      }
+      if (extra) {  // rows s·orows … of head h's o block
+        const int h = i / ph.splits, s = i % ph.splits;
+        T.n = 1;
+        T.src[0] = ph.wo + ((size_t)h * P->d + (size_t)s * ph.orows) * kDH;
+        T.bytes[0] = T.total = (unsigned)ph.orows * kDH * 4;
+        T.off[0] = 0;
+        extra = 0;
         return true;
       }
       i += G;
@@ -874,7 +900,7 @@ struct Cons {
   // with n = rms(x)·w.  Each CTA sums its hidden units' down columns on chip
   // and adds them, as int64 fixed point, into the phase's slot; CTA 0 also adds
   // the residual x.  The next phase reads x' from the slot.
-  __device__ __noinline__ void mlp_phase(const Phase& ph) {
+  __device__ __forceinline__ void mlp_phase(const Phase& ph) {
     unsigned long long t0 = P.trace && tid == 0 ? now_ns() : 0;
     rms_prologue(ph);  // the plan gives fused MLPs IN_RMS inputs
     if (t0) pro_ns += now_ns() - t0;
@@ -1218,6 +1244,111 @@ struct Cons {
     if (e0) epi_ns += now_ns() - e0;
   }
 
+  // Attention + o (S blocks).  The CTA of (head h, split s) has written its
+  // partial; it counts itself in for h and waits (bounded) for the head's
+  // other splits, merges the partials in split order (as the o prologue's
+  // merge does), multiplies rows s·R … s·R + R − 1 of h's o block (one tile;
+  // four threads per row) and adds them into the fixed-point slot; head 0's
+  // CTAs add the residual rows.  Every output row gets one part per head.
+  // The residual rows and the tile are fetched before the wait.
+  __device__ __forceinline__ void attn_o_tail(const Phase& ph, int h, int s) {
+    constexpr int RQ = kMaxItemOut / 64;  // rows per thread: r = tid / 4 + 64·k
+    const int R = ph.orows, q4 = tid & 3;
+    float res[RQ];
+#pragma unroll
+    for (int k = 0; k < RQ; k++) {
+      const int r = (tid >> 2) + 64 * k;
+      res[k] = 0.0f;
+      if (h == 0 && q4 == 0 && r < R)
+        res[k] = ph.fx_in ? fx_load1(ph.fx_in, s * R + r, P.d) : __ldcg(ph.in_a + s * R + r);
+    }
+    const float* w = take_warp();
+    if (tid == 0) {
+      red_release_add_u64(ph.cnt + h, 1ull);  // after the partial (ordered by the barrier above)
+      unsigned long long t0 = 0;
+      for (unsigned it = 0; ld_acquire_u64(ph.cnt + h) < (unsigned long long)ph.splits; it++) {
+        if ((it & 15) == 15) {
+          if (ld_volatile(P.err) & 8) {
+            sm.flag = 1;
+            break;
+          }
+          if (!t0) {
+            t0 = now_ns();
+          } else if (now_ns() - t0 > kWaitNs) {
+            atomicOr(P.err, 8);
+            sm.flag = 1;
+            break;
+          }
+        }
+      }
+    }
+    consumers_sync();
+    if (sm.flag == 1) ok = false;
+    // The merge, in split order: every load first (one round trip), the split
+    // weights c_j = e^(m_j − M) once per split through shared memory.
+    const float* pp = ph.part + (size_t)h * ph.splits * (kDH + 2);
+    float av[kMaxSplits];
+    if (ok && tid < kDH) {
+#pragma unroll
+      for (int j = 0; j < kMaxSplits; j++)
+        if (j < ph.splits) av[j] = __ldcg(pp + (size_t)j * (kDH + 2) + tid);
+    }
+    if (ok && tid >= kDH && tid < kDH + ph.splits) {
+      const int j = tid - kDH;
+      sm.cmb[j][0] = __ldcg(pp + (size_t)j * (kDH + 2) + kDH);
+      sm.cmb[j][1] = __ldcg(pp + (size_t)j * (kDH + 2) + kDH + 1);
+    }
+    consumers_sync();
+    if (ok && tid < ph.splits) {
+      float M = -INFINITY;
+      for (int j = 0; j < ph.splits; j++) M = fmaxf(M, sm.cmb[j][0]);
+      const float m = sm.cmb[tid][0];
+      sm.cmb[tid][2] = (M == -INFINITY || m == -INFINITY) ? 0.0f : expf(m - M);
+    }
+    consumers_sync();
+    if (ok && tid < kDH) {
+      float A = 0.0f, L = 0.0f;
+#pragma unroll
+      for (int j = 0; j < kMaxSplits; j++)
+        if (j < ph.splits) {
+          const float c = sm.cmb[j][2];
+          L += sm.cmb[j][1] * c;
+          A = fmaf(av[j], c, A);
+        }
+      sm.vec[0][tid] = L > 0.0f ? A / L : 0.0f;
+    }
+    consumers_sync();
+    // Row r = tid / 4 (+ 64·k): thread q4 takes columns 4·q4 + 16·i … + 3.
+    bool bad = false;
+    if (ok) {
+      const float4* y4 = reinterpret_cast<const float4*>(sm.vec[0]);
+      float4 yq[4];
+#pragma unroll
+      for (int i = 0; i < 4; i++) yq[i] = y4[q4 + 4 * i];
+#pragma unroll
+      for (int k = 0; k < RQ; k++) {
+        const int r = (tid >> 2) + 64 * k;
+        if (64 * k >= R) break;  // uniform
+        float v = 0.0f;
+        if (r < R) {
+          const uint32_t a = saddr(w + (size_t)r * kDH) + q4 * 16;
+#pragma unroll
+          for (int i = 0; i < 4; i++) v = dot4(lds4(a + 64 * i), yq[i], v);
+        }
+        v += __shfl_xor_sync(0xffffffffu, v, 1);
+        v += __shfl_xor_sync(0xffffffffu, v, 2);
+        if (q4 == 0 && r < R) {
+          v += res[k];
+          if (!(fabsf(v) < kFxMax)) bad = true;  // NaN included
+          red_add_u64(ph.fx_out + s * R + r, __float2ll_rn(v * kFxScale));
+        }
+      }
+    }
+    release();
+    if (bad) atomicOr(reinterpret_cast<unsigned long long*>(ph.fx_out + P.d), 1ull);
+    all_ok();  // sm.cmb and sm.vec are free; ok uniform
+  }
+
   __device__ void attn_item(const Phase& ph, int item) {
     if (!GL) {
       attn_item_t<1>(ph, item);
@@ -1312,6 +1443,8 @@ struct Cons {
         gemv_phase(ph);
       } else if (ph.kind == PH_ATTN) {
         for (int i = blockIdx.x; i < ph.items && ok; i += gridDim.x) attn_item(ph, i);
+        // S blocks with o: one item per CTA (items ≤ grid), QG = 1 (the cache head is the head).
+        if (ph.wo && blockIdx.x < ph.items && ok) attn_o_tail(ph, blockIdx.x / ph.splits, blockIdx.x % ph.splits);
       } else {
         for (int i = blockIdx.x; i < ph.items && ok; i += gridDim.x) gla_item(ph, i);
       }

@@ -312,6 +312,22 @@ __global__ void k_transpose(float* __restrict__ dst, const float* __restrict__ s
   }
 }
 
+// dst[h][r][c] = src[r][h·dh + c]: the column blocks of a [rows][heads·dh]
+// matrix, each contiguous.
+__global__ void k_head_blocks(float* __restrict__ dst, const float* __restrict__ src, size_t rows, int heads, int dh) {
+  const size_t cols = (size_t)heads * dh, n = rows * cols;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+    const size_t r = i / cols, k = i % cols, h = k / dh, c = k % dh;
+    dst[(h * rows + r) * dh + c] = src[i];
+  }
+}
+
+void ew_head_blocks(float* dst, const float* src, size_t rows, size_t heads, size_t dh, cudaStream_t st) {
+  if (!rows || !heads || !dh) return;
+  k_head_blocks<<<ew_grid(rows * heads * dh), EW, 0, st>>>(dst, src, rows, (int)heads, (int)dh);
+  SLM_LAUNCHED("k_head_blocks");
+}
+
 void ew_transpose(float* dst, const float* src, size_t rows, size_t cols, cudaStream_t st) {
   if (!rows || !cols) return;
   SLM_REQUIRE(rows <= (size_t)65535 * 32 && cols < (size_t)1 << 31, "matrix too large to transpose");

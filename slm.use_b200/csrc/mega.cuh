@@ -87,6 +87,13 @@ struct alignas(16) Phase {
   long long* fx_out;
   // Inputs: when set, the `a` input is this fixed-point slot instead of in_a
   const long long* fx_in;
+  // ATTN with o (S blocks): the o matrix as per-head column blocks [heads][d][dh];
+  // split s multiplies rows s·orows … of its head's block, after the head's
+  // `splits` partials have arrived (per-head counters `cnt`, zeroed each step),
+  // and adds them into fx_out (head 0's CTAs also add the residual in_a/fx_in).
+  const float* wo;
+  int orows;
+  unsigned long long* cnt;
   // ATTN: heads × splits items; partials and per-head arrival counters
   int heads, splits;
   float* part;
@@ -134,7 +141,7 @@ struct Plan {
   int test_stall;
   int global;  // the plan has global-attention layers (selects the kernel built for them)
   long long host_id;  // ≥ 0: this step's token, passed with the launch; < 0: read ids[0]
-  long long* fx;  // fixed-point slots of the fused MLP phases, zeroed at the start of each step
+  long long* fx;  // fixed-point slots of fused phases and their counters, zeroed at the start of each step
   int fx_words;
   int mlp_cta;    // 1: fused MLP tiles split by rows with a CTA barrier per tile (always for d > 768)
 };

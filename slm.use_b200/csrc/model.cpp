@@ -38,6 +38,7 @@ struct Mat {
   size_t rows = 0, cols = 0;
   const void* planes = nullptr;  // bf16 parts for chunk linears (gemm_bf16x3.cu), in the model's plane arena
   const float* t = nullptr;      // down only: the transpose ([cols][rows]) read by the fused decode MLP
+  const float* hb = nullptr;     // o of S blocks: per-head column blocks [heads][rows][dh] (fused attention + o)
 };
 
 struct Block {
@@ -110,6 +111,7 @@ struct slm_session {
   unsigned* attn_count = nullptr;        // per-head arrival counters of the attention phases
   float* attn_part = nullptr;            // attention partials of the persistent step
   bool fuse_mlp = false;                 // the persistent step runs each MLP as one phase
+  bool fuse_ao = false;                  // … and the o projection of S blocks in the attention phase
   long long* fx = nullptr;               // fixed-point slots of those phases
   bool plan_stale = false;               // a global cache moved: the phase descriptors need refreshing
   int in_batches = 0;                    // batches holding this session
@@ -459,6 +461,13 @@ bool fuse_mlp_enabled() {
   return !(e && e[0] == '0');
 }
 
+// SLM_MEGA_FUSE_ATTN_O=0 keeps the o projection of S blocks as its own phase
+// (the default runs it in the attention phase).
+bool fuse_attn_o_enabled() {
+  const char* e = std::getenv("SLM_MEGA_FUSE_ATTN_O");
+  return !(e && e[0] == '0');
+}
+
 // SLM_MEGA_MLP_CTA=1 splits each fused MLP tile's rows over the CTA's warps
 // (a CTA barrier per tile) instead of giving each warp whole hidden units.
 bool mlp_cta_setting() {
@@ -546,10 +555,18 @@ void build_plan(slm_session* se, bool refresh = false) {
   // is the slot holding buffer buf's current value when a fused MLP wrote it
   // last (its readers take the slot; the float buffer is stale).
   const size_t nmlp = md->prelude.size() + se->loops * md->core.size() + md->coda.size();
+  // S blocks: attention and o in one phase (items ≤ grid, so every split of a
+  // head is resident while it waits for the others; o rows split evenly).
+  auto nS = [](const std::string& k) { return (size_t)std::count(k.begin(), k.end(), 'S'); };
+  const size_t nao = nS(c.prelude) + se->loops * nS(c.core) + nS(c.coda);
+  const bool fuse_ao = se->fuse_mlp && se->fuse_ao && H * splits <= G && d % splits == 0 && d / splits <= kMaxItemOut &&
+                       (size_t)(d / splits) * kDH * 4 <= (size_t)kStageBytes;
   const size_t slot_words = (size_t)d + 2;
+  const size_t nslots = se->fuse_mlp ? nmlp + (fuse_ao ? nao : 0) : 0;
+  const size_t ncnt = fuse_ao ? nao * H : 0;
   if (!refresh && se->fuse_mlp)
-    se->fx = static_cast<long long*>(alloc_zero(se, nmlp * slot_words * sizeof(long long)));
-  size_t next_slot = 0;
+    se->fx = static_cast<long long*>(alloc_zero(se, (nslots * slot_words + ncnt) * sizeof(long long)));
+  size_t next_slot = 0, next_cnt = 0;
   std::vector<std::pair<const float*, long long*>> fxw;
   auto fx_of = [&](const float* buf) -> const long long* {
     for (auto& e : fxw)
@@ -569,6 +586,23 @@ void build_plan(slm_session* se, bool refresh = false) {
     const float *a, *b, *c;
     float* xout;
   };
+  auto block_mlp = [&](const Block& b, float* X) {
+    const int F = (int)b.down.cols;
+    if (se->fuse_mlp) {
+      Phase u = gemv(d, IN_RMS, X, nullptr, nullptr, b.norm2, nullptr, OUT_MLP, seg(b.up.w, F, per(F, G, 1), nullptr));
+      u.wt = b.down.t;
+      u.fx_in = fx_of(X);
+      u.fx_out = se->fx + slot_words * next_slot++;
+      ph.push_back(u);
+      fx_set(X, u.fx_out);
+      return;
+    }
+    ph.push_back(gemv(d, IN_RMS, X, nullptr, nullptr, b.norm2, nullptr, OUT_SILU,
+                      seg(b.up.w, F, per(F, G, 1), se->mid)));
+    ph.push_back(gemv(F, IN_PLAIN, se->mid, nullptr, nullptr, nullptr, nullptr, OUT_ADD,
+                      seg(b.down.w, d, per(d, G, 1), X)));
+    ph.back().res_smem = 1;
+  };
   auto block = [&](const Block& b, LState& st, float* X, In in) {
     const float* ia = in.mode == IN_RMS ? X : in.a;
     if (b.kind == 'S') {
@@ -577,11 +611,24 @@ void build_plan(slm_session* se, bool refresh = false) {
       p.q = se->q, p.kc = st.k, p.vc = st.v, p.cap = (long long)st.cap, p.inv_freq = md->inv_freq;
       p.fx_in = fx_of(ia);
       ph.push_back(p);
+      if (in.mode == IN_LOOP_RMS || in.mode == IN_EMBED_RMS) fx_set(X, nullptr);  // that prologue wrote x to X
       Phase a{};
       a.kind = PH_ATTN;
       a.kc = st.k, a.vc = st.v, a.q = se->q, a.cap = (long long)st.cap, a.window = (long long)c.window;
       a.heads = H, a.splits = splits, a.part = attn_part, a.counters = attn_count;
       a.y = se->y, a.scale = scale, a.items = H * splits;
+      if (fuse_ao && b.o.hb) {
+        a.wo = b.o.hb;
+        a.orows = d / splits;
+        a.cnt = reinterpret_cast<unsigned long long*>(se->fx + nslots * slot_words) + H * next_cnt++;
+        a.in_a = X;
+        a.fx_in = fx_of(X);  // the residual
+        a.fx_out = se->fx + slot_words * next_slot++;
+        ph.push_back(a);
+        fx_set(X, a.fx_out);
+        block_mlp(b, X);
+        return;
+      }
       ph.push_back(a);
     } else if (b.kind == 'G') {
       // q and kv from n = rms(x)·w (+ rms(e0)·w_e); n becomes the next shift
@@ -630,20 +677,7 @@ void build_plan(slm_session* se, bool refresh = false) {
     }
     ph.back().res_smem = 1;
     fx_set(X, nullptr);  // o wrote the float x
-    const int F = (int)b.down.cols;
-    if (se->fuse_mlp) {
-      Phase u = gemv(d, IN_RMS, X, nullptr, nullptr, b.norm2, nullptr, OUT_MLP, seg(b.up.w, F, per(F, G, 1), nullptr));
-      u.wt = b.down.t;
-      u.fx_out = se->fx + slot_words * next_slot++;
-      ph.push_back(u);
-      fx_set(X, u.fx_out);
-      return;
-    }
-    ph.push_back(gemv(d, IN_RMS, X, nullptr, nullptr, b.norm2, nullptr, OUT_SILU,
-                      seg(b.up.w, F, per(F, G, 1), se->mid)));
-    ph.push_back(gemv(F, IN_PLAIN, se->mid, nullptr, nullptr, nullptr, nullptr, OUT_ADD,
-                      seg(b.down.w, d, per(d, G, 1), X)));
-    ph.back().res_smem = 1;
+    block_mlp(b, X);
   };
   for (size_t i = 0; i < md->prelude.size(); i++)
     block(md->prelude[i], se->pre[i], X0, In{i == 0 ? IN_EMBED_RMS : IN_RMS, nullptr, nullptr, nullptr, nullptr});
@@ -670,7 +704,7 @@ void build_plan(slm_session* se, bool refresh = false) {
                     seg(md->embed.w, (int)c.vocab, per((int)c.vocab, G, 1), se->logits)));
   ph.back().fx_in = fx_of(X);
   const int logit_items = ph.back().items;
-  SLM_REQUIRE(next_slot == (se->fuse_mlp ? nmlp : 0), "fused MLP slots out of step");
+  SLM_REQUIRE(next_slot <= nslots && next_cnt * H <= ncnt, "fused-phase slots out of step");
 
   if (refresh) {
     SLM_REQUIRE((int)ph.size() == se->plan_host.nphases, "decode plan changed shape");
@@ -704,7 +738,7 @@ void build_plan(slm_session* se, bool refresh = false) {
   P.global = (c.prelude + c.core + c.coda).find('G') != std::string::npos ? 1 : 0;
   P.arg_part = static_cast<unsigned long long*>(alloc_zero(se, logit_items * sizeof(unsigned long long)));
   P.fx = se->fx;
-  P.fx_words = se->fuse_mlp ? (int)(nmlp * slot_words) : 0;
+  P.fx_words = se->fuse_mlp ? (int)(nslots * slot_words + ncnt) : 0;
   P.mlp_cta = d > kMaxCols / 4 || mlp_cta_setting() ? 1 : 0;
   P.next_id = se->ids_dev;
   P.err = se->ctx->err;
@@ -1084,19 +1118,29 @@ int slm_model_load(slm_ctx* ctx, const char* dir, slm_model** out) {
       }
       SLM_CUDA(cudaStreamSynchronize(ctx->stream));
     }
-    // The fused MLP phase of the persistent step reads down by columns: keep
-    // a transposed copy of each down matrix when that kernel can run.
+    // The fused phases of the persistent step read down by columns and the
+    // o of S blocks by head: keep those layouts beside the originals when that
+    // kernel can run.
     if (mega_unsupported(md.get()).empty() && fuse_mlp_enabled()) {
-      std::vector<Mat*> downs;
+      std::vector<Mat*> downs, os;
       for (auto* bs : {&md->prelude, &md->core, &md->coda})
-        for (auto& b : *bs) downs.push_back(&b.down);
+        for (auto& b : *bs) {
+          downs.push_back(&b.down);
+          if (b.kind == 'S') os.push_back(&b.o);
+        }
       size_t tot = 0;
       for (Mat* m : downs) tot += (m->rows * m->cols + 63) / 64 * 64;
+      for (Mat* m : os) tot += (m->rows * m->cols + 63) / 64 * 64;
       md->tarena = static_cast<float*>(dev_alloc(tot * sizeof(float)));
       float* at = md->tarena;
       for (Mat* m : downs) {
         ew_transpose(at, m->w, m->rows, m->cols, ctx->stream);
         m->t = at;
+        at += (m->rows * m->cols + 63) / 64 * 64;
+      }
+      for (Mat* m : os) {
+        ew_head_blocks(at, m->w, m->rows, c.heads, c.dh(), ctx->stream);
+        m->hb = at;
         at += (m->rows * m->cols + 63) / 64 * 64;
       }
       SLM_CUDA(cudaStreamSynchronize(ctx->stream));
@@ -1196,6 +1240,7 @@ int slm_session_new(slm_model* md, size_t loops, slm_session** out) {
             se->grid = se->ctx->sms;  // one CTA per SM, all resident (cooperative launch)
             // At most 255 CTAs add into a fused MLP slot, each part below 2^23.
             se->fuse_mlp = md->tarena != nullptr && se->grid <= 255 && fuse_mlp_enabled();
+            se->fuse_ao = fuse_attn_o_enabled();
             build_plan(se.get());
             se->mega_ok = true;
             se->use_mega = true;

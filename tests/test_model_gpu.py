@@ -153,7 +153,8 @@ def test_persistent_kernel_matches_graph_path(slm, ctx, small):
     a, b = model.session(), model.session()
     b.set_mega(False)
     assert a.mega and not b.mega
-    assert a.stat(slm.SLM_STAT_PHASES) == 4 * (2 + 3 * 2) + 2  # 8 blocks of 4 phases + inject + logits
+    # 5 S blocks of 3 phases (attention with o, one MLP phase), 3 L blocks of 4, inject, logits
+    assert a.stat(slm.SLM_STAT_PHASES) == 3 * 5 + 4 * 3 + 2
     a.feed(ids[:300])
     b.feed(ids[:300])
     worst = 0.0
@@ -185,21 +186,24 @@ def test_fused_mlp_matches_two_phase_mlp(slm, ctx, request, monkeypatch, which):
     monkeypatch.setenv("SLM_MEGA_MLP_CTA", "1")  # tiles split by rows, a CTA barrier per tile
     e = model.session()
     monkeypatch.delenv("SLM_MEGA_MLP_CTA")
-    assert a.mega and b.mega and c.mega and e.mega
-    blocks = b.stat(slm.SLM_STAT_PHASES) - a.stat(slm.SLM_STAT_PHASES)
-    assert blocks > 0 and c.stat(slm.SLM_STAT_PHASES) == a.stat(slm.SLM_STAT_PHASES) == e.stat(slm.SLM_STAT_PHASES)
-    if which == "small":
-        assert blocks == 2 + 3 * 2
+    monkeypatch.setenv("SLM_MEGA_FUSE_ATTN_O", "0")  # S blocks keep o as its own phase
+    f = model.session()
+    monkeypatch.delenv("SLM_MEGA_FUSE_ATTN_O")
+    assert a.mega and b.mega and c.mega and e.mega and f.mega
+    n = {k: se.stat(slm.SLM_STAT_PHASES) for k, se in zip("abcef", (a, b, c, e, f))}
+    assert n["a"] == n["c"] == n["e"] < n["f"] < n["b"]
+    if which == "small":  # 5 S and 3 L blocks
+        assert n["b"] - n["f"] == 8 and n["f"] - n["a"] == 5
     ids = np.random.default_rng(13).integers(0, 1000, 90)
-    for se in (a, b, c, e):
+    for se in (a, b, c, e, f):
         se.feed(ids)
     tok = int(np.argmax(b.logits()))
     worst = 0.0
     for _ in range(40):
-        for se in (a, b, c, e):
+        for se in (a, b, c, e, f):
             se.step(tok)
-        la, lb, lc, le = a.logits(), b.logits(), c.logits(), e.logits()
-        worst = max(worst, float(np.abs(la - lb).max()), float(np.abs(le - lb).max()))
+        la, lb, lc, le, lf = a.logits(), b.logits(), c.logits(), e.logits(), f.logits()
+        worst = max(worst, *(float(np.abs(x - lb).max()) for x in (la, le, lf)))
         np.testing.assert_array_equal(la, lc)
         tok = int(np.argmax(lb))
     assert worst < 2e-5, worst
