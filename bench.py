@@ -308,11 +308,11 @@ def ref_cuda_measure(cases, device: int) -> dict | None:
 def phase_kinds(cfg: dict, loops: int, fused: bool = True, attn_o: bool | None = None) -> list[str]:
     """Phase names of the persistent step, in plan order (model.cpp build_plan).
     fused: each MLP is one phase ("mlp"); else gate/up ("up") and down.
-    attn_o (default: fused): S blocks run o in their attention phase ("attn")."""
+    attn_o (default: fused): S and L blocks run o in their attention / GLA phase."""
     attn_o = fused if attn_o is None else attn_o
     mlp = ["mlp"] if fused else ["up", "down"]
-    s_mix = ["S1", "attn"] if attn_o else ["S1", "attn", "o"]
-    names = {"S": s_mix + mlp, "L": ["L1", "gla", "o"] + mlp, "G": ["G1", "gattn", "o"] + mlp}
+    o = [] if attn_o else ["o"]
+    names = {"S": ["S1", "attn"] + o + mlp, "L": ["L1", "gla"] + o + mlp, "G": ["G1", "gattn", "o"] + mlp}
     out = [n for k in cfg["prelude"] for n in names[k]]
     if cfg["core"]:
         out.append("inject")

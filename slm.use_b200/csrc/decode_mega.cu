@@ -251,9 +251,9 @@ struct Walker {
     } else if (ph.kind == PH_ATTN) {
       attn_slice(ph, pos, i % ph.splits, &t, &tend);
     } else {
-      t = 0, tend = 1;
+      t = 0, tend = !ph.wo || i % ph.splits == 0 ? 1 : 0;  // with o: the state goes to split 0
     }
-    extra = ph.kind == PH_ATTN && ph.wo ? 1 : 0;
+    extra = ph.wo ? 1 : 0;
   }
 
   __device__ bool next(Tile& T) {
@@ -322,7 +322,8 @@ struct Walker {
       }
       t += n;
     } else {
-      T.src[0] = ph.state + (size_t)i * kDH * kDH, T.bytes[0] = kDH * kDH * 4, T.off[0] = 0, T.n = 1;
+      const int h = ph.wo ? i / ph.splits : i;
+      T.src[0] = ph.state + (size_t)h * kDH * kDH, T.bytes[0] = kDH * kDH * 4, T.off[0] = 0, T.n = 1;
       t += 1;
     }
     T.total = 0;
@@ -1251,7 +1252,11 @@ struct Cons {
   // four threads per row) and adds them into the fixed-point slot; head 0's
   // CTAs add the residual rows.  Every output row gets one part per head.
   // The residual rows and the tile are fetched before the wait.
-  __device__ __forceinline__ void attn_o_tail(const Phase& ph, int h, int s) {
+  __device__ __forceinline__ void attn_o_tail(const Phase& ph, int h, int s) { mixer_o_tail(ph, h, s, false); }
+
+  // The same for L blocks: split 0 of head h ran the GLA and wrote y_h; every
+  // split of h waits for that one arrival and reads y_h instead of merging.
+  __device__ __forceinline__ void mixer_o_tail(const Phase& ph, int h, int s, bool gla) {
     constexpr int RQ = kMaxItemOut / 64;  // rows per thread: r = tid / 4 + 64·k
     const int R = ph.orows, q4 = tid & 3;
     float res[RQ];
@@ -1264,9 +1269,11 @@ struct Cons {
     }
     const float* w = take_warp();
     if (tid == 0) {
-      red_release_add_u64(ph.cnt + h, 1ull);  // after the partial (ordered by the barrier above)
+      // after the partial or y_h (ordered by the barrier above)
+      if (!gla || s == 0) red_release_add_u64(ph.cnt + h, 1ull);
+      const unsigned long long want = gla ? 1ull : (unsigned long long)ph.splits;
       unsigned long long t0 = 0;
-      for (unsigned it = 0; ld_acquire_u64(ph.cnt + h) < (unsigned long long)ph.splits; it++) {
+      for (unsigned it = 0; ld_acquire_u64(ph.cnt + h) < want; it++) {
         if ((it & 15) == 15) {
           if (ld_volatile(P.err) & 8) {
             sm.flag = 1;
@@ -1288,25 +1295,27 @@ struct Cons {
     // weights c_j = e^(m_j − M) once per split through shared memory.
     const float* pp = ph.part + (size_t)h * ph.splits * (kDH + 2);
     float av[kMaxSplits];
-    if (ok && tid < kDH) {
+    if (gla) {
+      if (ok && tid < kDH) sm.vec[0][tid] = __ldcg(ph.y + h * kDH + tid);
+    } else if (ok && tid < kDH) {
 #pragma unroll
       for (int j = 0; j < kMaxSplits; j++)
         if (j < ph.splits) av[j] = __ldcg(pp + (size_t)j * (kDH + 2) + tid);
     }
-    if (ok && tid >= kDH && tid < kDH + ph.splits) {
+    if (!gla && ok && tid >= kDH && tid < kDH + ph.splits) {
       const int j = tid - kDH;
       sm.cmb[j][0] = __ldcg(pp + (size_t)j * (kDH + 2) + kDH);
       sm.cmb[j][1] = __ldcg(pp + (size_t)j * (kDH + 2) + kDH + 1);
     }
     consumers_sync();
-    if (ok && tid < ph.splits) {
+    if (!gla && ok && tid < ph.splits) {
       float M = -INFINITY;
       for (int j = 0; j < ph.splits; j++) M = fmaxf(M, sm.cmb[j][0]);
       const float m = sm.cmb[tid][0];
       sm.cmb[tid][2] = (M == -INFINITY || m == -INFINITY) ? 0.0f : expf(m - M);
     }
     consumers_sync();
-    if (ok && tid < kDH) {
+    if (!gla && ok && tid < kDH) {
       float A = 0.0f, L = 0.0f;
 #pragma unroll
       for (int j = 0; j < kMaxSplits; j++)
@@ -1446,7 +1455,13 @@ struct Cons {
         // S blocks with o: one item per CTA (items ≤ grid), QG = 1 (the cache head is the head).
         if (ph.wo && blockIdx.x < ph.items && ok) attn_o_tail(ph, blockIdx.x / ph.splits, blockIdx.x % ph.splits);
       } else {
-        for (int i = blockIdx.x; i < ph.items && ok; i += gridDim.x) gla_item(ph, i);
+        if (!ph.wo) {
+          for (int i = blockIdx.x; i < ph.items && ok; i += gridDim.x) gla_item(ph, i);
+        } else if (blockIdx.x < ph.items) {  // L blocks with o: items are heads × splits, one per CTA
+          const int h = blockIdx.x / ph.splits, s = blockIdx.x % ph.splits;
+          if (s == 0) gla_item(ph, h);
+          if (ok) mixer_o_tail(ph, h, s, true);
+        }
       }
     }
     consumers_sync();

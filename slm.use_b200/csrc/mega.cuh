@@ -19,7 +19,7 @@ constexpr int kDH = 64;              // head size of the kernel
 constexpr int kAttnTile = 96;        // cache positions per attention tile (K + V = one stage)
 constexpr int kMaxSplits = 16;       // attention splits per head
 #ifndef SLM_LOOKAHEAD
-#define SLM_LOOKAHEAD 2
+#define SLM_LOOKAHEAD 0
 #endif
 constexpr int kLookahead = SLM_LOOKAHEAD;  // tiles prefetched into L2 ahead of the ring
 

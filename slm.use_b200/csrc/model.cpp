@@ -38,7 +38,7 @@ struct Mat {
   size_t rows = 0, cols = 0;
   const void* planes = nullptr;  // bf16 parts for chunk linears (gemm_bf16x3.cu), in the model's plane arena
   const float* t = nullptr;      // down only: the transpose ([cols][rows]) read by the fused decode MLP
-  const float* hb = nullptr;     // o of S blocks: per-head column blocks [heads][rows][dh] (fused attention + o)
+  const float* hb = nullptr;     // o of S and L blocks: per-head column blocks [heads][rows][dh] (mixer + o fused)
 };
 
 struct Block {
@@ -461,8 +461,8 @@ bool fuse_mlp_enabled() {
   return !(e && e[0] == '0');
 }
 
-// SLM_MEGA_FUSE_ATTN_O=0 keeps the o projection of S blocks as its own phase
-// (the default runs it in the attention phase).
+// SLM_MEGA_FUSE_ATTN_O=0 keeps the o projection of S and L blocks as its own
+// phase (the default runs it in the attention or GLA phase).
 bool fuse_attn_o_enabled() {
   const char* e = std::getenv("SLM_MEGA_FUSE_ATTN_O");
   return !(e && e[0] == '0');
@@ -555,9 +555,12 @@ void build_plan(slm_session* se, bool refresh = false) {
   // is the slot holding buffer buf's current value when a fused MLP wrote it
   // last (its readers take the slot; the float buffer is stale).
   const size_t nmlp = md->prelude.size() + se->loops * md->core.size() + md->coda.size();
-  // S blocks: attention and o in one phase (items ≤ grid, so every split of a
-  // head is resident while it waits for the others; o rows split evenly).
-  auto nS = [](const std::string& k) { return (size_t)std::count(k.begin(), k.end(), 'S'); };
+  // S and L blocks: the mixer (attention, GLA) and o in one phase (items ≤
+  // grid, so every split of a head is resident while it waits; o rows split
+  // evenly over the splits).
+  auto nS = [](const std::string& k) {
+    return (size_t)(std::count(k.begin(), k.end(), 'S') + std::count(k.begin(), k.end(), 'L'));
+  };
   const size_t nao = nS(c.prelude) + se->loops * nS(c.core) + nS(c.coda);
   const bool fuse_ao = se->fuse_mlp && se->fuse_ao && H * splits <= G && d % splits == 0 && d / splits <= kMaxItemOut &&
                        (size_t)(d / splits) * kDH * 4 <= (size_t)kStageBytes;
@@ -659,10 +662,25 @@ void build_plan(slm_session* se, bool refresh = false) {
       p.items = p.seg[0].items + p.seg[1].items;
       p.fx_in = fx_of(ia);
       ph.push_back(p);
+      if (in.mode == IN_LOOP_RMS || in.mode == IN_EMBED_RMS) fx_set(X, nullptr);  // that prologue wrote x to X
       Phase g{};
       g.kind = PH_GLA;
       g.state = st.s, g.mix = se->mix, g.dec = se->dec, g.bias = b.bias, g.hnw = b.head_norm, g.y = se->y;
       g.items = H;
+      if (fuse_ao && b.o.hb) {  // split 0 of each head runs the GLA, every split its o rows
+        g.items = H * splits;
+        g.splits = splits;
+        g.wo = b.o.hb;
+        g.orows = d / splits;
+        g.cnt = reinterpret_cast<unsigned long long*>(se->fx + nslots * slot_words) + H * next_cnt++;
+        g.in_a = X;
+        g.fx_in = fx_of(X);  // the residual
+        g.fx_out = se->fx + slot_words * next_slot++;
+        ph.push_back(g);
+        fx_set(X, g.fx_out);
+        block_mlp(b, X);
+        return;
+      }
       ph.push_back(g);
     }
     // The residual of o and down is the x of the phase two back, whose
@@ -1126,7 +1144,7 @@ int slm_model_load(slm_ctx* ctx, const char* dir, slm_model** out) {
       for (auto* bs : {&md->prelude, &md->core, &md->coda})
         for (auto& b : *bs) {
           downs.push_back(&b.down);
-          if (b.kind == 'S') os.push_back(&b.o);
+          if (b.kind == 'S' || b.kind == 'L') os.push_back(&b.o);
         }
       size_t tot = 0;
       for (Mat* m : downs) tot += (m->rows * m->cols + 63) / 64 * 64;

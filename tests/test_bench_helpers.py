@@ -44,12 +44,12 @@ def test_phase_kinds_match_the_plan_shape():
     assert len(b.phase_kinds(syn.GLOBAL, 4, fused=False)) == 57
     assert two.count("attn") == 6 and two.count("gla") == 4
     # Fused MLPs: one phase per block fewer (10 blocks at R = 4); o in the
-    # attention phase of the 6 S blocks: 6 fewer again.
+    # attention / GLA phase of the 6 S and 4 L blocks: 10 fewer again.
     mlp = b.phase_kinds(syn.BASE, 4, attn_o=False)
     assert len(mlp) == 42 and mlp[4] == "inject" and mlp.count("mlp") == 10
     kinds = b.phase_kinds(syn.BASE, 4)
-    assert len(kinds) == 36 and kinds[3] == "inject" and kinds.count("o") == 4 and kinds.count("attn") == 6
-    assert b.trace_kinds(np.zeros((36, 3, 8), dtype=np.int64), syn.BASE, 4) == kinds
+    assert len(kinds) == 32 and kinds[3] == "inject" and kinds.count("o") == 0 and kinds.count("attn") == 6
+    assert b.trace_kinds(np.zeros((32, 3, 8), dtype=np.int64), syn.BASE, 4) == kinds
     assert b.trace_kinds(np.zeros((42, 3, 8), dtype=np.int64), syn.BASE, 4) == mlp
     assert b.trace_kinds(np.zeros((52, 3, 8), dtype=np.int64), syn.BASE, 4) == two
     assert b.trace_kinds(np.zeros((7, 3, 8), dtype=np.int64), syn.BASE, 4) is None

@@ -153,8 +153,8 @@ def test_persistent_kernel_matches_graph_path(slm, ctx, small):
     a, b = model.session(), model.session()
     b.set_mega(False)
     assert a.mega and not b.mega
-    # 5 S blocks of 3 phases (attention with o, one MLP phase), 3 L blocks of 4, inject, logits
-    assert a.stat(slm.SLM_STAT_PHASES) == 3 * 5 + 4 * 3 + 2
+    # 8 blocks of 3 phases (projection, attention or GLA with o, one MLP phase), inject, logits
+    assert a.stat(slm.SLM_STAT_PHASES) == 3 * 8 + 2
     a.feed(ids[:300])
     b.feed(ids[:300])
     worst = 0.0
@@ -186,14 +186,14 @@ def test_fused_mlp_matches_two_phase_mlp(slm, ctx, request, monkeypatch, which):
     monkeypatch.setenv("SLM_MEGA_MLP_CTA", "1")  # tiles split by rows, a CTA barrier per tile
     e = model.session()
     monkeypatch.delenv("SLM_MEGA_MLP_CTA")
-    monkeypatch.setenv("SLM_MEGA_FUSE_ATTN_O", "0")  # S blocks keep o as its own phase
+    monkeypatch.setenv("SLM_MEGA_FUSE_ATTN_O", "0")  # S and L blocks keep o as its own phase
     f = model.session()
     monkeypatch.delenv("SLM_MEGA_FUSE_ATTN_O")
     assert a.mega and b.mega and c.mega and e.mega and f.mega
     n = {k: se.stat(slm.SLM_STAT_PHASES) for k, se in zip("abcef", (a, b, c, e, f))}
     assert n["a"] == n["c"] == n["e"] < n["f"] < n["b"]
     if which == "small":  # 5 S and 3 L blocks
-        assert n["b"] - n["f"] == 8 and n["f"] - n["a"] == 5
+        assert n["b"] - n["f"] == 8 and n["f"] - n["a"] == 8
     ids = np.random.default_rng(13).integers(0, 1000, 90)
     for se in (a, b, c, e, f):
         se.feed(ids)
