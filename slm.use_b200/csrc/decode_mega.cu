@@ -61,6 +61,14 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, unsigned by
                "l"(src), "r"(bytes), "r"(saddr(bar))
                : "memory");
 }
+__device__ __forceinline__ void bulk_g2s_hint(void* dst, const void* src, unsigned bytes, uint64_t* bar,
+                                              uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
+          saddr(dst)),
+      "l"(src), "r"(bytes), "r"(saddr(bar)), "l"(policy)
+      : "memory");
+}
 __device__ __forceinline__ void prefetch_l2(const void* src, unsigned bytes) {
   asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
 }
@@ -226,6 +234,7 @@ struct Tile {
   unsigned bytes[4];
   unsigned off[4];
   unsigned total;
+  int keep;  // weights read again within the step
 };
 
 // Resumable walk over this CTA's tiles, phase by phase (the order in which
@@ -251,7 +260,7 @@ struct Walker {
     } else if (ph.kind == PH_ATTN) {
       attn_slice(ph, pos, i % ph.splits, &t, &tend);
     } else {
-      t = 0, tend = !ph.wo || i % ph.splits == 0 ? 1 : 0;  // with o: the state goes to split 0
+      t = 0, tend = 1;  // with o: every split of the head reads the state
     }
     extra = ph.wo ? 1 : 0;
   }
@@ -274,6 +283,7 @@ struct Walker {
       if (extra) {  // rows s·orows … of head h's o block
         const int h = i / ph.splits, s = i % ph.splits;
         T.n = 1;
+        T.keep = ph.l2keep;
         T.src[0] = ph.wo + ((size_t)h * P->d + (size_t)s * ph.orows) * kDH;
         T.bytes[0] = T.total = (unsigned)ph.orows * kDH * 4;
         T.off[0] = 0;
@@ -292,6 +302,7 @@ struct Walker {
 
   __device__ void make(const Phase& ph, Tile& T) {
     T.n = 0;
+    T.keep = ph.kind == PH_GEMV ? ph.l2keep : 0;  // K/V and GLA state tiles stream
     if (ph.kind == PH_GEMV) {
       const Segment& sg = ph.seg[seg];
       const int Tn = tile_outs(ph);
@@ -356,6 +367,14 @@ __device__ void producer(const Plan& P, Smem& sm, char* ring, long long pos) {
   // ahead of data the consumers are about to wait for.
   Walker ring_w(&P, pos), ahead(&P, pos);
   Tile T, A;
+  uint64_t pol_keep = 0, pol_other = 0;
+  if (P.l2mode) {
+    asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(pol_keep));
+    if (P.l2mode == 1)
+      asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol_other));
+    else
+      asm volatile("createpolicy.fractional.L2::evict_normal.b64 %0, 1.0;" : "=l"(pol_other));
+  }
   for (int j = 0; j < kStages; j++)
     if (!ahead.next(A)) break;
   unsigned k = 0;
@@ -364,7 +383,12 @@ __device__ void producer(const Plan& P, Smem& sm, char* ring, long long pos) {
     if (k >= (unsigned)kStages && !wait_mbar(&sm.empty[s], ((k / kStages) - 1) & 1, P.err)) break;
     mbar_expect_tx(&sm.full[s], T.total);
     char* dst = ring + (size_t)s * kStageBytes;
-    for (int j = 0; j < T.n; j++) bulk_g2s(dst + T.off[j], T.src[j], T.bytes[j], &sm.full[s]);
+    if (P.l2mode) {
+      const uint64_t pol = T.keep ? pol_keep : pol_other;
+      for (int j = 0; j < T.n; j++) bulk_g2s_hint(dst + T.off[j], T.src[j], T.bytes[j], &sm.full[s], pol);
+    } else {
+      for (int j = 0; j < T.n; j++) bulk_g2s(dst + T.off[j], T.src[j], T.bytes[j], &sm.full[s]);
+    }
     k++;
     if (kLookahead > 0 && k >= (unsigned)kStages) {
       // One more tile of lookahead per tile issued, up to kLookahead beyond the ring.
@@ -1254,8 +1278,8 @@ struct Cons {
   // The residual rows and the tile are fetched before the wait.
   __device__ __forceinline__ void attn_o_tail(const Phase& ph, int h, int s) { mixer_o_tail(ph, h, s, false); }
 
-  // The same for L blocks: split 0 of head h ran the GLA and wrote y_h; every
-  // split of h waits for that one arrival and reads y_h instead of merging.
+  // The same for L blocks: every split of head h ran the GLA itself (gla_item)
+  // and holds y_h in sm.vec[0], so there is nothing to wait for or merge.
   __device__ __forceinline__ void mixer_o_tail(const Phase& ph, int h, int s, bool gla) {
     constexpr int RQ = kMaxItemOut / 64;  // rows per thread: r = tid / 4 + 64·k
     const int R = ph.orows, q4 = tid & 3;
@@ -1268,10 +1292,9 @@ struct Cons {
         res[k] = ph.fx_in ? fx_load1(ph.fx_in, s * R + r, P.d) : __ldcg(ph.in_a + s * R + r);
     }
     const float* w = take_warp();
-    if (tid == 0) {
-      // after the partial or y_h (ordered by the barrier above)
-      if (!gla || s == 0) red_release_add_u64(ph.cnt + h, 1ull);
-      const unsigned long long want = gla ? 1ull : (unsigned long long)ph.splits;
+    if (tid == 0 && !gla) {
+      red_release_add_u64(ph.cnt + h, 1ull);  // after the partial (ordered by the barrier above)
+      const unsigned long long want = (unsigned long long)ph.splits;
       unsigned long long t0 = 0;
       for (unsigned it = 0; ld_acquire_u64(ph.cnt + h) < want; it++) {
         if ((it & 15) == 15) {
@@ -1296,7 +1319,7 @@ struct Cons {
     const float* pp = ph.part + (size_t)h * ph.splits * (kDH + 2);
     float av[kMaxSplits];
     if (gla) {
-      if (ok && tid < kDH) sm.vec[0][tid] = __ldcg(ph.y + h * kDH + tid);
+      // y_h is in sm.vec[0] already (gla_item ran on this CTA)
     } else if (ok && tid < kDH) {
 #pragma unroll
       for (int j = 0; j < kMaxSplits; j++)
@@ -1371,7 +1394,11 @@ struct Cons {
   }
 
   // GLA for head h: l2norm q, k; S = d·S + kᵀv; y = q·S; head_norm; silu gate.
-  __device__ void gla_item(const Phase& ph, int h) {
+  // With o in the phase (ph.wo) every split s of the head runs it on its own
+  // copy of the state and keeps y_h in sm.vec[0]; splits other than 0 report
+  // that their copy has landed, and split 0 writes the new state back only
+  // after all of them have.
+  __device__ void gla_item(const Phase& ph, int h, int s = 0) {
     const int d = P.d;
     const float* row = ph.mix;  // [q | k | v | g], each d wide
     if (tid < kDH) {
@@ -1391,6 +1418,7 @@ struct Cons {
     }
     float* tile = const_cast<float*>(take());  // (its barrier also orders the l2norm above)
     if (!tile) return;
+    if (ph.wo && s != 0 && tid == 0) red_release_add_u64(ph.cnt + h, 1ull);  // the old state is read
     const int b = tid & 63, qa = tid >> 6;
     const float vb = sm.vec[2][b];
     float yp = 0.0f;
@@ -1402,9 +1430,7 @@ struct Cons {
     }
     sm.yp[qa][b] = yp;
     consumers_sync();
-    // State back to HBM (coalesced), then the gated, normalised output.
-    float* Sg = ph.state + (size_t)h * kDH * kDH;
-    for (int e = tid; e < kDH * kDH; e += 256) Sg[e] = tile[e];
+    // The gated, normalised output, then the state back to HBM (coalesced).
     if (warp < 2) {
       int bb = tid;
       float y = ((sm.yp[0][bb] + sm.yp[1][bb]) + sm.yp[2][bb]) + sm.yp[3][bb];
@@ -1413,8 +1439,42 @@ struct Cons {
       asm volatile("bar.sync 2, 64;" ::: "memory");
       float tot = sm.red[0] + sm.red[1];
       float r = 1.0f / sqrtf(tot / (float)kDH + P.eps);
-      ph.y[h * kDH + bb] = silu_mul(sm.vec[3][bb], y * r * __ldg(ph.hnw + bb));
+      const float o = silu_mul(sm.vec[3][bb], y * r * __ldg(ph.hnw + bb));
+      if (ph.wo)
+        sm.vec[0][bb] = o;  // q is no longer read: every thread passed the barrier above
+      else
+        ph.y[h * kDH + bb] = o;
     }
+    if (ph.wo && s != 0) {
+      consumers_sync();
+      release();
+      return;
+    }
+    if (ph.wo && tid == 0) {  // split 0: every other split's copy of the old state has landed
+      unsigned long long t0 = 0;
+      for (unsigned it = 0; ld_acquire_u64(ph.cnt + h) < (unsigned long long)(ph.splits - 1); it++) {
+        if ((it & 15) == 15) {
+          if (ld_volatile(P.err) & 8) {
+            sm.flag = 1;
+            break;
+          }
+          if (!t0) {
+            t0 = now_ns();
+          } else if (now_ns() - t0 > kWaitNs) {
+            atomicOr(P.err, 8);
+            sm.flag = 1;
+            break;
+          }
+        }
+      }
+    }
+    if (ph.wo) {
+      consumers_sync();
+      if (sm.flag == 1) ok = false;
+    }
+    float* Sg = ph.state + (size_t)h * kDH * kDH;
+    if (ok)
+      for (int e = tid; e < kDH * kDH; e += 256) Sg[e] = tile[e];
     consumers_sync();
     release();
   }
@@ -1459,7 +1519,7 @@ struct Cons {
           for (int i = blockIdx.x; i < ph.items && ok; i += gridDim.x) gla_item(ph, i);
         } else if (blockIdx.x < ph.items) {  // L blocks with o: items are heads × splits, one per CTA
           const int h = blockIdx.x / ph.splits, s = blockIdx.x % ph.splits;
-          if (s == 0) gla_item(ph, h);
+          gla_item(ph, h, s);
           if (ok) mixer_o_tail(ph, h, s, true);
         }
       }

@@ -94,6 +94,7 @@ struct alignas(16) Phase {
   const float* wo;
   int orows;
   unsigned long long* cnt;
+  int l2keep;  // the phase's weight tiles are read again within the step (loop blocks): keep them in L2
   // ATTN: heads × splits items; partials and per-head arrival counters
   int heads, splits;
   float* part;
@@ -144,6 +145,9 @@ struct Plan {
   long long* fx;  // fixed-point slots of fused phases and their counters, zeroed at the start of each step
   int fx_words;
   int mlp_cta;    // 1: fused MLP tiles split by rows with a CTA barrier per tile (always for d > 768)
+  // L2 priority of the bulk copies: 0 none; 1 weights of phases marked l2keep
+  // evict_last, every other tile evict_first; 2 the same with the others normal.
+  int l2mode;
 };
 
 }  // namespace mega

@@ -32,6 +32,10 @@ namespace slm {
 constexpr size_t CHUNK = 256;            // src/model.rs:27
 constexpr size_t MAX_SCORES = 1u << 28;  // src/model.rs:30
 constexpr size_t G_CAP0 = 1u << 13;      // first global cache capacity, src/model.rs:320
+#ifndef SLM_L2MODE
+#define SLM_L2MODE 1
+#endif
+constexpr int kL2ModeDefault = SLM_L2MODE;  // L2 priority mode of the persistent step's copies
 
 struct Mat {
   const float* w = nullptr;
@@ -468,6 +472,15 @@ bool fuse_attn_o_enabled() {
   return !(e && e[0] == '0');
 }
 
+// L2 priority of the persistent step's bulk copies (SLM_MEGA_L2MODE): 0 none,
+// 1 loop-block weights evict_last and the rest evict_first, 2 loop-block
+// weights evict_last and the rest normal.
+int l2mode_setting() {
+  const char* e = std::getenv("SLM_MEGA_L2MODE");
+  const int v = e && *e ? std::atoi(e) : kL2ModeDefault;
+  return v < 0 || v > 2 ? 0 : v;
+}
+
 // SLM_MEGA_MLP_CTA=1 splits each fused MLP tile's rows over the CTA's warps
 // (a CTA barrier per tile) instead of giving each warp whole hidden units.
 bool mlp_cta_setting() {
@@ -710,7 +723,9 @@ void build_plan(slm_session* se, bool refresh = false) {
       for (size_t j = 0; j < md->core.size(); j++) {
         In in = j == 0 ? In{IN_LOOP_RMS, sbuf, se->e_proj, md->loop_embed.w + r * c.d, xr}
                        : In{IN_RMS, nullptr, nullptr, nullptr, nullptr};
+        const size_t first = ph.size();
         block(md->core[j], se->core[r][j], xr, in);
+        for (size_t k = first; k < ph.size(); k++) ph[k].l2keep = 1;  // read again by the next loop
       }
       sbuf = xr;
     }
@@ -758,6 +773,7 @@ void build_plan(slm_session* se, bool refresh = false) {
   P.fx = se->fx;
   P.fx_words = se->fuse_mlp ? (int)(nslots * slot_words + ncnt) : 0;
   P.mlp_cta = d > kMaxCols / 4 || mlp_cta_setting() ? 1 : 0;
+  P.l2mode = l2mode_setting();
   P.next_id = se->ids_dev;
   P.err = se->ctx->err;
 }
