@@ -57,7 +57,7 @@ ROOT = Path(__file__).resolve().parent
 MODEL_BYTES_NOTE = "inputs larger than L2: 640 MB of weights and KV read per token at R=4"
 # DRAM bytes (read + write) of one k_decode_mega launch from an ncu capture of
 # this bench (profiles/k_decode_mega_R4.md), by loop count.
-MEGA_TRAFFIC = {4: 577.7e6}
+MEGA_TRAFFIC = {4: 447.6e6}
 
 
 def load_pkg():
@@ -386,6 +386,16 @@ def write_trace(tr: np.ndarray, cfg: dict, loops: int, path: str) -> None:
 # The B200 arm
 # ---------------------------------------------------------------------------
 
+def queue_behind_sleep(torch, stream, ms: float = 3.0) -> None:
+    """Holds `stream` in a device-side sleep of about `ms` (at the B200's
+    1965 MHz maximum clock), so the launches the host issues next are all
+    queued before the GPU reaches them: events recorded after the sleep time
+    the kernels back to back, not the host's per-call overhead (a Python
+    ctypes call per op costs more than the op's two short kernels)."""
+    with torch.cuda.stream(stream):
+        torch.cuda._sleep(int(ms * 1e-3 * 1.965e9))
+
+
 def run_b200(args, rank: int, world: int, local: int) -> dict | None:
     import torch
     import torch.distributed as dist
@@ -475,6 +485,7 @@ def run_b200(args, rank: int, world: int, local: int) -> dict | None:
             ops.linear(yv, mats[i % 4], V, cfg["d_model"], xv, 1)
         reps = 40
         a, b = events()
+        queue_behind_sleep(torch, stream)
         a.record(stream)
         for i in range(reps):
             ops.linear(yv, mats[i % 4], V, cfg["d_model"], xv, 1)
@@ -501,6 +512,7 @@ def run_b200(args, rank: int, world: int, local: int) -> dict | None:
         for i in range(6):
             attend(i)
         a, b = events()
+        queue_behind_sleep(torch, stream)
         a.record(stream)
         for i in range(36):
             attend(i)
@@ -512,9 +524,12 @@ def run_b200(args, rank: int, world: int, local: int) -> dict | None:
             vb.close()
 
     extra = {}
-    if not args.quick:
+    legs = set(args.extras.split(",")) if args.extras else (set() if args.quick else {"R8", "R16", "C4", "C5"})
+    if legs & {"R8", "R16"}:
         c3 = slm.Sampling(temperature=0.8, top_k=40, repeat_penalty=1.1, repeat_window=256)
         for loops in (8, 16):
+            if f"R{loops}" not in legs:
+                continue
             s2 = model.session(loops)
             torch.cuda.synchronize(dev)
             a, b = events()
@@ -540,7 +555,7 @@ def run_b200(args, rank: int, world: int, local: int) -> dict | None:
                                   "sampling": "T=0.8 top-k 40 repeat-penalty 1.1 (window 256) seed 0"}
             s2.close()
 
-    if not args.quick:
+    if "C4" in legs:
         # configs[3] ("C4"): the G-layer variant (S | LS | SG, the fixture's
         # global options), 16384-id prompt, then 256 greedy decodes.
         gcfg = syn.GLOBAL
@@ -577,7 +592,7 @@ def run_b200(args, rank: int, world: int, local: int) -> dict | None:
         s3.close()
         gmodel.close()
 
-    if not args.quick:
+    if "C5" in legs:
         # configs[4] ("C5"): 64 independent sequences (2048-id prompts, seeds
         # 0..63) partitioned over the ranks, each rank's share decoded as one
         # batch (weights read once per step), 256 greedy steps; the total is
@@ -603,6 +618,13 @@ def run_b200(args, rank: int, world: int, local: int) -> dict | None:
         torch.cuda.synchronize(dev)
         c5_ms = a.elapsed_time(b)
         c5_ms = max_over_ranks([c5_ms], dist, dev)[0]
+        if args.profile_c5:
+            # Two more batched steps, after the timed region, inside a profiler
+            # range (for `ncu --profile-from-start off`).
+            torch.cuda.cudart().cudaProfilerStart()
+            bt.decode(nxt, 2)
+            torch.cuda.synchronize(dev)
+            torch.cuda.cudart().cudaProfilerStop()
         extra["C5"] = {"value": 64 * 256 / (c5_ms / 1000.0), "unit": "tok/s (all ranks)", "sequences": 64,
                        "per_rank": len(mine), "prompt": 2048, "decode_steps": 256, "loops": args.loops,
                        "scaling": "strong", "ms_per_step": c5_ms / 256, "sampling": "greedy",
@@ -637,7 +659,11 @@ def main():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--loops", type=int, default=4)
     ap.add_argument("--prompt", type=int, default=4096)
-    ap.add_argument("--quick", action="store_true", help="skip the R=8/16 lines")
+    ap.add_argument("--quick", action="store_true", help="skip the extra legs (R=8/16, C4, C5)")
+    ap.add_argument("--profile-c5", action="store_true", help="bracket two C5 batched steps (after the timed "
+                    "region) with cudaProfilerStart/Stop, for ncu --profile-from-start off")
+    ap.add_argument("--extras", default="", help="comma list of extra legs to run (R8,R16,C4,C5); default all, "
+                    "none with --quick")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
     ap.add_argument("--no-ref-cuda", action="store_true", help="skip the reference CUDA baseline")
     ap.add_argument("--trace", default="", help="write the persistent step's phase timeline (markdown) here")
@@ -739,10 +765,12 @@ def main():
                      "bytes_per_launch": byts["total"], "traffic": MEGA_TRAFFIC.get(args.loops),
                      "peak_source": peak_src,
                      "gemv": {"kernel": "k_gemv<1,STORE> (32000x768 fp32, m=1)", "achieved": gemv_gbs,
-                              "frac": gemv_gbs / hbm},
+                              "frac": gemv_gbs / hbm, "how": "40 launches queued behind a device sleep, CUDA "
+                              "events around them"},
                      "attention": {"kernel": "k_attn_split + k_attn_combine (m=1, 12 heads x 4096 positions of a "
                                              "4352-slot ring, K and V from HBM)",
-                                   "achieved": attn_gbs, "frac": attn_gbs / hbm}},
+                                   "achieved": attn_gbs, "frac": attn_gbs / hbm, "how": "36 calls (two launches "
+                                   "each) queued behind a device sleep, CUDA events around them"}},
         "clocks": res["clocks"],
         "gpu_launches": K * (res["step_kernels"] + 1),
         "extra": res["extra"],
