@@ -9,11 +9,14 @@
 // shaped for bandwidth and occupancy: a CTA owns 64 weight rows × all tokens
 // (padded to 32 or 64) over one slice of K; slices split K so that about two
 // CTAs per SM are busy.  K tiles of 32 of W and x flow through a 4-stage
-// cp.async pipeline in rows padded to 36 floats (float4 reads without bank
-// conflicts); each thread accumulates 4 rows × TT/8 tokens.  With one slice
-// the epilogue writes y directly.  Otherwise every slice writes its partial
-// product to the workspace and k_skinny_reduce, spread over all SMs, sums the
-// slices in slice order (deterministic) and adds the residual.
+// cp.async pipeline in rows padded to 36 floats; thread (tr, tt) accumulates
+// rows tr + 16·j (j < 4) × tokens tt + 8·u (u < TT/8), so the 16 weight rows
+// a warp reads at once sit in 8 different bank groups (two addresses per
+// group: conflict-free for 16-byte loads) and its two token rows in two.
+// With one slice the epilogue writes y directly.  Otherwise every slice
+// writes its partial product to the workspace and k_skinny_reduce, spread
+// over all SMs, sums the slices in slice order (deterministic) and adds the
+// residual.
 #include <algorithm>
 
 #include "common.cuh"
@@ -50,7 +53,7 @@ __device__ __forceinline__ void wait_group() {
 }
 
 // grid (ceil(rows/64), slices, ceil(m/TT)); 128 threads.  Thread t: rows
-// 4·(t%16) …, tokens z·TT + (TT/8)·(t/16) ….
+// r0 + t%16 + 16·j, tokens z·TT + t/16 + 8·u.
 template <int TT, int EPI>
 __global__ void __launch_bounds__(128)
     k_skinny(const float* __restrict__ w, int rows, int cols, const float* __restrict__ x, int ldx, int m, int kper,
@@ -101,9 +104,9 @@ __global__ void __launch_bounds__(128)
     for (int kk = 0; kk < KT; kk += 4) {
       float4 wv[4], xv[TPT];
 #pragma unroll
-      for (int j = 0; j < 4; j++) wv[j] = *reinterpret_cast<const float4*>(&Ws[buf][4 * tr + j][kk]);
+      for (int j = 0; j < 4; j++) wv[j] = *reinterpret_cast<const float4*>(&Ws[buf][tr + 16 * j][kk]);
 #pragma unroll
-      for (int u = 0; u < TPT; u++) xv[u] = *reinterpret_cast<const float4*>(&Xs[buf][TPT * tt + u][kk]);
+      for (int u = 0; u < TPT; u++) xv[u] = *reinterpret_cast<const float4*>(&Xs[buf][tt + 8 * u][kk]);
 #pragma unroll
       for (int j = 0; j < 4; j++)
 #pragma unroll
@@ -121,10 +124,10 @@ __global__ void __launch_bounds__(128)
   if (!part) {
 #pragma unroll
     for (int u = 0; u < TPT; u++) {
-      const int i = i0 + TPT * tt + u;
+      const int i = i0 + tt + 8 * u;
 #pragma unroll
       for (int j = 0; j < 4; j++) {
-        const int r = r0 + 4 * tr + j;
+        const int r = r0 + tr + 16 * j;
         if (i < m && r < rows) out(i, r, acc[j][u]);
       }
     }
@@ -132,19 +135,49 @@ __global__ void __launch_bounds__(128)
   }
 #pragma unroll
   for (int u = 0; u < TPT; u++) {
-    const int i = i0 + TPT * tt + u;
+    const int i = i0 + tt + 8 * u;
 #pragma unroll
     for (int j = 0; j < 4; j++) {
-      const int r = r0 + 4 * tr + j;
+      const int r = r0 + tr + 16 * j;
       if (i < m && r < rows) part[((size_t)s * m + i) * rows + r] = acc[j][u];
     }
   }
 }
 
-// y[i][r] = (res[i][r] +) Σ_s part[s][i][r], slices in order.
+// y[i][r] = (res[i][r] +) Σ_s part[s][i][r], slices in order.  A thread
+// takes four consecutive r (rows % 4 == 0) and loads eight slices at a time
+// before adding them, so its L2 reads overlap; the adds keep slice order.
 template <int EPI>
 __global__ void k_skinny_reduce(const float* __restrict__ part, int slices, int m, int rows, float* __restrict__ y,
                                 int ldy, const float* __restrict__ res, int ldres) {
+  const size_t n4 = (size_t)m * rows / 4, plane = (size_t)m * rows;
+  for (size_t e = (size_t)blockIdx.x * blockDim.x + threadIdx.x; e < n4; e += (size_t)gridDim.x * blockDim.x) {
+    const size_t i = 4 * e / rows, r = 4 * e % rows;
+    const float4* p = reinterpret_cast<const float4*>(part + i * rows + r);
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int s0 = 0; s0 < slices; s0 += 8) {
+      float4 q[8];
+#pragma unroll
+      for (int u = 0; u < 8; u++)
+        if (s0 + u < slices) q[u] = __ldcg(p + (s0 + u) * plane / 4);
+#pragma unroll
+      for (int u = 0; u < 8; u++)
+        if (s0 + u < slices) v.x += q[u].x, v.y += q[u].y, v.z += q[u].z, v.w += q[u].w;
+    }
+    float o[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+      float a = o[k];
+      if (EPI == EPI_ADD) a = res[i * ldres + r + k] + a;
+      y[i * ldy + r + k] = a;
+    }
+  }
+}
+
+// The same sums for any row count, one output per thread.
+template <int EPI>
+__global__ void k_skinny_reduce1(const float* __restrict__ part, int slices, int m, int rows, float* __restrict__ y,
+                                 int ldy, const float* __restrict__ res, int ldres) {
   const size_t n = (size_t)m * rows;
   for (size_t e = (size_t)blockIdx.x * blockDim.x + threadIdx.x; e < n; e += (size_t)gridDim.x * blockDim.x) {
     const size_t i = e / rows, r = e % rows;
@@ -225,12 +258,21 @@ void skinny_linear(const LinearArgs& a, void* ws, cudaStream_t st) {
   }
   if (part) {
     const size_t n = (size_t)a.m * a.rows;
-    const unsigned grid = (unsigned)std::min<size_t>((n + 255) / 256, (size_t)8 * sm_count());
-    if (add)
-      k_skinny_reduce<EPI_ADD><<<grid, 256, 0, st>>>(part, slices, a.m, a.rows, a.y, a.ldy, a.res, a.ldres);
-    else
-      k_skinny_reduce<EPI_STORE><<<grid, 256, 0, st>>>(part, slices, a.m, a.rows, a.y, a.ldy, a.res, a.ldres);
-    SLM_LAUNCHED("k_skinny_reduce");
+    if (a.rows % 4 == 0) {  // float4 of the workspace: rows and m·rows are multiples of 4
+      const unsigned grid = (unsigned)std::min<size_t>((n / 4 + 255) / 256, (size_t)8 * sm_count());
+      if (add)
+        k_skinny_reduce<EPI_ADD><<<grid, 256, 0, st>>>(part, slices, a.m, a.rows, a.y, a.ldy, a.res, a.ldres);
+      else
+        k_skinny_reduce<EPI_STORE><<<grid, 256, 0, st>>>(part, slices, a.m, a.rows, a.y, a.ldy, a.res, a.ldres);
+      SLM_LAUNCHED("k_skinny_reduce");
+    } else {
+      const unsigned grid = (unsigned)std::min<size_t>((n + 255) / 256, (size_t)8 * sm_count());
+      if (add)
+        k_skinny_reduce1<EPI_ADD><<<grid, 256, 0, st>>>(part, slices, a.m, a.rows, a.y, a.ldy, a.res, a.ldres);
+      else
+        k_skinny_reduce1<EPI_STORE><<<grid, 256, 0, st>>>(part, slices, a.m, a.rows, a.y, a.ldy, a.res, a.ldres);
+      SLM_LAUNCHED("k_skinny_reduce1");
+    }
   }
 }
 
