@@ -36,6 +36,9 @@ constexpr int STAGES = SLM_SKINNY_STAGES;
 #ifndef SLM_SKINNY_MAX_M
 #define SLM_SKINNY_MAX_M 64  // token rows (above 64 in tiles of 64; 256-token chunks measured faster on FastFP32)
 #endif
+#ifndef SLM_SKINNY_K_MAX
+#define SLM_SKINNY_K_MAX 768  // linears with K at most this take the kernel for whole 256-token chunks too
+#endif
 
 template <int TT>
 constexpr size_t smem_bytes() {
@@ -232,9 +235,10 @@ void skinny_prepare() {
 
 bool skinny_ok(const LinearArgs& a) {
   auto al = [](const void* p) { return ((uintptr_t)p & 15) == 0; };
-  // Outputs of at most 128 rows (the GLA decay) take it for whole chunks too:
-  // a tensor-core GEMM launch costs ~20 µs for almost no work there.
-  const int max_m = a.rows <= 128 ? 256 : SLM_SKINNY_MAX_M;
+  // Outputs of at most 128 rows (the GLA decay) and short K (the o and inject
+  // projections of d 768) take it for whole chunks too: a tensor-core GEMM
+  // launch costs ~20-30 µs for little work there.
+  const int max_m = a.rows <= 128 || a.cols <= SLM_SKINNY_K_MAX ? 256 : SLM_SKINNY_MAX_M;
   return a.m > 8 && a.m <= max_m && (a.epi == EPI_STORE || a.epi == EPI_ADD) && a.cols % KT == 0 &&
          a.ldx % 4 == 0 &&
          al(a.w) && al(a.x);
