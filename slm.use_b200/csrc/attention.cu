@@ -17,6 +17,7 @@
 // The position of the first query comes from device memory, so the same
 // launch (and a CUDA graph holding it) serves every decode step.
 #include <algorithm>
+#include <mutex>
 
 #include "common.cuh"
 #include "kernels.cuh"
@@ -534,11 +535,19 @@ template <int DH>
 void launch_tile(const float* q, int ldq, const float* K, const float* V, const AttnGeom& g, const long long* pos_ptr,
                  int nsplit, float* part, cudaStream_t st) {
   if constexpr (DH == 64) {
-    static bool attr = [] {
+    // The shared-memory limit is a per-device function attribute: set it on
+    // the first launch on each device (a process may drive several).
+    constexpr int kDevices = 64;
+    static std::once_flag once[kDevices];
+    int dev = 0;
+    SLM_CUDA(cudaGetDevice(&dev));
+    auto set = [] {
       SLM_CUDA(cudaFuncSetAttribute(k_attn_flash, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kFlashSmem));
-      return true;
-    }();
-    (void)attr;
+    };
+    if (dev >= 0 && dev < kDevices)
+      std::call_once(once[dev], set);
+    else
+      set();
     k_attn_flash<<<dim3(nsplit, cdiv(g.m, FQ), g.heads), 256, kFlashSmem, st>>>(q, ldq, K, V, g, pos_ptr, nsplit,
                                                                                 part);
     SLM_LAUNCHED("k_attn_flash");
