@@ -154,8 +154,11 @@ int slm_op_attend(slm_ctx* ctx, slm_buf* y, slm_buf* scores, const slm_buf* q, s
  * scratch is a fixed 4 MiB __device__ array per device: calls need
  * m·heads·(dh + 2) ≤ 1,048,512 floats and fail with SLM_ERR_INVALID above
  * it.  The first call on a device looks up that array's address (set-up, no
- * allocation); make that first call before any stream capture.  All calls on
- * a device share the array, so calls that overlap on the GPU race. */
+ * allocation); make that first call before any stream capture.  The address is
+ * kept for the life of the process: it assumes the device's primary context
+ * stays alive (no cudaDeviceReset, no release of the primary context between
+ * calls).  All calls on a device share the array, so calls that overlap on the
+ * GPU race. */
 int slm_op_attend_noalloc(slm_ctx* ctx, float* y, const float* q, const float* k, const float* v,
                           const slm_attn* a);
 
@@ -187,6 +190,39 @@ int slm_step(slm_session* se, uint32_t id);
 int slm_logits(slm_session* se, float* out);
 /* Model::state_bytes (src/model.rs:674-690). */
 int slm_state_bytes(const slm_session* se, size_t* out);
+
+/* ---- Session state transfer ------------------------------------------------
+ * No counterpart in the reference, whose Session keeps its state private
+ * (src/model.rs:210-223).  The recurrent state of a session as host arrays:
+ * a snapshot to restore later, or a start at a chosen position without
+ * reading a prompt first (the parity tests start the library and the CPU
+ * oracle from the same state this way).  Arrays come in step order (the
+ * prelude's blocks, then the core's blocks for loop 0, 1, …, then the coda's);
+ * per block: window attention 'S' → k, v; GLA 'L' → s; global 'G' → k, v, p. */
+typedef struct slm_state_array {
+  char kind;     /* layer type of the block: 'S', 'L' or 'G' */
+  char part;     /* 'k', 'v': cache [heads][cap][dh] (slot = position mod cap
+                    for 'S'; positions in order for 'G'); 's': GLA state
+                    [heads][dh][dh]; 'p': a G block's previous normalised
+                    input (d floats, the shifted-key source) */
+  size_t heads;  /* cache or state heads (1 for 'p') */
+  size_t cap;    /* cache slots per head (0 for 's' and 'p') */
+  size_t dh;     /* head size (d for 'p') */
+  size_t floats; /* values in the array */
+} slm_state_array;
+int slm_session_state_count(const slm_session* se, size_t* out);
+int slm_session_state_info(const slm_session* se, size_t i, slm_state_array* out);
+/* Copies array i (info.floats values) to `out` on the host; synchronises. */
+int slm_session_state_read(slm_session* se, size_t i, float* out);
+/* Overwrites array i from the host.  A cache comes as [heads][cap][dh]: a
+ * window cache at exactly its own capacity (ring slots depend on it); for a
+ * global cache the first min(cap, info.cap) slots per head are copied and the
+ * rest zeroed.  Synchronises. */
+int slm_session_state_write(slm_session* se, size_t i, const float* in, size_t cap);
+/* Puts the session at position `pos` (global caches grow to hold the next
+ * step) without touching its arrays; write them before or after.  The next
+ * step runs at `pos`.  Synchronises. */
+int slm_session_set_pos(slm_session* se, size_t pos);
 
 /* Sampling (src/sample.rs:3-15). */
 typedef struct slm_sampling {
@@ -222,8 +258,11 @@ int slm_decode(slm_session* se, uint32_t first, size_t n, const slm_sampling* s,
 /* Execution switches of a session (for tests and measurement):
  *   SLM_OPT_GRAPH    1 = replay the m = 1 step as a CUDA graph (default 1)
  *   SLM_OPT_MEGA     1 = run the m = 1 step as one persistent kernel (default
- *                    1 where the model allows it: head size 64, no global
- *                    layers, damp 1; fails with SLM_ERR_INVALID otherwise) */
+ *                    1 where the model allows it: head size 64, d_model
+ *                    128·{1,2,3,4,6,8} up to 1024, damp 1, and global layers,
+ *                    if any, with heads / kv_heads ≤ 3 that open neither the
+ *                    prelude nor the loop; fails with SLM_ERR_INVALID
+ *                    otherwise) */
 #define SLM_OPT_GRAPH 1
 #define SLM_OPT_MEGA 2
 #define SLM_OPT_TRACE 3 /* 1 = record the per-phase timeline of each persistent step */

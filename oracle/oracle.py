@@ -56,6 +56,10 @@ def lib():
         L.orc_state_bytes.restype = ctypes.c_int64
         L.orc_state_bytes.argtypes = [ctypes.c_void_p]
         L.orc_session_fill.argtypes = [ctypes.c_void_p, ctypes.c_int64, ctypes.c_uint64]
+        L.orc_state_count.restype = ctypes.c_int64
+        L.orc_state_count.argtypes = [ctypes.c_void_p]
+        L.orc_state_info.restype = _f32p
+        L.orc_state_info.argtypes = [ctypes.c_void_p, ctypes.c_int64, _i64p]
         L.orc_pick.restype = ctypes.c_uint32
         L.orc_pick.argtypes = [_f32p, ctypes.c_int64, _u32p, ctypes.c_int64, ctypes.c_float,
                                ctypes.c_uint32, ctypes.c_float, ctypes.c_float, ctypes.c_uint32, _u64p]
@@ -199,6 +203,17 @@ class Session:
 
     def fill(self, pos: int, seed: int = 0) -> None:
         lib().orc_session_fill(self._h, pos, seed)
+
+    def state(self) -> list[dict]:
+        """The state arrays in step order (S k, v; L s; G k, v, prev per block), each a dict with
+        kind, part, cap and a copy of its values."""
+        out = []
+        info = np.zeros(4, dtype=np.int64)
+        for i in range(lib().orc_state_count(self._h)):
+            ptr = lib().orc_state_info(self._h, i, info.ctypes.data_as(_i64p))
+            data = np.ctypeslib.as_array(ptr, shape=(int(info[3]),)).copy()
+            out.append({"kind": chr(info[0]), "part": chr(info[1]), "cap": int(info[2]), "data": data})
+        return out
 
 
 def rng_new(seed: int) -> int:

@@ -820,6 +820,40 @@ int orc_session_fill(void* se_, int64_t pos, uint64_t seed) {
   return 0;
 }
 
+// The session's state arrays in step order (prelude, core per loop, coda);
+// per block: S k, v; L s; G k, v, prev — the order of orc_session_fill and of
+// the library's slm_session_state_* calls.
+static std::vector<std::pair<State*, char>> state_list(Session* se) {
+  std::vector<std::pair<State*, char>> out;
+  auto one = [&](State& s) {
+    if (s.kind == 'S') out.push_back({&s, 'k'}), out.push_back({&s, 'v'});
+    else if (s.kind == 'L') out.push_back({&s, 's'});
+    else out.push_back({&s, 'k'}), out.push_back({&s, 'v'}), out.push_back({&s, 'p'});
+  };
+  for (auto& s : se->prelude) one(s);
+  for (auto& l : se->core)
+    for (auto& s : l) one(s);
+  for (auto& s : se->coda) one(s);
+  return out;
+}
+
+int64_t orc_state_count(void* se_) { return (int64_t)state_list(static_cast<Session*>(se_)).size(); }
+
+// info = {kind, part, cap, floats}; returns the array's data (owned by the session).
+float* orc_state_info(void* se_, int64_t i, int64_t* info) {
+  auto* se = static_cast<Session*>(se_);
+  auto list = state_list(se);
+  if (i < 0 || (size_t)i >= list.size()) return nullptr;
+  State* st = list[i].first;
+  const char part = list[i].second;
+  std::vector<float>& v = part == 'k' ? st->k : part == 'v' ? st->v : part == 's' ? st->s : st->prev;
+  info[0] = st->kind;
+  info[1] = part;
+  info[2] = (part == 'k' || part == 'v') ? (int64_t)(st->kind == 'S' ? se->model->cap() : st->cap) : 0;
+  info[3] = (int64_t)v.size();
+  return v.data();
+}
+
 // sampling: temperature, top_p, repeat_penalty; top_k, repeat_window
 uint32_t orc_pick(const float* logits, int64_t vocab, const uint32_t* recent, int64_t nrecent,
                   float temperature, uint32_t top_k, float top_p, float repeat_penalty,

@@ -57,6 +57,10 @@ class _Sampling(_c.Structure):
                 ("repeat_penalty", _c.c_float), ("repeat_window", _c.c_uint32)]
 
 
+class _StateArray(_c.Structure):
+    _fields_ = [("kind", _c.c_char), ("part", _c.c_char)] + [(n, _sz) for n in ("heads", "cap", "dh", "floats")]
+
+
 class _Info(_c.Structure):
     _fields_ = [(n, _sz) for n in ("vocab", "d_model", "heads", "head_dim", "kv_heads", "hidden", "window",
                                    "max_loops", "default_loops", "params")] + [
@@ -114,6 +118,11 @@ _SIGS = {
     "slm_step": (_c.c_int, [_vp, _c.c_uint32]),
     "slm_logits": (_c.c_int, [_vp, _f32p]),
     "slm_state_bytes": (_c.c_int, [_vp, _c.POINTER(_sz)]),
+    "slm_session_state_count": (_c.c_int, [_vp, _c.POINTER(_sz)]),
+    "slm_session_state_info": (_c.c_int, [_vp, _sz, _c.POINTER(_StateArray)]),
+    "slm_session_state_read": (_c.c_int, [_vp, _sz, _f32p]),
+    "slm_session_state_write": (_c.c_int, [_vp, _sz, _f32p, _sz]),
+    "slm_session_set_pos": (_c.c_int, [_vp, _sz]),
     "slm_rng_seed": (_c.c_uint64, [_c.c_uint64]),
     "slm_sample": (_c.c_int, [_vp, _c.POINTER(_Sampling), _u32p, _sz, _u64p, _u32p]),
     "slm_pick": (_c.c_int, [_vp, _vp, _sz, _c.POINTER(_Sampling), _u32p, _sz, _u64p, _u32p]),
@@ -545,6 +554,39 @@ class Session:
         v = _sz()
         _check(lib().slm_state_bytes(self._h, _c.byref(v)))
         return v.value
+
+    def state_arrays(self) -> list[dict]:
+        """Descriptions of the session's state arrays in step order (kind, part, heads, cap, dh, floats)."""
+        n = _sz()
+        _check(lib().slm_session_state_count(self._h, _c.byref(n)))
+        out = []
+        for i in range(n.value):
+            a = _StateArray()
+            _check(lib().slm_session_state_info(self._h, i, _c.byref(a)))
+            out.append({"kind": a.kind.decode(), "part": a.part.decode(), "heads": a.heads, "cap": a.cap,
+                        "dh": a.dh, "floats": a.floats})
+        return out
+
+    def state_read(self, i: int) -> np.ndarray:
+        """State array i as a flat float32 array."""
+        a = _StateArray()
+        _check(lib().slm_session_state_info(self._h, i, _c.byref(a)))
+        out = np.empty(a.floats, dtype=np.float32)
+        _check(lib().slm_session_state_read(self._h, i, out.ctypes.data_as(_f32p)))
+        return out
+
+    def state_write(self, i: int, data, cap: int = 0) -> None:
+        """Overwrites state array i; a cache comes as [heads][cap][dh] (cap 0: the array's own)."""
+        data = _f32(data)
+        if cap == 0:
+            a = _StateArray()
+            _check(lib().slm_session_state_info(self._h, i, _c.byref(a)))
+            cap = a.cap or 1
+        _check(lib().slm_session_state_write(self._h, i, data.ctypes.data_as(_f32p), cap))
+
+    def set_pos(self, pos: int) -> None:
+        """Puts the session at position pos (its state arrays unchanged)."""
+        _check(lib().slm_session_set_pos(self._h, pos))
 
     def sample(self, s: Sampling, recent=(), rng_state: list | None = None) -> int:
         """pick (src/sample.rs:33-93) on the device; rng_state is a one-element list."""

@@ -22,14 +22,35 @@ INCLUDE = HERE.parent / "include"
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 
 
+# The CUTLASS release the gemm_*.cu kernels are written and tested against.
+CUTLASS_VERSION = (4, 5, 0)
+
+
+def _cutlass_version(root: Path) -> tuple:
+    import re
+    text = (root / "include" / "cutlass" / "version.h").read_text()
+    parts = dict(re.findall(r"#define CUTLASS_(MAJOR|MINOR|PATCH) (\d+)", text))
+    return tuple(int(parts.get(k, -1)) for k in ("MAJOR", "MINOR", "PATCH"))
+
+
 def _cutlass_includes() -> list[str]:
-    """CUTLASS/CuTe headers vendored in the image (flashinfer's copy), for the gemm_*.cu kernels."""
+    """CUTLASS/CuTe headers for the gemm_*.cu kernels: $SLM_CUTLASS_DIR (a
+    CUTLASS source tree), else the copy vendored in the image's flashinfer
+    wheel (flashinfer/data/cutlass).  The tree must be CUTLASS_VERSION."""
     import site
-    roots = [Path(p) / "flashinfer" / "data" / "cutlass" for p in site.getsitepackages()]
+    env = os.environ.get("SLM_CUTLASS_DIR", "")
+    roots = [Path(env)] if env else [Path(p) / "flashinfer" / "data" / "cutlass" for p in site.getsitepackages()]
     for r in roots:
         if (r / "include" / "cutlass" / "cutlass.h").exists():
+            got = _cutlass_version(r)
+            if got != CUTLASS_VERSION:
+                raise RuntimeError(f"CUTLASS at {r} is {'.'.join(map(str, got))}; the gemm_*.cu kernels are pinned "
+                                   f"to {'.'.join(map(str, CUTLASS_VERSION))} (set SLM_CUTLASS_DIR to such a tree)")
             return ["-I", str(r / "include"), "-I", str(r / "tools" / "util" / "include")]
-    raise RuntimeError("CUTLASS headers not found (flashinfer/data/cutlass); the gemm_*.cu kernels need them")
+    raise RuntimeError("CUTLASS headers not found: set SLM_CUTLASS_DIR to a CUTLASS "
+                       f"{'.'.join(map(str, CUTLASS_VERSION))} source tree")
+
+
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC,-O3", "--expt-relaxed-constexpr",
          "-I", str(INCLUDE)]

@@ -34,6 +34,8 @@ static __device__ __align__(256) float g_attend_scratch[kNoAllocFloats];
 
 // Device address of g_attend_scratch, per device.  In host code the symbol
 // is only a host-side stand-in; a kernel must be given this address instead.
+// It is looked up once per device and kept: valid while the device's primary
+// context lives (a cudaDeviceReset would make it stale).
 std::mutex g_mutex;
 std::vector<float*> g_scratch;
 

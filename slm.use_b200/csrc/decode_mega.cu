@@ -146,6 +146,23 @@ __device__ bool wait_mbar(uint64_t* b, unsigned parity, int* err) {
   }
 }
 
+// Bounded wait for a copy this CTA issued itself.  Such a copy completes
+// whatever other CTAs did, so the error word is not consulted: only the time
+// limit ends the wait (and then sets the error bit).  The producer's drain
+// uses it so that the CTA never exits with bulk copies into its shared memory
+// still in flight.
+__device__ bool wait_mbar_own(uint64_t* b, unsigned parity, int* err) {
+  if (mbar_try_wait(b, parity)) return true;
+  const unsigned long long t0 = now_ns();
+  for (unsigned it = 1;; it++) {
+    if (mbar_try_wait(b, parity)) return true;
+    if ((it & 63) == 0 && now_ns() - t0 > kWaitNs) {
+      atomicOr(err, 8);
+      return false;
+    }
+  }
+}
+
 __device__ __forceinline__ uint32_t total_key(float f) {
   uint32_t u = __float_as_uint(f + 0.0f);  // -0 → +0: equal values compare equal
   return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
@@ -399,9 +416,10 @@ __device__ void producer(const Plan& P, Smem& sm, char* ring, long long pos) {
       }
     }
   }
-  // Drain: every copy issued must land before the CTA may exit.
+  // Drain: every copy issued must land before the CTA may exit, also when the
+  // step is being abandoned because some CTA's wait ran out.
   unsigned first = k > (unsigned)kStages ? k - kStages : 0;
-  for (unsigned j = first; j < k; j++) wait_mbar(&sm.full[j % kStages], (j / kStages) & 1, P.err);
+  for (unsigned j = first; j < k; j++) wait_mbar_own(&sm.full[j % kStages], (j / kStages) & 1, P.err);
 }
 
 // ---------------------------------------------------------------------------

@@ -118,6 +118,7 @@ struct slm_session {
   bool fuse_ao = false;                  // … and the o projection of S blocks in the attention phase
   long long* fx = nullptr;               // fixed-point slots of those phases
   bool plan_stale = false;               // a global cache moved: the phase descriptors need refreshing
+  bool keys_stale = false;               // state was written from the host: the next shifted keys need recomputing
   int in_batches = 0;                    // batches holding this session
   uint32_t* argmax_dev = nullptr;        // the persistent step's arg-max of its logits
   bool argmax_valid = false;             // the logits come from a persistent step
@@ -788,10 +789,34 @@ void plan_outputs(slm_session* se, bool greedy, uint32_t* out, uint32_t* hist, u
   SLM_CUDA(cudaMemsetAsync(P.out_index, 0, sizeof(unsigned), se->ctx->stream));
 }
 
+// With kshift the persistent step expects the key of its own position in
+// every global cache already (W_k · prev, stored by the step or chunk before).
+// After the state was written from the host, compute those keys from prev.
+void refresh_next_keys(slm_session* se) {
+  slm_model* md = se->model;
+  const Config& c = md->cfg;
+  se->keys_stale = false;
+  if (!c.kshift) return;
+  g_ctx_for_linear = se->ctx;
+  g_capturing = false;
+  cudaStream_t s = se->ctx->stream;
+  const size_t kh = c.kv_heads, dh = c.dh(), kd = kh * dh;
+  auto one = [&](const Block& b, LState& st) {
+    if (b.kind != 'G') return;
+    run_linear(s, b.kv, st.prev, (int)c.d, 1, se->kvs, (int)kd, EPI_STORE, nullptr, 0, kd);  // key rows only
+    ew_store_next(st.k, se->kvs, se->pos_dev, 0, kh, dh, st.cap, s);
+  };
+  for (size_t i = 0; i < md->prelude.size(); i++) one(md->prelude[i], se->pre[i]);
+  for (size_t r = 0; r < se->loops; r++)
+    for (size_t j = 0; j < md->core.size(); j++) one(md->core[j], se->core[r][j]);
+  for (size_t i = 0; i < md->coda.size(); i++) one(md->coda[i], se->coda[i]);
+}
+
 // host_id ≥ 0: the step's token, passed in the launch parameters (no copy);
 // else the kernel reads ids_dev[0].
 void mega_step(slm_session* se, long long host_id = -1) {
   if (se->plan_stale) build_plan(se, true);
+  if (se->keys_stale) refresh_next_keys(se);
   if (host_id >= 0) {
     mega::Plan p = se->plan_host;
     p.host_id = host_id;
@@ -1073,6 +1098,48 @@ SampleArgs sample_args(slm_session* se, const slm_sampling* sp) {
   a.rng = se->rng_dev;
   a.err = se->ctx->err;
   return a;
+}
+
+// The session's state arrays in step order (prelude, core per loop, coda);
+// per layer: S k, v; L s; G k, v, prev.
+struct StateRef {
+  LState* st;
+  char part;
+};
+std::vector<StateRef> state_list(slm_session* se) {
+  std::vector<StateRef> out;
+  auto one = [&](LState& st) {
+    if (st.kind == 'S') out.push_back({&st, 'k'}), out.push_back({&st, 'v'});
+    else if (st.kind == 'L') out.push_back({&st, 's'});
+    else out.push_back({&st, 'k'}), out.push_back({&st, 'v'}), out.push_back({&st, 'p'});
+  };
+  for (auto& st : se->pre) one(st);
+  for (auto& l : se->core)
+    for (auto& st : l) one(st);
+  for (auto& st : se->coda) one(st);
+  return out;
+}
+
+slm_state_array state_desc(const slm_session* se, const StateRef& r) {
+  const Config& c = se->model->cfg;
+  slm_state_array a{};
+  a.kind = r.st->kind;
+  a.part = r.part;
+  a.dh = c.dh();
+  if (r.part == 's') {
+    a.heads = c.heads, a.cap = 0, a.floats = c.heads * c.dh() * c.dh();
+  } else if (r.part == 'p') {
+    a.heads = 1, a.cap = 0, a.dh = c.d, a.floats = c.d;
+  } else {
+    a.heads = r.st->kind == 'G' ? c.kv_heads : c.heads;
+    a.cap = r.st->cap;
+    a.floats = a.heads * a.cap * a.dh;
+  }
+  return a;
+}
+
+float* state_ptr(const StateRef& r) {
+  return r.part == 'k' ? r.st->k : r.part == 'v' ? r.st->v : r.part == 's' ? r.st->s : r.st->prev;
 }
 
 }  // namespace
@@ -1472,6 +1539,79 @@ int slm_state_bytes(const slm_session* se, size_t* out) {
       for (auto& st : l) total += one(st);
     for (auto& st : se->coda) total += one(st);
     *out = total * 4;
+  });
+}
+
+int slm_session_state_count(const slm_session* se, size_t* out) {
+  return guard([&] {
+    SLM_REQUIRE(se && out, "bad arguments");
+    *out = state_list(const_cast<slm_session*>(se)).size();
+  });
+}
+
+int slm_session_state_info(const slm_session* se, size_t i, slm_state_array* out) {
+  return guard([&] {
+    SLM_REQUIRE(se && out, "bad arguments");
+    auto list = state_list(const_cast<slm_session*>(se));
+    SLM_REQUIRE(i < list.size(), "state array index out of range");
+    *out = state_desc(se, list[i]);
+  });
+}
+
+int slm_session_state_read(slm_session* se, size_t i, float* out) {
+  return guard([&] {
+    SLM_REQUIRE(se && out, "bad arguments");
+    auto list = state_list(se);
+    SLM_REQUIRE(i < list.size(), "state array index out of range");
+    Device dev(se->ctx);
+    const slm_state_array a = state_desc(se, list[i]);
+    SLM_CUDA(cudaStreamSynchronize(se->ctx->stream));
+    SLM_CUDA(cudaMemcpy(out, state_ptr(list[i]), a.floats * sizeof(float), cudaMemcpyDeviceToHost));
+  });
+}
+
+int slm_session_state_write(slm_session* se, size_t i, const float* in, size_t cap) {
+  return guard([&] {
+    SLM_REQUIRE(se && in, "bad arguments");
+    auto list = state_list(se);
+    SLM_REQUIRE(i < list.size(), "state array index out of range");
+    Device dev(se->ctx);
+    const StateRef& r = list[i];
+    const slm_state_array a = state_desc(se, r);
+    float* dst = state_ptr(r);
+    cudaStream_t s = se->ctx->stream;
+    SLM_CUDA(cudaStreamSynchronize(s));
+    if (a.cap == 0) {
+      SLM_CUDA(cudaMemcpy(dst, in, a.floats * sizeof(float), cudaMemcpyHostToDevice));
+    } else {
+      // Ring slots are position mod cap: a window cache must come at its own
+      // capacity.  Global caches never wrap: copy the slots both hold.
+      if (r.st->kind == 'S')
+        SLM_REQUIRE(cap == a.cap, "a window cache must be written at its capacity " + std::to_string(a.cap));
+      SLM_REQUIRE(cap > 0, "cap must be positive");
+      const size_t rows = std::min(cap, a.cap);
+      if (rows < a.cap) SLM_CUDA(cudaMemset(dst, 0, a.floats * sizeof(float)));
+      SLM_CUDA(cudaMemcpy2D(dst, a.cap * a.dh * sizeof(float), in, cap * a.dh * sizeof(float),
+                            rows * a.dh * sizeof(float), a.heads, cudaMemcpyHostToDevice));
+    }
+    if (r.st->kind == 'G') se->keys_stale = true;
+    se->argmax_valid = false;
+  });
+}
+
+int slm_session_set_pos(slm_session* se, size_t pos) {
+  return guard([&] {
+    SLM_REQUIRE(se, "session is null");
+    Device dev(se->ctx);
+    cudaStream_t s = se->ctx->stream;
+    SLM_CUDA(cudaStreamSynchronize(s));
+    se->pos = pos;
+    long long p = (long long)pos;
+    SLM_CUDA(cudaMemcpy(se->pos_dev, &p, sizeof(p), cudaMemcpyHostToDevice));
+    ensure_caps(se, 1);  // global caches hold the next step
+    SLM_CUDA(cudaStreamSynchronize(s));
+    se->keys_stale = true;
+    se->argmax_valid = false;
   });
 }
 
