@@ -168,21 +168,104 @@ __device__ __forceinline__ uint32_t total_key(float f) {
   return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
 }
 
-// Four consecutive values of a fused MLP's fixed-point slot (d wide) as floats:
-// one rounding of the exact sum; NaN everywhere when a part was out of range.
-__device__ __forceinline__ float4 fx_load4(const long long* fx, int i4, int d) {
-  const longlong2* f = reinterpret_cast<const longlong2*>(fx) + 2 * i4;
-  const longlong2 a = __ldcg(f), b = __ldcg(f + 1);
-  if (__ldcg(fx + d) != 0) return make_float4(NAN, NAN, NAN, NAN);
-  return make_float4(__ll2float_rn(a.x) * kFxInv, __ll2float_rn(a.y) * kFxInv, __ll2float_rn(b.x) * kFxInv,
-                     __ll2float_rn(b.y) * kFxInv);
+__device__ __forceinline__ unsigned long long ld_relaxed_u64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ ulonglong2 ld_relaxed_u64x2(const unsigned long long* p) {
+  ulonglong2 v;
+  asm volatile("ld.relaxed.gpu.global.v2.u64 {%0,%1}, [%2];" : "=l"(v.x), "=l"(v.y) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_relaxed_u64(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ void red_add_fx(unsigned long long* p, unsigned long long v) {
+  asm volatile("red.relaxed.gpu.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
 
-// Value i of a fixed-point slot (d wide) as a float (NaN when the slot is flagged).
-__device__ __forceinline__ float fx_load1(const long long* fx, int i, int d) {
-  const long long a = __ldcg(fx + i);
-  if (__ldcg(fx + d) != 0) return NAN;
-  return __ll2float_rn(a) * kFxInv;
+// A bounded spin: again() is false once the wait has run past kWaitNs (the
+// error bit is set here) or another CTA has given up (error bit 8 seen).
+struct Spin {
+  unsigned it = 0;
+  unsigned long long t0 = 0;
+  __device__ __forceinline__ bool again(int* err) {
+    if ((++it & 15) != 0) return true;
+    if (ld_volatile(err) & 8) return false;
+    const unsigned long long t = now_ns();
+    if (!t0) {
+      t0 = t;
+    } else if (t - t0 > kWaitNs) {
+      atomicOr(err, 8);
+      return false;
+    }
+    return true;
+  }
+};
+
+// Fixed-point words: contributions so far, and the value they sum to.
+__device__ __forceinline__ unsigned fx_count(unsigned long long w) {
+  return (unsigned)((w + (1ull << 55)) >> 56);
+}
+__device__ __forceinline__ float fx_value(unsigned long long w) {
+  const long long v = (long long)(w - ((unsigned long long)fx_count(w) << 56));
+  return __ll2float_rn(v) * kFxInv;
+}
+// The word one CTA adds for a part: one count and the part in units of 2^-30
+// (a part out of range adds only the count, and *bad is set).
+__device__ __forceinline__ unsigned long long fx_word(float v, bool* bad) {
+  if (!(fabsf(v) < kFxMax)) {  // NaN included
+    *bad = true;
+    return kFxOne;
+  }
+  return kFxOne + (unsigned long long)__float2ll_rn(v * kFxScale);
+}
+
+// Four values i4·4 … of a fixed-point slot once all `cnt` parts of each have
+// landed (one load round per poll).  False when the wait gave up.
+__device__ __forceinline__ bool fx_poll4(const unsigned long long* fx, int i4, unsigned cnt, int* err, float4* out) {
+  const unsigned long long* f = fx + 4 * i4;
+  Spin sp;
+  do {
+    const ulonglong2 a = ld_relaxed_u64x2(f), b = ld_relaxed_u64x2(f + 2);
+    if (fx_count(a.x) == cnt && fx_count(a.y) == cnt && fx_count(b.x) == cnt && fx_count(b.y) == cnt) {
+      *out = make_float4(fx_value(a.x), fx_value(a.y), fx_value(b.x), fx_value(b.y));
+      return true;
+    }
+  } while (sp.again(err));
+  *out = make_float4(0.f, 0.f, 0.f, 0.f);
+  return false;
+}
+
+// Tagged words: the float in the low half, the producer's tag in the high half.
+__device__ __forceinline__ unsigned long long tagged(float v, unsigned tag) {
+  return ((unsigned long long)tag << 32) | __float_as_uint(v);
+}
+__device__ __forceinline__ void put_tagged(unsigned long long* p, float v, unsigned tag) {
+  st_relaxed_u64(p, tagged(v, tag));
+}
+// N tagged values p[i·stride] once each carries `tag`.  False when the wait gave up.
+template <int N>
+__device__ __forceinline__ bool poll_tagged(const unsigned long long* p, int stride, unsigned tag, int* err,
+                                            float (&out)[N]) {
+  Spin sp;
+  do {
+    unsigned long long w[N];
+#pragma unroll
+    for (int i = 0; i < N; i++) w[i] = ld_relaxed_u64(p + (size_t)i * stride);
+    bool all = true;
+#pragma unroll
+    for (int i = 0; i < N; i++) all &= (unsigned)(w[i] >> 32) == tag;
+    if (all) {
+#pragma unroll
+      for (int i = 0; i < N; i++) out[i] = __uint_as_float((unsigned)w[i]);
+      return true;
+    }
+  } while (sp.again(err));
+#pragma unroll
+  for (int i = 0; i < N; i++) out[i] = 0.0f;
+  return false;
 }
 
 // ---------------------------------------------------------------------------
@@ -438,11 +521,50 @@ struct Cons {
   bool ok = true;
   int tid, warp, lane;
   long long pos;
+  unsigned ep;   // the session's step counter at entry
+  int cur = 0;   // index of the running phase
 
-  __device__ Cons(const Plan& p, Smem& s, char* r, long long ps) : P(p), sm(s), ring(r), pos(ps) {
+  __device__ Cons(const Plan& p, Smem& s, char* r, long long ps, unsigned e)
+      : P(p), sm(s), ring(r), pos(ps), ep(e) {
     tid = threadIdx.x;
     warp = tid >> 5;
     lane = tid & 31;
+  }
+
+  // Tag of phase q's outputs in this step (never 0: zeroed buffers match no tag).
+  __device__ __forceinline__ unsigned tag_of(int q) const {
+    return (((ep & 0x7fffffu) | 0x800000u) << kTagPhaseBits) | (unsigned)q;
+  }
+  // A fixed-point slot or counter of this step's parity set.
+  template <class T>
+  __device__ __forceinline__ T* fxp(T* base) const {
+    return base + (ep & 1) * P.fx_stride;
+  }
+  // Contributions a fixed-point input needs; the stall test asks for one that never comes.
+  __device__ __forceinline__ unsigned fx_need(const Phase& ph) const {
+    return (unsigned)ph.fx_cnt + (P.test_stall ? 1u : 0u);
+  }
+  // Before reading a fixed-point input whose writers announce their adds:
+  // one thread polls the arrival word, the others wait at a consumers barrier.
+  __device__ __forceinline__ void fx_wait_arrivals(const Phase& ph) {
+    if (!ph.fx_in || !ph.fx_arrive) return;
+    if (tid == 0) {
+      const unsigned long long* a = fxp(ph.fx_in) + P.d;
+      const unsigned long long want = (unsigned long long)ph.fx_arrive + (P.test_stall ? 1u : 0u);
+      Spin sp;
+      while (ld_relaxed_u64(a) < want)
+        if (!sp.again(P.err)) {
+          ok = false;
+          break;
+        }
+    }
+    all_ok();
+  }
+  // One tagged value (bounded wait; clears ok when it gives up).
+  __device__ __forceinline__ float tval(const unsigned long long* p, unsigned tag) {
+    float v[1];
+    if (!poll_tagged<1>(p, 1, tag, P.err, v)) ok = false;
+    return v[0];
   }
 
   // Starts copying phase q's descriptor into sm.ph[q & 1]; it lands by the
@@ -521,10 +643,14 @@ struct Cons {
     if (sm.flag == 1) ok = false;
   }
 
-  // Float4 i4 of a phase's `a` input: the float buffer, or the fixed-point slot
-  // of the fused MLP phase that produced it.
+  // Float4 i4 of a phase's `a` input: the fixed-point slot of the fused phase
+  // that produced it, once final, or the float buffer (after a grid barrier).
   __device__ __forceinline__ float4 in4(const Phase& ph, int i4) {
-    if (ph.fx_in) return fx_load4(ph.fx_in, i4, P.d);
+    if (ph.fx_in) {
+      float4 v;
+      if (!fx_poll4(fxp(ph.fx_in), i4, fx_need(ph), P.err, &v)) ok = false;
+      return v;
+    }
     return __ldcg(reinterpret_cast<const float4*>(ph.in_a) + i4);
   }
 
@@ -537,29 +663,33 @@ struct Cons {
       return;
     }
     if (ph.in_mode == IN_PLAIN) {
+      fx_wait_arrivals(ph);
+      if (!ok) return;
       constexpr int J = kMaxCols / 4 / 256;
       float4 v[J];
       const float4* a4 = reinterpret_cast<const float4*>(ph.in_a);
 #pragma unroll
       for (int j = 0; j < J; j++)
-        if (tid + j * 256 < n4)
-          v[j] = ph.fx_in ? fx_load4(ph.fx_in, tid + j * 256, P.d) : __ldcg(a4 + tid + j * 256);
+        if (tid + j * 256 < n4) v[j] = ph.fx_in ? in4(ph, tid + j * 256) : __ldcg(a4 + tid + j * 256);
 #pragma unroll
       for (int j = 0; j < J; j++)
         if (tid + j * 256 < n4) reinterpret_cast<float4*>(sm.xin)[tid + j * 256] = v[j];
-      consumers_sync();
+      all_ok();
       return;
     }
     if (GL && ph.in_mode == IN_RMS_E) {
       // G: v = rms(x)·w (+ rms(e0)·w_e), as two normalisations and one add.
+      fx_wait_arrivals(ph);
+      if (!ok) return;
       const bool own = tid < n4;
       float4 x = make_float4(0.f, 0.f, 0.f, 0.f), e = x, w = x, we = x;
       if (own) {
         w = __ldg(reinterpret_cast<const float4*>(ph.norm_w) + tid);
         x = in4(ph, tid);
-        if (ph.in_c) {
+        if (ph.in_c) {  // e0: this step's embedding row, read from the weights
+          const uint32_t id = P.host_id >= 0 ? (uint32_t)P.host_id : P.ids[0];
           we = __ldg(reinterpret_cast<const float4*>(ph.in_c) + tid);
-          e = __ldcg(reinterpret_cast<const float4*>(P.e0) + tid);
+          e = __ldg(reinterpret_cast<const float4*>(P.embed + (size_t)id * ph.cols) + tid);
         }
         reinterpret_cast<float4*>(sm.xraw)[tid] = x;
       }
@@ -569,7 +699,7 @@ struct Cons {
       s1 = fmaf(x.w, x.w, s1), s2 = fmaf(e.w, e.w, s2);
       s1 = warp_sum(s1), s2 = warp_sum(s2);
       if (lane == 0) sm.red[warp] = s1, sm.red[kConsumerWarps + warp] = s2;
-      consumers_sync();
+      if (!all_ok()) return;
       float t1 = 0.0f, t2 = 0.0f;
 #pragma unroll
       for (int q = 0; q < kConsumerWarps; q++) t1 += sm.red[q], t2 += sm.red[kConsumerWarps + q];
@@ -592,6 +722,8 @@ struct Cons {
   // Normalised input (IN_RMS, IN_EMBED_RMS, IN_LOOP_RMS): d ≤ kMaxD, at most
   // one float4 per thread.
   __device__ __forceinline__ void rms_prologue(const Phase& ph) {
+    fx_wait_arrivals(ph);
+    if (!ok) return;
     const int n4 = ph.cols / 4;
     const bool own = tid < n4;
     float4 x = make_float4(0.f, 0.f, 0.f, 0.f), w = x;
@@ -605,8 +737,14 @@ struct Cons {
           reinterpret_cast<float4*>(P.x0)[tid] = x;
         }
       } else if (ph.in_mode == IN_LOOP_RMS) {
-        float4 a = in4(ph, tid);
-        float4 b = __ldcg(reinterpret_cast<const float4*>(ph.in_b) + tid);
+        float4 a = in4(ph, tid), b;
+        if (ph.tin_b) {  // the inject output, tagged by its phase
+          float bv[4];
+          if (!poll_tagged<4>(ph.tin_b + 4 * tid, 1, tag_of(ph.tag_in), P.err, bv)) ok = false;
+          b = make_float4(bv[0], bv[1], bv[2], bv[3]);
+        } else {
+          b = __ldcg(reinterpret_cast<const float4*>(ph.in_b) + tid);
+        }
         float4 c = __ldg(reinterpret_cast<const float4*>(ph.in_c) + tid);
         x = make_float4((a.x + b.x) + c.x, (a.y + b.y) + c.y, (a.z + b.z) + c.z, (a.w + b.w) + c.w);
         if (blockIdx.x == 0) reinterpret_cast<float4*>(ph.xout)[tid] = x;
@@ -621,7 +759,7 @@ struct Cons {
     ss = fmaf(x.w, x.w, ss);
     ss = warp_sum(ss);
     if (lane == 0) sm.red[warp] = ss;
-    consumers_sync();
+    if (!all_ok()) return;  // every input final (or the step is being abandoned)
     float tsum = 0.0f;
 #pragma unroll
     for (int q = 0; q < kConsumerWarps; q++) tsum += sm.red[q];
@@ -639,9 +777,10 @@ struct Cons {
     constexpr int QQ = Q > 0 ? Q : 1, SS = S > 0 ? S : 1;
     float* ml = &sm.cmb[0][0];          // [H·S][2]: m, l; then c = e^{m − M_h}
     float* Lh = &sm.cmb[kMaxSplits / 2][0];  // [H]: Σ_s c·l (after the H·S·2 ≤ 512 floats above)
+    const unsigned tg = tag_of(ph.tag_in);  // partials of the attention phase
     for (int i = tid; i < H * Srt; i += 256) {
-      ml[2 * i] = __ldcg(ph.in_a + (size_t)i * (kDH + 2) + kDH);
-      ml[2 * i + 1] = __ldcg(ph.in_a + (size_t)i * (kDH + 2) + kDH + 1);
+      ml[2 * i] = tval(ph.tpart + (size_t)i * (kDH + 2) + kDH, tg);
+      ml[2 * i + 1] = tval(ph.tpart + (size_t)i * (kDH + 2) + kDH + 1, tg);
     }
     float av[QQ][SS];
     if (Q > 0 && S > 0) {
@@ -649,12 +788,12 @@ struct Cons {
       for (int q = 0; q < QQ; q++) {
         const int o = tid + 256 * q;
         if (o >= d) break;
-        const float* src = ph.in_a + (size_t)(o / kDH) * S * (kDH + 2) + (o % kDH);
+        const unsigned long long* src = ph.tpart + (size_t)(o / kDH) * S * (kDH + 2) + (o % kDH);
 #pragma unroll
-        for (int j = 0; j < SS; j++) av[q][j] = __ldcg(src + (size_t)j * (kDH + 2));
+        for (int j = 0; j < SS; j++) av[q][j] = tval(src + (size_t)j * (kDH + 2), tg);
       }
     }
-    consumers_sync();
+    if (!all_ok()) return;
     if (tid < H) {  // per head: the split weights, in split order
       float* m = ml + 2 * tid * Srt;
       float M = -INFINITY;
@@ -672,7 +811,7 @@ struct Cons {
       const int o = tid + 256 * q;
       if (o >= d) break;
       const float* c = ml + 2 * (o / kDH) * Srt;
-      const float* src = ph.in_a + (size_t)(o / kDH) * Srt * (kDH + 2) + (o % kDH);
+      const unsigned long long* src = ph.tpart + (size_t)(o / kDH) * Srt * (kDH + 2) + (o % kDH);
       float A = 0.0f;
 #pragma unroll
       for (int j = 0; j < (S > 0 ? S : kMaxSplits); j++) {
@@ -684,14 +823,14 @@ struct Cons {
           for (int qq = 0; qq < QQ; qq++)
             if (qq == q) a = av[qq][j];
         } else {
-          a = __ldcg(src + (size_t)j * (kDH + 2));
+          a = tval(src + (size_t)j * (kDH + 2), tg);
         }
         A = fmaf(a, c[2 * j], A);
       }
       const float L = Lh[o / kDH];
       sm.xin[o] = L > 0.0f ? A / L : 0.0f;
     }
-    consumers_sync();
+    all_ok();
   }
 
   // Attention output y = Σ_s e^{m_s−M}·acc_s / Σ_s e^{m_s−M}·l_s per (head, dim)
@@ -947,8 +1086,14 @@ struct Cons {
     unsigned long long t0 = P.trace && tid == 0 ? now_ns() : 0;
     rms_prologue(ph);  // the plan gives fused MLPs IN_RMS inputs
     if (t0) pro_ns += now_ns() - t0;
-    if (blockIdx.x >= ph.items) return;
+    if (!ok) return;
     const int d = ph.cols;
+    if (blockIdx.x >= ph.items) {  // no hidden units here: count in, so readers know the sum is final
+      for (int c = tid; c < d; c += 256) red_add_fx(fxp(ph.fx_out) + c, kFxOne);
+      consumers_sync();
+      if (tid == 0) red_add_fx(fxp(ph.fx_out) + d, 1ull);  // this CTA's adds are issued
+      return;
+    }
     float y[kMaxD / 256];
 #pragma unroll
     for (int q = 0; q < kMaxD / 256; q++) y[q] = 0.0f;
@@ -980,16 +1125,15 @@ struct Cons {
     if (!ok) return;
     unsigned long long e0 = P.trace && tid == 0 ? now_ns() : 0;
     bool bad = false;
+    unsigned long long* fo = fxp(ph.fx_out);
 #pragma unroll
     for (int q = 0; q < kMaxD / 256; q++) {
       const int c = tid + 256 * q;
-      if (c < d) {
-        const float v = y[q];
-        if (!(fabsf(v) < kFxMax)) bad = true;  // NaN included
-        red_add_u64(ph.fx_out + c, __float2ll_rn(v * kFxScale));
-      }
+      if (c < d) red_add_fx(fo + c, fx_word(y[q], &bad));
     }
-    if (bad) atomicOr(reinterpret_cast<unsigned long long*>(ph.fx_out + d), 1ull);
+    if (bad) atomicOr(P.err, 16);
+    consumers_sync();
+    if (tid == 0) red_add_fx(fo + d, 1ull);  // this CTA's adds are issued
     if (e0) epi_ns += now_ns() - e0;
   }
 
@@ -1004,7 +1148,7 @@ struct Cons {
     unsigned long long t0 = P.trace && tid == 0 ? now_ns() : 0;
     prologue(ph);
     if (t0) pro_ns += now_ns() - t0;
-    if (blockIdx.x >= ph.items) return;
+    if (!ok || blockIdx.x >= ph.items) return;
     const int K = ph.cols / (ph.cols > 1536 ? 2 : 1) / 128;
     switch (K) {
       case 1: gemv_phase_k<1>(ph); break;
@@ -1023,9 +1167,14 @@ struct Cons {
     if (GL && ph.out_mode == OUT_G) {
       if (&sg == &ph.seg[0]) {  // q rows, scaled as the graph path does (k_g_post)
         const float f = ph.inv_log > 0.0f ? log1pf((float)pos) * ph.inv_log : 1.0f;
+        const unsigned tg = tag_of(cur);
         for (int t = tid; t < n; t += 256) {
           const float a = sm.acc[0][0][t];
-          sg.out[o0 + t] = ph.inv_log > 0.0f ? a * f : a;
+          const float v = ph.inv_log > 0.0f ? a * f : a;
+          if (sg.tout)
+            put_tagged(sg.tout + o0 + t, v, tg);
+          else
+            sg.out[o0 + t] = v;
         }
       } else {  // kv rows: [keys (heads · dh) | values (heads · dh)]
         const int kd = ph.heads * kDH;
@@ -1044,30 +1193,30 @@ struct Cons {
       return;
     }
     if (ph.out_mode == OUT_ROPE) {
+      // q, k, v of this position: tagged into tq ([q | k | v], d each) for
+      // the attention phase; k and v also into the ring (later steps).
       const int d = P.d;
       const size_t slot = (size_t)(pos % ph.cap);
+      const unsigned tg = tag_of(cur);
       for (int t = tid; t < n; t += 256) {
         int o = o0 + t;
         int sec = o / (d / 2), rem = o % (d / 2), h = rem / 32, j = rem % 32;
         float a = sm.acc[0][0][t], b = sm.acc[0][1][t];
+        float u = a, v = b;
         if (sec < 2) {
           float ang = (float)pos * sm.inv_freq[j];
           float sn, cs;
           sincosf(ang, &sn, &cs);
-          float u = a * cs - b * sn, v = a * sn + b * cs;
-          if (sec == 0) {
-            ph.q[h * kDH + j] = u;
-            ph.q[h * kDH + 32 + j] = v;
-          } else {
-            float* kr = ph.kc + ((size_t)h * ph.cap + slot) * kDH;
-            kr[j] = u;
-            kr[32 + j] = v;
-          }
-        } else {
-          float* vr = ph.vc + ((size_t)h * ph.cap + slot) * kDH;
-          vr[j] = a;
-          vr[32 + j] = b;
+          u = a * cs - b * sn, v = a * sn + b * cs;
         }
+        if (sec > 0) {
+          float* r = (sec == 1 ? ph.kc : ph.vc) + ((size_t)h * ph.cap + slot) * kDH;
+          r[j] = u;
+          r[32 + j] = v;
+        }
+        unsigned long long* tq = ph.tq + (size_t)sec * d + h * kDH;
+        put_tagged(tq + j, u, tg);
+        put_tagged(tq + 32 + j, v, tg);
       }
       return;
     }
@@ -1078,6 +1227,8 @@ struct Cons {
         sg.out[o] = (ph.res_smem ? sm.xraw[o] : __ldcg(sg.out + o)) + a;
       else if (ph.out_mode == OUT_SILU)
         sg.out[o] = silu_mul(a, sm.acc[0][1][t]);
+      else if (sg.tout)
+        put_tagged(sg.tout + o, a, tag_of(cur));
       else
         sg.out[o] = a;
     }
@@ -1155,11 +1306,15 @@ struct Cons {
     // so a group reads each cached row as two contiguous 128-byte runs.
     const int d0 = sub * 4, d1 = 32 + sub * 4;
     float qv[QG][8], mx[QG], l[QG], acc[QG][8];
+    const unsigned tg_in = tag_of(ph.tag_in);  // q (and k, v) of the projection phase
 #pragma unroll
     for (int g = 0; g < QG; g++) {
-      const float* qp = ph.q + (c * QG + g) * kDH;
+      const unsigned long long* qp = ph.tq + (c * QG + g) * kDH;
+      float a[4], b[4];
+      if (!poll_tagged<4>(qp + d0, 1, tg_in, P.err, a)) ok = false;
+      if (!poll_tagged<4>(qp + d1, 1, tg_in, P.err, b)) ok = false;
 #pragma unroll
-      for (int e = 0; e < 4; e++) qv[g][e] = __ldcg(qp + d0 + e), qv[g][4 + e] = __ldcg(qp + d1 + e);
+      for (int e = 0; e < 4; e++) qv[g][e] = a[e], qv[g][4 + e] = b[e];
       mx[g] = -INFINITY, l[g] = 0.0f;
 #pragma unroll
       for (int e = 0; e < 8; e++) acc[g][e] = 0.0f;
@@ -1221,15 +1376,28 @@ struct Cons {
       ntiles++;
     }
     if ((!GL || ph.gap == 0) && s == ph.splits - 1 && warp == 0 && grp == 0) {
-      // The step's own position, stored by the projection phase.
-      const size_t slot = (size_t)(pos % ph.cap);
-      const float* kr = ph.kc + ((size_t)c * ph.cap + slot) * kDH;
-      const float* vr = ph.vc + ((size_t)c * ph.cap + slot) * kDH;
+      // The step's own position: tagged by the projection phase, or (after a
+      // grid barrier) in the cache where it stored them.
       float kk[8], vv[8];
+      if (ph.tkv) {
+        const unsigned long long* kr = ph.tkv + c * kDH;
+        const unsigned long long* vr = kr + P.d;
+        float a[4], b[4], e4[4], f4[4];
+        if (!poll_tagged<4>(kr + d0, 1, tg_in, P.err, a)) ok = false;
+        if (!poll_tagged<4>(kr + d1, 1, tg_in, P.err, b)) ok = false;
+        if (!poll_tagged<4>(vr + d0, 1, tg_in, P.err, e4)) ok = false;
+        if (!poll_tagged<4>(vr + d1, 1, tg_in, P.err, f4)) ok = false;
 #pragma unroll
-      for (int e = 0; e < 4; e++) {
-        kk[e] = __ldcg(kr + d0 + e), kk[4 + e] = __ldcg(kr + d1 + e);
-        vv[e] = __ldcg(vr + d0 + e), vv[4 + e] = __ldcg(vr + d1 + e);
+        for (int e = 0; e < 4; e++) kk[e] = a[e], kk[4 + e] = b[e], vv[e] = e4[e], vv[4 + e] = f4[e];
+      } else {
+        const size_t slot = (size_t)(pos % ph.cap);
+        const float* kr = ph.kc + ((size_t)c * ph.cap + slot) * kDH;
+        const float* vr = ph.vc + ((size_t)c * ph.cap + slot) * kDH;
+#pragma unroll
+        for (int e = 0; e < 4; e++) {
+          kk[e] = __ldcg(kr + d0 + e), kk[4 + e] = __ldcg(kr + d1 + e);
+          vv[e] = __ldcg(vr + d0 + e), vv[4 + e] = __ldcg(vr + d1 + e);
+        }
       }
 #pragma unroll
       for (int g = 0; g < QG; g++) {
@@ -1268,7 +1436,7 @@ struct Cons {
         if (sub == 0) sm.wsm[warp][kDH] = mx[g], sm.wsm[warp][kDH + 1] = l[g];
       }
       if (!all_ok()) return;
-      float* out = ph.part + ((size_t)(c * QG + g) * ph.splits + s) * (kDH + 2);
+      unsigned long long* out = ph.tpart + ((size_t)(c * QG + g) * ph.splits + s) * (kDH + 2);
       if (tid < kDH + 2) {
         const int e = tid < kDH ? tid : 0;
         float m0 = sm.wsm[0][kDH], l0 = sm.wsm[0][kDH + 1], a0 = sm.wsm[0][e];
@@ -1280,7 +1448,7 @@ struct Cons {
           a0 = a0 * ca + sm.wsm[w][e] * cb;
           m0 = M;
         }
-        out[tid] = tid < kDH ? a0 : (tid == kDH ? m0 : l0);
+        put_tagged(out + tid, tid < kDH ? a0 : (tid == kDH ? m0 : l0), tag_of(cur));
       }
       consumers_sync();  // sm.wsm is free for the next head / item
     }
@@ -1301,71 +1469,59 @@ struct Cons {
   __device__ __forceinline__ void mixer_o_tail(const Phase& ph, int h, int s, bool gla) {
     constexpr int RQ = kMaxItemOut / 64;  // rows per thread: r = tid / 4 + 64·k
     const int R = ph.orows, q4 = tid & 3;
-    float res[RQ];
+    float res[RQ];  // the block's input x, which this CTA's own prologue left in sm.xraw
 #pragma unroll
     for (int k = 0; k < RQ; k++) {
       const int r = (tid >> 2) + 64 * k;
-      res[k] = 0.0f;
-      if (h == 0 && q4 == 0 && r < R)
-        res[k] = ph.fx_in ? fx_load1(ph.fx_in, s * R + r, P.d) : __ldcg(ph.in_a + s * R + r);
+      res[k] = h == 0 && q4 == 0 && r < R ? sm.xraw[s * R + r] : 0.0f;
     }
     const float* w = take_warp();
-    if (tid == 0 && !gla) {
-      red_release_add_u64(ph.cnt + h, 1ull);  // after the partial (ordered by the barrier above)
-      const unsigned long long want = (unsigned long long)ph.splits;
-      unsigned long long t0 = 0;
-      for (unsigned it = 0; ld_acquire_u64(ph.cnt + h) < want; it++) {
-        if ((it & 15) == 15) {
-          if (ld_volatile(P.err) & 8) {
-            sm.flag = 1;
-            break;
+    // The merge, in split order: the head's partials ([split][acc | m | l]),
+    // polled by all threads into sm.cmb until every split has tagged its own
+    // (one load round per poll); the split weights c_j = e^(m_j − M) once per
+    // split, in sm.red.
+    if (!gla) {
+      const unsigned long long* pp = ph.tpart + (size_t)h * ph.splits * (kDH + 2);
+      const unsigned tg = tag_of(cur);
+      constexpr int NV = (kMaxSplits * (kDH + 2) + 255) / 256;
+      const int nv = ph.splits * (kDH + 2);
+      Spin sp;
+      for (;;) {
+        unsigned long long wv[NV];
+#pragma unroll
+        for (int k = 0; k < NV; k++)
+          if (tid + 256 * k < nv) wv[k] = ld_relaxed_u64(pp + tid + 256 * k);
+        bool all = true;
+#pragma unroll
+        for (int k = 0; k < NV; k++)
+          if (tid + 256 * k < nv) {
+            const int i = tid + 256 * k;
+            all &= (unsigned)(wv[k] >> 32) == tg;
+            sm.cmb[i / (kDH + 2)][i % (kDH + 2)] = __uint_as_float((unsigned)wv[k]);
           }
-          if (!t0) {
-            t0 = now_ns();
-          } else if (now_ns() - t0 > kWaitNs) {
-            atomicOr(P.err, 8);
-            sm.flag = 1;
-            break;
-          }
+        if (all) break;
+        if (!sp.again(P.err)) {
+          ok = false;
+          break;
         }
       }
-    }
-    consumers_sync();
-    if (sm.flag == 1) ok = false;
-    // The merge, in split order: every load first (one round trip), the split
-    // weights c_j = e^(m_j − M) once per split through shared memory.
-    const float* pp = ph.part + (size_t)h * ph.splits * (kDH + 2);
-    float av[kMaxSplits];
-    if (gla) {
-      // y_h is in sm.vec[0] already (gla_item ran on this CTA)
-    } else if (ok && tid < kDH) {
-#pragma unroll
-      for (int j = 0; j < kMaxSplits; j++)
-        if (j < ph.splits) av[j] = __ldcg(pp + (size_t)j * (kDH + 2) + tid);
-    }
-    if (!gla && ok && tid >= kDH && tid < kDH + ph.splits) {
-      const int j = tid - kDH;
-      sm.cmb[j][0] = __ldcg(pp + (size_t)j * (kDH + 2) + kDH);
-      sm.cmb[j][1] = __ldcg(pp + (size_t)j * (kDH + 2) + kDH + 1);
-    }
-    consumers_sync();
-    if (!gla && ok && tid < ph.splits) {
-      float M = -INFINITY;
-      for (int j = 0; j < ph.splits; j++) M = fmaxf(M, sm.cmb[j][0]);
-      const float m = sm.cmb[tid][0];
-      sm.cmb[tid][2] = (M == -INFINITY || m == -INFINITY) ? 0.0f : expf(m - M);
-    }
-    consumers_sync();
-    if (!gla && ok && tid < kDH) {
-      float A = 0.0f, L = 0.0f;
-#pragma unroll
-      for (int j = 0; j < kMaxSplits; j++)
-        if (j < ph.splits) {
-          const float c = sm.cmb[j][2];
-          L += sm.cmb[j][1] * c;
-          A = fmaf(av[j], c, A);
+      all_ok();
+      if (ok && tid < ph.splits) {
+        float M = -INFINITY;
+        for (int j = 0; j < ph.splits; j++) M = fmaxf(M, sm.cmb[j][kDH]);
+        const float m = sm.cmb[tid][kDH];
+        sm.red[tid] = (M == -INFINITY || m == -INFINITY) ? 0.0f : expf(m - M);
+      }
+      consumers_sync();
+      if (ok && tid < kDH) {
+        float A = 0.0f, L = 0.0f;
+        for (int j = 0; j < ph.splits; j++) {
+          const float c = sm.red[j];
+          L += sm.cmb[j][kDH + 1] * c;
+          A = fmaf(sm.cmb[j][tid], c, A);
         }
-      sm.vec[0][tid] = L > 0.0f ? A / L : 0.0f;
+        sm.vec[0][tid] = L > 0.0f ? A / L : 0.0f;
+      }
     }
     consumers_sync();
     // Row r = tid / 4 (+ 64·k): thread q4 takes columns 4·q4 + 16·i … + 3.
@@ -1387,15 +1543,11 @@ struct Cons {
         }
         v += __shfl_xor_sync(0xffffffffu, v, 1);
         v += __shfl_xor_sync(0xffffffffu, v, 2);
-        if (q4 == 0 && r < R) {
-          v += res[k];
-          if (!(fabsf(v) < kFxMax)) bad = true;  // NaN included
-          red_add_u64(ph.fx_out + s * R + r, __float2ll_rn(v * kFxScale));
-        }
+        if (q4 == 0 && r < R) red_add_fx(fxp(ph.fx_out) + s * R + r, fx_word(v + res[k], &bad));
       }
     }
     release();
-    if (bad) atomicOr(reinterpret_cast<unsigned long long*>(ph.fx_out + P.d), 1ull);
+    if (bad) atomicOr(P.err, 16);
     all_ok();  // sm.cmb and sm.vec are free; ok uniform
   }
 
@@ -1418,15 +1570,16 @@ struct Cons {
   // after all of them have.
   __device__ void gla_item(const Phase& ph, int h, int s = 0) {
     const int d = P.d;
-    const float* row = ph.mix;  // [q | k | v | g], each d wide
+    // [q | k | v | g] rows (each d wide) and the decay, tagged by the projection phase.
+    const unsigned tg = tag_of(ph.tag_in);
     if (tid < kDH) {
-      sm.vec[0][tid] = __ldcg(row + h * kDH + tid);
-      sm.vec[1][tid] = __ldcg(row + d + h * kDH + tid);
-      sm.vec[2][tid] = __ldcg(row + 2 * d + h * kDH + tid);
-      sm.vec[3][tid] = __ldcg(row + 3 * d + h * kDH + tid);
+      float v[4];
+      if (!poll_tagged<4>(ph.tmix + h * kDH + tid, d, tg, P.err, v)) ok = false;
+#pragma unroll
+      for (int k = 0; k < 4; k++) sm.vec[k][tid] = v[k];
     }
-    const float dcy = 1.0f / (1.0f + expf(__ldcg(ph.dec + h) + __ldg(ph.bias + h)));
-    consumers_sync();
+    const float dcy = 1.0f / (1.0f + expf(tval(ph.tdec + h, tg) + __ldg(ph.bias + h)));
+    if (!all_ok()) return;
     if (warp < 2) {  // warp 0: |q|, warp 1: |k|
       float a = sm.vec[warp][lane], b = sm.vec[warp][lane + 32];
       float ss = warp_sum(a * a + b * b);
@@ -1436,7 +1589,8 @@ struct Cons {
     }
     float* tile = const_cast<float*>(take());  // (its barrier also orders the l2norm above)
     if (!tile) return;
-    if (ph.wo && s != 0 && tid == 0) red_release_add_u64(ph.cnt + h, 1ull);  // the old state is read
+    unsigned long long* cnt = ph.wo ? fxp(ph.cnt) + h : nullptr;
+    if (ph.wo && s != 0 && tid == 0) red_release_add_u64(cnt, 1ull);  // the old state is read
     const int b = tid & 63, qa = tid >> 6;
     const float vb = sm.vec[2][b];
     float yp = 0.0f;
@@ -1470,7 +1624,7 @@ struct Cons {
     }
     if (ph.wo && tid == 0) {  // split 0: every other split's copy of the old state has landed
       unsigned long long t0 = 0;
-      for (unsigned it = 0; ld_acquire_u64(ph.cnt + h) < (unsigned long long)(ph.splits - 1); it++) {
+      for (unsigned it = 0; ld_acquire_u64(cnt) < (unsigned long long)(ph.splits - 1); it++) {
         if ((it & 15) == 15) {
           if (ld_volatile(P.err) & 8) {
             sm.flag = 1;
@@ -1510,9 +1664,11 @@ struct Cons {
 
   __device__ void run() {
     if (tid < kDH / 2 && P.inv_freq) sm.inv_freq[tid] = __ldg(P.inv_freq + tid);
-    // The fused MLP slots start the step at zero (the previous step's readers
-    // ended with its launch; the first MLP comes after at least one barrier).
-    for (int e = blockIdx.x * 256 + tid; e < P.fx_words; e += gridDim.x * 256) P.fx[e] = 0;
+    // This step adds into the fixed-point set of its parity; the other set,
+    // last read by the previous step (ended with its launch), is zeroed here
+    // for the next step.
+    unsigned long long* nx = P.fx + ((ep + 1) & 1) * P.fx_stride;
+    for (int e = blockIdx.x * 256 + tid; e < P.fx_words; e += gridDim.x * 256) nx[e] = 0;
     stage_phase(0);
     stage_wait();
     consumers_sync();
@@ -1520,9 +1676,16 @@ struct Cons {
       if (p > 0) {
         stamp(p - 1, 1);
         stage_wait();  // phase p's descriptor, requested one phase ago
-        grid_sync();
-        if (!ok) return;
+        if (!consumers_and(ok ? 1 : 0)) {
+          ok = false;
+          return;
+        }
+        if (P.all_sync || sm.ph[p & 1].sync) {
+          grid_sync();
+          if (!ok) return;
+        }
       }
+      cur = p;
       stamp(p, 0);
       stage_phase(p + 1);
       const Phase& ph = sm.ph[p & 1];
@@ -1552,6 +1715,7 @@ struct Cons {
       if (prev == gridDim.x - 1) {
         atomicExch(P.bar, 0u);
         atomicExch(P.bar + 1, 0u);
+        atomicExch(P.epoch, ep + 1u);  // every CTA read the epoch at entry
       }
     }
   }
@@ -1576,7 +1740,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_mega(const __grid_consta
     if (threadIdx.x == kConsumerWarps * 32) producer(P, sm, ring, pos);
     return;
   }
-  Cons<GL> c(P, sm, ring, pos);
+  Cons<GL> c(P, sm, ring, pos, *P.epoch);
   c.run();
 }
 

@@ -1,6 +1,8 @@
 // Plan of the persistent decode kernel (decode_mega.cu): the m = 1 token step
-// as a list of phases separated by grid barriers.  Built once per session on
-// the host (model.cpp) and read by every CTA.
+// as a list of phases.  Each CTA runs them in order and waits only for the
+// values it reads (counted fixed-point sums and tagged words); phases that read
+// plain data other CTAs wrote in the step start after a grid barrier.  Built
+// once per session on the host (model.cpp) and read by every CTA.
 #pragma once
 
 #include <stdint.h>
@@ -48,13 +50,28 @@ enum OutMode : int {
                    // Σ_j h_j·downᵀ[j] (+ the residual on CTA 0) added into the fixed-point sum fx_out
 };
 
-// Fixed-point residual sums of fused MLP phases: int64 in units of 2^-32, one
-// slot of d + 2 words per MLP of the step ([d] sums, [d] a flag set when a part
-// was non-finite or beyond ±2^23, [d + 1] padding).  Integer adds are exact, so
-// the sum does not depend on the order in which CTAs arrive.
-constexpr float kFxScale = 4294967296.0f;       // 2^32
-constexpr float kFxInv = 1.0f / 4294967296.0f;  // 2^-32
-constexpr float kFxMax = 8388608.0f;            // 2^23: 255 parts of this size stay below 2^31
+// Fixed-point residual sums of fused phases (the MLP, and the mixer with o):
+// one 64-bit word per value that carries its own completion count.  Each
+// contributing CTA adds kFxOne + round(part · 2^30); the top 8 bits count the
+// contributions, the low 56 bits hold the signed sum.  Integer adds are exact,
+// so the result does not depend on the order in which CTAs arrive, and a
+// reader knows the value is final when the count reaches the phase's number of
+// contributors: no barrier and no second read.  Parts are bounded by 2^16, so
+// 255 of them stay below 2^54 in magnitude; a part that is non-finite or
+// larger is not added (its count is) and the step reports an error.  Word d of
+// a slot counts the CTAs that have issued their adds (a hint: readers of an
+// MLP's slot poll it before the values, so 148 readers do not poll 768 words
+// while 148 writers add into them).
+constexpr float kFxScale = 1073741824.0f;         // 2^30
+constexpr float kFxInv = 1.0f / 1073741824.0f;    // 2^-30
+constexpr float kFxMax = 65536.0f;                // 2^16
+constexpr unsigned long long kFxOne = 1ull << 56;
+
+// Values that one CTA writes and others read within a step (q, the current
+// k and v, attention partials, GLA inputs, the inject output) are 64-bit
+// words: the float in the low half, a tag (step epoch << 8 | producing phase)
+// in the high half.  A reader polls until the tag is the one it expects.
+constexpr int kTagPhaseBits = 8;  // phases per step < 256
 
 struct Segment {
   const float* w;   // weight rows, row-major, `cols` wide
@@ -62,10 +79,21 @@ struct Segment {
   int per_item;     // logical outputs per item
   int items;
   float* out;       // output (OUT_STORE/ADD/SILU/LOGITS)
+  unsigned long long* tout;  // OUT_STORE, OUT_G q: tagged output (instead of out)
 };
 
 struct alignas(16) Phase {
   int kind;
+  int sync;     // a grid barrier before this phase: it reads plain data other CTAs wrote in this step
+  int fx_cnt;   // contributions per value of fx_in when it is final
+  int fx_arrive;  // CTAs that announce their adds in word d of fx_in (0: poll the values only)
+  int tag_in;   // the phase whose tagged outputs this phase reads (tq, tmix, tpart, tin_b)
+  // Tagged buffers: q | k | v of this position (3 × d: OUT_ROPE writes, ATTN reads; OUT_G writes q),
+  // attention partials [head][split][dh + 2], GLA inputs (q|k|v|g rows, 4 × d, and decay, heads),
+  // and the loop input's inject term.
+  unsigned long long *tq, *tpart, *tmix, *tdec;
+  unsigned long long* tkv;  // ATTN: tagged k | v of this position (d each), or null: read them from the cache
+  const unsigned long long* tin_b;
   // GEMV
   int cols;
   int in_mode, out_mode;
@@ -84,9 +112,9 @@ struct alignas(16) Phase {
   const float* inv_freq;
   // OUT_MLP: downᵀ ([F][d], row j = column j of down) and the slot its sums go to
   const float* wt;
-  long long* fx_out;
+  unsigned long long* fx_out;
   // Inputs: when set, the `a` input is this fixed-point slot instead of in_a
-  const long long* fx_in;
+  const unsigned long long* fx_in;
   // ATTN with o (S blocks): the o matrix as per-head column blocks [heads][d][dh];
   // split s multiplies rows s·orows … of its head's block, after the head's
   // `splits` partials have arrived (per-head counters `cnt`, zeroed each step),
@@ -129,7 +157,7 @@ struct Plan {
   uint32_t* hist;       // optional history array (same index as out + hist_base)
   unsigned long long hist_base;
   unsigned* bar;        // grid barrier: [0] arrivals (monotonic in a step), [1] CTAs done
-  int* err;             // error word: 8 = a bounded wait expired
+  int* err;             // error word: 8 = a bounded wait expired, 16 = a residual part out of range
   long long spin_limit;
   // Optional timeline, per phase and CTA, eight words at (phase·grid + cta)·8:
   // globaltimer (ns) when the CTA starts the phase's work and when it reaches
@@ -142,8 +170,14 @@ struct Plan {
   int test_stall;
   int global;  // the plan has global-attention layers (selects the kernel built for them)
   long long host_id;  // ≥ 0: this step's token, passed with the launch; < 0: read ids[0]
-  long long* fx;  // fixed-point slots of fused phases and their counters, zeroed at the start of each step
+  // Fixed-point slots of fused phases and per-head counters: two sets of
+  // fx_words words, fx_stride apart; a step uses set (epoch & 1) and zeroes
+  // the other one for the next step.  Phase descriptors point into set 0.
+  unsigned long long* fx;
   int fx_words;
+  long long fx_stride;
+  unsigned* epoch;  // step counter of the session (tags, fixed-point set parity)
+  int all_sync;     // a grid barrier before every phase (the unfused variants)
   int mlp_cta;    // 1: fused MLP tiles split by rows with a CTA barrier per tile (always for d > 768)
   // L2 priority of the bulk copies: 0 none; 1 weights of phases marked l2keep
   // evict_last, every other tile evict_first; 2 the same with the others normal.

@@ -116,7 +116,13 @@ struct slm_session {
   float* attn_part = nullptr;            // attention partials of the persistent step
   bool fuse_mlp = false;                 // the persistent step runs each MLP as one phase
   bool fuse_ao = false;                  // … and the o projection of S blocks in the attention phase
-  long long* fx = nullptr;               // fixed-point slots of those phases
+  unsigned long long* fx = nullptr;      // counted fixed-point slots of those phases (two parity sets)
+  size_t fx_set_words = 0;               // words of one set (the stride between the sets)
+  unsigned* epoch = nullptr;             // the persistent step's counter (tags and set parity)
+  // Tagged words the persistent step's CTAs pass to each other within a step:
+  // q | k | v of the position, attention partials, GLA inputs (q|k|v|g rows,
+  // decay), the inject output.
+  unsigned long long *tq = nullptr, *tpart = nullptr, *tmix = nullptr, *tdec = nullptr, *te = nullptr;
   bool plan_stale = false;               // a global cache moved: the phase descriptors need refreshing
   bool keys_stale = false;               // state was written from the host: the next shifted keys need recomputing
   int in_batches = 0;                    // batches holding this session
@@ -561,6 +567,14 @@ void build_plan(slm_session* se, bool refresh = false) {
     se->attn_part = static_cast<float*>(
         alloc_zero(se, (size_t)H * std::max(splits, gsplits) * (kDH + 2) * sizeof(float)));
     se->attn_count = static_cast<unsigned*>(alloc_zero(se, (size_t)H * sizeof(unsigned)));
+    using u64 = unsigned long long;
+    auto tw = [&](size_t n) { return static_cast<u64*>(alloc_zero(se, n * sizeof(u64))); };
+    se->tq = tw((size_t)3 * d);
+    se->tpart = tw((size_t)H * std::max(splits, gsplits) * (kDH + 2));
+    se->tmix = tw((size_t)4 * d);
+    se->tdec = tw((size_t)H);
+    se->te = tw((size_t)d);
+    se->epoch = static_cast<unsigned*>(alloc_zero(se, 64 * sizeof(unsigned)));
   }
   float* attn_part = se->attn_part;
   unsigned* attn_count = se->attn_count;
@@ -581,22 +595,45 @@ void build_plan(slm_session* se, bool refresh = false) {
   const size_t slot_words = (size_t)d + 2;
   const size_t nslots = se->fuse_mlp ? nmlp + (fuse_ao ? nao : 0) : 0;
   const size_t ncnt = fuse_ao ? nao * H : 0;
-  if (!refresh && se->fuse_mlp)
-    se->fx = static_cast<long long*>(alloc_zero(se, (nslots * slot_words + ncnt) * sizeof(long long)));
+  if (!refresh && se->fuse_mlp) {
+    se->fx_set_words = (nslots * slot_words + ncnt + 31) / 32 * 32;
+    se->fx = static_cast<unsigned long long*>(alloc_zero(se, 2 * se->fx_set_words * sizeof(unsigned long long)));
+  }
   size_t next_slot = 0, next_cnt = 0;
-  std::vector<std::pair<const float*, long long*>> fxw;
-  auto fx_of = [&](const float* buf) -> const long long* {
+  // Which fixed-point slot holds each buffer's current value, and how many
+  // contributions make it final (every CTA for an MLP, one per head for a
+  // mixer with o).
+  struct FxHold {
+    const float* buf;
+    unsigned long long* slot;
+    int cnt;
+    int arrive;  // CTAs that announce their adds in the slot's word d (MLP slots)
+  };
+  std::vector<FxHold> fxw;
+  auto fx_of = [&](const float* buf) -> const unsigned long long* {
     for (auto& e : fxw)
-      if (e.first == buf) return e.second;
+      if (e.buf == buf) return e.slot;
     return nullptr;
   };
-  auto fx_set = [&](const float* buf, long long* slot) {
+  auto fx_cnt_of = [&](const float* buf) -> int {
     for (auto& e : fxw)
-      if (e.first == buf) {
-        e.second = slot;
+      if (e.buf == buf) return e.cnt;
+    return 0;
+  };
+  auto fx_set = [&](const float* buf, unsigned long long* slot, int cnt = 0, int arrive = 0) {
+    for (auto& e : fxw)
+      if (e.buf == buf) {
+        e.slot = slot, e.cnt = cnt, e.arrive = arrive;
         return;
       }
-    fxw.emplace_back(buf, slot);
+    fxw.push_back(FxHold{buf, slot, cnt, arrive});
+  };
+  // A phase reading buffer `buf` as its `a` input.
+  auto read_x = [&](Phase& p, const float* buf) {
+    p.fx_in = fx_of(buf);
+    p.fx_cnt = fx_cnt_of(buf);
+    for (auto& e : fxw)
+      if (e.buf == buf) p.fx_arrive = e.arrive;
   };
   struct In {
     int mode;
@@ -608,10 +645,11 @@ void build_plan(slm_session* se, bool refresh = false) {
     if (se->fuse_mlp) {
       Phase u = gemv(d, IN_RMS, X, nullptr, nullptr, b.norm2, nullptr, OUT_MLP, seg(b.up.w, F, per(F, G, 1), nullptr));
       u.wt = b.down.t;
-      u.fx_in = fx_of(X);
+      read_x(u, X);
+      u.sync = u.fx_in ? 0 : 1;  // after a G block's o, x is a float buffer
       u.fx_out = se->fx + slot_words * next_slot++;
       ph.push_back(u);
-      fx_set(X, u.fx_out);
+      fx_set(X, u.fx_out, G, G);  // every CTA adds into every value, and announces it
       return;
     }
     ph.push_back(gemv(d, IN_RMS, X, nullptr, nullptr, b.norm2, nullptr, OUT_SILU,
@@ -620,13 +658,23 @@ void build_plan(slm_session* se, bool refresh = false) {
                       seg(b.down.w, d, per(d, G, 1), X)));
     ph.back().res_smem = 1;
   };
+  // The loop input's inject term, tagged by the inject phase.
+  int inject_phase = -1;
+  auto loop_input = [&](Phase& p, const In& in) {
+    if (in.mode != IN_LOOP_RMS) return;
+    p.tin_b = se->te;
+    p.tag_in = inject_phase;
+  };
   auto block = [&](const Block& b, LState& st, float* X, In in) {
     const float* ia = in.mode == IN_RMS ? X : in.a;
     if (b.kind == 'S') {
       Phase p = gemv(d, in.mode, ia, in.b, in.c, b.norm1, in.xout, OUT_ROPE,
                      seg(b.qkv.w, 3 * d / 2, per(3 * d / 2, G, 8), nullptr));
       p.q = se->q, p.kc = st.k, p.vc = st.v, p.cap = (long long)st.cap, p.inv_freq = md->inv_freq;
-      p.fx_in = fx_of(ia);
+      p.tq = se->tq;
+      read_x(p, ia);
+      loop_input(p, in);
+      const int proj = (int)ph.size();
       ph.push_back(p);
       if (in.mode == IN_LOOP_RMS || in.mode == IN_EMBED_RMS) fx_set(X, nullptr);  // that prologue wrote x to X
       Phase a{};
@@ -634,15 +682,15 @@ void build_plan(slm_session* se, bool refresh = false) {
       a.kc = st.k, a.vc = st.v, a.q = se->q, a.cap = (long long)st.cap, a.window = (long long)c.window;
       a.heads = H, a.splits = splits, a.part = attn_part, a.counters = attn_count;
       a.y = se->y, a.scale = scale, a.items = H * splits;
+      a.tq = se->tq, a.tkv = se->tq + d, a.tpart = se->tpart, a.tag_in = proj;
       if (fuse_ao && b.o.hb) {
         a.wo = b.o.hb;
         a.orows = d / splits;
-        a.cnt = reinterpret_cast<unsigned long long*>(se->fx + nslots * slot_words) + H * next_cnt++;
+        a.cnt = se->fx + nslots * slot_words + H * next_cnt++;
         a.in_a = X;
-        a.fx_in = fx_of(X);  // the residual
         a.fx_out = se->fx + slot_words * next_slot++;
         ph.push_back(a);
-        fx_set(X, a.fx_out);
+        fx_set(X, a.fx_out, H);  // one part per head
         block_mlp(b, X);
         return;
       }
@@ -659,7 +707,9 @@ void build_plan(slm_session* se, bool refresh = false) {
       p.items = p.seg[0].items + p.seg[1].items;
       p.kc = st.k, p.vc = st.v, p.cap = (long long)st.cap, p.heads = kh, p.kshift = c.kshift ? 1 : 0;
       p.inv_log = c.logn ? 1.0f / std::log((float)c.logn) : 0.0f;
-      p.fx_in = fx_of(X);
+      p.seg[0].tout = se->tq;
+      read_x(p, X);
+      const int proj = (int)ph.size();
       ph.push_back(p);
       Phase a{};
       a.kind = PH_ATTN;
@@ -667,6 +717,8 @@ void build_plan(slm_session* se, bool refresh = false) {
       a.gap = c.far ? (long long)c.window : 0;
       a.heads = H, a.qg = H / kh, a.splits = gsplits, a.part = attn_part, a.counters = attn_count;
       a.y = se->y, a.scale = scale, a.items = kh * gsplits;
+      a.tq = se->tq, a.tpart = se->tpart, a.tag_in = proj;
+      a.sync = 1;  // the projection stored this position's value (and key) in the cache
       ph.push_back(a);
     } else {
       Phase p = gemv(d, in.mode, ia, in.b, in.c, b.norm1, in.xout, OUT_STORE,
@@ -674,24 +726,27 @@ void build_plan(slm_session* se, bool refresh = false) {
       p.nseg = 2;
       p.seg[1] = seg(b.decay.w, H, per(H, 1, 1), se->dec);
       p.items = p.seg[0].items + p.seg[1].items;
-      p.fx_in = fx_of(ia);
+      p.seg[0].tout = se->tmix, p.seg[1].tout = se->tdec;
+      read_x(p, ia);
+      loop_input(p, in);
+      const int proj = (int)ph.size();
       ph.push_back(p);
       if (in.mode == IN_LOOP_RMS || in.mode == IN_EMBED_RMS) fx_set(X, nullptr);  // that prologue wrote x to X
       Phase g{};
       g.kind = PH_GLA;
       g.state = st.s, g.mix = se->mix, g.dec = se->dec, g.bias = b.bias, g.hnw = b.head_norm, g.y = se->y;
+      g.tmix = se->tmix, g.tdec = se->tdec, g.tag_in = proj;
       g.items = H;
-      if (fuse_ao && b.o.hb) {  // split 0 of each head runs the GLA, every split its o rows
+      if (fuse_ao && b.o.hb) {  // every split of a head runs the GLA, every split its o rows
         g.items = H * splits;
         g.splits = splits;
         g.wo = b.o.hb;
         g.orows = d / splits;
-        g.cnt = reinterpret_cast<unsigned long long*>(se->fx + nslots * slot_words) + H * next_cnt++;
+        g.cnt = se->fx + nslots * slot_words + H * next_cnt++;
         g.in_a = X;
-        g.fx_in = fx_of(X);  // the residual
         g.fx_out = se->fx + slot_words * next_slot++;
         ph.push_back(g);
-        fx_set(X, g.fx_out);
+        fx_set(X, g.fx_out, H);  // one part per head
         block_mlp(b, X);
         return;
       }
@@ -703,6 +758,8 @@ void build_plan(slm_session* se, bool refresh = false) {
     if (b.kind == 'S' || b.kind == 'G') {
       Phase o = gemv(d, IN_ATTN, attn_part, nullptr, nullptr, nullptr, nullptr, OUT_ADD, seg(b.o.w, d, per(d, G, 1), X));
       o.heads = H, o.splits = b.kind == 'G' ? gsplits : splits;
+      o.tpart = se->tpart, o.tag_in = (int)ph.size() - 1;  // the attention phase's partials
+      o.sync = 1;
       ph.push_back(o);
     } else {
       ph.push_back(gemv(d, IN_PLAIN, se->y, nullptr, nullptr, nullptr, nullptr, OUT_ADD, seg(b.o.w, d, per(d, G, 1), X)));
@@ -715,9 +772,12 @@ void build_plan(slm_session* se, bool refresh = false) {
     block(md->prelude[i], se->pre[i], X0, In{i == 0 ? IN_EMBED_RMS : IN_RMS, nullptr, nullptr, nullptr, nullptr});
   float* X = X0;
   if (md->looped) {
+    inject_phase = (int)ph.size();
     ph.push_back(gemv(d, IN_PLAIN, X0, nullptr, nullptr, nullptr, nullptr, OUT_STORE,
                       seg(md->inject.w, d, per(d, G, 1), se->e_proj)));
-    ph.back().fx_in = fx_of(X0);
+    read_x(ph.back(), X0);
+    ph.back().seg[0].tout = se->te;
+    ph.back().sync = ph.back().fx_in ? 0 : 1;
     const float* sbuf = X0;
     for (size_t r = 0; r < se->loops; r++) {
       float* xr = (r % 2 == 0) ? se->xb : se->xc;
@@ -736,7 +796,9 @@ void build_plan(slm_session* se, bool refresh = false) {
     block(md->coda[i], se->coda[i], X, In{IN_RMS, nullptr, nullptr, nullptr, nullptr});
   ph.push_back(gemv(d, IN_RMS, X, nullptr, nullptr, md->norm_f, nullptr, OUT_LOGITS,
                     seg(md->embed.w, (int)c.vocab, per((int)c.vocab, G, 1), se->logits)));
-  ph.back().fx_in = fx_of(X);
+  read_x(ph.back(), X);
+  ph.back().sync = ph.back().fx_in ? 0 : 1;
+  SLM_REQUIRE(ph.size() < (1u << kTagPhaseBits), "too many phases for the decode kernel's tags");
   const int logit_items = ph.back().items;
   SLM_REQUIRE(next_slot <= nslots && next_cnt * H <= ncnt, "fused-phase slots out of step");
 
@@ -773,6 +835,10 @@ void build_plan(slm_session* se, bool refresh = false) {
   P.arg_part = static_cast<unsigned long long*>(alloc_zero(se, logit_items * sizeof(unsigned long long)));
   P.fx = se->fx;
   P.fx_words = se->fuse_mlp ? (int)(nslots * slot_words + ncnt) : 0;
+  P.fx_stride = (long long)se->fx_set_words;
+  P.epoch = se->epoch;
+  // The unfused variants pass plain buffers between phases: a barrier before each.
+  P.all_sync = !se->fuse_mlp || !fuse_ao ? 1 : 0;
   P.mlp_cta = d > kMaxCols / 4 || mlp_cta_setting() ? 1 : 0;
   P.l2mode = l2mode_setting();
   P.next_id = se->ids_dev;
@@ -884,15 +950,28 @@ void check_device_error(slm_ctx* c, slm_session* se = nullptr) {
   const int h = *c->err_host;
   if (h) {
     SLM_CUDA(cudaMemsetAsync(c->err, 0, sizeof(int), c->stream));
-    if ((h & 8) && se && se->mega_ok) {
-      // A step that gave up left its barrier and arrival counters mid-way.
+    if ((h & (8 | 16)) && se && se->mega_ok) {
+      // A step that gave up left its barrier and arrival counters and its
+      // fixed-point sums mid-way, and did not advance the step counter: reset
+      // them, and advance the counter so no tag of that step is taken for a
+      // later one.
       SLM_CUDA(cudaMemsetAsync(se->plan_host.arg_count, 0, 16 * sizeof(unsigned), c->stream));
       SLM_CUDA(cudaMemsetAsync(se->attn_count, 0, se->model->cfg.heads * sizeof(unsigned), c->stream));
+      if (se->fx)
+        SLM_CUDA(cudaMemsetAsync(se->fx, 0, 2 * se->fx_set_words * sizeof(unsigned long long), c->stream));
+      unsigned e = 0;
+      SLM_CUDA(cudaMemcpyAsync(&e, se->epoch, sizeof(e), cudaMemcpyDeviceToHost, c->stream));
+      SLM_CUDA(cudaStreamSynchronize(c->stream));
+      e += 1;
+      SLM_CUDA(cudaMemcpyAsync(se->epoch, &e, sizeof(e), cudaMemcpyHostToDevice, c->stream));
       SLM_CUDA(cudaStreamSynchronize(c->stream));
     }
     std::string why;
     if (h & 1) why += " token id out of range;";
     if (h & 8) why += " a bounded wait in the decode kernel expired (state of this step is undefined);";
+    if (h & 16)
+      why += " a residual value in the decode kernel was non-finite or beyond 2^22 in magnitude (state of this step "
+             "is undefined);";
     fail(SLM_ERR_DEVICE, "device reported:" + why);
   }
 }
