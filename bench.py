@@ -77,6 +77,14 @@ def prompt_for(rank: int, vocab: int, n: int) -> np.ndarray:
     return np.random.default_rng(rank).integers(0, vocab, n).astype(np.uint32)
 
 
+def c5_partition(n_seq: int, rank: int, world: int) -> list[int]:
+    """configs[4]'s sequences of rank r: q = r, r + world, r + 2·world, … (round robin,
+    each sequence on exactly one rank; no collective on the data path)."""
+    if not 0 <= rank < world:
+        raise ValueError(f"rank {rank} outside a world of {world}")
+    return list(range(rank, n_seq, world))
+
+
 def max_over_ranks(values, dist=None, device=None):
     """Element-wise max of per-rank timings (the slowest rank sets the job's time)."""
     if dist is None or not dist.is_initialized() or dist.get_world_size() == 1:
@@ -597,7 +605,7 @@ def run_b200(args, rank: int, world: int, local: int) -> dict | None:
         # 0..63) partitioned over the ranks, each rank's share decoded as one
         # batch (weights read once per step), 256 greedy steps; the total is
         # fixed, so this part scales strongly.
-        mine = [q for q in range(64) if q % world == rank]
+        mine = c5_partition(64, rank, world)
         sessions = []
         firsts = []
         for q in mine:

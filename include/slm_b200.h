@@ -318,6 +318,18 @@ int slm_batch_logits(slm_batch* b, float* out);
  * with temperature 0).  out[t·n + i] (host) receives session i's id of step t.
  * Synchronises once at the end. */
 int slm_batch_decode(slm_batch* b, const uint32_t* first, size_t steps, uint32_t* out);
+/* `steps` decode steps of every session with per-row sampling, pick
+ * (src/sample.rs:33-93) on the device for each row, as a server that samples
+ * each request with its own settings would: row i uses s[i], the history
+ * recent[i] (n_recent[i] ids, host; null when n_recent is null or 0) for its
+ * repeat penalty, to which its sampled ids are appended, and the xorshift64*
+ * state rng_state[i] (read and advanced).  Feeds first[i] to session i, then
+ * each sampled id; out[t·n + i] (host) receives row i's id of step t.
+ * Candidates after top-k keep slm_sample's canonical order.  Synchronises
+ * once at the end. */
+int slm_batch_sample_decode(slm_batch* b, const uint32_t* first, size_t steps, const slm_sampling* s,
+                            const uint32_t* const* recent, const size_t* n_recent, uint64_t* rng_state,
+                            uint32_t* out);
 
 #ifdef __cplusplus
 }

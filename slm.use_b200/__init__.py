@@ -133,6 +133,8 @@ _SIGS = {
     "slm_batch_step": (_c.c_int, [_vp, _u32p]),
     "slm_batch_logits": (_c.c_int, [_vp, _f32p]),
     "slm_batch_decode": (_c.c_int, [_vp, _u32p, _sz, _u32p]),
+    "slm_batch_sample_decode": (_c.c_int, [_vp, _u32p, _sz, _c.POINTER(_Sampling), _c.POINTER(_u32p),
+                                           _c.POINTER(_sz), _u64p, _u32p]),
 }
 
 
@@ -651,6 +653,27 @@ class Batch:
         """[n][vocab] logits of the last step."""
         out = np.empty((self.n, self.vocab), dtype=np.float32)
         _check(lib().slm_batch_logits(self._h, out.ctypes.data_as(_f32p)))
+        return out
+
+    def sample_decode(self, first, steps: int, samplings, recents=None, rng_states=None) -> np.ndarray:
+        """`steps` steps of every session with per-row sampling: row i uses samplings[i], the
+        history recents[i] (sampled ids join it) and the xorshift64* state rng_states[i] (a list,
+        updated in place).  Returns [steps][n] sampled ids."""
+        first = _u32(first)
+        n = self.n
+        if first.size != n or len(samplings) != n:
+            raise ValueError(f"expected {n} ids and samplings")
+        sc = (_Sampling * n)(*[sp._c() for sp in samplings])
+        recents = recents if recents is not None else [[] for _ in range(n)]
+        arrs = [_u32(r if len(r) else [0]) for r in recents]
+        ptrs = (_u32p * n)(*[a.ctypes.data_as(_u32p) for a in arrs])
+        counts = (_sz * n)(*[len(r) for r in recents])
+        st = np.array(rng_states if rng_states is not None else [rng_seed(0)] * n, dtype=np.uint64)
+        out = np.empty((steps, n), dtype=np.uint32)
+        _check(lib().slm_batch_sample_decode(self._h, first.ctypes.data_as(_u32p), steps, sc, ptrs, counts,
+                                             st.ctypes.data_as(_u64p), out.ctypes.data_as(_u32p)))
+        if rng_states is not None:
+            rng_states[:] = [int(v) for v in st]
         return out
 
     def decode(self, first, steps: int) -> np.ndarray:

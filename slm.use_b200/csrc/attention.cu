@@ -48,6 +48,63 @@ __device__ __forceinline__ void merge(float& m, float& l, float* acc, float om, 
   m = M;
 }
 
+// Merge of the nsplit slices of (query i, head h) into y, by the NT threads
+// of a CTA: M = max_s m_s, c_s = e^{m_s − M}, L = Σ c_s l_s, then thread
+// (q, e) sums c_s·acc_s[e] over splits q, q + Q, … and the Q sums are added in
+// order.  cw holds up to 256 split weights; acc_sh is [4][dh + 4].
+template <int NT>
+__device__ void combine_pair(const float* __restrict__ part, int nsplit, int m, int heads, int dh, int i, int h,
+                             float* __restrict__ y, int ldy, float* red, float* cw, float* acc_sh) {
+  constexpr int NW = NT / 32;
+  const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+  const size_t stride = (size_t)m * heads * (dh + 2);
+  const float* p0 = part + ((size_t)i * heads + h) * (dh + 2);
+  float mx = -INFINITY;
+  for (int s = t; s < nsplit; s += NT) mx = fmaxf(mx, __ldcg(p0 + s * stride + dh));
+  mx = warp_max(mx);
+  if (lane == 0) red[warp] = mx;
+  __syncthreads();
+  float M = red[0];
+  for (int w = 1; w < NW; w++) M = fmaxf(M, red[w]);
+  __syncthreads();
+  float lsum = 0.0f;
+  for (int s = t; s < nsplit; s += NT) {
+    const float ms = __ldcg(p0 + s * stride + dh);
+    const float c = (M == -INFINITY || ms == -INFINITY) ? 0.0f : expf(ms - M);
+    if (s < 256) cw[s] = c;
+    lsum += __ldcg(p0 + s * stride + dh + 1) * c;
+  }
+  lsum = warp_sum(lsum);
+  if (lane == 0) red[warp] = lsum;
+  __syncthreads();
+  float L = 0.0f;
+  for (int w = 0; w < NW; w++) L += red[w];
+  const int Q = NT / dh >= 1 ? (NT / dh > 4 ? 4 : NT / dh) : 1;
+  const int q = t / dh, e = t % dh;
+  float a = 0.0f;
+  if (q < Q && dh <= NT)
+    for (int s = q; s < nsplit; s += Q) {
+      const float ms = __ldcg(p0 + s * stride + dh);
+      const float c = s < 256 ? cw[s] : ((M == -INFINITY || ms == -INFINITY) ? 0.0f : expf(ms - M));
+      a = fmaf(__ldcg(p0 + s * stride + e), c, a);
+    }
+  if (q < Q && dh <= NT) acc_sh[q * (dh + 4) + e] = a;
+  __syncthreads();
+  for (int d = t; d < dh; d += NT) {
+    float v = 0.0f;
+    if (dh <= NT) {
+      for (int qq = 0; qq < Q; qq++) v += acc_sh[qq * (dh + 4) + d];
+    } else {  // heads wider than the CTA: one thread per dimension, splits in order
+      for (int s = 0; s < nsplit; s++) {
+        const float ms = __ldcg(p0 + s * stride + dh);
+        const float c = s < 256 ? cw[s] : ((M == -INFINITY || ms == -INFINITY) ? 0.0f : expf(ms - M));
+        v = fmaf(__ldcg(p0 + s * stride + d), c, v);
+      }
+    }
+    y[(size_t)i * ldy + (size_t)h * dh + d] = L > 0.0f ? v / L : 0.0f;
+  }
+}
+
 // ---------------------------------------------------------------------------
 // Slice pass for a few queries.  grid (nsplit, heads, m), 128 threads.
 // ---------------------------------------------------------------------------
@@ -58,7 +115,7 @@ template <int DH>
 __global__ void __launch_bounds__(128)
     k_attn_split(const float* __restrict__ q, int ldq, const float* __restrict__ K, const float* __restrict__ V,
                  AttnGeom g, const long long* __restrict__ pos_ptr, int nsplit, float* __restrict__ part,
-                 AttnRows rows) {
+                 AttnRows rows, unsigned* __restrict__ cnt, float* __restrict__ y, int ldy) {
   constexpr int G = DH / 8;        // lanes per cache row
   constexpr int PPW = 32 / G;      // rows per warp step
   constexpr int WARPS = 4;
@@ -175,6 +232,22 @@ __global__ void __launch_bounds__(128)
       out[DH + 1] = l0;
     }
   }
+  if (!cnt) return;  // a separate combine launch merges the slices
+  // The last slice of (i, h) to finish merges them all and puts its counter
+  // back to zero for the next launch.
+  __shared__ int last;
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    unsigned* c = cnt + (size_t)i * g.heads + h;
+    last = atomicAdd(c, 1u) == (unsigned)nsplit - 1;
+    if (last) *c = 0;
+  }
+  __syncthreads();
+  if (!last) return;
+  __threadfence();
+  __shared__ float red[WARPS], cw[256], acc_sh[4 * (DH + 4)];
+  combine_pair<128>(part, nsplit, g.m, g.heads, DH, i, h, y, ldy, red, cw, acc_sh);
 }
 
 // ---------------------------------------------------------------------------
@@ -557,16 +630,18 @@ void launch_tile(const float* q, int ldq, const float* K, const float* V, const 
   }
 }
 
+// True when the slice pass merged the slices itself (a fused merge needs counters).
 template <int DH>
-void launch_dh(const float* q, int ldq, const float* K, const float* V, const AttnGeom& g, const long long* pos_ptr,
-               int nsplit, float* part, cudaStream_t st) {
+bool launch_dh(const float* q, int ldq, const float* K, const float* V, const AttnGeom& g, const long long* pos_ptr,
+               int nsplit, float* part, unsigned* cnt, float* y, int ldy, cudaStream_t st) {
   if (g.m <= 8 || DH > 128) {
     k_attn_split<DH><<<dim3(nsplit, g.heads, g.m), 128, 0, st>>>(q, ldq, K, V, g, pos_ptr, nsplit, part,
-                                                                 AttnRows{});
+                                                                 AttnRows{}, cnt, y, ldy);
     SLM_LAUNCHED("k_attn_split");
-  } else {
-    launch_tile<DH>(q, ldq, K, V, g, pos_ptr, nsplit, part, st);
+    return cnt != nullptr;
   }
+  launch_tile<DH>(q, ldq, K, V, g, pos_ptr, nsplit, part, st);
+  return false;
 }
 
 }  // namespace
@@ -590,37 +665,43 @@ int attn_splits(const AttnGeom& g, long long max_span) {
 size_t attn_part_floats(const AttnGeom& g, int nsplit) { return (size_t)nsplit * g.m * g.heads * (g.dh + 2); }
 
 void attention(const float* q, int ldq, const float* K, const float* V, const AttnGeom& g, const long long* pos_ptr,
-               int nsplit, float* part, float* y, int ldy, cudaStream_t st) {
+               int nsplit, float* part, float* y, int ldy, cudaStream_t st, unsigned* cnt) {
   if (g.m == 0) return;
   SLM_REQUIRE(g.key_heads > 0 && g.heads % g.key_heads == 0, "attend: heads must be a multiple of key_heads");
+  bool merged = false;
   switch (g.dh) {
-    case 8: launch_dh<8>(q, ldq, K, V, g, pos_ptr, nsplit, part, st); break;
-    case 16: launch_dh<16>(q, ldq, K, V, g, pos_ptr, nsplit, part, st); break;
-    case 32: launch_dh<32>(q, ldq, K, V, g, pos_ptr, nsplit, part, st); break;
-    case 64: launch_dh<64>(q, ldq, K, V, g, pos_ptr, nsplit, part, st); break;
-    case 128: launch_dh<128>(q, ldq, K, V, g, pos_ptr, nsplit, part, st); break;
-    case 256: launch_dh<256>(q, ldq, K, V, g, pos_ptr, nsplit, part, st); break;
+    case 8: merged = launch_dh<8>(q, ldq, K, V, g, pos_ptr, nsplit, part, cnt, y, ldy, st); break;
+    case 16: merged = launch_dh<16>(q, ldq, K, V, g, pos_ptr, nsplit, part, cnt, y, ldy, st); break;
+    case 32: merged = launch_dh<32>(q, ldq, K, V, g, pos_ptr, nsplit, part, cnt, y, ldy, st); break;
+    case 64: merged = launch_dh<64>(q, ldq, K, V, g, pos_ptr, nsplit, part, cnt, y, ldy, st); break;
+    case 128: merged = launch_dh<128>(q, ldq, K, V, g, pos_ptr, nsplit, part, cnt, y, ldy, st); break;
+    case 256: merged = launch_dh<256>(q, ldq, K, V, g, pos_ptr, nsplit, part, cnt, y, ldy, st); break;
     default: fail(SLM_ERR_INVALID, "attend: head size must be one of 8, 16, 32, 64, 128, 256");
   }
+  if (merged) return;
   k_attn_combine<<<g.m * g.heads, 256, 0, st>>>(part, nsplit, g.m, g.heads, g.dh, y, ldy);
   SLM_LAUNCHED("k_attn_combine");
 }
 
 void attention_rows(const float* q, int ldq, const AttnRows& rows, const AttnGeom& g, int nsplit, float* part,
-                    float* y, int ldy, cudaStream_t st) {
+                    float* y, int ldy, cudaStream_t st, unsigned* cnt) {
   if (g.m == 0) return;
   SLM_REQUIRE(g.key_heads > 0 && g.heads % g.key_heads == 0, "attend: heads must be a multiple of key_heads");
   const dim3 grid(nsplit, g.heads, g.m);
+#define SLM_ROWS(DHV) \
+  k_attn_split<DHV><<<grid, 128, 0, st>>>(q, ldq, nullptr, nullptr, g, nullptr, nsplit, part, rows, cnt, y, ldy)
   switch (g.dh) {
-    case 8: k_attn_split<8><<<grid, 128, 0, st>>>(q, ldq, nullptr, nullptr, g, nullptr, nsplit, part, rows); break;
-    case 16: k_attn_split<16><<<grid, 128, 0, st>>>(q, ldq, nullptr, nullptr, g, nullptr, nsplit, part, rows); break;
-    case 32: k_attn_split<32><<<grid, 128, 0, st>>>(q, ldq, nullptr, nullptr, g, nullptr, nsplit, part, rows); break;
-    case 64: k_attn_split<64><<<grid, 128, 0, st>>>(q, ldq, nullptr, nullptr, g, nullptr, nsplit, part, rows); break;
-    case 128: k_attn_split<128><<<grid, 128, 0, st>>>(q, ldq, nullptr, nullptr, g, nullptr, nsplit, part, rows); break;
-    case 256: k_attn_split<256><<<grid, 128, 0, st>>>(q, ldq, nullptr, nullptr, g, nullptr, nsplit, part, rows); break;
+    case 8: SLM_ROWS(8); break;
+    case 16: SLM_ROWS(16); break;
+    case 32: SLM_ROWS(32); break;
+    case 64: SLM_ROWS(64); break;
+    case 128: SLM_ROWS(128); break;
+    case 256: SLM_ROWS(256); break;
     default: fail(SLM_ERR_INVALID, "attend: head size must be one of 8, 16, 32, 64, 128, 256");
   }
+#undef SLM_ROWS
   SLM_LAUNCHED("k_attn_split");
+  if (cnt) return;
   k_attn_combine<<<g.m * g.heads, 256, 0, st>>>(part, nsplit, g.m, g.heads, g.dh, y, ldy);
   SLM_LAUNCHED("k_attn_combine");
 }

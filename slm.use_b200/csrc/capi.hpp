@@ -23,6 +23,8 @@ struct slm_ctx {
   void* gemm_ws = nullptr;      // tensor-core GEMM workspace (grown on demand, outside captures)
   size_t gemm_ws_bytes = 0;
   unsigned long long gemm_ws_gen = 0;  // bumped whenever gemm_ws moves (graphs holding it must be re-captured)
+  unsigned* merge_cnt = nullptr;  // attention slice counters of slm_op_attend (zero between launches)
+  size_t merge_cnt_len = 0;
 };
 
 struct slm_buf {

@@ -84,6 +84,14 @@ __device__ __forceinline__ float lds1(uint32_t a) {
   asm volatile("ld.shared.f32 %0, [%1];" : "=f"(v) : "r"(a));
   return v;
 }
+__device__ __forceinline__ void st_release_cta_shared(unsigned* p, unsigned v) {
+  asm volatile("st.release.cta.shared.u32 [%0], %1;" ::"r"(saddr(p)), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned ld_acquire_cta_shared(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.cta.shared.u32 %0, [%1];" : "=r"(v) : "r"(saddr(p)) : "memory");
+  return v;
+}
 __device__ __forceinline__ void red_release_add_u64(unsigned long long* p, unsigned long long v) {
   asm volatile("red.release.gpu.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
@@ -335,6 +343,8 @@ struct Tile {
   unsigned off[4];
   unsigned total;
   int keep;  // weights read again within the step
+  int step;  // step of the launch the tile belongs to
+  int mut;   // cache or state written by earlier steps (not weights)
 };
 
 // Resumable walk over this CTA's tiles, phase by phase (the order in which
@@ -346,6 +356,7 @@ struct Walker {
   int p = 0, i = -1, seg = 0;
   long long t = 0, tend = 0;
   int extra = 0;  // ATTN with o: the o tile follows the item's K/V tiles
+  int step = 0;   // step of the launch
 
   __device__ Walker(const Plan* pl, long long ps) : P(pl), pos(ps) {
     me = blockIdx.x;
@@ -366,7 +377,11 @@ struct Walker {
   }
 
   __device__ bool next(Tile& T) {
-    while (p < P->nphases) {
+    for (;;) {
+      if (p >= P->nphases) {  // the next step of the launch, one position on
+        if (step + 1 >= P->nsteps) return false;
+        step++, pos++, p = 0, i = -1;
+      }
       const Phase& ph = P->phases[p];
       if (i < 0) {
         i = me;
@@ -384,6 +399,7 @@ struct Walker {
         const int h = i / ph.splits, s = i % ph.splits;
         T.n = 1;
         T.keep = ph.l2keep;
+        T.step = step, T.mut = 0;
         T.src[0] = ph.wo + ((size_t)h * P->d + (size_t)s * ph.orows) * kDH;
         T.bytes[0] = T.total = (unsigned)ph.orows * kDH * 4;
         T.off[0] = 0;
@@ -397,12 +413,12 @@ struct Walker {
       }
       start_item(ph);
     }
-    return false;
   }
 
   __device__ void make(const Phase& ph, Tile& T) {
     T.n = 0;
     T.keep = ph.kind == PH_GEMV ? ph.l2keep : 0;  // K/V and GLA state tiles stream
+    T.step = step, T.mut = ph.kind != PH_GEMV;
     if (ph.kind == PH_GEMV) {
       const Segment& sg = ph.seg[seg];
       const int Tn = tile_outs(ph);
@@ -456,6 +472,8 @@ struct Smem {
   float inv_freq[kDH / 2];
   unsigned long long best;
   int flag;
+  uint32_t cur_id;   // the token of the running step (steps after the first: the previous arg-max)
+  unsigned step_ok;  // steps whose start the consumers have seen (the producer may read caches after it)
 };
 
 // ---------------------------------------------------------------------------
@@ -478,9 +496,32 @@ __device__ void producer(const Plan& P, Smem& sm, char* ring, long long pos) {
   for (int j = 0; j < kStages; j++)
     if (!ahead.next(A)) break;
   unsigned k = 0;
+  const unsigned inflight = P.inflight >= 1 && P.inflight < kStages ? (unsigned)P.inflight : (unsigned)kStages;
+  int ready = 0;  // the last step whose caches and states this thread may read
   while (ring_w.next(T)) {
+    if (T.mut && T.step > ready) {
+      // K/V and GLA state of step s were written by step s - 1: wait until
+      // the consumers have seen that step end (their acquire of its arg-max),
+      // then order those writes before this thread's bulk copies.
+      Spin sp;
+      bool good = true;
+      while ((int)ld_acquire_cta_shared(&sm.step_ok) < T.step)
+        if (!sp.again(P.err)) {
+          good = false;
+          break;
+        }
+      if (!good) break;
+      ready = T.step;
+      asm volatile("fence.proxy.async.global;" ::: "memory");
+    }
     const int s = k % kStages;
     if (k >= (unsigned)kStages && !wait_mbar(&sm.empty[s], ((k / kStages) - 1) & 1, P.err)) break;
+    // Tile k - inflight must have landed first: fewer bytes queued in the
+    // memory system keep its round trips (the CTAs' exchanges) short.
+    if (inflight < (unsigned)kStages && k >= inflight) {
+      const unsigned j = k - inflight;
+      if (!wait_mbar(&sm.full[j % kStages], (j / kStages) & 1, P.err)) break;
+    }
     mbar_expect_tx(&sm.full[s], T.total);
     char* dst = ring + (size_t)s * kStageBytes;
     if (P.l2mode) {
@@ -549,6 +590,7 @@ struct Cons {
   __device__ __forceinline__ void fx_wait_arrivals(const Phase& ph) {
     if (!ph.fx_in || !ph.fx_arrive) return;
     if (tid == 0) {
+      const unsigned long long ta = P.trace ? now_ns() : 0;
       const unsigned long long* a = fxp(ph.fx_in) + P.d;
       const unsigned long long want = (unsigned long long)ph.fx_arrive + (P.test_stall ? 1u : 0u);
       Spin sp;
@@ -557,6 +599,7 @@ struct Cons {
           ok = false;
           break;
         }
+      if (ta) xwait += now_ns() - ta;
     }
     all_ok();
   }
@@ -567,19 +610,18 @@ struct Cons {
     return v[0];
   }
 
-  // Starts copying phase q's descriptor into sm.ph[q & 1]; it lands by the
+  // Starts copying phase q's descriptor into sm.ph[slot]; it lands by the
   // next consumers barrier after stage_wait().  Reading descriptors from
-  // shared memory keeps them off the post-barrier critical path (a gpu-scope
-  // acquire leaves L1 cold).
-  __device__ void stage_phase(int q) {
+  // shared memory keeps them off the critical path of the phase start.
+  __device__ void stage_phase(int slot, int q) {
     constexpr int chunks = sizeof(Phase) / 16;
     if (q < P.nphases && tid < chunks)
-      cp_async16(reinterpret_cast<char*>(&sm.ph[q & 1]) + tid * 16,
+      cp_async16(reinterpret_cast<char*>(&sm.ph[slot]) + tid * 16,
                  reinterpret_cast<const char*>(P.phases + q) + tid * 16);
   }
   __device__ void stage_wait() { cp_async_wait_all(); }
 
-  unsigned long long waited = 0, pro_ns = 0, comp_ns = 0, epi_ns = 0, ntiles = 0;  // for the timeline
+  unsigned long long waited = 0, pro_ns = 0, comp_ns = 0, epi_ns = 0, ntiles = 0, xwait = 0;  // for the timeline
 
   __device__ const float* take() {
     int s = k % kStages;
@@ -687,7 +729,7 @@ struct Cons {
         w = __ldg(reinterpret_cast<const float4*>(ph.norm_w) + tid);
         x = in4(ph, tid);
         if (ph.in_c) {  // e0: this step's embedding row, read from the weights
-          const uint32_t id = P.host_id >= 0 ? (uint32_t)P.host_id : P.ids[0];
+          const uint32_t id = sm.cur_id;
           we = __ldg(reinterpret_cast<const float4*>(ph.in_c) + tid);
           e = __ldg(reinterpret_cast<const float4*>(P.embed + (size_t)id * ph.cols) + tid);
         }
@@ -730,7 +772,7 @@ struct Cons {
     if (own) {
       w = __ldg(reinterpret_cast<const float4*>(ph.norm_w) + tid);
       if (ph.in_mode == IN_EMBED_RMS) {
-        const uint32_t id = P.host_id >= 0 ? (uint32_t)P.host_id : P.ids[0];
+        const uint32_t id = sm.cur_id;
         x = __ldg(reinterpret_cast<const float4*>(P.embed + (size_t)id * ph.cols) + tid);
         if (blockIdx.x == 0) {
           reinterpret_cast<float4*>(P.e0)[tid] = x;
@@ -1282,13 +1324,16 @@ struct Cons {
         if (P.argmax2) *P.argmax2 = id;
         if (P.greedy) {
           P.next_id[0] = id;
-          unsigned at = *P.out_index;
+          const unsigned at = atomicAdd(P.out_index, 1u);
           if (P.out_ids) P.out_ids[at] = id;
           if (P.hist) P.hist[P.hist_base + at] = id;
-          *P.out_index = at + 1;
         }
         *P.arg_count = 0;
         P.pos[0] = pos + 1;  // every CTA read the position at entry
+        if (P.nsteps > 1) {  // the next step's token, once the count above is reset
+          __threadfence();
+          st_relaxed_u64(P.next_tagged, ((unsigned long long)tag_of(cur) << 32) | id);
+        }
         sm.flag = 0;
       }
       consumers_sync();
@@ -1307,6 +1352,7 @@ struct Cons {
     const int d0 = sub * 4, d1 = 32 + sub * 4;
     float qv[QG][8], mx[QG], l[QG], acc[QG][8];
     const unsigned tg_in = tag_of(ph.tag_in);  // q (and k, v) of the projection phase
+    const unsigned long long tq0 = P.trace && tid == 0 ? now_ns() : 0;
 #pragma unroll
     for (int g = 0; g < QG; g++) {
       const unsigned long long* qp = ph.tq + (c * QG + g) * kDH;
@@ -1322,6 +1368,7 @@ struct Cons {
     long long a, b;
     attn_slice<GL>(ph, pos, s, &a, &b);
     unsigned long long c0 = P.trace && tid == 0 ? now_ns() : 0;
+    if (tq0) pro_ns += c0 - tq0;
     for (long long t0 = a; t0 < b; t0 += kAttnTile) {
       const int n = (int)min((long long)kAttnTile, b - t0);
       const float* tile = take_warp();
@@ -1469,6 +1516,7 @@ struct Cons {
   __device__ __forceinline__ void mixer_o_tail(const Phase& ph, int h, int s, bool gla) {
     constexpr int RQ = kMaxItemOut / 64;  // rows per thread: r = tid / 4 + 64·k
     const int R = ph.orows, q4 = tid & 3;
+    const unsigned long long to0 = P.trace && tid == 0 ? now_ns() : 0;
     float res[RQ];  // the block's input x, which this CTA's own prologue left in sm.xraw
 #pragma unroll
     for (int k = 0; k < RQ; k++) {
@@ -1486,6 +1534,7 @@ struct Cons {
       constexpr int NV = (kMaxSplits * (kDH + 2) + 255) / 256;
       const int nv = ph.splits * (kDH + 2);
       Spin sp;
+      const unsigned long long tw0 = to0 ? now_ns() : 0;
       for (;;) {
         unsigned long long wv[NV];
 #pragma unroll
@@ -1505,6 +1554,7 @@ struct Cons {
           break;
         }
       }
+      if (tw0) xwait += now_ns() - tw0;
       all_ok();
       if (ok && tid < ph.splits) {
         float M = -INFINITY;
@@ -1549,6 +1599,7 @@ struct Cons {
     release();
     if (bad) atomicOr(P.err, 16);
     all_ok();  // sm.cmb and sm.vec are free; ok uniform
+    if (to0) epi_ns += now_ns() - to0;
   }
 
   __device__ void attn_item(const Phase& ph, int item) {
@@ -1656,66 +1707,101 @@ struct Cons {
       unsigned long long* t = P.trace + ((size_t)p * gridDim.x + blockIdx.x) * 8;
       t[which] = now_ns();
       if (which == 1) {
-        t[2] = waited, t[3] = pro_ns, t[4] = comp_ns, t[5] = epi_ns, t[6] = ntiles, t[7] = 0;
-        waited = pro_ns = comp_ns = epi_ns = ntiles = 0;
+        t[2] = waited, t[3] = pro_ns, t[4] = comp_ns, t[5] = epi_ns, t[6] = ntiles, t[7] = xwait;
+        waited = pro_ns = comp_ns = epi_ns = ntiles = xwait = 0;
+      }
+    }
+  }
+
+  // Zeroes the fixed-point set the next step adds into.  Its last readers
+  // were in the previous step; the caller guarantees every CTA is past them.
+  __device__ void zero_next_set() {
+    unsigned long long* nx = P.fx + ((ep + 1) & 1) * P.fx_stride;
+    for (int e = blockIdx.x * 256 + tid; e < P.fx_words; e += gridDim.x * 256) nx[e] = 0;
+  }
+
+  __device__ void run_phase(const Phase& ph) {
+    if (ph.kind == PH_GEMV) {
+      gemv_phase(ph);
+    } else if (ph.kind == PH_ATTN) {
+      for (int i = blockIdx.x; i < ph.items && ok; i += gridDim.x) attn_item(ph, i);
+      // S blocks with o: one item per CTA (items ≤ grid), QG = 1 (the cache head is the head).
+      if (ph.wo && blockIdx.x < ph.items && ok) attn_o_tail(ph, blockIdx.x / ph.splits, blockIdx.x % ph.splits);
+    } else {
+      if (!ph.wo) {
+        for (int i = blockIdx.x; i < ph.items && ok; i += gridDim.x) gla_item(ph, i);
+      } else if (blockIdx.x < ph.items) {  // L blocks with o: items are heads × splits, one per CTA
+        const int h = blockIdx.x / ph.splits, s = blockIdx.x % ph.splits;
+        gla_item(ph, h, s);
+        if (ok) mixer_o_tail(ph, h, s, true);
       }
     }
   }
 
   __device__ void run() {
     if (tid < kDH / 2 && P.inv_freq) sm.inv_freq[tid] = __ldg(P.inv_freq + tid);
-    // This step adds into the fixed-point set of its parity; the other set,
-    // last read by the previous step (ended with its launch), is zeroed here
-    // for the next step.
-    unsigned long long* nx = P.fx + ((ep + 1) & 1) * P.fx_stride;
-    for (int e = blockIdx.x * 256 + tid; e < P.fx_words; e += gridDim.x * 256) nx[e] = 0;
-    stage_phase(0);
+    if (tid == 0) sm.cur_id = P.host_id >= 0 ? (uint32_t)P.host_id : P.ids[0];
+    const int np = P.nphases;
+    stage_phase(0, 0);
     stage_wait();
     consumers_sync();
-    for (int p = 0; p < P.nphases && ok; p++) {
-      if (p > 0) {
-        stamp(p - 1, 1);
-        stage_wait();  // phase p's descriptor, requested one phase ago
-        if (!consumers_and(ok ? 1 : 0)) {
-          ok = false;
-          return;
+    long long g = 0;  // phases run in this launch (descriptor buffer parity)
+    for (int st = 0; st < P.nsteps && ok; st++) {
+      if (st > 0) {
+        // The previous step's arg-max is this step's token: tagged by its
+        // logits phase once every CTA had finished that step.
+        if (tid == 0) {
+          const unsigned want = tag_of(np - 1);
+          unsigned long long w = 0;
+          Spin sp;
+          while (((w = ld_relaxed_u64(P.next_tagged)) >> 32) != want)
+            if (!sp.again(P.err)) {
+              ok = false;
+              break;
+            }
+          asm volatile("fence.acq_rel.gpu;" ::: "memory");
+          sm.cur_id = (uint32_t)w;
+          st_release_cta_shared(&sm.step_ok, (unsigned)st);  // the producer may read this step's caches
         }
-        if (P.all_sync || sm.ph[p & 1].sync) {
-          grid_sync();
-          if (!ok) return;
-        }
+        if (!all_ok()) return;
+        pos++, ep++;
       }
-      cur = p;
-      stamp(p, 0);
-      stage_phase(p + 1);
-      const Phase& ph = sm.ph[p & 1];
-      if (ph.kind == PH_GEMV) {
-        gemv_phase(ph);
-      } else if (ph.kind == PH_ATTN) {
-        for (int i = blockIdx.x; i < ph.items && ok; i += gridDim.x) attn_item(ph, i);
-        // S blocks with o: one item per CTA (items ≤ grid), QG = 1 (the cache head is the head).
-        if (ph.wo && blockIdx.x < ph.items && ok) attn_o_tail(ph, blockIdx.x / ph.splits, blockIdx.x % ph.splits);
-      } else {
-        if (!ph.wo) {
-          for (int i = blockIdx.x; i < ph.items && ok; i += gridDim.x) gla_item(ph, i);
-        } else if (blockIdx.x < ph.items) {  // L blocks with o: items are heads × splits, one per CTA
-          const int h = blockIdx.x / ph.splits, s = blockIdx.x % ph.splits;
-          gla_item(ph, h, s);
-          if (ok) mixer_o_tail(ph, h, s, true);
+      // Single steps (no zero point) zero the next set at their start: the
+      // previous step ended with its launch.
+      if (P.zero_phase < 0) zero_next_set();
+      for (int p = 0; p < np && ok; p++, g++) {
+        if (g > 0) {
+          stamp(p > 0 ? p - 1 : np - 1, 1);
+          stage_wait();  // phase p's descriptor, requested one phase ago
+          if (!consumers_and(ok ? 1 : 0)) {
+            ok = false;
+            return;
+          }
+          if (P.all_sync || sm.ph[g & 1].sync) {
+            grid_sync();
+            if (!ok) return;
+          }
         }
+        // Past the zero point every CTA has finished the previous step.
+        if (p == P.zero_phase + 1) zero_next_set();
+        cur = p;
+        stamp(p, 0);
+        if (g + 1 < (long long)np * P.nsteps) stage_phase((int)((g + 1) & 1), (p + 1) % np);
+        run_phase(sm.ph[g & 1]);
       }
     }
     consumers_sync();
-    stamp(P.nphases - 1, 1);
+    stamp(np - 1, 1);
     if (tid == 0 && ok) {
-      // The last CTA to finish resets the barrier count for the next step:
-      // every CTA has passed every barrier by then.
+      // The last CTA to finish resets the barrier count for the next launch
+      // and advances the step counter: every CTA has passed every barrier and
+      // read the counter by then.
       __threadfence();
       unsigned prev = atomicAdd(P.bar + 1, 1u);
       if (prev == gridDim.x - 1) {
         atomicExch(P.bar, 0u);
         atomicExch(P.bar + 1, 0u);
-        atomicExch(P.epoch, ep + 1u);  // every CTA read the epoch at entry
+        atomicExch(P.epoch, ep + 1u);
       }
     }
   }
@@ -1733,6 +1819,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_mega(const __grid_consta
       mbar_init(&sm.empty[s], kConsumerWarps);
     }
     sm.flag = 0;
+    sm.step_ok = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   __syncthreads();

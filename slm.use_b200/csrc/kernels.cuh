@@ -63,9 +63,11 @@ struct AttnRows {
 };
 int attn_splits(const AttnGeom& g, long long max_span);
 size_t attn_part_floats(const AttnGeom& g, int nsplit);
-// y[i][h·dh + e]; part holds attn_part_floats(g, nsplit) floats.
+// y[i][h·dh + e]; part holds attn_part_floats(g, nsplit) floats.  With cnt
+// (heads·m counters, zero on entry and left zero) decode-sized calls merge
+// their slices in the same launch: the last slice of each (query, head) does.
 void attention(const float* q, int ldq, const float* K, const float* V, const AttnGeom& g, const long long* pos_ptr,
-               int nsplit, float* part, float* y, int ldy, cudaStream_t st);
+               int nsplit, float* part, float* y, int ldy, cudaStream_t st, unsigned* cnt = nullptr);
 
 struct GlaArgs {
   float* S;
@@ -83,7 +85,7 @@ void gla(const GlaArgs& a, cudaStream_t st);
 void gla_rows(const GlaArgs& a, float* const* S_rows, cudaStream_t st);
 // Attention of g.m single-token queries, each over its own cache and position.
 void attention_rows(const float* q, int ldq, const AttnRows& rows, const AttnGeom& g, int nsplit, float* part,
-                    float* y, int ldy, cudaStream_t st);
+                    float* y, int ldy, cudaStream_t st, unsigned* cnt = nullptr);
 
 struct SampleArgs {
   const float* logits;
@@ -100,6 +102,9 @@ struct SampleArgs {
   int* err;
 };
 void sample(const SampleArgs& a, cudaStream_t st);
+// Batched: row i samples with rows[i] (a device array), its history count
+// advanced by *step, its id written to outs[*step · m + i] (and next_id, hist_out).
+void sample_rows(const SampleArgs* rows, size_t m, const unsigned* step, uint32_t* outs, cudaStream_t st);
 
 // elementwise.cu
 void ew_gather(float* y, const float* w, const uint32_t* ids, size_t m, size_t d, size_t vocab, int* err,

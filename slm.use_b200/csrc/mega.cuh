@@ -182,6 +182,15 @@ struct Plan {
   // L2 priority of the bulk copies: 0 none; 1 weights of phases marked l2keep
   // evict_last, every other tile evict_first; 2 the same with the others normal.
   int l2mode;
+  // Most tiles a producer keeps in flight (issued, not landed); 1 … kStages.
+  int inflight;
+  // Steps of one launch (greedy decode): step s + 1 takes the arg-max of step
+  // s, passed between CTAs as a tagged word; 1 for a single step.
+  int nsteps;
+  unsigned long long* next_tagged;
+  // The phase after which every CTA has finished the previous step, so the
+  // fixed-point set the next step uses may be zeroed (see run()).
+  int zero_phase;
 };
 
 }  // namespace mega

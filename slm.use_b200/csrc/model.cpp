@@ -127,6 +127,7 @@ struct slm_session {
   bool keys_stale = false;               // state was written from the host: the next shifted keys need recomputing
   int in_batches = 0;                    // batches holding this session
   uint32_t* argmax_dev = nullptr;        // the persistent step's arg-max of its logits
+  unsigned* merge_cnt = nullptr;         // attention slice counters of the graph path (zero between launches)
   bool argmax_valid = false;             // the logits come from a persistent step
   // Pinned host words for the per-token transfers (ids in and out, RNG state).
   struct HostIO {
@@ -150,6 +151,7 @@ struct slm_batch {
         *kb = nullptr, *y = nullptr, *mid = nullptr, *dec = nullptr, *part = nullptr, *logits = nullptr,
         *upbuf = nullptr;
   uint32_t* ids = nullptr;           // [n] this step's tokens (the arg-max writes the next ones)
+  unsigned* merge_cnt = nullptr;     // [heads·n] attention slice counters (zero between launches)
   long long** posr = nullptr;        // [n] the sessions' device positions
   std::vector<float**> tab;          // per layer instance, in step order: [3][n] k, v, s pointers
   unsigned* out_index = nullptr;     // steps taken since the last reset
@@ -159,6 +161,15 @@ struct slm_batch {
   cudaGraphExec_t graph = nullptr;
   unsigned long long graph_ws_gen = 0;  // the context's GEMM workspace generation the graph holds
   bool capturing = false;
+  // Per-row sampling (slm_batch_sample_decode): the step ends with one
+  // sampler CTA per row instead of the greedy arg-max; its own graph.
+  cudaGraphExec_t graph_s = nullptr;
+  unsigned long long graph_s_ws_gen = 0;
+  SampleArgs* srows = nullptr;          // [n] device: each row's settings, history and state
+  float* swork = nullptr;               // [n][3·vocab] sampler work space
+  uint32_t* shist = nullptr;            // [n][shist_cap] histories (penalty windows), sampled ids appended
+  size_t shist_cap = 0;
+  unsigned long long* srng = nullptr;   // [n] xorshift64* states
 };
 
 namespace slm {
@@ -359,7 +370,7 @@ void block(slm_session* se, const Block& b, LState& st, float* x, size_t m) {
     ew_rope_store(se->mix, 3 * d, md->inv_freq, se->pos_dev, m, heads, dh, st.cap, se->q, st.k, st.v, s);
     AttnGeom g{im, (long long)c.window, 0, (long long)st.cap, (int)heads, (int)heads, (int)dh, scale};
     int ns = attn_splits(g, (long long)(c.window + m - 1));
-    attention(se->q, id, st.k, st.v, g, se->pos_dev, ns, se->part, se->y, id, s);
+    attention(se->q, id, st.k, st.v, g, se->pos_dev, ns, se->part, se->y, id, s, se->merge_cnt);
   } else if (b.kind == 'L') {
     run_linear(s, b.qkvg, se->n, id, im, se->mix, (int)(4 * d), EPI_STORE, nullptr, 0, 0, np);
     run_linear(s, b.decay, se->n, id, im, se->dec, (int)heads, EPI_STORE);
@@ -405,7 +416,7 @@ void block(slm_session* se, const Block& b, LState& st, float* x, size_t m) {
       AttnGeom g{im, 0, (long long)far, (long long)st.cap, (int)heads, (int)kh, (int)dh, scale};
       long long span = (long long)(se->capturing ? st.cap : se->pos + m);
       int ns = attn_splits(g, span);
-      attention(se->q, id, st.k, st.v, g, se->pos_dev, ns, se->part, se->y, id, s);
+      attention(se->q, id, st.k, st.v, g, se->pos_dev, ns, se->part, se->y, id, s, se->merge_cnt);
     } else {
       has_h = false;
     }
@@ -841,6 +852,24 @@ void build_plan(slm_session* se, bool refresh = false) {
   P.all_sync = !se->fuse_mlp || !fuse_ao ? 1 : 0;
   P.mlp_cta = d > kMaxCols / 4 || mlp_cta_setting() ? 1 : 0;
   P.l2mode = l2mode_setting();
+  {
+    const char* e = std::getenv("SLM_MEGA_INFLIGHT");
+    P.inflight = e && *e ? std::atoi(e) : kStages;
+  }
+  P.nsteps = 1;
+  P.next_tagged = static_cast<unsigned long long*>(alloc_zero(se, 4 * sizeof(unsigned long long)));
+  // Zero point: the first phase whose input every CTA reads from an MLP's
+  // fixed-point slot (every CTA adds into it, so by then every CTA has
+  // finished the previous step).  Without one, steps run one per launch.
+  P.zero_phase = -1;
+  for (size_t i = 0; i + 1 < ph.size(); i++) {
+    const Phase& q = ph[i];
+    const bool everyone = q.kind == PH_GEMV && q.in_mode != IN_PLAIN && q.in_mode != IN_ATTN;
+    if (everyone && q.fx_in && q.fx_cnt == G) {
+      P.zero_phase = (int)i;
+      break;
+    }
+  }
   P.next_id = se->ids_dev;
   P.err = se->ctx->err;
 }
@@ -891,6 +920,34 @@ void mega_step(slm_session* se, long long host_id = -1) {
     mega::launch(se->plan_host, se->grid, se->ctx->stream);
   }
   se->pos += 1;
+  se->argmax_valid = true;
+  se->ctx->argmax_owner = se;
+}
+
+// n greedy persistent steps for the id in ids_dev[0], as few launches as the
+// plan allows: one launch runs the steps back to back (each step's arg-max is
+// the next one's token), so later steps pay neither a launch nor a cold
+// start.  Global caches grow first to hold all n positions.
+// SLM_MEGA_STEPS=1 runs one step per launch (for comparison).
+size_t mega_steps_per_launch() {
+  const char* e = std::getenv("SLM_MEGA_STEPS");
+  const long v = e && *e ? std::atol(e) : 4096;
+  return v < 1 ? 1 : (size_t)v;
+}
+
+void mega_steps(slm_session* se, size_t n) {
+  const size_t most = mega_steps_per_launch();
+  while (n > 0) {
+    const size_t m = se->plan_host.zero_phase >= 0 ? std::min(n, most) : 1;
+    ensure_caps(se, m);
+    if (se->plan_stale) build_plan(se, true);
+    if (se->keys_stale) refresh_next_keys(se);
+    mega::Plan p = se->plan_host;
+    p.nsteps = (int)m;
+    mega::launch(p, se->grid, se->ctx->stream);
+    se->pos += m;
+    n -= m;
+  }
   se->argmax_valid = true;
   se->ctx->argmax_owner = se;
 }
@@ -1008,7 +1065,7 @@ void batch_block(slm_batch* bt, const Block& b, size_t li, float* x) {
     AttnGeom g{im, (long long)c.window, 0, (long long)cap, (int)heads, (int)heads, (int)dh, scale};
     AttnRows rows;
     rows.k = K, rows.v = V, rows.pos = bt->posr;
-    attention_rows(bt->q, id, rows, g, bt->nsplit, bt->part, bt->y, id, s);
+    attention_rows(bt->q, id, rows, g, bt->nsplit, bt->part, bt->y, id, s, bt->merge_cnt);
   } else {  // 'L' (global layers are refused when the batch is made)
     run_linear(s, b.qkvg, bt->nb, id, im, bt->mix, (int)(4 * d), EPI_STORE);
     run_linear(s, b.decay, bt->nb, id, im, bt->dec, (int)heads, EPI_STORE);
@@ -1039,7 +1096,7 @@ void batch_block(slm_batch* bt, const Block& b, size_t li, float* x) {
 
 // One step of every session: tokens in bt->ids; the greedy ids of the next
 // step go back to bt->ids and to outs[*out_index]; positions advance.
-void batch_advance(slm_batch* bt) {
+void batch_advance(slm_batch* bt, bool sampled) {
   g_ctx_for_linear = bt->ctx;
   g_capturing = bt->capturing;
   slm_model* md = bt->model;
@@ -1068,15 +1125,19 @@ void batch_advance(slm_batch* bt) {
   for (size_t i = 0; i < md->coda.size(); i++) batch_block(bt, md->coda[i], li++, x);
   ew_rms(bt->nb, x, md->norm_f, m, d, c.eps, nullptr, s);
   run_linear(s, md->embed, bt->nb, (int)d, (int)m, bt->logits, (int)c.vocab, EPI_STORE);  // tied head, every row
-  argmax_rows(bt->logits, c.vocab, m, bt->ids, bt->outs, bt->out_index, s);
+  if (sampled)
+    sample_rows(bt->srows, m, bt->out_index, bt->outs, s);  // next ids into bt->ids, histories extended
+  else
+    argmax_rows(bt->logits, c.vocab, m, bt->ids, bt->outs, bt->out_index, s);
   ew_advance_rows(bt->posr, m, bt->out_index, s);
 }
 
 void batch_drop_graph(slm_batch* bt) {
-  if (bt->graph) {
-    cudaGraphExecDestroy(bt->graph);
-    bt->graph = nullptr;
-  }
+  for (cudaGraphExec_t* g : {&bt->graph, &bt->graph_s})
+    if (*g) {
+      cudaGraphExecDestroy(*g);
+      *g = nullptr;
+    }
 }
 
 // Grows the context's GEMM workspace for every linear of a batch step, so
@@ -1108,17 +1169,19 @@ void batch_workspace(slm_batch* bt) {
 
 // One step, replayed from a CUDA graph captured on first use (and again
 // after the context's GEMM workspace has moved).
-void batch_step_device(slm_batch* bt) {
+void batch_step_device(slm_batch* bt, bool sampled = false) {
   cudaStream_t s = bt->ctx->stream;
-  if (bt->graph && bt->graph_ws_gen != bt->ctx->gemm_ws_gen) batch_drop_graph(bt);
-  if (!bt->graph) {
+  cudaGraphExec_t& graph = sampled ? bt->graph_s : bt->graph;
+  unsigned long long& gen = sampled ? bt->graph_s_ws_gen : bt->graph_ws_gen;
+  if (graph && gen != bt->ctx->gemm_ws_gen) batch_drop_graph(bt);
+  if (!graph) {
     batch_workspace(bt);
-    bt->graph_ws_gen = bt->ctx->gemm_ws_gen;
+    gen = bt->ctx->gemm_ws_gen;
     cudaGraph_t g = nullptr;
     SLM_CUDA(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
     bt->capturing = true;
     try {
-      batch_advance(bt);
+      batch_advance(bt, sampled);
     } catch (...) {
       bt->capturing = false;
       cudaStreamEndCapture(s, &g);
@@ -1127,11 +1190,11 @@ void batch_step_device(slm_batch* bt) {
     }
     bt->capturing = false;
     SLM_CUDA(cudaStreamEndCapture(s, &g));
-    cudaError_t e = cudaGraphInstantiate(&bt->graph, g, 0);
+    cudaError_t e = cudaGraphInstantiate(&graph, g, 0);
     cudaGraphDestroy(g);
     SLM_CUDA(e);
   }
-  SLM_CUDA(cudaGraphLaunch(bt->graph, s));
+  SLM_CUDA(cudaGraphLaunch(graph, s));
   for (auto* se : bt->ses) se->pos += 1;
 }
 
@@ -1403,6 +1466,7 @@ int slm_session_new(slm_model* md, size_t loops, slm_session** out) {
         part = std::max(part, attn_part_floats(g, attn_splits(g, 1ll << 40)));
       }
       se->part = f(part);
+      se->merge_cnt = static_cast<unsigned*>(alloc_zero(se.get(), c.heads * CHUNK * sizeof(unsigned)));
       se->xc = f(CHUNK * d);
       se->pos_dev = reinterpret_cast<long long*>(alloc_zero(se.get(), sizeof(long long)));
       se->ids_dev = reinterpret_cast<uint32_t*>(alloc_zero(se.get(), CHUNK * sizeof(uint32_t)));
@@ -1806,12 +1870,15 @@ int slm_decode(slm_session* se, uint32_t first, size_t n, const slm_sampling* sp
     const bool fused = se->use_mega && sp->temperature <= 0.0f && sp->repeat_penalty == 1.0f;
     if (fused) plan_outputs(se, true, se->outs_dev, se->hist_dev, n_recent);
     try {
-      for (size_t t = 0; t < n; t++) {
-        step_device(se);
-        if (fused) continue;  // the step's own arg-max wrote the id
-        a.nrecent = (long long)(n_recent + t);
-        a.out = se->outs_dev + t;
-        sample(a, s);
+      if (fused) {
+        mega_steps(se, n);  // each step's own arg-max is the next id
+      } else {
+        for (size_t t = 0; t < n; t++) {
+          step_device(se);
+          a.nrecent = (long long)(n_recent + t);
+          a.out = se->outs_dev + t;
+          sample(a, s);
+        }
       }
     } catch (...) {
       if (fused) plan_outputs(se, false, nullptr, nullptr, 0);
@@ -1858,6 +1925,7 @@ int slm_batch_new(slm_session* const* sessions, size_t n, slm_batch** out) {
       bt->nsplit = (int)std::max<long long>(1, std::min<long long>(std::min(want, most), 256));
       AttnGeom g{(int)n, 0, 0, 1, (int)c.heads, 1, (int)c.dh(), 1.0f};
       bt->part = f(attn_part_floats(g, bt->nsplit));
+      bt->merge_cnt = static_cast<unsigned*>(balloc(bt.get(), c.heads * n * sizeof(unsigned)));
       bt->ids = static_cast<uint32_t*>(balloc(bt.get(), n * sizeof(uint32_t)));
       bt->out_index = static_cast<unsigned*>(balloc(bt.get(), 4 * sizeof(unsigned)));
       bt->outs = static_cast<uint32_t*>(balloc(bt.get(), n * sizeof(uint32_t)));
@@ -1950,6 +2018,70 @@ int slm_batch_decode(slm_batch* bt, const uint32_t* first, size_t steps, uint32_
     SLM_CUDA(cudaMemsetAsync(bt->out_index, 0, sizeof(unsigned), s));
     for (size_t t = 0; t < steps; t++) batch_step_device(bt);
     SLM_CUDA(cudaMemcpyAsync(out, bt->outs, steps * bt->n * sizeof(uint32_t), cudaMemcpyDeviceToHost, s));
+    check_device_error(bt->ctx);
+  });
+}
+
+int slm_batch_sample_decode(slm_batch* bt, const uint32_t* first, size_t steps, const slm_sampling* sp,
+                            const uint32_t* const* recent, const size_t* n_recent, uint64_t* rng_state,
+                            uint32_t* out) {
+  return guard([&] {
+    SLM_REQUIRE(bt && first && sp && rng_state && (out || steps == 0), "bad arguments");
+    const size_t n = bt->n, V = bt->model->cfg.vocab;
+    size_t most = 0;
+    for (size_t i = 0; i < n; i++) {
+      SLM_REQUIRE(first[i] < V, "token id out of range");
+      check_sampling(sp + i);
+      const size_t r = n_recent ? n_recent[i] : 0;
+      SLM_REQUIRE(r == 0 || (recent && recent[i]), "bad arguments");
+      most = std::max(most, r);
+    }
+    if (steps == 0) return;
+    Device dev(bt->ctx);
+    cudaStream_t s = bt->ctx->stream;
+    batch_outs(bt, steps);
+    if (!bt->srows) {
+      bt->srows = static_cast<SampleArgs*>(balloc(bt, n * sizeof(SampleArgs)));
+      bt->swork = static_cast<float*>(balloc(bt, n * 3 * V * sizeof(float)));
+      bt->srng = static_cast<unsigned long long*>(balloc(bt, n * sizeof(unsigned long long)));
+    }
+    if (most + steps > bt->shist_cap) {  // the rows' histories, each with room for the sampled ids
+      SLM_CUDA(cudaStreamSynchronize(s));
+      const size_t cap = std::max<size_t>(1024, std::max(most + steps, 2 * bt->shist_cap));
+      auto* p = static_cast<uint32_t*>(dev_alloc(n * cap * sizeof(uint32_t)));
+      for (auto& o : bt->owned)
+        if (o == bt->shist) {
+          dev_free(o);
+          o = p;
+        }
+      if (!bt->shist) bt->owned.push_back(p);
+      bt->shist = p;
+      bt->shist_cap = cap;
+    }
+    std::vector<SampleArgs> rows(n);
+    for (size_t i = 0; i < n; i++) {
+      const size_t r = n_recent ? n_recent[i] : 0;
+      uint32_t* h = bt->shist + i * bt->shist_cap;
+      if (r) SLM_CUDA(cudaMemcpyAsync(h, recent[i], r * sizeof(uint32_t), cudaMemcpyHostToDevice, s));
+      SampleArgs& a = rows[i];
+      a = SampleArgs{};
+      a.logits = bt->logits + i * V;
+      a.work = bt->swork + i * 3 * V;
+      a.vocab = (int)V;
+      a.temperature = sp[i].temperature, a.top_p = sp[i].top_p, a.penalty = sp[i].repeat_penalty;
+      a.top_k = sp[i].top_k, a.window = sp[i].repeat_window;
+      a.recent = h, a.nrecent = (long long)r, a.hist_out = h;
+      a.rng = bt->srng + i;
+      a.next_id = bt->ids + i;
+      a.err = bt->ctx->err;
+    }
+    SLM_CUDA(cudaMemcpyAsync(bt->srows, rows.data(), n * sizeof(SampleArgs), cudaMemcpyHostToDevice, s));
+    SLM_CUDA(cudaMemcpyAsync(bt->srng, rng_state, n * sizeof(uint64_t), cudaMemcpyHostToDevice, s));
+    SLM_CUDA(cudaMemcpyAsync(bt->ids, first, n * sizeof(uint32_t), cudaMemcpyHostToDevice, s));
+    SLM_CUDA(cudaMemsetAsync(bt->out_index, 0, sizeof(unsigned), s));
+    for (size_t t = 0; t < steps; t++) batch_step_device(bt, true);
+    SLM_CUDA(cudaMemcpyAsync(out, bt->outs, steps * n * sizeof(uint32_t), cudaMemcpyDeviceToHost, s));
+    SLM_CUDA(cudaMemcpyAsync(rng_state, bt->srng, n * sizeof(uint64_t), cudaMemcpyDeviceToHost, s));
     check_device_error(bt->ctx);
   });
 }

@@ -151,6 +151,7 @@ int slm_ctx_free(slm_ctx* c) {
       cudaStreamSynchronize(c->stream);
       dev_free(c->stage);
       dev_free(c->gemm_ws);
+      dev_free(c->merge_cnt);
       dev_free(c->err);
       if (c->err_host) cudaFreeHost(c->err_host);
       cudaStreamDestroy(c->stream);
@@ -488,8 +489,18 @@ int slm_op_attend(slm_ctx* c, slm_buf* y, slm_buf* scores, const slm_buf* q, siz
       SLM_CUDA(cudaMemcpyAsync(scores->ptr + qat, qs, nq * sizeof(float), cudaMemcpyDeviceToDevice, c->stream));
       qs = scores->ptr + qat;
     }
+    // Counters for merging the slices in the slice launch (kept zero between calls).
+    const size_t ncnt = at->m * at->heads;
+    if (c->merge_cnt_len < ncnt) {
+      SLM_CUDA(cudaStreamSynchronize(c->stream));
+      dev_free(c->merge_cnt);
+      c->merge_cnt = nullptr, c->merge_cnt_len = 0;
+      c->merge_cnt = static_cast<unsigned*>(dev_alloc(ncnt * sizeof(unsigned)));
+      SLM_CUDA(cudaMemsetAsync(c->merge_cnt, 0, ncnt * sizeof(unsigned), c->stream));
+      c->merge_cnt_len = ncnt;
+    }
     attention(qs, (int)(at->heads * at->dh), k->ptr, v->ptr, g, pd, nsplit, scores->ptr + 2, y->ptr,
-              (int)(at->heads * at->dh), c->stream);
+              (int)(at->heads * at->dh), c->stream, c->merge_cnt);
   });
 }
 

@@ -160,8 +160,7 @@ __device__ void finish(const SampleArgs& a, uint32_t chosen) {
   if (a.next_id) a.next_id[0] = chosen;
 }
 
-__global__ void __launch_bounds__(ST) k_sample(SampleArgs a) {
-  __shared__ Shared sh;
+__device__ void sample_body(const SampleArgs& a, Shared& sh) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int V = a.vocab;
   float* work = a.work;
@@ -338,6 +337,24 @@ __global__ void __launch_bounds__(ST) k_sample(SampleArgs a) {
 
 }  // namespace
 
+__global__ void __launch_bounds__(ST) k_sample(SampleArgs a) {
+  __shared__ Shared sh;
+  sample_body(a, sh);
+}
+
+// One CTA per row of a batched step: row i's settings, history, RNG state and
+// work space come from rows[i]; its history and outputs are offset by the
+// steps the batch has taken so far (*step).
+__global__ void __launch_bounds__(ST) k_sample_rows(const SampleArgs* rows, const unsigned* step, uint32_t* outs,
+                                                    size_t m) {
+  __shared__ Shared sh;
+  SampleArgs a = rows[blockIdx.x];
+  const unsigned t = *step;
+  a.nrecent += t;
+  a.out = outs + (size_t)t * m + blockIdx.x;
+  sample_body(a, sh);
+}
+
 namespace {
 
 // One CTA per row: the largest composite key (logit, then the smaller id);
@@ -395,6 +412,12 @@ void argmax_rows(const float* logits, size_t vocab, size_t m, uint32_t* next, ui
 void sample(const SampleArgs& a, cudaStream_t st) {
   k_sample<<<1, ST, 0, st>>>(a);
   SLM_LAUNCHED("k_sample");
+}
+
+void sample_rows(const SampleArgs* rows, size_t m, const unsigned* step, uint32_t* outs, cudaStream_t st) {
+  if (!m) return;
+  k_sample_rows<<<(unsigned)m, ST, 0, st>>>(rows, step, outs, m);
+  SLM_LAUNCHED("k_sample_rows");
 }
 
 }  // namespace slm

@@ -121,3 +121,76 @@ def test_batch_refusals(slm, ctx, small, tmp_path_factory):
     gm = slm.Model(ctx, g)
     with pytest.raises(slm.SlmError):
         slm.Batch([gm.session(), gm.session()])
+
+
+def test_batch_sampled_decode_matches_single_sessions(slm, ctx, small):
+    # Per-row sampling: each row its own settings, history and RNG state; the
+    # device sampler of a single session (slm_decode) gives the same ids.
+    model = slm.Model(ctx, small)
+    lengths = [40, 77, 12, 130, 64, 99]
+    ses, twins, first = _pairs(slm, model, lengths, 1000, 6)
+    batch = slm.Batch(ses)
+    settings = [slm.Sampling(temperature=0.8, top_k=40, repeat_penalty=1.1, repeat_window=64),
+                slm.Sampling(),  # greedy row
+                slm.Sampling(temperature=1.0, top_p=0.9),
+                slm.Sampling(temperature=0.7, top_k=5, top_p=0.8, repeat_penalty=1.3, repeat_window=16),
+                slm.Sampling(temperature=1.2),
+                slm.Sampling(temperature=0.8, top_k=40, repeat_penalty=1.1, repeat_window=256)]
+    rng = np.random.default_rng(7)
+    hists = [[int(t) for t in rng.integers(0, 1000, n)] for n in (50, 0, 10, 300, 5, 70)]
+    states = [slm.rng_seed(100 + i) for i in range(len(ses))]
+    out = batch.sample_decode(first, 20, settings, hists, states)
+    for i, tw in enumerate(twins):
+        st = [slm.rng_seed(100 + i)]
+        want = tw.decode(first[i], 20, settings[i], hists[i], st)
+        np.testing.assert_array_equal(out[:, i], want, err_msg=str(i))
+        assert states[i] == st[0]
+    batch.close()
+
+
+def test_batch_rows_match_oracle_on_a_wrapped_window(slm, ctx, oracle, tmp_path_factory):
+    # 86M-class shapes with a full, wrapped 4096 window: every row restored
+    # from its own oracle state at positions past the ring's capacity (4352),
+    # then stepped in the batch with the oracle's tokens; logits within 1e-3
+    # of the oracle's, and per-row sampling (configs[2]'s settings) draw for
+    # draw against the oracle's pick.
+    syn = __import__("slm_b200.synthetic").synthetic
+    folder = syn.write_model(tmp_path_factory.mktemp("b_m86w"), syn.BASE, seed=0)
+    model, omodel = slm.Model(ctx, folder), oracle.Model(folder)
+    positions = [4400, 4610, 5000, 4353]
+    ses, refs = [], []
+    for i, pos in enumerate(positions):
+        dev, ref = model.session(4), omodel.session(4)
+        ref.fill(pos, 30 + i)
+        dev.set_pos(pos)
+        for j, a in enumerate(ref.state()):
+            dev.state_write(j, a["data"], a["cap"])
+        ses.append(dev)
+        refs.append(ref)
+    batch = slm.Batch(ses)
+    toks = [11, 222, 3333, 4444]
+    worst = 0.0
+    for _ in range(6):
+        batch.step(toks)
+        got = batch.logits()
+        nxt = []
+        for i, ref in enumerate(refs):
+            ref.step(toks[i])
+            lg = ref.logits()
+            worst = max(worst, float(np.abs(got[i] - lg).max()))
+            nxt.append(int(np.argmax(lg)))
+        toks = nxt
+    assert worst < 1e-3, worst
+    # Sampled rows against the oracle's pick, teacher-forced through slm_batch_step.
+    c3 = dict(temperature=0.8, top_k=40, top_p=1.0, repeat_penalty=1.1, repeat_window=256)
+    s = slm.Sampling(**c3)
+    hists = [[int(t) for t in np.random.default_rng(40 + i).integers(0, 32000, 256)] for i in range(4)]
+    st_ref = [oracle.rng_new(i) for i in range(4)]
+    st_dev = [slm.rng_seed(i) for i in range(4)]
+    got = batch.sample_decode(toks, 1, [s] * 4, hists, st_dev)[0]
+    for i, ref in enumerate(refs):
+        ref.step(toks[i])
+        st = [st_ref[i]]
+        want = oracle.pick(ref.logits(), np.array(hists[i], dtype=np.uint32), rng_state=st, **c3)
+        assert int(got[i]) == want and st_dev[i] == st[0], i
+    batch.close()

@@ -27,7 +27,12 @@ def _worker(rank, world, port, out):
         import bench
         prompt = bench.prompt_for(rank, 32000, 64)
         mine = [10.0 + rank, 5.0 - rank]
-        out[rank] = (bench.max_over_ranks(mine, dist), prompt.tolist())
+        # this rank's share of the 64 sequences, gathered to check
+        # that the ranks cover every sequence exactly once.
+        share = bench.c5_partition(64, rank, world)
+        seqs = [None] * world
+        dist.all_gather_object(seqs, share)
+        out[rank] = (bench.max_over_ranks(mine, dist), prompt.tolist(), seqs)
     finally:
         dist.destroy_process_group()
 
@@ -43,6 +48,22 @@ def test_two_ranks_partition_sequences_and_take_the_slowest():
     assert not np.array_equal(p0, p1)  # each rank has its own sequence
     import bench
     assert np.array_equal(p0, bench.prompt_for(0, 32000, 64))
+    # The C5 partition seen by both ranks: 0..63, each once, 32 per rank.
+    for r in range(world):
+        seqs = res[r][2]
+        flat = sorted(q for share in seqs for q in share)
+        assert flat == list(range(64))
+        assert [len(share) for share in seqs] == [32, 32]
+
+
+@pytest.mark.parametrize("world", [1, 2, 4, 8])
+def test_c5_partition_covers_every_sequence_once(world):
+    import bench
+    shares = [bench.c5_partition(64, r, world) for r in range(world)]
+    assert sorted(q for s in shares for q in s) == list(range(64))
+    assert all(len(s) == 64 // world for s in shares)
+    with pytest.raises(ValueError):
+        bench.c5_partition(64, world, world)
 
 
 def test_single_process_needs_no_group():
