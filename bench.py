@@ -57,7 +57,9 @@ ROOT = Path(__file__).resolve().parent
 MODEL_BYTES_NOTE = "inputs larger than L2: 640 MB of weights and KV read per token at R=4"
 # DRAM bytes (read + write) of one k_decode_mega launch from an ncu capture of
 # this bench (profiles/k_decode_mega_R4.md), by loop count.
-MEGA_TRAFFIC = {4: 447.6e6}
+# DRAM bytes (read + write) of one R = 4 step, ncu dram__bytes of one launch
+# (profiles/k_decode_mega_R4.md); no capture exists for other loop counts.
+MEGA_TRAFFIC = {4: 439.2e6}
 
 
 def load_pkg():
@@ -420,7 +422,9 @@ def run_b200(args, rank: int, world: int, local: int) -> dict | None:
     folder = model_dir(cfg, 0)
 
     ctx = slm.Context(local)
+    t_load = time.perf_counter()
     model = slm.Model(ctx, folder)
+    load_s = time.perf_counter() - t_load  # file read, pinned upload, bf16x3 splits and layouts
     stream = torch.cuda.ExternalStream(ctx.stream, device=dev)
     V = cfg["vocab_size"]
     greedy = slm.Sampling()
@@ -560,8 +564,34 @@ def run_b200(args, rank: int, world: int, local: int) -> dict | None:
             torch.cuda.synchronize(dev)
             extra[f"R{loops}"] = {"decode_tok_s": n2 / (a.elapsed_time(b) / 1000.0),
                                   "prefill_tok_s": len(prompt) / (pre_ms / 1000.0), "decode_steps": n2,
+                                  "prompt": len(prompt),
                                   "sampling": "T=0.8 top-k 40 repeat-penalty 1.1 (window 256) seed 0"}
             s2.close()
+            # configs[2] as written: a 2048-id prompt, then 512 sampled steps
+            # (the window fills up to 2560 positions).
+            s3 = model.session(loops)
+            p3 = prompt_for(rank, V, 2048)
+            torch.cuda.synchronize(dev)
+            a, b = events()
+            a.record(stream)
+            s3.feed(p3, 256)
+            s3.logits()
+            b.record(stream)
+            torch.cuda.synchronize(dev)
+            pre3 = a.elapsed_time(b)
+            st = [slm.rng_seed(0)]
+            hist = list(p3[-256:])
+            first = s3.sample(c3, hist, st)
+            hist.append(first)
+            a, b = events()
+            a.record(stream)
+            s3.decode(first, 512, c3, hist, st)
+            b.record(stream)
+            torch.cuda.synchronize(dev)
+            extra[f"R{loops}"]["configs2"] = {"decode_tok_s": 512 / (a.elapsed_time(b) / 1000.0),
+                                              "prefill_tok_s": 2048 / (pre3 / 1000.0), "prompt": 2048,
+                                              "decode_steps": 512}
+            s3.close()
 
     if "C4" in legs:
         # configs[3] ("C4"): the G-layer variant (S | LS | SG, the fixture's
@@ -649,8 +679,9 @@ def run_b200(args, rank: int, world: int, local: int) -> dict | None:
             write_trace(tr, cfg, args.loops, args.trace)
 
     step_kernels = se.step_kernels
+    mega = se.mega
     res = {"dec_ms": dec_ms, "e2e_s": e2e_s, "prefill_ms": prefill_ms, "prefill_host_s": prefill_host_s,
-           "gemv_us": gemv_us, "attn_us": attn_us, "attn_phase": attn_phase, "clocks": clocks.summary(), "extra": extra, "step_kernels": step_kernels,
+           "gemv_us": gemv_us, "attn_us": attn_us, "attn_phase": attn_phase, "clocks": clocks.summary(), "extra": extra, "step_kernels": step_kernels, "mega": mega, "load_s": load_s,
            "device": ctx.name, "state_bytes": se.state_bytes()}
     res["dec_ms"], res["e2e_s"], res["prefill_ms"] = max_over_ranks([dec_ms, e2e_s, prefill_ms], dist, dev)
     se.close()
@@ -771,19 +802,28 @@ def main():
         "roofline": {"bound": "hbm", "kernel": "k_decode_mega (one m=1 token step, R=%d)" % args.loops,
                      "achieved": step_gbs, "peak": hbm, "unit": "GB/s", "frac": step_gbs / hbm,
                      "bytes_per_launch": byts["total"], "traffic": MEGA_TRAFFIC.get(args.loops),
+                     "traffic_source": ("ncu dram__bytes_read.sum + dram__bytes_write.sum of one R=4 launch "
+                                        "(profiles/k_decode_mega_R4.md)" if args.loops in MEGA_TRAFFIC else
+                                        "not captured for this loop count"),
                      "peak_source": peak_src,
                      "gemv": {"kernel": "k_gemv<1,STORE> (32000x768 fp32, m=1)", "achieved": gemv_gbs,
                               "frac": gemv_gbs / hbm, "how": "40 launches queued behind a device sleep, CUDA "
                               "events around them"},
-                     "attention": {"kernel": "k_attn_split + k_attn_combine (m=1, 12 heads x 4096 positions of a "
-                                             "4352-slot ring, K and V from HBM)",
-                                   "achieved": attn_gbs, "frac": attn_gbs / hbm, "how": "36 calls (two launches "
+                     "attention": {"kernel": "k_attn_split (m=1, 12 heads x 4096 positions of a 4352-slot ring, "
+                                             "K and V from HBM; the last slice of each head merges)",
+                                   "achieved": attn_gbs, "frac": attn_gbs / hbm, "how": "36 calls (one launch "
                                    "each) queued behind a device sleep, CUDA events around them"}},
         "clocks": res["clocks"],
-        "gpu_launches": K * (res["step_kernels"] + 1),
+        # Greedy persistent decode runs up to 4096 steps per launch.
+        "gpu_launches": (math.ceil(K / int(os.environ.get("SLM_MEGA_STEPS", "4096"))) if res["mega"]
+                         else K * (res["step_kernels"] + 1)),
         "extra": res["extra"],
         "device": res["device"],
         "state_mib": res["state_bytes"] / 2**20,
+        "model_load": {"seconds": res["load_s"],
+                       "weights_mb": (model_dir(cfg, 0) / "model.safetensors").stat().st_size / 1e6,
+                       "how": "slm_model_load: safetensors read, f32 upload through pinned double buffers, "
+                              "derived layouts (bf16x3 parts, transposed down, per-head o) on the device"},
     }
     if res.get("attn_phase"):
         ap = res["attn_phase"]

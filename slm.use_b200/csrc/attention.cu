@@ -82,24 +82,26 @@ __device__ void combine_pair(const float* __restrict__ part, int nsplit, int m, 
   const int Q = NT / dh >= 1 ? (NT / dh > 4 ? 4 : NT / dh) : 1;
   const int q = t / dh, e = t % dh;
   float a = 0.0f;
-  if (q < Q && dh <= NT)
-    for (int s = q; s < nsplit; s += Q) {
-      const float ms = __ldcg(p0 + s * stride + dh);
-      const float c = s < 256 ? cw[s] : ((M == -INFINITY || ms == -INFINITY) ? 0.0f : expf(ms - M));
-      a = fmaf(__ldcg(p0 + s * stride + e), c, a);
+  if (q < Q && dh <= NT) {
+    // Splits q, q + Q, … in order; eight loads in flight at a time.
+    int s = q;
+    for (; s + 7 * Q < nsplit; s += 8 * Q) {
+      float v[8];
+#pragma unroll
+      for (int u = 0; u < 8; u++) v[u] = __ldcg(p0 + (size_t)(s + u * Q) * stride + e);
+#pragma unroll
+      for (int u = 0; u < 8; u++) a = fmaf(v[u], cw[s + u * Q], a);
     }
-  if (q < Q && dh <= NT) acc_sh[q * (dh + 4) + e] = a;
+    for (; s < nsplit; s += Q) a = fmaf(__ldcg(p0 + (size_t)s * stride + e), cw[s], a);
+    acc_sh[q * (dh + 4) + e] = a;
+  }
   __syncthreads();
   for (int d = t; d < dh; d += NT) {
     float v = 0.0f;
     if (dh <= NT) {
       for (int qq = 0; qq < Q; qq++) v += acc_sh[qq * (dh + 4) + d];
     } else {  // heads wider than the CTA: one thread per dimension, splits in order
-      for (int s = 0; s < nsplit; s++) {
-        const float ms = __ldcg(p0 + s * stride + dh);
-        const float c = s < 256 ? cw[s] : ((M == -INFINITY || ms == -INFINITY) ? 0.0f : expf(ms - M));
-        v = fmaf(__ldcg(p0 + s * stride + d), c, v);
-      }
+      for (int s = 0; s < nsplit; s++) v = fmaf(__ldcg(p0 + (size_t)s * stride + d), cw[s], v);
     }
     y[(size_t)i * ldy + (size_t)h * dh + d] = L > 0.0f ? v / L : 0.0f;
   }
@@ -111,14 +113,16 @@ __device__ void combine_pair(const float* __restrict__ part, int nsplit, int m, 
 // With `rows` set, query i belongs to its own sequence: its cache is
 // rows->k[i] / rows->v[i] and its position *rows->pos[i] (batched decode of
 // independent sessions, one token each).
+constexpr int kSplitThreads = 256;  // 8 warps: a 128-position slice is one round of loads
+
 template <int DH>
-__global__ void __launch_bounds__(128)
+__global__ void __launch_bounds__(kSplitThreads)
     k_attn_split(const float* __restrict__ q, int ldq, const float* __restrict__ K, const float* __restrict__ V,
                  AttnGeom g, const long long* __restrict__ pos_ptr, int nsplit, float* __restrict__ part,
                  AttnRows rows, unsigned* __restrict__ cnt, float* __restrict__ y, int ldy) {
   constexpr int G = DH / 8;        // lanes per cache row
   constexpr int PPW = 32 / G;      // rows per warp step
-  constexpr int WARPS = 4;
+  constexpr int WARPS = kSplitThreads / 32;
   const int s = blockIdx.x, h = blockIdx.y, i = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int sub = lane % G, grp = lane / G;
@@ -126,7 +130,7 @@ __global__ void __launch_bounds__(128)
     K = rows.k[i];
     V = rows.v[i];
   }
-  const long long p = rows.pos ? *rows.pos[i] : pos_ptr[0] + i;
+  const long long p = rows.pos ? *rows.pos[i] : (pos_ptr ? pos_ptr[0] : g.pos0) + i;
   Range r = visible(p, g.reach, g.gap);
   long long count = r.hi - r.lo;
   long long chunk = (count + nsplit - 1) / nsplit;
@@ -247,7 +251,7 @@ __global__ void __launch_bounds__(128)
   if (!last) return;
   __threadfence();
   __shared__ float red[WARPS], cw[256], acc_sh[4 * (DH + 4)];
-  combine_pair<128>(part, nsplit, g.m, g.heads, DH, i, h, y, ldy, red, cw, acc_sh);
+  combine_pair<kSplitThreads>(part, nsplit, g.m, g.heads, DH, i, h, y, ldy, red, cw, acc_sh);
 }
 
 // ---------------------------------------------------------------------------
@@ -264,7 +268,7 @@ __global__ void __launch_bounds__(128)
   __shared__ __align__(16) float Qs[4][DH][QW];  // per warp, transposed: [warp][d][query]
   const int s = blockIdx.x, i0 = blockIdx.y * QT, h = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const long long pos = pos_ptr[0];
+  const long long pos = pos_ptr ? pos_ptr[0] : g.pos0;
   const int kvh = h / (g.heads / g.key_heads);
   const float* Kb = K + (size_t)kvh * g.cap * DH;
   const float* Vb = V + (size_t)kvh * g.cap * DH;
@@ -408,7 +412,7 @@ __global__ void __launch_bounds__(256, 2)
   float(*Ps)[FLD] = reinterpret_cast<float(*)[FLD]>(fsm + (FQ + 4 * FKT) * FLD);
   const int s = blockIdx.x, i0 = blockIdx.y * FQ, h = blockIdx.z;
   const int t = threadIdx.x, ty = t >> 4, tx = t & 15;
-  const long long pos = pos_ptr[0];
+  const long long pos = pos_ptr ? pos_ptr[0] : g.pos0;
   const int kvh = h / (g.heads / g.key_heads);
   const float* Kb = K + (size_t)kvh * g.cap * DH;
   const float* Vb = V + (size_t)kvh * g.cap * DH;
@@ -588,13 +592,18 @@ __global__ void __launch_bounds__(256) k_attn_combine(const float* __restrict__ 
   const int Q = 256 / dh >= 1 ? (256 / dh > 4 ? 4 : 256 / dh) : 1;
   const int q = t / dh, e = t % dh;
   float a = 0.0f;
-  if (q < Q && dh <= 256)
-    for (int s = q; s < nsplit; s += Q) {
-      const float c = s < 256 ? cw[s] : ((M == -INFINITY || p0[s * stride + dh] == -INFINITY)
-                                             ? 0.0f
-                                             : expf(p0[s * stride + dh] - M));
-      a = fmaf(p0[s * stride + e], c, a);
+  if (q < Q && dh <= 256) {
+    // Splits q, q + Q, … in order; eight loads in flight at a time.
+    int s = q;
+    for (; s + 7 * Q < nsplit; s += 8 * Q) {
+      float v[8];
+#pragma unroll
+      for (int u = 0; u < 8; u++) v[u] = p0[(size_t)(s + u * Q) * stride + e];
+#pragma unroll
+      for (int u = 0; u < 8; u++) a = fmaf(v[u], cw[s + u * Q], a);
     }
+    for (; s < nsplit; s += Q) a = fmaf(p0[(size_t)s * stride + e], cw[s], a);
+  }
   if (q < Q) acc_sh[q][e] = a;
   __syncthreads();
   for (int d = t; d < dh; d += 256) {
@@ -635,7 +644,7 @@ template <int DH>
 bool launch_dh(const float* q, int ldq, const float* K, const float* V, const AttnGeom& g, const long long* pos_ptr,
                int nsplit, float* part, unsigned* cnt, float* y, int ldy, cudaStream_t st) {
   if (g.m <= 8 || DH > 128) {
-    k_attn_split<DH><<<dim3(nsplit, g.heads, g.m), 128, 0, st>>>(q, ldq, K, V, g, pos_ptr, nsplit, part,
+    k_attn_split<DH><<<dim3(nsplit, g.heads, g.m), kSplitThreads, 0, st>>>(q, ldq, K, V, g, pos_ptr, nsplit, part,
                                                                  AttnRows{}, cnt, y, ldy);
     SLM_LAUNCHED("k_attn_split");
     return cnt != nullptr;
@@ -651,11 +660,19 @@ int attn_splits(const AttnGeom& g, long long max_span) {
   long long ctas = (g.m <= 8 || g.dh > 128) ? (long long)g.heads * g.m
                   : g.dh == 64               ? (long long)g.heads * ((g.m + FQ - 1) / FQ)
                                              : (long long)g.heads * ((g.m + 15) / 16);
-  // Two CTAs per SM (more splits measured slower: per-slice set-up and the
-  // merge outweigh the extra loads in flight).  The flash tiles hold exactly
-  // two per SM, so their count rounds down to one full wave.
-  long long want = (g.m > 8 && g.dh == 64) ? std::max(1ll, (2 * 148) / ctas) : (2 * 148 + ctas - 1) / ctas;
-  long long most = (max_span + 127) / 128;  // at least 128 positions per slice
+  // Decode-sized calls (the slice pass): at most two 256-thread CTAs per SM
+  // (one wave at 127 registers a thread) and slices of at least 256
+  // positions; the last slice of each (query, head) merges them.  Measured on
+  // the m = 1 op over a 4096 window: 12.5 µs per call with 16 slices, 12.4–18
+  // µs for 8 to 64 slices of 4 or 8 warps.  Chunks: two CTAs per SM; the flash tiles hold
+  // exactly two per SM, so their count rounds down to one full wave.
+  const bool slices = g.m <= 8 || g.dh > 128;
+  constexpr long long per_sm = 2, min_pos = 256;
+  long long want = (g.m > 8 && g.dh == 64) ? std::max(1ll, (2 * 148) / ctas)
+                   : slices                ? (per_sm * 148 + ctas - 1) / ctas
+                                           : (2 * 148 + ctas - 1) / ctas;
+  const long long step = slices ? min_pos : 128;  // positions per slice at least
+  long long most = (max_span + step - 1) / step;
   long long n = want < most ? want : most;
   if (n < 1) n = 1;
   if (n > 256) n = 256;
@@ -689,7 +706,8 @@ void attention_rows(const float* q, int ldq, const AttnRows& rows, const AttnGeo
   SLM_REQUIRE(g.key_heads > 0 && g.heads % g.key_heads == 0, "attend: heads must be a multiple of key_heads");
   const dim3 grid(nsplit, g.heads, g.m);
 #define SLM_ROWS(DHV) \
-  k_attn_split<DHV><<<grid, 128, 0, st>>>(q, ldq, nullptr, nullptr, g, nullptr, nsplit, part, rows, cnt, y, ldy)
+  k_attn_split<DHV><<<grid, kSplitThreads, 0, st>>>(q, ldq, nullptr, nullptr, g, nullptr, nsplit, part, rows, cnt, y, \
+                                                     ldy)
   switch (g.dh) {
     case 8: SLM_ROWS(8); break;
     case 16: SLM_ROWS(16); break;

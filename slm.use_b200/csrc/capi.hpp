@@ -25,6 +25,12 @@ struct slm_ctx {
   unsigned long long gemm_ws_gen = 0;  // bumped whenever gemm_ws moves (graphs holding it must be re-captured)
   unsigned* merge_cnt = nullptr;  // attention slice counters of slm_op_attend (zero between launches)
   size_t merge_cnt_len = 0;
+  // Live buffers and models of this context.  slm_ctx_free while some live
+  // only marks the context closing; the last of them to be freed frees it
+  // (callers whose finalisers run in any order, such as a garbage collector,
+  // stay safe).
+  int refs = 0;
+  bool closing = false;
 };
 
 struct slm_buf {
@@ -45,6 +51,10 @@ struct Device {
   explicit Device(slm_ctx* c);
   ~Device();
 };
+
+// Takes / drops a reference to a context (see slm_ctx::refs).
+void ctx_retain(slm_ctx* c);
+void ctx_release(slm_ctx* c);
 
 void* dev_alloc(size_t bytes);
 void dev_free(void* p);

@@ -54,6 +54,7 @@ struct AttnGeom {
   long long reach, gap, cap;
   int heads, key_heads, dh;
   float scale;
+  long long pos0 = 0;  // position of the first query when no device position pointer is given
 };
 // Per-row sequences of a batched decode step (device arrays of g.m entries).
 struct AttnRows {

@@ -78,6 +78,10 @@ struct slm_model {
   const float* norm_f = nullptr;
   const float* inv_freq = nullptr;
   size_t params = 0, hidden = 0, mix_cols = 0;
+  // Live sessions; slm_model_free while some live marks the model closing and
+  // the last session's free frees it (as slm_ctx does for its children).
+  int refs = 0;
+  bool closing = false;
 };
 
 struct slm_session {
@@ -194,6 +198,48 @@ struct Loading {
   std::vector<std::pair<const float**, size_t>> fix;  // pointers to patch with arena offsets
   std::string error;
 };
+
+// Copies every tensor of `up` to its offset in `arena` (device) through two
+// pinned staging buffers: the host copies chunk i + 1 into one while the copy
+// engine moves chunk i out of the other, on the context's stream.
+void upload_pinned(slm_ctx* ctx, float* arena, const Uploader& up) {
+  constexpr size_t kChunk = size_t(16) << 20;  // bytes per staging buffer
+  cudaStream_t s = ctx->stream;
+  char* stage[2] = {nullptr, nullptr};
+  cudaEvent_t done[2] = {nullptr, nullptr};
+  struct Release {
+    char** st;
+    cudaEvent_t* ev;
+    ~Release() {
+      for (int i = 0; i < 2; i++) {
+        if (ev[i]) cudaEventSynchronize(ev[i]), cudaEventDestroy(ev[i]);
+        if (st[i]) cudaFreeHost(st[i]);
+      }
+    }
+  } rel{stage, done};
+  for (int i = 0; i < 2; i++) {
+    SLM_CUDA(cudaHostAlloc(reinterpret_cast<void**>(&stage[i]), kChunk, cudaHostAllocDefault));
+    SLM_CUDA(cudaEventCreateWithFlags(&done[i], cudaEventDisableTiming));
+  }
+  int b = 0;
+  bool used[2] = {false, false};
+  for (size_t t = 0; t < up.items.size(); t++) {
+    const char* src = reinterpret_cast<const char*>(up.items[t].first);
+    char* dst = reinterpret_cast<char*>(arena + up.offsets[t]);
+    size_t left = up.items[t].second * sizeof(float);
+    while (left > 0) {
+      const size_t n = std::min(left, kChunk);
+      if (used[b]) SLM_CUDA(cudaEventSynchronize(done[b]));  // its previous copy has left the buffer
+      std::memcpy(stage[b], src, n);
+      SLM_CUDA(cudaMemcpyAsync(dst, stage[b], n, cudaMemcpyHostToDevice, s));
+      SLM_CUDA(cudaEventRecord(done[b], s));
+      used[b] = true;
+      src += n, dst += n, left -= n;
+      b ^= 1;
+    }
+  }
+  SLM_CUDA(cudaStreamSynchronize(s));
+}
 
 const TensorView& take(Loading& L, const std::string& name) {
   auto it = L.t.map.find(name);
@@ -1323,9 +1369,7 @@ int slm_model_load(slm_ctx* ctx, const char* dir, slm_model** out) {
     L.t.map["__inv_freq"] = TensorView{{dh / 2}, inv.data(), dh / 2};
     vec(L, "__inv_freq", &md->inv_freq, dh / 2);
     md->arena = static_cast<float*>(dev_alloc(L.up.total * sizeof(float)));
-    for (size_t i = 0; i < L.up.items.size(); i++)
-      SLM_CUDA(cudaMemcpy(md->arena + L.up.offsets[i], L.up.items[i].first, L.up.items[i].second * sizeof(float),
-                          cudaMemcpyHostToDevice));
+    upload_pinned(ctx, md->arena, L.up);
     for (auto& f : L.fix) *f.first = md->arena + f.second;
     // Model::params (src/model.rs:275-302).
     size_t p = 0;
@@ -1388,19 +1432,37 @@ int slm_model_load(slm_ctx* ctx, const char* dir, slm_model** out) {
       }
       SLM_CUDA(cudaStreamSynchronize(ctx->stream));
     }
+    ctx_retain(ctx);
     *out = md.release();
   });
 }
 
-int slm_model_free(slm_model* md) {
-  return guard([&] {
-    if (!md) return;
-    Device dev(md->ctx);
-    cudaStreamSynchronize(md->ctx->stream);
+namespace {
+void destroy_model(slm_model* md) {
+  slm_ctx* c = md->ctx;
+  {
+    Device dev(c);
+    cudaStreamSynchronize(c->stream);
     dev_free(md->arena);
     dev_free(md->planes);
     dev_free(md->tarena);
-    delete md;
+  }
+  delete md;
+  ctx_release(c);
+}
+void model_release(slm_model* md) {
+  if (--md->refs == 0 && md->closing) destroy_model(md);
+}
+}  // namespace
+
+int slm_model_free(slm_model* md) {
+  return guard([&] {
+    if (!md || md->closing) return;
+    if (md->refs > 0) {  // sessions still live: the last of them frees the model
+      md->closing = true;
+      return;
+    }
+    destroy_model(md);
   });
 }
 
@@ -1509,6 +1571,7 @@ int slm_session_new(slm_model* md, size_t loops, slm_session** out) {
           if (st.kind == 'G') dev_free(st.k), dev_free(st.v);
       throw;
     }
+    md->refs++;
     *out = se.release();
   });
 }
@@ -1533,7 +1596,9 @@ int slm_session_free(slm_session* se) {
     if (se->io) cudaFreeHost(se->io);
     if (se->io_event) cudaEventDestroy(se->io_event);
     if (se->ctx->argmax_owner == se) se->ctx->argmax_owner = nullptr;
+    slm_model* md = se->model;
     delete se;
+    model_release(md);
   });
 }
 

@@ -97,6 +97,29 @@ void gemm_workspace(slm_ctx* c, LinearArgs& a, bool capturing) {
 
 using namespace slm;
 
+namespace {
+void destroy_ctx(slm_ctx* c) {
+  {
+    Device dev(c);
+    cudaStreamSynchronize(c->stream);
+    dev_free(c->stage);
+    dev_free(c->gemm_ws);
+    dev_free(c->merge_cnt);
+    dev_free(c->err);
+    if (c->err_host) cudaFreeHost(c->err_host);
+    cudaStreamDestroy(c->stream);
+  }
+  delete c;
+}
+}  // namespace
+
+namespace slm {
+void ctx_retain(slm_ctx* c) { c->refs++; }
+void ctx_release(slm_ctx* c) {
+  if (--c->refs == 0 && c->closing) destroy_ctx(c);
+}
+}  // namespace slm
+
 extern "C" {
 
 const char* slm_last_error(void) { return g_last_error.c_str(); }
@@ -145,18 +168,12 @@ int slm_ctx_new(int device, slm_ctx** out) {
 
 int slm_ctx_free(slm_ctx* c) {
   return guard([&] {
-    if (!c) return;
-    {
-      Device dev(c);
-      cudaStreamSynchronize(c->stream);
-      dev_free(c->stage);
-      dev_free(c->gemm_ws);
-      dev_free(c->merge_cnt);
-      dev_free(c->err);
-      if (c->err_host) cudaFreeHost(c->err_host);
-      cudaStreamDestroy(c->stream);
+    if (!c || c->closing) return;
+    if (c->refs > 0) {  // buffers or models still live: the last of them frees the context
+      c->closing = true;
+      return;
     }
-    delete c;
+    destroy_ctx(c);
   });
 }
 
@@ -189,6 +206,7 @@ int slm_zeros(slm_ctx* c, size_t n, slm_buf** out) {
     SLM_REQUIRE(c && out, "bad arguments");
     Device dev(c);
     auto* b = new slm_buf{c, nullptr, 0};
+    ctx_retain(c);
     try {
       size_t len = n ? n : 1;  // zeros(n.max(1)), src/cuda.rs:152-154
       b->ptr = static_cast<float*>(dev_alloc(len * sizeof(float)));
@@ -196,6 +214,7 @@ int slm_zeros(slm_ctx* c, size_t n, slm_buf** out) {
       SLM_CUDA(cudaMemsetAsync(b->ptr, 0, len * sizeof(float), c->stream));
     } catch (...) {
       delete b;
+      c->refs--;
       throw;
     }
     *out = b;
@@ -207,6 +226,7 @@ int slm_upload(slm_ctx* c, const float* data, size_t n, slm_buf** out) {
     SLM_REQUIRE(c && out && (data || n == 0), "bad arguments");
     Device dev(c);
     auto* b = new slm_buf{c, nullptr, 0};
+    ctx_retain(c);
     try {
       b->ptr = static_cast<float*>(dev_alloc((n ? n : 1) * sizeof(float)));
       b->len = n ? n : 1;
@@ -215,6 +235,7 @@ int slm_upload(slm_ctx* c, const float* data, size_t n, slm_buf** out) {
     } catch (...) {
       dev_free(b->ptr);
       delete b;
+      c->refs--;
       throw;
     }
     *out = b;
@@ -234,10 +255,14 @@ int slm_read(slm_ctx* c, const slm_buf* b, size_t n, float* out) {
 int slm_buf_free(slm_buf* b) {
   return guard([&] {
     if (!b) return;
-    Device dev(b->ctx);
-    cudaStreamSynchronize(b->ctx->stream);
-    dev_free(b->ptr);
+    slm_ctx* c = b->ctx;
+    {
+      Device dev(c);
+      cudaStreamSynchronize(c->stream);
+      dev_free(b->ptr);
+    }
     delete b;
+    ctx_release(c);
   });
 }
 
@@ -477,14 +502,13 @@ int slm_op_attend(slm_ctx* c, slm_buf* y, slm_buf* scores, const slm_buf* q, siz
     long long span = (long long)(at->pos + at->m) - g.gap - base;
     int nsplit = attn_splits(g, span < 1 ? 1 : span);
     long long pos = (long long)at->pos;
-    // Scratch: the position (8 bytes), the partials, and room for q when the
-    // view is not 16-byte aligned (the kernels read q in 16-byte vectors).
+    // Scratch: two leading floats (unused), the partials, and room for q when
+    // the view is not 16-byte aligned (the kernels read q in 16-byte vectors).
     const size_t parts = attn_part_floats(g, nsplit), nq = at->m * at->heads * at->dh;
     const bool copy_q = ((uintptr_t)qs & 15) != 0;
     const size_t qat = (2 + parts + 3) / 4 * 4;  // 16-byte aligned float offset
     ensure(scores, copy_q ? qat + nq : parts + 2);
-    auto* pd = reinterpret_cast<long long*>(scores->ptr);  // first 8 bytes hold the position
-    SLM_CUDA(cudaMemcpyAsync(pd, &pos, sizeof(pos), cudaMemcpyHostToDevice, c->stream));
+    g.pos0 = pos;  // the query position travels in the launch parameters
     if (copy_q) {
       SLM_CUDA(cudaMemcpyAsync(scores->ptr + qat, qs, nq * sizeof(float), cudaMemcpyDeviceToDevice, c->stream));
       qs = scores->ptr + qat;
@@ -499,7 +523,7 @@ int slm_op_attend(slm_ctx* c, slm_buf* y, slm_buf* scores, const slm_buf* q, siz
       SLM_CUDA(cudaMemsetAsync(c->merge_cnt, 0, ncnt * sizeof(unsigned), c->stream));
       c->merge_cnt_len = ncnt;
     }
-    attention(qs, (int)(at->heads * at->dh), k->ptr, v->ptr, g, pd, nsplit, scores->ptr + 2, y->ptr,
+    attention(qs, (int)(at->heads * at->dh), k->ptr, v->ptr, g, nullptr, nsplit, scores->ptr + 2, y->ptr,
               (int)(at->heads * at->dh), c->stream, c->merge_cnt);
   });
 }

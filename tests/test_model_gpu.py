@@ -350,3 +350,21 @@ def test_persistent_kernel_is_refused_where_it_does_not_apply(slm, tiny):
     assert not se.mega  # head size 8 and a global layer
     with pytest.raises(slm.SlmError):
         se.set_mega(True)
+
+
+def test_handles_free_in_any_order(slm):
+    # A garbage collector may finalise a context before its buffers, or a
+    # model before its sessions: freeing a handle that still has live
+    # children defers its release to the last child.
+    ctx = slm.Context(0)
+    ops = slm.Ops(ctx)
+    buf = ops.upload(np.arange(8, dtype=np.float32))
+    model = slm.Model(ctx, TINY)
+    se = model.session(3)
+    ctx.close()
+    model.close()
+    se.feed([1, 2, 3])  # the session still works: its model and context live on
+    assert se.logits().shape == (97,)
+    np.testing.assert_array_equal(buf.read(8), np.arange(8, dtype=np.float32))
+    se.close()
+    buf.close()
