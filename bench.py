@@ -536,7 +536,31 @@ def run_b200(args, rank: int, world: int, local: int) -> dict | None:
             vb.close()
 
     extra = {}
-    legs = set(args.extras.split(",")) if args.extras else (set() if args.quick else {"R8", "R16", "C4", "C5"})
+    legs = set(args.extras.split(",")) if args.extras else (set() if args.quick else {"R8", "R16", "C4", "C5", "BF16"})
+    if "BF16" in legs:
+        # The same decode with the persistent step streaming bf16 copies of
+        # the weights (f32 arithmetic and caches): a separate line, never the
+        # headline (logits differ by the weights' rounding).
+        sb = model.session(args.loops)
+        sb.set_bf16(True)
+        sb.feed(prompt, 256)
+        tb = int(np.argmax(sb.logits()))
+        sb.decode(tb, args.warmup, greedy)
+        tb = int(sb.sample(greedy))
+        torch.cuda.synchronize(dev)
+        a, b = events()
+        a.record(stream)
+        sb.decode(tb, args.steps, greedy)
+        b.record(stream)
+        torch.cuda.synchronize(dev)
+        bf_ms = a.elapsed_time(b) / args.steps
+        bf_bytes = decode_bytes(cfg, args.loops)
+        bf_total = bf_bytes["total"] - bf_bytes["weights"] / 2
+        extra["BF16"] = {"decode_tok_s": 1000.0 / bf_ms, "ms_per_step": bf_ms, "loops": args.loops,
+                         "bytes_per_token": bf_total, "achieved_gbs": bf_total / (bf_ms / 1000.0) / 1e9,
+                         "weights": "bf16 copies (round to nearest even), f32 arithmetic, caches and state",
+                         "sampling": "greedy"}
+        sb.close()
     if legs & {"R8", "R16"}:
         c3 = slm.Sampling(temperature=0.8, top_k=40, repeat_penalty=1.1, repeat_window=256)
         for loops in (8, 16):

@@ -271,6 +271,14 @@ int slm_decode(slm_session* se, uint32_t first, size_t n, const slm_sampling* s,
  * SLM_ERR_DEVICE at the next synchronising call.  The session's state is then
  * undefined; the context stays usable. */
 #define SLM_OPT_TEST_STALL 4
+/* 1 = the persistent step streams bf16 copies of its matrices (rounded to
+ * nearest once per model, on the first request) with f32 arithmetic, caches
+ * and state: half the weight bytes per token.  Not a parity mode: logits
+ * differ from f32 weights by the weights' rounding.  Needs the persistent
+ * kernel with its fused phases and d_model a multiple of 256, at most 768;
+ * SLM_ERR_INVALID otherwise.  No counterpart in the reference (its MLX
+ * backend offers fp16 weights, src/mlx.rs:14-23). */
+#define SLM_OPT_BF16 5
 int slm_session_set(slm_session* se, int option, int64_t value);
 
 /* Counters of a session:

@@ -37,6 +37,7 @@ SLM_OPT_GRAPH = 1
 SLM_OPT_MEGA = 2
 SLM_OPT_TRACE = 3
 SLM_OPT_TEST_STALL = 4
+SLM_OPT_BF16 = 5
 SLM_STAT_STEP_KERNELS, SLM_STAT_GRAPHS, SLM_STAT_MEGA, SLM_STAT_PHASES = 1, 2, 3, 4
 SIZE_MAX = (1 << 64) - 1
 
@@ -259,6 +260,7 @@ class Buf:
 
     def __init__(self, ctx: Context, handle):
         self.ctx = ctx
+        self._ctx_h = ctx._h  # stays valid while the buffer lives (the library defers the context's release)
         self._h = handle
         self._free = lib().slm_buf_free
 
@@ -282,7 +284,7 @@ class Buf:
     def read(self, n: int | None = None) -> np.ndarray:
         n = len(self) if n is None else n
         out = np.empty(n, dtype=np.float32)
-        _check(lib().slm_read(self.ctx._h, self._h, n, out.ctypes.data_as(_f32p)))
+        _check(lib().slm_read(self._ctx_h, self._h, n, out.ctypes.data_as(_f32p)))
         return out
 
 
@@ -518,6 +520,10 @@ class Session:
     def set_mega(self, on: bool) -> None:
         """Run m = 1 steps as one persistent kernel (where the model allows it)."""
         _check(lib().slm_session_set(self._h, SLM_OPT_MEGA, 1 if on else 0))
+
+    def set_bf16(self, on: bool) -> None:
+        """Stream bf16 copies of the weights in persistent steps (f32 arithmetic; not a parity mode)."""
+        _check(lib().slm_session_set(self._h, SLM_OPT_BF16, 1 if on else 0))
 
     def set_stall_test(self, on: bool) -> None:
         """Test hook: the next persistent steps wait for a barrier arrival that never comes."""

@@ -84,6 +84,26 @@ __device__ __forceinline__ float lds1(uint32_t a) {
   asm volatile("ld.shared.f32 %0, [%1];" : "=f"(v) : "r"(a));
   return v;
 }
+// 16 bytes of weights in shared memory as floats: 4 f32, or 8 bf16 (a bf16
+// value is the top half of an f32, so widening is exact).
+template <int WB>
+__device__ __forceinline__ void wchunk(uint32_t a, float (&v)[16 / WB]) {
+  const float4 x = lds4(a);
+  if constexpr (WB == 4) {
+    v[0] = x.x, v[1] = x.y, v[2] = x.z, v[3] = x.w;
+  } else {
+    const uint32_t u[4] = {__float_as_uint(x.x), __float_as_uint(x.y), __float_as_uint(x.z), __float_as_uint(x.w)};
+#pragma unroll
+    for (int i = 0; i < 4; i++) v[2 * i] = __uint_as_float(u[i] << 16), v[2 * i + 1] = __uint_as_float(u[i] & 0xffff0000u);
+  }
+}
+template <int E>
+__device__ __forceinline__ float dotn(const float (&w)[E], const float (&x)[E], float acc) {
+#pragma unroll
+  for (int e = 0; e < E; e++) acc = fmaf(w[e], x[e], acc);
+  return acc;
+}
+
 __device__ __forceinline__ void st_release_cta_shared(unsigned* p, unsigned v) {
   asm volatile("st.release.cta.shared.u32 [%0], %1;" ::"r"(saddr(p)), "r"(v) : "memory");
 }
@@ -286,9 +306,10 @@ __device__ __forceinline__ bool is_pair(const Phase& ph) {
 
 // Logical outputs per tile of a GEMV phase (a fused MLP unit takes three rows:
 // gate, up and downᵀ).
-__device__ __forceinline__ int tile_outs(const Phase& ph) {
-  int rows = kStageBytes / (ph.cols * 4);
-  if (rows > 16) rows = 16;
+__device__ __forceinline__ int tile_outs(const Phase& ph, int wb) {
+  int rows = kStageBytes / (ph.cols * wb);
+  const int most = wb == 2 ? 32 : 16;  // two (f32) or four (bf16) rows per consumer warp
+  if (rows > most) rows = most;
   if (ph.out_mode == OUT_MLP) return rows / 3;
   return is_pair(ph) ? rows / 2 : rows;
 }
@@ -400,8 +421,8 @@ struct Walker {
         T.n = 1;
         T.keep = ph.l2keep;
         T.step = step, T.mut = 0;
-        T.src[0] = ph.wo + ((size_t)h * P->d + (size_t)s * ph.orows) * kDH;
-        T.bytes[0] = T.total = (unsigned)ph.orows * kDH * 4;
+        T.src[0] = reinterpret_cast<const char*>(ph.wo) + ((size_t)h * P->d + (size_t)s * ph.orows) * kDH * P->wbytes;
+        T.bytes[0] = T.total = (unsigned)ph.orows * kDH * P->wbytes;
         T.off[0] = 0;
         extra = 0;
         return true;
@@ -421,15 +442,17 @@ struct Walker {
     T.step = step, T.mut = ph.kind != PH_GEMV;
     if (ph.kind == PH_GEMV) {
       const Segment& sg = ph.seg[seg];
-      const int Tn = tile_outs(ph);
+      const int Tn = tile_outs(ph, P->wbytes);
       int n = (int)min((long long)Tn, tend - t);
       int r0, r1;
       out_rows(ph, sg, (int)t, P->d, &r0, &r1);
-      const unsigned rowb = (unsigned)ph.cols * 4;
-      T.src[0] = sg.w + (size_t)r0 * ph.cols, T.bytes[0] = n * rowb, T.off[0] = 0, T.n = 1;
-      if (is_pair(ph)) T.src[1] = sg.w + (size_t)r1 * ph.cols, T.bytes[1] = n * rowb, T.off[1] = n * rowb, T.n = 2;
+      const unsigned rowb = (unsigned)ph.cols * P->wbytes;
+      const char* wb = reinterpret_cast<const char*>(sg.w);
+      T.src[0] = wb + (size_t)r0 * rowb, T.bytes[0] = n * rowb, T.off[0] = 0, T.n = 1;
+      if (is_pair(ph)) T.src[1] = wb + (size_t)r1 * rowb, T.bytes[1] = n * rowb, T.off[1] = n * rowb, T.n = 2;
       if (ph.out_mode == OUT_MLP)  // [gate n][up n][downᵀ n]
-        T.src[2] = ph.wt + (size_t)t * ph.cols, T.bytes[2] = n * rowb, T.off[2] = 2 * n * rowb, T.n = 3;
+        T.src[2] = reinterpret_cast<const char*>(ph.wt) + (size_t)t * rowb, T.bytes[2] = n * rowb,
+        T.off[2] = 2 * n * rowb, T.n = 3;
       t += n;
     } else if (ph.kind == PH_ATTN) {
       const int h = i / ph.splits;
@@ -552,7 +575,7 @@ __device__ void producer(const Plan& P, Smem& sm, char* ring, long long pos) {
 
 // GL: the plan has global-attention layers (G projection, GQA items, gap);
 // the kernel without them keeps the smaller code of the S/L path.
-template <bool GL>
+template <bool GL, int WB>
 struct Cons {
   const Plan& P;
   Smem& sm;
@@ -892,19 +915,26 @@ struct Cons {
   // warp walks the rows of a tile two at a time (two independent chains).
   // Partial sums land in sm.acc[column half][pair half][output] and are
   // combined, in a fixed order, in the epilogue.
-  template <int K>
+  // NC 16-byte weight chunks per lane per row half (WB bytes a weight).
+  template <int NC>
   __device__ void gemv_phase_k(const Phase& ph) {
+    constexpr int E = 16 / WB;
     const int G = gridDim.x;
     const int S = ph.cols > 1536 ? 2 : 1;
     const int span = ph.cols / S;
     const int sgi = warp % S, rowslot = warp / S, rstride = kConsumerWarps / S;
-    float4 xr[K];
+    float xr[NC][E];
     {
-      const float4* xin4 = reinterpret_cast<const float4*>(sm.xin) + sgi * span / 4 + lane;
+      const float* xin = sm.xin + sgi * span + lane * E;
 #pragma unroll
-      for (int k = 0; k < K; k++) xr[k] = xin4[32 * k];
+      for (int c = 0; c < NC; c++)
+#pragma unroll
+        for (int e = 0; e < E; e += 4) {
+          const float4 v = *reinterpret_cast<const float4*>(xin + 32 * E * c + e);
+          xr[c][e] = v.x, xr[c][e + 1] = v.y, xr[c][e + 2] = v.z, xr[c][e + 3] = v.w;
+        }
     }
-    const int T = tile_outs(ph);
+    const int T = tile_outs(ph, WB);
     const bool pair = is_pair(ph);
     for (int i = blockIdx.x; i < ph.items && ok; i += G) {
       int s, o0, o1;
@@ -913,23 +943,25 @@ struct Cons {
       for (int t0 = o0; t0 < o1; t0 += T) {
         const int n = min(T, o1 - t0);
         const int rows = pair ? 2 * n : n;
-        const float* w = take_warp();
+        const char* w = reinterpret_cast<const char*>(take_warp());
         unsigned long long c0 = P.trace && tid == 0 ? now_ns() : 0;
         for (int r = rowslot; r < rows; r += 2 * rstride) {
           const int r2 = r + rstride;
           const bool two = r2 < rows;
-          const uint32_t w0 = saddr(w + (size_t)r * ph.cols + sgi * span) + lane * 16;
-          const uint32_t w1 = saddr(w + (size_t)(two ? r2 : r) * ph.cols + sgi * span) + lane * 16;
+          const uint32_t w0 = saddr(w + ((size_t)r * ph.cols + sgi * span) * WB) + lane * 16;
+          const uint32_t w1 = saddr(w + ((size_t)(two ? r2 : r) * ph.cols + sgi * span) * WB) + lane * 16;
           float a0 = 0.0f, b0 = 0.0f, a1 = 0.0f, b1 = 0.0f;
 #pragma unroll
-          for (int k = 0; k < K; k++) {
-            float4 u = lds4(w0 + 512 * k), v = lds4(w1 + 512 * k);
-            if (k & 1) {
-              b0 = dot4(u, xr[k], b0);
-              b1 = dot4(v, xr[k], b1);
+          for (int c = 0; c < NC; c++) {
+            float u[E], v[E];
+            wchunk<WB>(w0 + 512 * c, u);
+            wchunk<WB>(w1 + 512 * c, v);
+            if (c & 1) {
+              b0 = dotn(u, xr[c], b0);
+              b1 = dotn(v, xr[c], b1);
             } else {
-              a0 = dot4(u, xr[k], a0);
-              a1 = dot4(v, xr[k], a1);
+              a0 = dotn(u, xr[c], a0);
+              a1 = dotn(v, xr[c], a1);
             }
           }
           a0 += b0;
@@ -976,7 +1008,7 @@ struct Cons {
 #pragma unroll
       for (int k = 0; k < K; k++) xr[k] = xin4[32 * k];
     }
-    const int T = tile_outs(ph);
+    const int T = tile_outs(ph, 4);  // f32 weights only (bf16 plans use mlp_items_w)
     unsigned tile = 0;
     for (int i = blockIdx.x; i < ph.items && ok; i += G) {
       int s, o0, o1;
@@ -1036,43 +1068,51 @@ struct Cons {
   // (columns 4·lane + 128·k).  No CTA barrier per tile; the eight partials are
   // summed once at the end, in a fixed order (needs 4·d ≤ kMaxCols floats of
   // sm.xin).
-  template <int K>
+  template <int NC>
   __device__ __forceinline__ void mlp_items_w(const Phase& ph, float (&y)[kMaxD / 256]) {
+    constexpr int E = 16 / WB;
     const int G = gridDim.x, d = ph.cols;
-    float4 xr[K], yv[K];
+    // Lane `lane` owns columns (lane + 32·c)·E … + E − 1 of x and of its partial.
+    float xr[NC][E], yv[NC][E];
     {
-      const float4* xin4 = reinterpret_cast<const float4*>(sm.xin) + lane;
-      const float4* xraw4 = reinterpret_cast<const float4*>(sm.xraw) + lane;
       const bool res = blockIdx.x == 0 && warp == 0;  // the residual, once per slot
 #pragma unroll
-      for (int k = 0; k < K; k++) {
-        xr[k] = xin4[32 * k];
-        yv[k] = res ? xraw4[32 * k] : make_float4(0.f, 0.f, 0.f, 0.f);
-      }
+      for (int c = 0; c < NC; c++)
+#pragma unroll
+        for (int e = 0; e < E; e += 4) {
+          const int col = (lane + 32 * c) * E + e;
+          const float4 v = *reinterpret_cast<const float4*>(sm.xin + col);
+          const float4 r = res ? *reinterpret_cast<const float4*>(sm.xraw + col) : make_float4(0.f, 0.f, 0.f, 0.f);
+          xr[c][e] = v.x, xr[c][e + 1] = v.y, xr[c][e + 2] = v.z, xr[c][e + 3] = v.w;
+          yv[c][e] = r.x, yv[c][e + 1] = r.y, yv[c][e + 2] = r.z, yv[c][e + 3] = r.w;
+        }
     }
-    const int T = tile_outs(ph);
+    const int T = tile_outs(ph, WB);
+    const size_t rowb = (size_t)d * WB;
     int u = 0;  // units of this CTA before the current tile
     for (int i = blockIdx.x; i < ph.items && ok; i += G) {
       int s, o0, o1;
       gemv_item(ph, i, &s, &o0, &o1);
       for (int t0 = o0; t0 < o1; t0 += T) {
         const int n = min(T, o1 - t0);
-        const float* w = take_warp();
+        const char* w = reinterpret_cast<const char*>(take_warp());
         unsigned long long c0 = P.trace && tid == 0 ? now_ns() : 0;
         for (int j = (warp - u % kConsumerWarps + kConsumerWarps) % kConsumerWarps; j < n; j += kConsumerWarps) {
-          const uint32_t g0 = saddr(w + (size_t)j * d) + lane * 16;
-          const uint32_t u0 = saddr(w + (size_t)(n + j) * d) + lane * 16;
-          const uint32_t r0 = saddr(w + (size_t)(2 * n + j) * d) + lane * 16;
+          const uint32_t g0 = saddr(w + (size_t)j * rowb) + lane * 16;
+          const uint32_t u0 = saddr(w + (size_t)(n + j) * rowb) + lane * 16;
+          const uint32_t r0 = saddr(w + (size_t)(2 * n + j) * rowb) + lane * 16;
           float a0 = 0.0f, b0 = 0.0f, a1 = 0.0f, b1 = 0.0f;
 #pragma unroll
-          for (int k = 0; k < K; k++) {
-            float4 gq = lds4(g0 + 512 * k), uq = lds4(u0 + 512 * k);
-            if (k & 1) {
-              b0 = dot4(gq, xr[k], b0);
-              b1 = dot4(uq, xr[k], b1);
+          for (int c = 0; c < NC; c++) {
+            float gq[E], uq[E];
+            wchunk<WB>(g0 + 512 * c, gq);
+            wchunk<WB>(u0 + 512 * c, uq);
+            if (c & 1) {
+              b0 = dotn(gq, xr[c], b0);
+              b1 = dotn(uq, xr[c], b1);
             } else {
-              a0 = dot4(gq, xr[k], a0);
-              a1 = dot4(uq, xr[k], a1);
+              a0 = dotn(gq, xr[c], a0);
+              a1 = dotn(uq, xr[c], a1);
             }
           }
           a0 += b0;
@@ -1084,10 +1124,11 @@ struct Cons {
           }
           const float h = silu_mul(a0, a1);
 #pragma unroll
-          for (int k = 0; k < K; k++) {
-            const float4 dq = lds4(r0 + 512 * k);
-            yv[k].x = fmaf(h, dq.x, yv[k].x), yv[k].y = fmaf(h, dq.y, yv[k].y);
-            yv[k].z = fmaf(h, dq.z, yv[k].z), yv[k].w = fmaf(h, dq.w, yv[k].w);
+          for (int c = 0; c < NC; c++) {
+            float dq[E];
+            wchunk<WB>(r0 + 512 * c, dq);
+#pragma unroll
+            for (int e = 0; e < E; e++) yv[c][e] = fmaf(h, dq[e], yv[c][e]);
           }
         }
         release();
@@ -1097,20 +1138,25 @@ struct Cons {
       if (!all_ok()) return;
     }
     // ((w0 + w4) + (w1 + w5)) + ((w2 + w6) + (w3 + w7)) per column, through sm.xin.
-    float4* buf = reinterpret_cast<float4*>(sm.xin);  // [4][d / 4]
-    const int d4 = d / 4;
+    float* buf = sm.xin;  // [4][d]
     consumers_sync();  // every warp has read its x from sm.xin
     if (warp >= 4)
 #pragma unroll
-      for (int k = 0; k < K; k++) buf[(warp - 4) * d4 + lane + 32 * k] = yv[k];
+      for (int c = 0; c < NC; c++)
+#pragma unroll
+        for (int e = 0; e < E; e += 4)
+          *reinterpret_cast<float4*>(buf + (warp - 4) * d + (lane + 32 * c) * E + e) =
+              make_float4(yv[c][e], yv[c][e + 1], yv[c][e + 2], yv[c][e + 3]);
     consumers_sync();
     if (warp < 4)
 #pragma unroll
-      for (int k = 0; k < K; k++) {
-        float4& o = buf[warp * d4 + lane + 32 * k];
-        const float4 v = o;
-        o = make_float4(yv[k].x + v.x, yv[k].y + v.y, yv[k].z + v.z, yv[k].w + v.w);
-      }
+      for (int c = 0; c < NC; c++)
+#pragma unroll
+        for (int e = 0; e < E; e += 4) {
+          float4& o = *reinterpret_cast<float4*>(buf + warp * d + (lane + 32 * c) * E + e);
+          const float4 v = o;
+          o = make_float4(yv[c][e] + v.x, yv[c][e + 1] + v.y, yv[c][e + 2] + v.z, yv[c][e + 3] + v.w);
+        }
     consumers_sync();
     const float* b = sm.xin;
 #pragma unroll
@@ -1140,7 +1186,7 @@ struct Cons {
 #pragma unroll
     for (int q = 0; q < kMaxD / 256; q++) y[q] = 0.0f;
     if (!P.mlp_cta) {
-      switch (d / 128) {
+      switch (d / (512 / WB)) {  // 16-byte chunks per lane
         case 1: mlp_items_w<1>(ph, y); break;
         case 2: mlp_items_w<2>(ph, y); break;
         case 3: mlp_items_w<3>(ph, y); break;
@@ -1148,7 +1194,7 @@ struct Cons {
         case 6: mlp_items_w<6>(ph, y); break;
         default: break;  // d > 768 takes the per-tile CTA split (mlp_cta set by the plan)
       }
-    } else {
+    } else if constexpr (WB == 4) {  // the row-split variant reads f32 tiles only
 #pragma unroll
       for (int q = 0; q < kMaxD / 256; q++) {
         const int c = tid + 256 * q;
@@ -1191,7 +1237,7 @@ struct Cons {
     prologue(ph);
     if (t0) pro_ns += now_ns() - t0;
     if (!ok || blockIdx.x >= ph.items) return;
-    const int K = ph.cols / (ph.cols > 1536 ? 2 : 1) / 128;
+    const int K = ph.cols / (ph.cols > 1536 ? 2 : 1) / (512 / WB);  // 16-byte chunks per lane and row half
     switch (K) {
       case 1: gemv_phase_k<1>(ph); break;
       case 2: gemv_phase_k<2>(ph); break;
@@ -1574,22 +1620,29 @@ struct Cons {
       }
     }
     consumers_sync();
-    // Row r = tid / 4 (+ 64·k): thread q4 takes columns 4·q4 + 16·i … + 3.
+    // Row r = tid / 4 (+ 64·k): thread q4 takes the 16-byte chunks q4 + 4·i
+    // of the row (E columns each).
     bool bad = false;
     if (ok) {
-      const float4* y4 = reinterpret_cast<const float4*>(sm.vec[0]);
-      float4 yq[4];
+      constexpr int E = 16 / WB, CPT = kDH / E / 4;
+      float yq[CPT][E];
 #pragma unroll
-      for (int i = 0; i < 4; i++) yq[i] = y4[q4 + 4 * i];
+      for (int i = 0; i < CPT; i++)
+#pragma unroll
+        for (int e = 0; e < E; e++) yq[i][e] = sm.vec[0][(q4 + 4 * i) * E + e];
 #pragma unroll
       for (int k = 0; k < RQ; k++) {
         const int r = (tid >> 2) + 64 * k;
         if (64 * k >= R) break;  // uniform
         float v = 0.0f;
         if (r < R) {
-          const uint32_t a = saddr(w + (size_t)r * kDH) + q4 * 16;
+          const uint32_t a = saddr(reinterpret_cast<const char*>(w) + (size_t)r * kDH * WB) + q4 * 16;
 #pragma unroll
-          for (int i = 0; i < 4; i++) v = dot4(lds4(a + 64 * i), yq[i], v);
+          for (int i = 0; i < CPT; i++) {
+            float wq[E];
+            wchunk<WB>(a + 64 * i, wq);
+            v = dotn(wq, yq[i], v);
+          }
         }
         v += __shfl_xor_sync(0xffffffffu, v, 1);
         v += __shfl_xor_sync(0xffffffffu, v, 2);
@@ -1807,7 +1860,7 @@ struct Cons {
   }
 };
 
-template <bool GL>
+template <bool GL, int WB>
 __global__ void __launch_bounds__(kThreads, 1) k_decode_mega(const __grid_constant__ Plan P) {
   extern __shared__ __align__(1024) char smem_raw[];
   Smem& sm = *reinterpret_cast<Smem*>(smem_raw);
@@ -1827,7 +1880,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_mega(const __grid_consta
     if (threadIdx.x == kConsumerWarps * 32) producer(P, sm, ring, pos);
     return;
   }
-  Cons<GL> c(P, sm, ring, pos, *P.epoch);
+  Cons<GL, WB> c(P, sm, ring, pos, *P.epoch);
   c.run();
 }
 
@@ -1838,17 +1891,18 @@ static_assert(((sizeof(Smem) + 1023) / 1024) * 1024 + (size_t)kStages * kStageBy
               "decode kernel shared memory above the 227 KB an sm_100 CTA may use");
 
 void prepare() {
-  SLM_CUDA(
-      cudaFuncSetAttribute(k_decode_mega<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_bytes()));
-  SLM_CUDA(
-      cudaFuncSetAttribute(k_decode_mega<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_bytes()));
+  for (auto f : {k_decode_mega<false, 4>, k_decode_mega<true, 4>, k_decode_mega<false, 2>, k_decode_mega<true, 2>})
+    SLM_CUDA(cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_bytes()));
 }
 
 int blocks_per_sm() {
-  int a = 0, b = 0;
-  SLM_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&a, k_decode_mega<false>, kThreads, smem_bytes()));
-  SLM_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, k_decode_mega<true>, kThreads, smem_bytes()));
-  return a < b ? a : b;
+  int least = 1 << 30;
+  for (auto f : {k_decode_mega<false, 4>, k_decode_mega<true, 4>, k_decode_mega<false, 2>, k_decode_mega<true, 2>}) {
+    int a = 0;
+    SLM_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&a, f, kThreads, smem_bytes()));
+    least = a < least ? a : least;
+  }
+  return least;
 }
 
 void launch(const Plan& plan, int grid, cudaStream_t st) {
@@ -1862,10 +1916,11 @@ void launch(const Plan& plan, int grid, cudaStream_t st) {
   attr[0].val.cooperative = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
+  const bool bf = plan.wbytes == 2;
   if (plan.global)
-    SLM_CUDA(cudaLaunchKernelEx(&cfg, k_decode_mega<true>, plan));
+    SLM_CUDA(cudaLaunchKernelEx(&cfg, bf ? k_decode_mega<true, 2> : k_decode_mega<true, 4>, plan));
   else
-    SLM_CUDA(cudaLaunchKernelEx(&cfg, k_decode_mega<false>, plan));
+    SLM_CUDA(cudaLaunchKernelEx(&cfg, bf ? k_decode_mega<false, 2> : k_decode_mega<false, 4>, plan));
 }
 
 }  // namespace mega

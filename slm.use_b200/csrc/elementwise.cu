@@ -3,6 +3,8 @@
 // model step uses in their place (embedding + copy, rope + ring store,
 // l2norm of q/k, the loop input, the G layer's logn scaling and key shift).
 // Row reductions use one CTA per row, so results do not depend on timing.
+#include <cuda_bf16.h>
+
 #include "common.cuh"
 #include "kernels.cuh"
 
@@ -326,6 +328,19 @@ void ew_head_blocks(float* dst, const float* src, size_t rows, size_t heads, siz
   if (!rows || !heads || !dh) return;
   k_head_blocks<<<ew_grid(rows * heads * dh), EW, 0, st>>>(dst, src, rows, (int)heads, (int)dh);
   SLM_LAUNCHED("k_head_blocks");
+}
+
+namespace {
+__global__ void k_to_bf16(__nv_bfloat16* dst, const float* src, size_t n) {
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+    dst[i] = __float2bfloat16_rn(src[i]);
+}
+}  // namespace
+
+void ew_to_bf16(void* dst, const float* src, size_t n, cudaStream_t st) {
+  if (!n) return;
+  k_to_bf16<<<ew_grid(n), EW, 0, st>>>(static_cast<__nv_bfloat16*>(dst), src, n);
+  SLM_LAUNCHED("k_to_bf16");
 }
 
 void ew_transpose(float* dst, const float* src, size_t rows, size_t cols, cudaStream_t st) {

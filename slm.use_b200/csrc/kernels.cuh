@@ -120,6 +120,8 @@ void ew_add_row(float* y, const float* x, const float* row, size_t m, size_t d, 
 void ew_scale_rows(float* y, const float* x, const float* f, size_t m, size_t d, cudaStream_t st);
 void ew_mix(float* y, const float* a, const float* b, size_t n, float t, cudaStream_t st);
 void ew_transpose(float* dst, const float* src, size_t rows, size_t cols, cudaStream_t st);
+// dst[i] = src[i] rounded to bf16 (nearest, ties to even).
+void ew_to_bf16(void* dst, const float* src, size_t n, cudaStream_t st);
 void ew_head_blocks(float* dst, const float* src, size_t rows, size_t heads, size_t dh, cudaStream_t st);
 void ew_silu_mul(float* y, const float* g, const float* u, size_t n, cudaStream_t st);
 void ew_loop_in(float* x, const float* s, const float* e, const float* row, size_t m, size_t d, cudaStream_t st);

@@ -182,6 +182,9 @@ struct Plan {
   // L2 priority of the bulk copies: 0 none; 1 weights of phases marked l2keep
   // evict_last, every other tile evict_first; 2 the same with the others normal.
   int l2mode;
+  // Bytes of one weight value in the GEMV, MLP and o tiles: 4 (f32) or 2
+  // (bf16 copies of the same matrices; caches and arithmetic stay f32).
+  int wbytes;
   // Most tiles a producer keeps in flight (issued, not landed); 1 … kStages.
   int inflight;
   // Steps of one launch (greedy decode): step s + 1 takes the arg-max of step

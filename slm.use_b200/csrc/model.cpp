@@ -43,6 +43,8 @@ struct Mat {
   const void* planes = nullptr;  // bf16 parts for chunk linears (gemm_bf16x3.cu), in the model's plane arena
   const float* t = nullptr;      // down only: the transpose ([cols][rows]) read by the fused decode MLP
   const float* hb = nullptr;     // o of S and L blocks: per-head column blocks [heads][rows][dh] (mixer + o fused)
+  // bf16 copies of w, t and hb for the persistent step's bf16 plans (SLM_OPT_BF16), or null.
+  const void *w16 = nullptr, *t16 = nullptr, *hb16 = nullptr;
 };
 
 struct Block {
@@ -72,6 +74,7 @@ struct slm_model {
   float* arena = nullptr;
   void* planes = nullptr;  // bf16x3 parts of the block and inject matrices
   float* tarena = nullptr;  // transposed down matrices (Mat::t)
+  void* arena16 = nullptr;  // bf16 copies of the persistent step's matrices (Mat::w16, t16, hb16), built on request
   std::vector<Block> prelude, core, coda;
   Mat embed, inject, loop_embed;
   bool looped = false;
@@ -129,6 +132,7 @@ struct slm_session {
   unsigned long long *tq = nullptr, *tpart = nullptr, *tmix = nullptr, *tdec = nullptr, *te = nullptr;
   bool plan_stale = false;               // a global cache moved: the phase descriptors need refreshing
   bool keys_stale = false;               // state was written from the host: the next shifted keys need recomputing
+  bool wbf16 = false;                    // the persistent step reads bf16 copies of its matrices
   int in_batches = 0;                    // batches holding this session
   uint32_t* argmax_dev = nullptr;        // the persistent step's arg-max of its logits
   unsigned* merge_cnt = nullptr;         // attention slice counters of the graph path (zero between launches)
@@ -578,6 +582,53 @@ std::string mega_unsupported(const slm_model* md) {
   return "";
 }
 
+// bf16 copies (round to nearest even) of every matrix the persistent step
+// streams, in one device arena: each block's projections, o (row-major and
+// per-head blocks), up, down (transposed), the inject matrix and the tied
+// head.  Built once per model, on the first request.
+void build_bf16(slm_model* md) {
+  if (md->arena16) return;
+  std::vector<std::pair<const float*, const void**>> parts;
+  std::vector<size_t> sizes;
+  auto add = [&](const float* src, const void** dst, size_t n) {
+    if (!src) return;
+    parts.emplace_back(src, dst);
+    sizes.push_back(n);
+  };
+  auto mat = [&](Mat& m) {
+    const size_t n = m.rows * m.cols;
+    add(m.w, &m.w16, n);
+    add(m.t, &m.t16, n);
+    add(m.hb, &m.hb16, n);
+  };
+  for (auto* bs : {&md->prelude, &md->core, &md->coda})
+    for (auto& b : *bs)
+      for (Mat* m : {&b.qkv, &b.o, &b.up, &b.down, &b.qkvg, &b.decay, &b.q, &b.kv}) mat(*m);
+  mat(md->inject);
+  mat(md->embed);
+  size_t total = 0;
+  for (size_t n : sizes) total += (n * 2 + 255) / 256 * 256;
+  char* at = static_cast<char*>(dev_alloc(total));
+  md->arena16 = at;
+  cudaStream_t s = md->ctx->stream;
+  for (size_t i = 0; i < parts.size(); i++) {
+    ew_to_bf16(at, parts[i].first, sizes[i], s);
+    *parts[i].second = at;
+    at += (sizes[i] * 2 + 255) / 256 * 256;
+  }
+  SLM_CUDA(cudaStreamSynchronize(s));
+}
+
+// Why the persistent step cannot read bf16 weights for this session ("" if it can).
+std::string bf16_unsupported(const slm_session* se) {
+  const Config& c = se->model->cfg;
+  if (!se->mega_ok) return "the persistent decode kernel is unavailable: " + se->mega_why;
+  if (!se->fuse_mlp || !se->fuse_ao) return "bf16 weights need the fused MLP and mixer phases";
+  if (se->plan_host.mlp_cta) return "bf16 weights need d_model <= 768";
+  if (c.d % 256 != 0) return "bf16 weights need d_model a multiple of 256";
+  return "";
+}
+
 // The m = 1 step as phases (decode_mega.cu), for this session's buffers.
 // refresh: only regenerate the phase descriptors (a global cache moved or
 // grew); counters, outputs and the rest of the plan stay.
@@ -587,6 +638,11 @@ void build_plan(slm_session* se, bool refresh = false) {
   const Config& c = md->cfg;
   const int G = se->grid;
   const int d = (int)c.d, H = (int)c.heads;
+  // The matrices the step streams: f32, or their bf16 copies (SLM_OPT_BF16).
+  const bool bf = se->wbf16;
+  auto W = [&](const Mat& m) { return bf ? static_cast<const float*>(m.w16) : m.w; };
+  auto WT = [&](const Mat& m) { return bf ? static_cast<const float*>(m.t16) : m.t; };
+  auto WH = [&](const Mat& m) { return bf ? static_cast<const float*>(m.hb16) : m.hb; };
   std::vector<Phase> ph;
   auto per = [&](int rows, int items_wanted, int multiple) {
     int p = (rows + items_wanted - 1) / items_wanted;
@@ -700,8 +756,8 @@ void build_plan(slm_session* se, bool refresh = false) {
   auto block_mlp = [&](const Block& b, float* X) {
     const int F = (int)b.down.cols;
     if (se->fuse_mlp) {
-      Phase u = gemv(d, IN_RMS, X, nullptr, nullptr, b.norm2, nullptr, OUT_MLP, seg(b.up.w, F, per(F, G, 1), nullptr));
-      u.wt = b.down.t;
+      Phase u = gemv(d, IN_RMS, X, nullptr, nullptr, b.norm2, nullptr, OUT_MLP, seg(W(b.up), F, per(F, G, 1), nullptr));
+      u.wt = WT(b.down);
       read_x(u, X);
       u.sync = u.fx_in ? 0 : 1;  // after a G block's o, x is a float buffer
       u.fx_out = se->fx + slot_words * next_slot++;
@@ -710,7 +766,7 @@ void build_plan(slm_session* se, bool refresh = false) {
       return;
     }
     ph.push_back(gemv(d, IN_RMS, X, nullptr, nullptr, b.norm2, nullptr, OUT_SILU,
-                      seg(b.up.w, F, per(F, G, 1), se->mid)));
+                      seg(W(b.up), F, per(F, G, 1), se->mid)));
     ph.push_back(gemv(F, IN_PLAIN, se->mid, nullptr, nullptr, nullptr, nullptr, OUT_ADD,
                       seg(b.down.w, d, per(d, G, 1), X)));
     ph.back().res_smem = 1;
@@ -726,7 +782,7 @@ void build_plan(slm_session* se, bool refresh = false) {
     const float* ia = in.mode == IN_RMS ? X : in.a;
     if (b.kind == 'S') {
       Phase p = gemv(d, in.mode, ia, in.b, in.c, b.norm1, in.xout, OUT_ROPE,
-                     seg(b.qkv.w, 3 * d / 2, per(3 * d / 2, G, 8), nullptr));
+                     seg(W(b.qkv), 3 * d / 2, per(3 * d / 2, G, 8), nullptr));
       p.q = se->q, p.kc = st.k, p.vc = st.v, p.cap = (long long)st.cap, p.inv_freq = md->inv_freq;
       p.tq = se->tq;
       read_x(p, ia);
@@ -741,7 +797,7 @@ void build_plan(slm_session* se, bool refresh = false) {
       a.y = se->y, a.scale = scale, a.items = H * splits;
       a.tq = se->tq, a.tkv = se->tq + d, a.tpart = se->tpart, a.tag_in = proj;
       if (fuse_ao && b.o.hb) {
-        a.wo = b.o.hb;
+        a.wo = WH(b.o);
         a.orows = d / splits;
         a.cnt = se->fx + nslots * slot_words + H * next_cnt++;
         a.in_a = X;
@@ -758,9 +814,9 @@ void build_plan(slm_session* se, bool refresh = false) {
       const int kd = kh * kDH;
       const int qi = std::max(1, G * d / (d + 2 * kd)), ki = std::max(1, G - qi);
       Phase p = gemv(d, IN_RMS_E, X, nullptr, b.norm_e, b.norm1, c.kshift ? st.prev : nullptr, OUT_G,
-                     seg(b.q.w, d, per(d, qi, 1), se->q));
+                     seg(W(b.q), d, per(d, qi, 1), se->q));
       p.nseg = 2;
-      p.seg[1] = seg(b.kv.w, 2 * kd, per(2 * kd, ki, 1), nullptr);
+      p.seg[1] = seg(W(b.kv), 2 * kd, per(2 * kd, ki, 1), nullptr);
       p.items = p.seg[0].items + p.seg[1].items;
       p.kc = st.k, p.vc = st.v, p.cap = (long long)st.cap, p.heads = kh, p.kshift = c.kshift ? 1 : 0;
       p.inv_log = c.logn ? 1.0f / std::log((float)c.logn) : 0.0f;
@@ -779,9 +835,9 @@ void build_plan(slm_session* se, bool refresh = false) {
       ph.push_back(a);
     } else {
       Phase p = gemv(d, in.mode, ia, in.b, in.c, b.norm1, in.xout, OUT_STORE,
-                     seg(b.qkvg.w, 4 * d, per(4 * d, std::max(1, G - 1), 1), se->mix));
+                     seg(W(b.qkvg), 4 * d, per(4 * d, std::max(1, G - 1), 1), se->mix));
       p.nseg = 2;
-      p.seg[1] = seg(b.decay.w, H, per(H, 1, 1), se->dec);
+      p.seg[1] = seg(W(b.decay), H, per(H, 1, 1), se->dec);
       p.items = p.seg[0].items + p.seg[1].items;
       p.seg[0].tout = se->tmix, p.seg[1].tout = se->tdec;
       read_x(p, ia);
@@ -797,7 +853,7 @@ void build_plan(slm_session* se, bool refresh = false) {
       if (fuse_ao && b.o.hb) {  // every split of a head runs the GLA, every split its o rows
         g.items = H * splits;
         g.splits = splits;
-        g.wo = b.o.hb;
+        g.wo = WH(b.o);
         g.orows = d / splits;
         g.cnt = se->fx + nslots * slot_words + H * next_cnt++;
         g.in_a = X;
@@ -813,13 +869,13 @@ void build_plan(slm_session* se, bool refresh = false) {
     // normalising prologue left it in shared memory on every CTA.  After an
     // S mixer, o's input is merged from the attention partials.
     if (b.kind == 'S' || b.kind == 'G') {
-      Phase o = gemv(d, IN_ATTN, attn_part, nullptr, nullptr, nullptr, nullptr, OUT_ADD, seg(b.o.w, d, per(d, G, 1), X));
+      Phase o = gemv(d, IN_ATTN, attn_part, nullptr, nullptr, nullptr, nullptr, OUT_ADD, seg(W(b.o), d, per(d, G, 1), X));
       o.heads = H, o.splits = b.kind == 'G' ? gsplits : splits;
       o.tpart = se->tpart, o.tag_in = (int)ph.size() - 1;  // the attention phase's partials
       o.sync = 1;
       ph.push_back(o);
     } else {
-      ph.push_back(gemv(d, IN_PLAIN, se->y, nullptr, nullptr, nullptr, nullptr, OUT_ADD, seg(b.o.w, d, per(d, G, 1), X)));
+      ph.push_back(gemv(d, IN_PLAIN, se->y, nullptr, nullptr, nullptr, nullptr, OUT_ADD, seg(W(b.o), d, per(d, G, 1), X)));
     }
     ph.back().res_smem = 1;
     fx_set(X, nullptr);  // o wrote the float x
@@ -831,7 +887,7 @@ void build_plan(slm_session* se, bool refresh = false) {
   if (md->looped) {
     inject_phase = (int)ph.size();
     ph.push_back(gemv(d, IN_PLAIN, X0, nullptr, nullptr, nullptr, nullptr, OUT_STORE,
-                      seg(md->inject.w, d, per(d, G, 1), se->e_proj)));
+                      seg(W(md->inject), d, per(d, G, 1), se->e_proj)));
     read_x(ph.back(), X0);
     ph.back().seg[0].tout = se->te;
     ph.back().sync = ph.back().fx_in ? 0 : 1;
@@ -852,7 +908,7 @@ void build_plan(slm_session* se, bool refresh = false) {
   for (size_t i = 0; i < md->coda.size(); i++)
     block(md->coda[i], se->coda[i], X, In{IN_RMS, nullptr, nullptr, nullptr, nullptr});
   ph.push_back(gemv(d, IN_RMS, X, nullptr, nullptr, md->norm_f, nullptr, OUT_LOGITS,
-                    seg(md->embed.w, (int)c.vocab, per((int)c.vocab, G, 1), se->logits)));
+                    seg(W(md->embed), (int)c.vocab, per((int)c.vocab, G, 1), se->logits)));
   read_x(ph.back(), X);
   ph.back().sync = ph.back().fx_in ? 0 : 1;
   SLM_REQUIRE(ph.size() < (1u << kTagPhaseBits), "too many phases for the decode kernel's tags");
@@ -897,6 +953,7 @@ void build_plan(slm_session* se, bool refresh = false) {
   // The unfused variants pass plain buffers between phases: a barrier before each.
   P.all_sync = !se->fuse_mlp || !fuse_ao ? 1 : 0;
   P.mlp_cta = d > kMaxCols / 4 || mlp_cta_setting() ? 1 : 0;
+  P.wbytes = bf ? 2 : 4;
   P.l2mode = l2mode_setting();
   {
     const char* e = std::getenv("SLM_MEGA_INFLIGHT");
@@ -1446,6 +1503,7 @@ void destroy_model(slm_model* md) {
     dev_free(md->arena);
     dev_free(md->planes);
     dev_free(md->tarena);
+    dev_free(md->arena16);
   }
   delete md;
   ctx_release(c);
@@ -1633,6 +1691,22 @@ int slm_session_set(slm_session* se, int option, int64_t value) {
         se->trace = static_cast<unsigned long long*>(alloc_zero(se, n * sizeof(unsigned long long)));
       }
       se->plan_host.trace = value ? se->trace : nullptr;
+      return;
+    }
+    if (option == SLM_OPT_BF16) {
+      Device dev(se->ctx);
+      const bool on = value != 0;
+      if (on) {
+        const std::string why = bf16_unsupported(se);
+        if (!why.empty()) fail(SLM_ERR_INVALID, "bf16 weights unavailable: " + why);
+        build_bf16(se->model);
+      }
+      if (on == se->wbf16) return;
+      SLM_CUDA(cudaStreamSynchronize(se->ctx->stream));
+      se->wbf16 = on;
+      build_plan(se, true);  // the phase descriptors point at the other copies
+      se->plan_host.wbytes = on ? 2 : 4;
+      SLM_CUDA(cudaStreamSynchronize(se->ctx->stream));
       return;
     }
     if (option == SLM_OPT_TEST_STALL) {
