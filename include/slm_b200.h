@@ -308,8 +308,9 @@ int slm_session_trace(slm_session* se, uint64_t* out, size_t cap, size_t* n_out)
  * independent sequences per GPU.
  *
  * The sessions must share the model and the loop count, appear once each,
- * have no global-attention layers, and outlive the batch (slm_session_free
- * fails while a session belongs to a batch).  Stepping a session on its own
+ * and outlive the batch (slm_session_free fails while a session belongs to a
+ * batch).  Global-attention caches grow per session (8192 positions, then
+ * doubled, as slm_step grows them) before the step that needs the room.  Stepping a session on its own
  * between batch steps is allowed.  After batch steps a session's own logits
  * (slm_logits) are those of its last own step; read the batch's with
  * slm_batch_logits. */

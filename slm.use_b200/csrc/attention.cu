@@ -126,9 +126,11 @@ __global__ void __launch_bounds__(kSplitThreads)
   const int s = blockIdx.x, h = blockIdx.y, i = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int sub = lane % G, grp = lane / G;
+  long long cap = g.cap;
   if (rows.pos) {
     K = rows.k[i];
     V = rows.v[i];
+    if (rows.cap) cap = rows.cap[i];
   }
   const long long p = rows.pos ? *rows.pos[i] : (pos_ptr ? pos_ptr[0] : g.pos0) + i;
   Range r = visible(p, g.reach, g.gap);
@@ -138,8 +140,8 @@ __global__ void __launch_bounds__(kSplitThreads)
   long long end = min(r.hi, start + chunk);
 
   const int kvh = h / (g.heads / g.key_heads);
-  const float* Kb = K + (size_t)kvh * g.cap * DH + sub * 8;
-  const float* Vb = V + (size_t)kvh * g.cap * DH + sub * 8;
+  const float* Kb = K + (size_t)kvh * cap * DH + sub * 8;
+  const float* Vb = V + (size_t)kvh * cap * DH + sub * 8;
   const float* qp = q + (size_t)i * ldq + (size_t)h * DH + sub * 8;
   float qv[8];
   {
@@ -153,7 +155,7 @@ __global__ void __launch_bounds__(kSplitThreads)
   // U cache rows per lane group per round: all their loads are issued before
   // any is used, and the running max / rescale is applied once per round.
   constexpr int U = 4;
-  const long long slot0 = start < end ? start % g.cap : 0;
+  const long long slot0 = start < end ? start % cap : 0;
   for (long long base = start + warp * PPW * U; base < end; base += (long long)WARPS * PPW * U) {
     float4 k0[U], k1[U], v0[U], v1[U];
     bool okk[U];
@@ -164,8 +166,8 @@ __global__ void __launch_bounds__(kSplitThreads)
       k0[u] = k1[u] = v0[u] = v1[u] = make_float4(0.f, 0.f, 0.f, 0.f);
       if (okk[u]) {
         long long sl = slot0 + (pp - start);
-        if (sl >= g.cap) sl -= g.cap;
-        if (sl >= g.cap) sl %= g.cap;
+        if (sl >= cap) sl -= cap;
+        if (sl >= cap) sl %= cap;
         const size_t slot = (size_t)sl;
         const float4* kr = reinterpret_cast<const float4*>(Kb + slot * DH);
         const float4* vr = reinterpret_cast<const float4*>(Vb + slot * DH);

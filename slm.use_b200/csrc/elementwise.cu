@@ -252,6 +252,41 @@ __global__ void k_rope_store_rows(const float* mix, size_t ldmix, const float* i
   }
 }
 
+// Batched global layers: row i belongs to its own session (position *posr[i],
+// caches kr[i] / vr[i] of capr[i] slots per head, previous input prev[i]).
+__global__ void k_gather_rows(float* dst, float* const* src, size_t m, size_t d) {
+  GRID_STRIDE(t, m * d) dst[t] = src[t / d][t % d];
+}
+__global__ void k_scatter_rows(float* const* dst, const float* src, size_t m, size_t d) {
+  GRID_STRIDE(t, m * d) dst[t / d][t % d] = src[t];
+}
+// As k_g_post, per row: q scaled by log1p(pos_i)/ln(logn), key and value
+// stored at slot pos_i of row i's cache (global caches never wrap).
+__global__ void k_g_post_rows(float* q, size_t d, size_t m, long long* const* posr, float inv_log, int logn,
+                              const float* keys, size_t ldk, const float* vals, size_t ldv, size_t kd, size_t dh,
+                              float* const* kr, float* const* vr, const long long* capr) {
+  GRID_STRIDE(t, m * d) {
+    const size_t i = t / d;
+    if (logn) q[t] = q[t] * (log1pf((float)(*posr[i])) * inv_log);
+  }
+  GRID_STRIDE(t, m * kd) {
+    const size_t i = t / kd, c = t % kd, hh = c / dh, e = c % dh;
+    const size_t cap = (size_t)capr[i], slot = (size_t)(*posr[i]);
+    if (slot >= cap) continue;
+    kr[i][(hh * cap + slot) * dh + e] = keys[i * ldk + c];
+    vr[i][(hh * cap + slot) * dh + e] = vals[i * ldv + c];
+  }
+}
+// kr[i][h][*posr[i] + off] = src[i][h·dh …], skipped past row i's capacity.
+__global__ void k_store_next_rows(float* const* kr, const float* src, long long* const* posr, long long off,
+                                  size_t m, size_t kh, size_t dh, const long long* capr) {
+  GRID_STRIDE(t, m * kh * dh) {
+    const size_t i = t / (kh * dh), c = t % (kh * dh), h = c / dh, e = c % dh;
+    const size_t cap = (size_t)capr[i], slot = (size_t)(*posr[i] + off);
+    if (slot < cap) kr[i][(h * cap + slot) * dh + e] = src[t];
+  }
+}
+
 __global__ void k_advance_rows(long long* const* posr, size_t m, unsigned* counter) {
   for (size_t i = threadIdx.x; i < m; i += blockDim.x) *posr[i] += 1;
   if (counter && threadIdx.x == 0) *counter += 1;
@@ -430,6 +465,30 @@ void ew_rope_store_rows(const float* mix, size_t ldmix, const float* inv, long l
   k_rope_store_rows<<<ew_grid(m * heads * (dh / 2)), EW, 0, st>>>(mix, ldmix, inv, posr, m, heads, dh, cap, qout,
                                                                   kr, vr);
   SLM_LAUNCHED("k_rope_store_rows");
+}
+void ew_gather_rows(float* dst, float* const* src, size_t m, size_t d, cudaStream_t st) {
+  if (!m) return;
+  k_gather_rows<<<ew_grid(m * d), EW, 0, st>>>(dst, src, m, d);
+  SLM_LAUNCHED("k_gather_rows");
+}
+void ew_scatter_rows(float* const* dst, const float* src, size_t m, size_t d, cudaStream_t st) {
+  if (!m) return;
+  k_scatter_rows<<<ew_grid(m * d), EW, 0, st>>>(dst, src, m, d);
+  SLM_LAUNCHED("k_scatter_rows");
+}
+void ew_g_post_rows(float* q, size_t d, size_t m, long long* const* posr, float inv_log, int logn, const float* keys,
+                    size_t ldk, const float* vals, size_t ldv, size_t kd, size_t dh, float* const* kr,
+                    float* const* vr, const long long* capr, cudaStream_t st) {
+  if (!m) return;
+  k_g_post_rows<<<ew_grid(m * d), EW, 0, st>>>(q, d, m, posr, inv_log, logn, keys, ldk, vals, ldv, kd, dh, kr, vr,
+                                               capr);
+  SLM_LAUNCHED("k_g_post_rows");
+}
+void ew_store_next_rows(float* const* kr, const float* src, long long* const* posr, long long off, size_t m, size_t kh,
+                        size_t dh, const long long* capr, cudaStream_t st) {
+  if (!m) return;
+  k_store_next_rows<<<ew_grid(m * kh * dh), EW, 0, st>>>(kr, src, posr, off, m, kh, dh, capr);
+  SLM_LAUNCHED("k_store_next_rows");
 }
 void ew_advance_rows(long long* const* posr, size_t m, unsigned* counter, cudaStream_t st) {
   k_advance_rows<<<1, 256, 0, st>>>(posr, m, counter);

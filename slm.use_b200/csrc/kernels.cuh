@@ -61,6 +61,7 @@ struct AttnRows {
   float* const* k = nullptr;
   float* const* v = nullptr;
   long long* const* pos = nullptr;
+  const long long* cap = nullptr;  // per-row capacities (global caches of different sizes), or null: g.cap
 };
 int attn_splits(const AttnGeom& g, long long max_span);
 size_t attn_part_floats(const AttnGeom& g, int nsplit);
@@ -148,6 +149,15 @@ void ew_store_next(float* kc, const float* src, const long long* pos_ptr, long l
 void ew_rope_store_rows(const float* mix, size_t ldmix, const float* inv, long long* const* posr, size_t m,
                         size_t heads, size_t dh, size_t cap, float* qout, float* const* kr, float* const* vr,
                         cudaStream_t st);
+// Batched global layers (row i: its session's position *posr[i], caches kr[i] /
+// vr[i] of capr[i] slots per head, previous input rows src/dst[i]).
+void ew_gather_rows(float* dst, float* const* src, size_t m, size_t d, cudaStream_t st);
+void ew_scatter_rows(float* const* dst, const float* src, size_t m, size_t d, cudaStream_t st);
+void ew_g_post_rows(float* q, size_t d, size_t m, long long* const* posr, float inv_log, int logn, const float* keys,
+                    size_t ldk, const float* vals, size_t ldv, size_t kd, size_t dh, float* const* kr,
+                    float* const* vr, const long long* capr, cudaStream_t st);
+void ew_store_next_rows(float* const* kr, const float* src, long long* const* posr, long long off, size_t m, size_t kh,
+                        size_t dh, const long long* capr, cudaStream_t st);
 // *posr[i] += 1 for every row; *counter += 1 when counter is set.
 void ew_advance_rows(long long* const* posr, size_t m, unsigned* counter, cudaStream_t st);
 // Greedy pick per row of logits [m][vocab] (first maximum, NaN never wins):

@@ -161,11 +161,14 @@ struct slm_batch {
   uint32_t* ids = nullptr;           // [n] this step's tokens (the arg-max writes the next ones)
   unsigned* merge_cnt = nullptr;     // [heads·n] attention slice counters (zero between launches)
   long long** posr = nullptr;        // [n] the sessions' device positions
-  std::vector<float**> tab;          // per layer instance, in step order: [3][n] k, v, s pointers
+  std::vector<float**> tab;          // per layer instance, in step order: [4][n] k, v, s, prev pointers
+  std::vector<long long*> caps;      // per layer instance: [n] cache capacities (global caches differ by session)
+  float* kvs = nullptr;              // [n][kv_heads·dh] shifted keys of global layers
   unsigned* out_index = nullptr;     // steps taken since the last reset
   uint32_t* outs = nullptr;          // [outs_cap][n] picked ids
   size_t outs_cap = 0;
   int nsplit = 1;
+  int gsplit = 1;  // attention splits of global layers (their reach grows with the position)
   cudaGraphExec_t graph = nullptr;
   unsigned long long graph_ws_gen = 0;  // the context's GEMM workspace generation the graph holds
   bool capturing = false;
@@ -1150,6 +1153,68 @@ void* balloc(slm_batch* bt, size_t bytes) {
   return p;
 }
 
+// The sessions' per-layer pointers and capacities, in step order (prelude,
+// each loop's core, coda), copied into the batch's device tables (whose
+// addresses the captured step holds).
+void batch_tables(slm_batch* bt) {
+  slm_model* md = bt->model;
+  const size_t n = bt->n;
+  std::vector<const LState*> inst;  // [instance][session], flattened
+  for (size_t i = 0; i < n; i++) {
+    slm_session* se = bt->ses[i];
+    size_t at = 0;
+    auto put = [&](const LState& st) {
+      if (inst.size() < (at + 1) * n) inst.resize((at + 1) * n);
+      inst[at * n + i] = &st;
+      at++;
+    };
+    for (auto& st : se->pre) put(st);
+    for (auto& l : se->core)
+      for (auto& st : l) put(st);
+    for (auto& st : se->coda) put(st);
+  }
+  cudaStream_t s = bt->ctx->stream;
+  std::vector<float*> host(4 * n);
+  std::vector<long long> caps(n);
+  for (size_t k = 0; k < bt->tab.size(); k++) {
+    for (size_t i = 0; i < n; i++) {
+      const LState* st = inst[k * n + i];
+      host[i] = st->k, host[n + i] = st->v, host[2 * n + i] = st->s, host[3 * n + i] = st->prev;
+      caps[i] = (long long)st->cap;
+    }
+    SLM_CUDA(cudaMemcpyAsync(bt->tab[k], host.data(), 4 * n * sizeof(float*), cudaMemcpyHostToDevice, s));
+    SLM_CUDA(cudaMemcpyAsync(bt->caps[k], caps.data(), n * sizeof(long long), cudaMemcpyHostToDevice, s));
+    SLM_CUDA(cudaStreamSynchronize(s));  // host arrays are reused for the next instance
+  }
+  (void)md;
+}
+
+// Global caches of every session hold the next step (grown on the device if
+// not); the batch's tables follow them.
+void batch_caps(slm_batch* bt) {
+  const Config& c = bt->model->cfg;
+  if ((c.prelude + c.core + c.coda).find('G') == std::string::npos) return;
+  bool grew = false;
+  for (auto* se : bt->ses) {
+    std::vector<size_t> before;
+    auto note = [&](std::vector<LState>& v) {
+      for (auto& st : v) before.push_back(st.cap);
+    };
+    note(se->pre);
+    for (auto& l : se->core) note(l);
+    note(se->coda);
+    ensure_caps(se, 1);
+    size_t at = 0;
+    auto cmp = [&](std::vector<LState>& v) {
+      for (auto& st : v) grew |= st.cap != before[at++];
+    };
+    cmp(se->pre);
+    for (auto& l : se->core) cmp(l);
+    cmp(se->coda);
+  }
+  if (grew) batch_tables(bt);
+}
+
 void batch_block(slm_batch* bt, const Block& b, size_t li, float* x) {
   slm_model* md = bt->model;
   const Config& c = md->cfg;
@@ -1160,6 +1225,8 @@ void batch_block(slm_batch* bt, const Block& b, size_t li, float* x) {
   float* const* K = bt->tab[li];
   float* const* V = bt->tab[li] + m;
   float* const* S = bt->tab[li] + 2 * m;
+  float* const* PV = bt->tab[li] + 3 * m;
+  const long long* CAP = bt->caps[li];
   ew_rms(bt->nb, x, b.norm1, m, d, c.eps, nullptr, s);
   if (b.kind == 'S') {
     run_linear(s, b.qkv, bt->nb, id, im, bt->mix, (int)(3 * d), EPI_STORE);
@@ -1169,7 +1236,37 @@ void batch_block(slm_batch* bt, const Block& b, size_t li, float* x) {
     AttnRows rows;
     rows.k = K, rows.v = V, rows.pos = bt->posr;
     attention_rows(bt->q, id, rows, g, bt->nsplit, bt->part, bt->y, id, s, bt->merge_cnt);
-  } else {  // 'L' (global layers are refused when the batch is made)
+  } else if (b.kind == 'G') {
+    // Model::block's global mixer (src/model.rs:487-543) per row, on the
+    // row's own cache, position and previous input.
+    if (b.norm_e) ew_rms(bt->nb, bt->e0, b.norm_e, m, d, c.eps, bt->nb, s);  // n += rms(e0)·w_e
+    const size_t kh = c.kv_heads, kd = kh * dh;
+    run_linear(s, b.q, bt->nb, id, im, bt->q, id, EPI_STORE);
+    run_linear(s, b.kv, bt->nb, id, im, bt->mix, (int)(2 * kd), EPI_STORE);
+    const float* keys = bt->mix;
+    size_t ldk = 2 * kd;
+    if (c.kshift) {  // this position's key from the row's previous input, which becomes this n
+      ew_gather_rows(bt->kb, PV, m, d, s);
+      run_linear(s, b.kv, bt->kb, id, im, bt->kvs, (int)kd, EPI_STORE, nullptr, 0, kd);  // key rows only
+      ew_scatter_rows(PV, bt->nb, m, d, s);
+      keys = bt->kvs;
+      ldk = kd;
+    }
+    const float inv_log = c.logn ? 1.0f / std::log((float)c.logn) : 0.0f;
+    ew_g_post_rows(bt->q, d, m, bt->posr, inv_log, c.logn ? 1 : 0, keys, ldk, bt->mix + kd, 2 * kd, kd, dh, K, V,
+                   CAP, s);
+    if (c.kshift) {  // the next position's key (the persistent step relies on it)
+      run_linear(s, b.kv, bt->nb, id, im, bt->kvs, (int)kd, EPI_STORE, nullptr, 0, kd);
+      ew_store_next_rows(K, bt->kvs, bt->posr, 1, m, kh, dh, CAP, s);
+    }
+    // A row that sees nothing yet (position within the far gap) gets y = 0,
+    // so o adds exactly 0 — what the reference's skipped o gives.
+    const long long far = c.far ? (long long)c.window : 0;
+    AttnGeom g{im, 0, far, 1ll << 40, (int)heads, (int)kh, (int)dh, scale};
+    AttnRows rows;
+    rows.k = K, rows.v = V, rows.pos = bt->posr, rows.cap = CAP;
+    attention_rows(bt->q, id, rows, g, bt->gsplit, bt->part, bt->y, id, s, bt->merge_cnt);
+  } else {  // 'L'
     run_linear(s, b.qkvg, bt->nb, id, im, bt->mix, (int)(4 * d), EPI_STORE);
     run_linear(s, b.decay, bt->nb, id, im, bt->dec, (int)heads, EPI_STORE);
     ew_l2norm(bt->q, d, bt->mix, 4 * d, m, heads, dh, s);
@@ -1259,6 +1356,10 @@ void batch_workspace(slm_batch* bt) {
   auto block = [&](const Block& b) {
     if (b.kind == 'S') one(b.qkv, d, 3 * d, EPI_STORE);
     if (b.kind == 'L') one(b.qkvg, d, 4 * d, EPI_STORE), one(b.decay, d, (int)c.heads, EPI_STORE);
+    if (b.kind == 'G') {
+      const int kd = (int)(c.kv_heads * c.dh());
+      one(b.q, d, d, EPI_STORE), one(b.kv, d, 2 * kd, EPI_STORE), one(b.kv, d, kd, EPI_STORE, (size_t)kd);
+    }
     one(b.o, d, d, EPI_ADD);
     one(b.up, d, (int)(2 * b.down.cols), EPI_STORE);
     one(b.down, (int)b.down.cols, d, EPI_ADD);
@@ -1274,6 +1375,7 @@ void batch_workspace(slm_batch* bt) {
 // after the context's GEMM workspace has moved).
 void batch_step_device(slm_batch* bt, bool sampled = false) {
   cudaStream_t s = bt->ctx->stream;
+  batch_caps(bt);  // global caches hold this step (their tables are updated in place)
   cudaGraphExec_t& graph = sampled ? bt->graph_s : bt->graph;
   unsigned long long& gen = sampled ? bt->graph_s_ws_gen : bt->graph_ws_gen;
   if (graph && gen != bt->ctx->gemm_ws_gen) batch_drop_graph(bt);
@@ -2042,8 +2144,6 @@ int slm_batch_new(slm_session* const* sessions, size_t n, slm_batch** out) {
       SLM_REQUIRE(sessions[i]->loops == sessions[0]->loops, "every session of a batch must run the same loops");
       for (size_t j = 0; j < i; j++) SLM_REQUIRE(sessions[j] != sessions[i], "a session appears twice in the batch");
     }
-    for (const std::string* part : {&c.prelude, &c.core, &c.coda})
-      SLM_REQUIRE(part->find('G') == std::string::npos, "batched decode does not support global-attention layers");
     Device dev(md->ctx);
     auto bt = std::make_unique<slm_batch>();
     bt->model = md, bt->ctx = md->ctx, bt->n = n;
@@ -2062,8 +2162,11 @@ int slm_batch_new(slm_session* const* sessions, size_t n, slm_batch** out) {
       const long long ctas = (long long)c.heads * (long long)n;
       long long want = (16 * bt->ctx->sms + ctas - 1) / ctas, most = ((long long)c.window + 127) / 128;
       bt->nsplit = (int)std::max<long long>(1, std::min<long long>(std::min(want, most), 256));
+      // Global layers see up to the whole history: as many splits as a
+      // window's worth of CTAs allows, slices of at least 512 positions.
+      bt->gsplit = (int)std::max<long long>(1, std::min<long long>(want * 2, 256));
       AttnGeom g{(int)n, 0, 0, 1, (int)c.heads, 1, (int)c.dh(), 1.0f};
-      bt->part = f(attn_part_floats(g, bt->nsplit));
+      bt->part = f(attn_part_floats(g, std::max(bt->nsplit, bt->gsplit)));
       bt->merge_cnt = static_cast<unsigned*>(balloc(bt.get(), c.heads * n * sizeof(unsigned)));
       bt->ids = static_cast<uint32_t*>(balloc(bt.get(), n * sizeof(uint32_t)));
       bt->out_index = static_cast<unsigned*>(balloc(bt.get(), 4 * sizeof(unsigned)));
@@ -2073,25 +2176,13 @@ int slm_batch_new(slm_session* const* sessions, size_t n, slm_batch** out) {
       for (size_t i = 0; i < n; i++) pos[i] = sessions[i]->pos_dev;
       bt->posr = static_cast<long long**>(balloc(bt.get(), n * sizeof(long long*)));
       SLM_CUDA(cudaMemcpyAsync(bt->posr, pos.data(), n * sizeof(long long*), cudaMemcpyHostToDevice, s));
-      // Layer instances in step order: prelude, each loop's core, coda.
-      std::vector<std::vector<const LState*>> inst;  // [instance][session]
-      auto add = [&](auto get) {
-        std::vector<const LState*> row(n);
-        for (size_t i = 0; i < n; i++) row[i] = get(sessions[i]);
-        inst.push_back(row);
-      };
-      for (size_t k = 0; k < md->prelude.size(); k++) add([&](slm_session* se) { return &se->pre[k]; });
-      for (size_t r = 0; r < sessions[0]->loops; r++)
-        for (size_t j = 0; j < md->core.size(); j++) add([&](slm_session* se) { return &se->core[r][j]; });
-      for (size_t k = 0; k < md->coda.size(); k++) add([&](slm_session* se) { return &se->coda[k]; });
-      std::vector<float*> host(3 * n);
-      for (auto& row : inst) {
-        for (size_t i = 0; i < n; i++) host[i] = row[i]->k, host[n + i] = row[i]->v, host[2 * n + i] = row[i]->s;
-        auto* t = static_cast<float**>(balloc(bt.get(), 3 * n * sizeof(float*)));
-        SLM_CUDA(cudaMemcpyAsync(t, host.data(), 3 * n * sizeof(float*), cudaMemcpyHostToDevice, s));
-        bt->tab.push_back(t);
+      bt->kvs = f(n * c.kv_heads * c.dh());
+      const size_t ninst = md->prelude.size() + sessions[0]->loops * md->core.size() + md->coda.size();
+      for (size_t k = 0; k < ninst; k++) {
+        bt->tab.push_back(static_cast<float**>(balloc(bt.get(), 4 * n * sizeof(float*))));
+        bt->caps.push_back(static_cast<long long*>(balloc(bt.get(), n * sizeof(long long))));
       }
-      SLM_CUDA(cudaStreamSynchronize(s));
+      batch_tables(bt.get());
     } catch (...) {
       cudaStreamSynchronize(s);
       for (void* p : bt->owned) dev_free(p);

@@ -99,7 +99,7 @@ def test_batch_86m_shapes(slm, ctx, tmp_path_factory):
     batch.close()
 
 
-def test_batch_refusals(slm, ctx, small, tmp_path_factory):
+def test_batch_refusals(slm, ctx, small):
     model = slm.Model(ctx, small)
     a, b = model.session(3), model.session(2)
     with pytest.raises(slm.SlmError):
@@ -116,11 +116,7 @@ def test_batch_refusals(slm, ctx, small, tmp_path_factory):
         batch.step([1, 5000])  # id out of range
     batch.close()
     c.close()
-    g = _synthetic(tmp_path_factory, "b_g", "GLOBAL", vocab_size=500, d_model=64, n_heads=4, hidden=128, window=16,
-                   max_loops=3, default_loops=2, global_kv_heads=2)
-    gm = slm.Model(ctx, g)
-    with pytest.raises(slm.SlmError):
-        slm.Batch([gm.session(), gm.session()])
+
 
 
 def test_batch_sampled_decode_matches_single_sessions(slm, ctx, small):
@@ -193,4 +189,72 @@ def test_batch_rows_match_oracle_on_a_wrapped_window(slm, ctx, oracle, tmp_path_
         st = [st_ref[i]]
         want = oracle.pick(ref.logits(), np.array(hists[i], dtype=np.uint32), rng_state=st, **c3)
         assert int(got[i]) == want and st_dev[i] == st[0], i
+    batch.close()
+
+
+@pytest.fixture(scope="module")
+def small_g(tmp_path_factory):
+    load_pkg()
+    # Global variant with GQA (4 heads over 2 cache heads), kshift, norm_e, logn
+    # and a far gap that opens after 16 positions.
+    return _synthetic(tmp_path_factory, "b_g", "GLOBAL", vocab_size=500, d_model=64, n_heads=4, hidden=128,
+                      window=16, max_loops=3, default_loops=2, global_kv_heads=2)
+
+
+def test_batch_global_layers_match_single_sessions(slm, ctx, small_g):
+    # Rows before and after the far gap opens (prompts of 3 … 90 ids), each
+    # with its own global cache, position and shifted-key input.
+    model = slm.Model(ctx, small_g)
+    ses, twins, first = _pairs(slm, model, [3, 10, 15, 16, 40, 90], 500, 8)
+    batch = slm.Batch(ses)
+    rng = np.random.default_rng(9)
+    worst = 0.0
+    for _ in range(20):
+        ids = rng.integers(0, 500, len(ses))
+        batch.step(ids)
+        got = batch.logits()
+        for i, tw in enumerate(twins):
+            tw.step(int(ids[i]))
+            worst = max(worst, float(np.abs(got[i] - tw.logits()).max()))
+    assert worst < 2e-4, worst
+    out = batch.decode([int(np.argmax(got[i])) for i in range(len(ses))], 12)
+    greedy = slm.Sampling()
+    for i, tw in enumerate(twins):
+        np.testing.assert_array_equal(out[:, i], tw.decode(int(np.argmax(got[i])), 12, greedy))
+    batch.close()
+
+
+def test_batch_global_rows_match_oracle_across_cache_growth(slm, ctx, oracle, tmp_path_factory):
+    # The 86M-class G variant (S | LS | SG): rows restored from the oracle at
+    # positions past 16384 and one just below 8192, whose global caches grow
+    # from 8192 to 16384 slots during the batch's steps.
+    syn = __import__("slm_b200.synthetic").synthetic
+    folder = syn.write_model(tmp_path_factory.mktemp("b_g86"), syn.GLOBAL, seed=0)
+    model, omodel = slm.Model(ctx, folder), oracle.Model(folder)
+    positions = [16400, 8188, 17000]
+    ses, refs = [], []
+    for i, pos in enumerate(positions):
+        dev, ref = model.session(4), omodel.session(4)
+        ref.fill(pos, 50 + i)
+        dev.set_pos(pos)
+        for j, a in enumerate(ref.state()):
+            dev.state_write(j, a["data"], a["cap"])
+        ses.append(dev)
+        refs.append(ref)
+    batch = slm.Batch(ses)
+    toks = [7, 77, 777]
+    worst = 0.0
+    for _ in range(8):
+        batch.step(toks)
+        got = batch.logits()
+        nxt = []
+        for i, ref in enumerate(refs):
+            ref.step(toks[i])
+            lg = ref.logits()
+            worst = max(worst, float(np.abs(got[i] - lg).max()))
+            nxt.append(int(np.argmax(lg)))
+        toks = nxt
+    assert worst < 1e-3, worst
+    grown = [a for a in ses[1].state_arrays() if a["kind"] == "G" and a["part"] == "k"]
+    assert grown and all(a["cap"] == 16384 for a in grown)
     batch.close()
