@@ -87,8 +87,7 @@ __device__ __forceinline__ float lds1(uint32_t a) {
 // 16 bytes of weights in shared memory as floats: 4 f32, or 8 bf16 (a bf16
 // value is the top half of an f32, so widening is exact).
 template <int WB>
-__device__ __forceinline__ void wchunk(uint32_t a, float (&v)[16 / WB]) {
-  const float4 x = lds4(a);
+__device__ __forceinline__ void widen(const float4 x, float (&v)[16 / WB]) {
   if constexpr (WB == 4) {
     v[0] = x.x, v[1] = x.y, v[2] = x.z, v[3] = x.w;
   } else {
@@ -96,6 +95,10 @@ __device__ __forceinline__ void wchunk(uint32_t a, float (&v)[16 / WB]) {
 #pragma unroll
     for (int i = 0; i < 4; i++) v[2 * i] = __uint_as_float(u[i] << 16), v[2 * i + 1] = __uint_as_float(u[i] & 0xffff0000u);
   }
+}
+template <int WB>
+__device__ __forceinline__ void wchunk(uint32_t a, float (&v)[16 / WB]) {
+  widen<WB>(lds4(a), v);
 }
 template <int E>
 __device__ __forceinline__ float dotn(const float (&w)[E], const float (&x)[E], float acc) {
@@ -1101,12 +1104,20 @@ struct Cons {
           const uint32_t g0 = saddr(w + (size_t)j * rowb) + lane * 16;
           const uint32_t u0 = saddr(w + (size_t)(n + j) * rowb) + lane * 16;
           const uint32_t r0 = saddr(w + (size_t)(2 * n + j) * rowb) + lane * 16;
+          // Every load of the unit (gate, up and its down column) is issued
+          // before the first product, so their latencies overlap; bf16
+          // chunks stay packed until they are used.
+          float4 gr[NC], ur[NC], dr[NC];
+#pragma unroll
+          for (int c = 0; c < NC; c++) gr[c] = lds4(g0 + 512 * c), ur[c] = lds4(u0 + 512 * c);
+#pragma unroll
+          for (int c = 0; c < NC; c++) dr[c] = lds4(r0 + 512 * c);
           float a0 = 0.0f, b0 = 0.0f, a1 = 0.0f, b1 = 0.0f;
 #pragma unroll
           for (int c = 0; c < NC; c++) {
             float gq[E], uq[E];
-            wchunk<WB>(g0 + 512 * c, gq);
-            wchunk<WB>(u0 + 512 * c, uq);
+            widen<WB>(gr[c], gq);
+            widen<WB>(ur[c], uq);
             if (c & 1) {
               b0 = dotn(gq, xr[c], b0);
               b1 = dotn(uq, xr[c], b1);
@@ -1126,7 +1137,7 @@ struct Cons {
 #pragma unroll
           for (int c = 0; c < NC; c++) {
             float dq[E];
-            wchunk<WB>(r0 + 512 * c, dq);
+            widen<WB>(dr[c], dq);
 #pragma unroll
             for (int e = 0; e < E; e++) yv[c][e] = fmaf(h, dq[e], yv[c][e]);
           }
