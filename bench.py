@@ -59,7 +59,7 @@ MODEL_BYTES_NOTE = "inputs larger than L2: 640 MB of weights and KV read per tok
 # this bench (profiles/k_decode_mega_R4.md), by loop count.
 # DRAM bytes (read + write) of one R = 4 step, ncu dram__bytes of one launch
 # (profiles/k_decode_mega_R4.md); no capture exists for other loop counts.
-MEGA_TRAFFIC = {4: 439.2e6}
+MEGA_TRAFFIC = {4: 444.9e6}
 
 
 def load_pkg():
@@ -351,43 +351,57 @@ def traced_step(se, greedy) -> np.ndarray:
 
 
 def attention_phases(tr: np.ndarray, cfg: dict, loops: int) -> dict | None:
-    """The persistent step's window-attention phases at a full window: their
-    K/V bytes over their critical spans (first CTA start to last arrival)."""
+    """The persistent step's window-attention phases (attention and the o
+    projection fused) at a full window: their K/V and o bytes over what each
+    adds to the step (its last CTA arrival minus the previous phase's; the
+    phases overlap, so first start to last arrival would count time that the
+    previous phase's stragglers take)."""
     kinds = trace_kinds(tr, cfg, loops)
     if kinds is None:
         return None
-    spans = [int(tr[p, :, 1].max() - tr[p, :, 0].min()) for p in range(tr.shape[0]) if kinds[p] == "attn"]
-    h, dh = cfg["n_heads"], cfg["d_model"] // cfg["n_heads"]
-    per = 2 * h * cfg["window"] * dh * 4
+    spans = [int(tr[p, :, 1].max() - tr[p - 1, :, 1].max()) for p in range(1, tr.shape[0]) if kinds[p] == "attn"]
+    h, dh, d = cfg["n_heads"], cfg["d_model"] // cfg["n_heads"], cfg["d_model"]
+    per = 2 * h * cfg["window"] * dh * 4 + d * d * 4
     return {"phases": len(spans), "bytes_per_phase": per, "us_per_phase": sum(spans) / len(spans) / 1000.0,
             "achieved": per * len(spans) / (sum(spans) * 1e-9) / 1e9}
 
 
 def write_trace(tr: np.ndarray, cfg: dict, loops: int, path: str) -> None:
     """Per-phase sums of a traced step, grouped by phase kind, as a markdown
-    table (critical span = first CTA start to last CTA arrival; gap = last
-    arrival to the next phase's first start)."""
+    table.  Step span: each phase's last CTA arrival minus the previous
+    phase's (the first phase: minus the step's first start), i.e. what the
+    phase adds to the step; phases overlap, since a CTA starts the next phase
+    when its own part of this one is done.  Per CTA (medians over the CTAs,
+    summed over the phases of the kind): duration from the CTA's start of the
+    phase to its arrival, the input prologue (waiting for and building the
+    input vector), work on its tiles, waits for tiles to land, and epilogues
+    (output adds, the o tail of mixer phases).  globaltimer ticks are 32 ns
+    to 1 µs depending on the GPU, so single values are coarse; the sums over
+    148 CTAs' medians are not."""
     kinds = trace_kinds(tr, cfg, loops)
     if kinds is None:
         return
     t0 = tr[0, :, 0].min()
     st, en = tr[:, :, 0] - t0, tr[:, :, 1] - t0
     rows: dict = {}
+    prev_end = 0.0
     for p in range(tr.shape[0]):
-        gap = st[p + 1].min() - en[p].max() if p + 1 < tr.shape[0] else 0
-        r = rows.setdefault(kinds[p], [0, 0.0, 0.0, 0.0, 0.0, 0.0])
+        r = rows.setdefault(kinds[p], [0, 0.0, 0.0, 0.0, 0.0, 0.0, 0.0])
         r[0] += 1
-        r[1] += en[p].max() - st[p].min()
-        r[2] += gap
+        r[1] += en[p].max() - prev_end
+        prev_end = en[p].max()
+        r[2] += float(np.median(tr[p, :, 1] - tr[p, :, 0]))
         r[3] += float(np.median(tr[p, :, 3]))
         r[4] += float(np.median(tr[p, :, 4]))
         r[5] += float(np.median(tr[p, :, 2]))
+        r[6] += float(np.median(tr[p, :, 5]))
     lines = [f"Total step (trace run): {en[-1].max() / 1000:.1f} us over {tr.shape[0]} phases", "",
-             "| phase kind | count | critical span µs (sum) | barrier gap µs (sum) | input prologue µs (median, sum)"
-             " | tile work µs (median, sum) | tile waits µs (median, sum) |", "|---|---|---|---|---|---|---|"]
+             "| phase kind | count | step span µs (sum) | per-CTA duration µs (median, sum) | input prologue µs"
+             " (median, sum) | tile work µs (median, sum) | tile waits µs (median, sum) | epilogues µs (median, sum) |",
+             "|---|---|---|---|---|---|---|---|"]
     for k, r in sorted(rows.items(), key=lambda kv: -kv[1][1]):
         lines.append(f"| {k} | {r[0]} | {r[1] / 1000:.1f} | {r[2] / 1000:.1f} | {r[3] / 1000:.1f} | "
-                     f"{r[4] / 1000:.1f} | {r[5] / 1000:.1f} |")
+                     f"{r[4] / 1000:.1f} | {r[5] / 1000:.1f} | {r[6] / 1000:.1f} |")
     Path(path).parent.mkdir(parents=True, exist_ok=True)
     Path(path).write_text("\n".join(lines) + "\n")
 
@@ -852,10 +866,11 @@ def main():
     if res.get("attn_phase"):
         ap = res["attn_phase"]
         line["roofline"]["attention_in_step"] = {
-            "kernel": "k_decode_mega window-attention phases (12 heads x 4096 positions, 12 splits per head)",
+            "kernel": "k_decode_mega window-attention + o phases (12 heads x 4096 positions, 12 splits per head, "
+                      "then the 768x768 o projection)",
             "achieved": ap["achieved"], "frac": ap["achieved"] / hbm, "us_per_phase": ap["us_per_phase"],
-            "bytes_per_phase": ap["bytes_per_phase"], "how": "globaltimer trace of one step (first start to last "
-            "arrival of each attention phase)"}
+            "bytes_per_phase": ap["bytes_per_phase"], "how": "globaltimer trace of one step (each attention phase's "
+            "last CTA arrival minus the previous phase's)"}
     if cpu:
         line["cpu_baseline"] = {"value": cpu["decode_tok_s"], "unit": "tok/s", "cores": cpu["cores"], "kind": "port",
                                 "sample": cpu["sample"], "prefill_tok_s": cpu["prefill_tok_s"]}

@@ -18,6 +18,12 @@ struct slm_ctx {
                                 // the last persistent step on this context (that of `argmax_owner`)
   int* err_host = nullptr;      // pinned copy of it (read after a synchronisation)
   const void* argmax_owner = nullptr;  // session whose persistent step wrote err[1] last
+  // Mapped pinned words a persistent step launched by slm_step writes when it
+  // ends: [0] its sequence number, [1] its arg-max | error word << 32
+  // (slm_sample polls them instead of a copy and a stream synchronisation).
+  unsigned long long* mbox = nullptr;      // host address
+  unsigned long long* mbox_dev = nullptr;  // device address of the same words
+  unsigned long long mbox_seq = 0;         // last sequence number given to a launch
   void* stage = nullptr;        // staging buffer for host arrays (ids, factors)
   size_t stage_bytes = 0;
   void* gemm_ws = nullptr;      // tensor-core GEMM workspace (grown on demand, outside captures)

@@ -1866,6 +1866,16 @@ struct Cons {
         atomicExch(P.bar, 0u);
         atomicExch(P.bar + 1, 0u);
         atomicExch(P.epoch, ep + 1u);
+        if (P.host_mbox) {
+          // Every CTA has finished the step (each fenced its writes before its
+          // count above): hand the arg-max and the error word to the host.
+          __threadfence();
+          const unsigned am = *(const volatile unsigned*)P.argmax;
+          const unsigned ew = (unsigned)ld_volatile(P.err);
+          *(volatile unsigned long long*)(P.host_mbox + 1) = ((unsigned long long)ew << 32) | am;
+          __threadfence_system();
+          *(volatile unsigned long long*)P.host_mbox = P.host_seq;
+        }
       }
     }
   }

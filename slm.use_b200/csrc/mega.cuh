@@ -194,6 +194,13 @@ struct Plan {
   // The phase after which every CTA has finished the previous step, so the
   // fixed-point set the next step uses may be zeroed (see run()).
   int zero_phase;
+  // Optional mailbox in mapped pinned host memory (single steps launched by
+  // slm_step): once every CTA has finished the step, the last one writes
+  // host_mbox[1] = arg-max | error word << 32, then host_mbox[0] = host_seq
+  // after a system-scope fence; the host polls word 0 instead of copying the
+  // arg-max back and synchronising the stream.
+  unsigned long long* host_mbox;
+  unsigned long long host_seq;
 };
 
 }  // namespace mega

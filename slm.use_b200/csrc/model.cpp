@@ -4,6 +4,7 @@
 // block.  The m = 1 step is captured once as a CUDA graph and replayed: every
 // kernel reads the position from device memory and the next token id from a
 // device slot that the on-device sampler writes.
+#include <atomic>
 #include <algorithm>
 #include <cmath>
 #include <cstdlib>
@@ -137,6 +138,7 @@ struct slm_session {
   uint32_t* argmax_dev = nullptr;        // the persistent step's arg-max of its logits
   unsigned* merge_cnt = nullptr;         // attention slice counters of the graph path (zero between launches)
   bool argmax_valid = false;             // the logits come from a persistent step
+  unsigned long long mbox_want = 0;      // mailbox sequence number of this session's pending slm_step (0: none)
   // Pinned host words for the per-token transfers (ids in and out, RNG state).
   struct HostIO {
     uint32_t id_in, id_out;
@@ -1021,6 +1023,9 @@ void mega_step(slm_session* se, long long host_id = -1) {
   if (host_id >= 0) {
     mega::Plan p = se->plan_host;
     p.host_id = host_id;
+    p.host_mbox = se->ctx->mbox_dev;
+    p.host_seq = ++se->ctx->mbox_seq;
+    se->mbox_want = p.host_seq;
     mega::launch(p, se->grid, se->ctx->stream);
   } else {
     mega::launch(se->plan_host, se->grid, se->ctx->stream);
@@ -2014,6 +2019,38 @@ int slm_sample(slm_session* se, const slm_sampling* sp, const uint32_t* recent, 
     const bool fast = se->argmax_valid && sp->temperature <= 0.0f && (sp->repeat_penalty == 1.0f || n_recent == 0);
     if (fast) {
       slm_ctx* c = se->ctx;
+      if (c->argmax_owner == se && se->mbox_want) {
+        // slm_step's launch hands its arg-max over in the mailbox: poll it
+        // while the stream runs; a step that gave up writes none, so once the
+        // stream is idle without it, the copy below reports the error.
+        const unsigned long long want = se->mbox_want;
+        se->mbox_want = 0;
+        const volatile unsigned long long* mb = c->mbox;
+        bool got = false;
+        for (unsigned it = 1;; it++) {
+          if (mb[0] == want) {
+            got = true;
+            break;
+          }
+          if ((it & 255) == 0 && cudaStreamQuery(s) != cudaErrorNotReady) {
+            got = mb[0] == want;
+            break;
+          }
+#if defined(__x86_64__)
+          __builtin_ia32_pause();
+#endif
+        }
+        if (cudaPeekAtLastError() == cudaErrorNotReady) (void)cudaGetLastError();  // the queries' answer, not an error
+        if (got) {
+          std::atomic_thread_fence(std::memory_order_acquire);
+          const unsigned long long w = mb[1];
+          if ((w >> 32) == 0) {
+            se->io_busy = false;
+            *out_id = static_cast<uint32_t>(w);
+            return;
+          }
+        }
+      }
       if (c->argmax_owner == se) {  // one copy: the error word and this step's arg-max beside it
         SLM_CUDA(cudaMemcpyAsync(c->err_host, c->err, 2 * sizeof(int), cudaMemcpyDeviceToHost, s));
         SLM_CUDA(cudaStreamSynchronize(s));

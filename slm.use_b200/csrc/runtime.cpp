@@ -107,6 +107,7 @@ void destroy_ctx(slm_ctx* c) {
     dev_free(c->merge_cnt);
     dev_free(c->err);
     if (c->err_host) cudaFreeHost(c->err_host);
+    if (c->mbox) cudaFreeHost(c->mbox);
     cudaStreamDestroy(c->stream);
   }
   delete c;
@@ -158,6 +159,9 @@ int slm_ctx_new(int device, slm_ctx** out) {
       c->err = static_cast<int*>(dev_alloc(sizeof(int) * 4));
       SLM_CUDA(cudaMemsetAsync(c->err, 0, sizeof(int) * 4, c->stream));
       SLM_CUDA(cudaHostAlloc(reinterpret_cast<void**>(&c->err_host), sizeof(int) * 4, cudaHostAllocDefault));
+      SLM_CUDA(cudaHostAlloc(reinterpret_cast<void**>(&c->mbox), 64, cudaHostAllocMapped));
+      c->mbox[0] = c->mbox[1] = 0;
+      SLM_CUDA(cudaHostGetDevicePointer(reinterpret_cast<void**>(&c->mbox_dev), c->mbox, 0));
     } catch (...) {
       delete c;
       throw;
