@@ -239,7 +239,11 @@ uint64_t slm_rng_seed(uint64_t seed);
 /* pick (src/sample.rs:33-93) on the device, from the session's logits.
  * `recent` (host, n_recent ids) is the history the repeat penalty reads;
  * `rng_state` is read and advanced.  Candidates after top-k are kept in a
- * canonical order (logit descending, then id ascending).  Synchronises. */
+ * canonical order (logit descending, then id ascending).  Synchronises.
+ * Greedy without a penalty, right after this session's slm_step on the
+ * persistent kernel: returns the arg-max that step computed, as soon as the
+ * step's mailbox (mapped pinned host memory) shows it, busy-waiting the
+ * calling thread for the step (about one step's time, 0.2 ms at R = 4). */
 int slm_sample(slm_session* se, const slm_sampling* s, const uint32_t* recent, size_t n_recent,
                uint64_t* rng_state, uint32_t* out_id);
 
