@@ -269,6 +269,14 @@ __device__ __forceinline__ bool fx_poll4(const unsigned long long* fx, int i4, u
   return false;
 }
 
+// One read of the same four values: true when every one is final.
+__device__ __forceinline__ bool fx_try4(const unsigned long long* fx, int i4, unsigned cnt, float4* out) {
+  const unsigned long long* f = fx + 4 * i4;
+  const ulonglong2 a = ld_relaxed_u64x2(f), b = ld_relaxed_u64x2(f + 2);
+  *out = make_float4(fx_value(a.x), fx_value(a.y), fx_value(b.x), fx_value(b.y));
+  return fx_count(a.x) == cnt && fx_count(a.y) == cnt && fx_count(b.x) == cnt && fx_count(b.y) == cnt;
+}
+
 // Tagged words: the float in the low half, the producer's tag in the high half.
 __device__ __forceinline__ unsigned long long tagged(float v, unsigned tag) {
   return ((unsigned long long)tag << 32) | __float_as_uint(v);
@@ -297,6 +305,14 @@ __device__ __forceinline__ bool poll_tagged(const unsigned long long* p, int str
 #pragma unroll
   for (int i = 0; i < N; i++) out[i] = 0.0f;
   return false;
+}
+// One read of four consecutive tagged values: true when all carry `tag`.
+__device__ __forceinline__ bool try_tagged4(const unsigned long long* p, unsigned tag, float4* out) {
+  const ulonglong2 a = ld_relaxed_u64x2(p), b = ld_relaxed_u64x2(p + 2);
+  *out = make_float4(__uint_as_float((unsigned)a.x), __uint_as_float((unsigned)a.y), __uint_as_float((unsigned)b.x),
+                     __uint_as_float((unsigned)b.y));
+  return (unsigned)(a.x >> 32) == tag && (unsigned)(a.y >> 32) == tag && (unsigned)(b.x >> 32) == tag &&
+         (unsigned)(b.y >> 32) == tag;
 }
 
 // ---------------------------------------------------------------------------
@@ -805,15 +821,26 @@ struct Cons {
           reinterpret_cast<float4*>(P.x0)[tid] = x;
         }
       } else if (ph.in_mode == IN_LOOP_RMS) {
-        float4 a = in4(ph, tid), b;
-        if (ph.tin_b) {  // the inject output, tagged by its phase
-          float bv[4];
-          if (!poll_tagged<4>(ph.tin_b + 4 * tid, 1, tag_of(ph.tag_in), P.err, bv)) ok = false;
-          b = make_float4(bv[0], bv[1], bv[2], bv[3]);
-        } else {
-          b = __ldcg(reinterpret_cast<const float4*>(ph.in_b) + tid);
-        }
-        float4 c = __ldg(reinterpret_cast<const float4*>(ph.in_c) + tid);
+        // All three terms in one round of loads per poll (the loop
+        // embedding row, the slot's values and the tagged inject term), so
+        // their latencies overlap.
+        const float4 c = __ldg(reinterpret_cast<const float4*>(ph.in_c) + tid);
+        float4 a, b;
+        Spin sp;
+        bool done;
+        do {
+          bool ga = true, gb = true;
+          if (ph.fx_in)
+            ga = fx_try4(fxp(ph.fx_in), tid, fx_need(ph), &a);
+          else
+            a = __ldcg(reinterpret_cast<const float4*>(ph.in_a) + tid);
+          if (ph.tin_b)  // the inject output, tagged by its phase
+            gb = try_tagged4(ph.tin_b + 4 * tid, tag_of(ph.tag_in), &b);
+          else
+            b = __ldcg(reinterpret_cast<const float4*>(ph.in_b) + tid);
+          done = ga && gb;
+        } while (!done && sp.again(P.err));
+        if (!done) ok = false;
         x = make_float4((a.x + b.x) + c.x, (a.y + b.y) + c.y, (a.z + b.z) + c.z, (a.w + b.w) + c.w);
         if (blockIdx.x == 0) reinterpret_cast<float4*>(ph.xout)[tid] = x;
       } else {
@@ -1685,6 +1712,9 @@ struct Cons {
   // after all of them have.
   __device__ void gla_item(const Phase& ph, int h, int s = 0) {
     const int d = P.d;
+    // The layer's constants first, so their loads overlap the polls below.
+    const float bias = __ldg(ph.bias + h);
+    const float hn = warp < 2 ? __ldg(ph.hnw + tid) : 0.0f;
     // [q | k | v | g] rows (each d wide) and the decay, tagged by the projection phase.
     const unsigned tg = tag_of(ph.tag_in);
     if (tid < kDH) {
@@ -1693,7 +1723,7 @@ struct Cons {
 #pragma unroll
       for (int k = 0; k < 4; k++) sm.vec[k][tid] = v[k];
     }
-    const float dcy = 1.0f / (1.0f + expf(tval(ph.tdec + h, tg) + __ldg(ph.bias + h)));
+    const float dcy = 1.0f / (1.0f + expf(tval(ph.tdec + h, tg) + bias));
     if (!all_ok()) return;
     if (warp < 2) {  // warp 0: |q|, warp 1: |k|
       float a = sm.vec[warp][lane], b = sm.vec[warp][lane + 32];
@@ -1726,7 +1756,7 @@ struct Cons {
       asm volatile("bar.sync 2, 64;" ::: "memory");
       float tot = sm.red[0] + sm.red[1];
       float r = 1.0f / sqrtf(tot / (float)kDH + P.eps);
-      const float o = silu_mul(sm.vec[3][bb], y * r * __ldg(ph.hnw + bb));
+      const float o = silu_mul(sm.vec[3][bb], y * r * hn);
       if (ph.wo)
         sm.vec[0][bb] = o;  // q is no longer read: every thread passed the barrier above
       else
