@@ -16,6 +16,8 @@
 // needs no barrier, only two shuffles per token to sum a column's y.  The
 // head_norm and gate of the staged tokens then run in parallel, one warp per
 // token.
+#include <mutex>
+
 #include "common.cuh"
 #include "kernels.cuh"
 
@@ -248,6 +250,201 @@ __global__ void __launch_bounds__(256)
   }
 }
 
+// ---------------------------------------------------------------------------
+// Many tokens, head size 64: the chunked form of the same recurrence.  Over a
+// sub-chunk of C tokens, with l_t = Σ_{u≤t} ln d_u (inclusive, from the
+// sub-chunk's start) and S_0 the state before it:
+//   y_t = e^{l_t} q_t·S_0 + Σ_{s≤t} e^{l_t − l_s} (q_t·k_s) v_s
+//   S_C = e^{l_{C−1}} S_0 + Σ_s e^{l_{C−1} − l_s} k_s v_sᵀ
+// which is the token recurrence written out (Π_{s<u≤t} d_u = e^{l_t − l_s});
+// only the order of the additions differs.  The ln d_u (of the same float d
+// the recurrence multiplies by; clamped at −87, below which d·S is lost to
+// f32 anyway) are summed in double, so the differences l_t − l_s keep full
+// precision however small the sub-chunk's decay product gets.  The
+// sequential steps fall from m tokens to m / C sub-chunks of small matrix
+// products in shared memory.
+//
+// A CTA owns kGCG columns of one head's state (grid heads × 64/kGCG, 256
+// threads).  Every CTA of a head forms the same C × C matrix
+// A[t][s] = e^{l_t − l_s} q_t·k_s (s ≤ t).  Rows of q, k and A are padded to
+// 68 floats, so float4 reads of 8 consecutive rows fall in distinct banks.
+// Sub-chunks are staged with cp.async, double-buffered.
+// ---------------------------------------------------------------------------
+constexpr int kGC = 64;   // tokens per sub-chunk
+constexpr int kGCG = 8;   // state columns per CTA
+constexpr int kGLD = 68;  // padded row of q, k and A
+struct GlaChunkSmem {
+  float q[2][kGC][kGLD], k[2][kGC][kGLD];
+  float v[2][kGC][kGCG];
+  float gd[2][kGC];    // ln d of each token (clamped), computed when the sub-chunk is staged
+  float a[kGC][kGLD];  // A
+  float s[64][kGCG];   // this CTA's state columns
+  float w[kGC];        // e^{l_last − l_s}
+  float el[kGC];       // e^{l_t}
+  double l[kGC];
+  float elast;
+};
+
+__global__ void __launch_bounds__(256)
+    k_gla_chunk(float* __restrict__ S, const float* __restrict__ q, int ldq, const float* __restrict__ k, int ldk,
+                const float* __restrict__ v, int ldv, const float* __restrict__ dec, int lddec,
+                const float* __restrict__ bias, int m, float* __restrict__ out, int ldo) {
+  constexpr int DH = 64;
+  extern __shared__ __align__(16) char gsm_raw[];
+  GlaChunkSmem& sm = *reinterpret_cast<GlaChunkSmem*>(gsm_raw);
+  const int h = blockIdx.x, cg = blockIdx.y, t = threadIdx.x;
+  const int col0 = h * DH + cg * kGCG;  // this CTA's columns of v and out
+  float* Sh = S + (size_t)h * DH * DH;
+  for (int e = t; e < DH * kGCG; e += 256) sm.s[e / kGCG][e % kGCG] = Sh[(size_t)(e / kGCG) * DH + cg * kGCG + e % kGCG];
+  const float bh = bias[h];
+
+  auto stage = [&](int c, int buf) {
+    const int c0 = c * kGC, n = min(kGC, m - c0);
+    for (int e = t; e < n * (DH / 4); e += 256) {
+      const int i = e / (DH / 4), x = (e % (DH / 4)) * 4;
+      const size_t row = (size_t)(c0 + i);
+      cp16(&sm.q[buf][i][x], q + row * ldq + (size_t)h * DH + x);
+      cp16(&sm.k[buf][i][x], k + row * ldk + (size_t)h * DH + x);
+    }
+    for (int e = t; e < n * (kGCG / 4); e += 256) {
+      const int i = e / (kGCG / 4), x = (e % (kGCG / 4)) * 4;
+      cp16(&sm.v[buf][i][x], v + (size_t)(c0 + i) * ldv + col0 + x);
+    }
+    cp_commit();
+    for (int i = t; i < n; i += 256)
+      sm.gd[buf][i] = fmaxf(logf(1.0f / (1.0f + expf(dec[(size_t)(c0 + i) * lddec + h] + bh))), -87.0f);
+  };
+
+  const int nch = (m + kGC - 1) / kGC;
+  const int rb = t >> 4, cb = t & 15;    // A: rows rb + 16j, columns cb + 16k
+  const int r4 = t >> 2, j2 = (t & 3) * 2;  // y row / state row, and two columns
+  stage(0, 0);
+  for (int c = 0; c < nch; c++) {
+    const int c0 = c * kGC, n = min(kGC, m - c0), buf = c & 1;
+    if (c + 1 < nch) {
+      stage(c + 1, buf ^ 1);
+      cp_wait<1>();
+    } else {
+      cp_wait<0>();
+    }
+    __syncthreads();
+    // 1. Warp 0: ln d, their inclusive running sum (double), e^{l_t} and the
+    // state weights e^{l_last − l_s}.  Rows ≥ n are never used.
+    if (t < 32) {
+      const int i0 = 2 * t, i1 = 2 * t + 1;
+      double g0 = 0.0, g1 = 0.0;
+      if (i0 < n) g0 = (double)sm.gd[buf][i0];
+      if (i1 < n) g1 = (double)sm.gd[buf][i1];
+      double p = g0 + g1;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const double u = __shfl_up_sync(0xffffffffu, p, o);
+        if (t >= o) p += u;
+      }
+      double ex = __shfl_up_sync(0xffffffffu, p, 1);
+      if (t == 0) ex = 0.0;
+      sm.l[i0] = ex + g0;
+      sm.l[i1] = (ex + g0) + g1;
+      __syncwarp();
+      const double lL = sm.l[n - 1];
+      for (int i = t; i < kGC; i += 32) {
+        sm.w[i] = i < n ? expf((float)(lL - sm.l[i])) : 0.0f;
+        sm.el[i] = expf((float)sm.l[i]);
+      }
+      if (t == 0) sm.elast = expf((float)lL);
+    }
+    // 2. q_t·k_s for this thread's entries (rows rb + 16j, columns cb + 16k):
+    // those with k > j lie above the diagonal (cb + 16(k − j) > rb) and are
+    // not formed.
+    float acc[4][4];
+#pragma unroll
+    for (int j = 0; j < 4; j++)
+#pragma unroll
+      for (int kk = 0; kk < 4; kk++) acc[j][kk] = 0.0f;
+#pragma unroll 4
+    for (int x = 0; x < DH; x += 4) {
+      float4 qv[4], kv[4];
+#pragma unroll
+      for (int j = 0; j < 4; j++) qv[j] = *reinterpret_cast<const float4*>(&sm.q[buf][rb + 16 * j][x]);
+#pragma unroll
+      for (int kk = 0; kk < 4; kk++) kv[kk] = *reinterpret_cast<const float4*>(&sm.k[buf][cb + 16 * kk][x]);
+#pragma unroll
+      for (int j = 0; j < 4; j++)
+#pragma unroll
+        for (int kk = 0; kk <= j; kk++) acc[j][kk] = dot4(qv[j], kv[kk], acc[j][kk]);
+    }
+    __syncthreads();  // l, w, el from warp 0
+#pragma unroll
+    for (int j = 0; j < 4; j++)
+#pragma unroll
+      for (int kk = 0; kk < 4; kk++) {
+        const int r = rb + 16 * j, s = cb + 16 * kk;
+        sm.a[r][s] = (s <= r && r < n) ? acc[j][kk] * expf((float)(sm.l[r] - sm.l[s])) : 0.0f;
+      }
+    __syncthreads();
+    // 3. y_t = e^{l_t} q_t·S_0 + Σ_{s≤t} A[t][s] v_s, two columns per thread.
+    if (r4 < n) {
+      float y0 = 0.0f, y1 = 0.0f, z0 = 0.0f, z1 = 0.0f;
+#pragma unroll 8
+      for (int a = 0; a < DH; a++) {
+        const float qa = sm.q[buf][r4][a];
+        y0 = fmaf(qa, sm.s[a][j2], y0);
+        y1 = fmaf(qa, sm.s[a][j2 + 1], y1);
+      }
+      for (int s = 0; s <= r4; s++) {
+        const float as = sm.a[r4][s];
+        z0 = fmaf(as, sm.v[buf][s][j2], z0);
+        z1 = fmaf(as, sm.v[buf][s][j2 + 1], z1);
+      }
+      const float e = sm.el[r4];
+      float* o = out + (size_t)(c0 + r4) * ldo + col0 + j2;
+      o[0] = fmaf(e, y0, z0);
+      o[1] = fmaf(e, y1, z1);
+    }
+    __syncthreads();  // every y has read S_0
+    // 4. S_C = e^{l_last} S_0 + Σ_s e^{l_last − l_s} k_s v_sᵀ for state row r4.
+    {
+      float n0 = sm.elast * sm.s[r4][j2], n1 = sm.elast * sm.s[r4][j2 + 1];
+      for (int s = 0; s < n; s++) {
+        const float kw = sm.k[buf][s][r4] * sm.w[s];
+        n0 = fmaf(kw, sm.v[buf][s][j2], n0);
+        n1 = fmaf(kw, sm.v[buf][s][j2 + 1], n1);
+      }
+      sm.s[r4][j2] = n0;
+      sm.s[r4][j2 + 1] = n1;
+    }
+    __syncthreads();  // the next sub-chunk reads the new state; this buffer is restaged
+  }
+  for (int e = t; e < DH * kGCG; e += 256) Sh[(size_t)(e / kGCG) * DH + cg * kGCG + e % kGCG] = sm.s[e / kGCG][e % kGCG];
+}
+
+#ifndef SLM_GLA_CHUNK_MIN
+#define SLM_GLA_CHUNK_MIN 32  // fewer tokens keep the column-parallel recurrence
+#endif
+
+void launch_chunk(const GlaArgs& g, cudaStream_t st) {
+  constexpr int kDevices = 64;
+  static std::once_flag once[kDevices];
+  int dev = 0;
+  SLM_CUDA(cudaGetDevice(&dev));
+  auto set = [] {
+    SLM_CUDA(cudaFuncSetAttribute(k_gla_chunk, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  (int)sizeof(GlaChunkSmem)));
+  };
+  if (dev >= 0 && dev < kDevices)
+    std::call_once(once[dev], set);
+  else
+    set();
+  k_gla_chunk<<<dim3(g.heads, 64 / kGCG), 256, sizeof(GlaChunkSmem), st>>>(g.S, g.q, g.ldq, g.k, g.ldk, g.v, g.ldv,
+                                                                          g.dec, g.lddec, g.bias, g.m, g.out, g.ldo);
+  SLM_LAUNCHED("k_gla_chunk");
+  if (g.fuse) {
+    const int warps = g.m * g.heads;
+    k_gla_norm<64><<<(warps + 7) / 8, 256, 0, st>>>(g.out, g.ldo, g.g, g.ldg, g.hnw, g.eps, g.m, g.heads);
+    SLM_LAUNCHED("k_gla_norm");
+  }
+}
+
 template <int DH>
 bool cols_ok(const GlaArgs& g) {
   auto al = [](const void* p) { return ((uintptr_t)p & 15) == 0; };
@@ -290,7 +487,12 @@ void gla(const GlaArgs& g, cudaStream_t st) {
     case 8: launch<8>(g, st); break;
     case 16: launch<16>(g, st); break;
     case 32: cols_ok<32>(g) ? launch_cols<32>(g, st) : launch<32>(g, st); break;
-    case 64: cols_ok<64>(g) ? launch_cols<64>(g, st) : launch<64>(g, st); break;
+    case 64:
+      if (cols_ok<64>(g) && g.m >= SLM_GLA_CHUNK_MIN && g.ldv % 4 == 0)
+        launch_chunk(g, st);
+      else
+        cols_ok<64>(g) ? launch_cols<64>(g, st) : launch<64>(g, st);
+      break;
     case 128: cols_ok<128>(g) ? launch_cols<128>(g, st) : launch<128>(g, st); break;
     default: fail(SLM_ERR_INVALID, "gla: head size must be one of 8, 16, 32, 64, 128");
   }

@@ -81,14 +81,36 @@ def test_l2norm(ops, oracle):
     close(y.read(37 * 64), oracle.l2norm(x, 37, 64))
 
 
-# m >= 8 with head size 32/64/128 takes the column-parallel kernel (ragged last
-# stages included); the rest the per-head kernel.
+# Head size 64 with m >= 32 takes the chunked kernel (64-token sub-chunks,
+# ragged last ones included); other m >= 8 with head size 32/64/128 the
+# column-parallel one; the rest the per-head kernel.
 @pytest.mark.parametrize("m,heads,dh", [(1, 12, 64), (37, 4, 8), (256, 12, 64), (5, 2, 128), (100, 12, 64),
-                                        (40, 3, 32), (33, 2, 128), (8, 1, 64)])
+                                        (40, 3, 32), (33, 2, 128), (8, 1, 64), (32, 2, 64), (64, 3, 64),
+                                        (65, 2, 64), (129, 1, 64), (300, 4, 64)])
 def test_gla(ops, oracle, m, heads, dh):
     n = m * heads * dh
     q, k, v = rand(n, scale=0.2), rand(n, scale=0.2), rand(n)
     dec, bias = rand(m * heads), rand(heads)
+    s0 = rand(heads * dh * dh, scale=0.1)
+    sd = ops.upload(s0)
+    y = ops.zeros(1)
+    ops.gla(y, sd, ops.upload(q), ops.upload(k), ops.upload(v), ops.upload(dec), ops.upload(bias), m, heads, dh)
+    s_cpu = s0.copy()
+    want = oracle.gla(s_cpu, q, k, v, dec, bias, m, heads, dh)
+    close(y.read(n), want, atol=1e-4)
+    close(sd.read(heads * dh * dh), s_cpu, atol=1e-4)
+
+
+def test_gla_extreme_decays(ops, oracle):
+    # Decays near 1 (z = -12), near 0 (z = +30) and exactly 0 (z = +100:
+    # e^z overflows) in long runs, so the chunked kernel's running log-decay
+    # reaches its clamp and spans a wide range within a sub-chunk.
+    m, heads, dh = 256, 4, 64
+    n = m * heads * dh
+    q, k, v = rand(n, scale=0.2), rand(n, scale=0.2), rand(n)
+    z = np.where(np.arange(m * heads) % 7 == 0, 30.0, -12.0).astype(np.float32)
+    z[5 * heads:6 * heads] = 100.0
+    dec, bias = z, np.zeros(heads, dtype=np.float32)
     s0 = rand(heads * dh * dh, scale=0.1)
     sd = ops.upload(s0)
     y = ops.zeros(1)
