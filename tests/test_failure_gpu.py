@@ -44,3 +44,31 @@ def test_expired_wait_is_reported_and_the_context_survives(slm, ctx, small_model
     good.feed(ids)
     good.step(7)
     np.testing.assert_allclose(good.logits(), want, atol=1e-6)
+
+
+def test_expired_wait_reaches_the_sampler_not_a_stale_id(slm, ctx, small_model):
+    # A greedy slm_sample right after slm_step polls the step's mailbox; a step
+    # that gave up writes none, so the sampler must report the error once the
+    # stream is idle (never the arg-max of an earlier step).
+    model = slm.Model(ctx, small_model)
+    ids = np.arange(40) % 500
+    greedy = slm.Sampling()
+    ref = model.session()
+    ref.feed(ids)
+    ref.step(7)
+    want = ref.sample(greedy)
+
+    bad = model.session()
+    bad.feed(ids)
+    bad.step(3)
+    bad.sample(greedy)  # a good step first: its mailbox holds an id
+    bad.set_stall_test(True)
+    bad.step(7)
+    with pytest.raises(slm.SlmError) as e:
+        bad.sample(greedy)
+    assert e.value.code == 5 and "bounded wait" in str(e.value)
+
+    good = model.session()
+    good.feed(ids)
+    good.step(7)
+    assert good.sample(greedy) == want
