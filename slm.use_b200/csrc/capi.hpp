@@ -30,6 +30,7 @@ struct slm_ctx {
   size_t gemm_ws_bytes = 0;
   unsigned long long gemm_ws_gen = 0;  // bumped whenever gemm_ws moves (graphs holding it must be re-captured)
   unsigned* merge_cnt = nullptr;  // attention slice counters of slm_op_attend (zero between launches)
+  unsigned* gemv_cnt = nullptr;   // kGemvCounters row-block counters of the split GEMV (zero between launches)
   size_t merge_cnt_len = 0;
   // Live buffers and models of this context.  slm_ctx_free while some live
   // only marks the context closing; the last of them to be freed frees it

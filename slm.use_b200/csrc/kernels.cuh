@@ -25,7 +25,13 @@ struct LinearArgs {
   const void* wplanes = nullptr;
   // x already split the same way (written by b3_rms_split), or null.
   const void* xplanes = nullptr;
+  // Per-row-block arrival counters for the split GEMV (m ≤ 8), zero between
+  // launches (the last CTA of a block resets its own), or null: no split.
+  unsigned* cnt = nullptr;
 };
+// Workspace bytes of the m ≤ 8 GEMV's K slices for `a` (0: K is not split).
+size_t gemv_workspace(const LinearArgs& a);
+constexpr int kGemvCounters = 1 << 14;  // counters a context keeps for it
 void linear(const LinearArgs& a, cudaStream_t st);
 // SIMT path for 8 < m ≤ 64 tokens (skinny.cu): STORE/ADD epilogues, cols % 32
 // == 0; needs skinny_workspace(a) bytes of a.ws (0 when K is not split).

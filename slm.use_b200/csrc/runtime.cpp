@@ -77,8 +77,12 @@ void* stage(slm_ctx* c, const void* host, size_t bytes) {
 
 void gemm_workspace(slm_ctx* c, LinearArgs& a, bool capturing) {
   const bool b3 = b3_linear_ok(a), skinny = !b3 && skinny_ok(a), tc = !skinny && !b3 && a.m > 64 && tc_linear_ok(a);
-  if (skinny || b3 || tc) {
-    const size_t need = skinny ? skinny_workspace(a) : b3 ? b3_linear_workspace(a) : tc_linear_workspace(a);
+  const bool gemv = !b3 && !skinny && !tc && a.m <= 8;
+  if (skinny || b3 || tc || gemv) {
+    const size_t need = skinny ? skinny_workspace(a)
+                        : b3   ? b3_linear_workspace(a)
+                        : tc   ? tc_linear_workspace(a)
+                               : gemv_workspace(a);
     if (need > c->gemm_ws_bytes && !capturing) {
       SLM_CUDA(cudaStreamSynchronize(c->stream));
       dev_free(c->gemm_ws);
@@ -91,6 +95,7 @@ void gemm_workspace(slm_ctx* c, LinearArgs& a, bool capturing) {
   }
   a.ws = c->gemm_ws;
   a.ws_bytes = c->gemm_ws_bytes;
+  a.cnt = c->gemv_cnt;
 }
 
 }  // namespace slm
@@ -105,6 +110,7 @@ void destroy_ctx(slm_ctx* c) {
     dev_free(c->stage);
     dev_free(c->gemm_ws);
     dev_free(c->merge_cnt);
+    dev_free(c->gemv_cnt);
     dev_free(c->err);
     if (c->err_host) cudaFreeHost(c->err_host);
     if (c->mbox) cudaFreeHost(c->mbox);
@@ -159,6 +165,8 @@ int slm_ctx_new(int device, slm_ctx** out) {
       c->err = static_cast<int*>(dev_alloc(sizeof(int) * 4));
       SLM_CUDA(cudaMemsetAsync(c->err, 0, sizeof(int) * 4, c->stream));
       SLM_CUDA(cudaHostAlloc(reinterpret_cast<void**>(&c->err_host), sizeof(int) * 4, cudaHostAllocDefault));
+      c->gemv_cnt = static_cast<unsigned*>(dev_alloc(kGemvCounters * sizeof(unsigned)));
+      SLM_CUDA(cudaMemsetAsync(c->gemv_cnt, 0, kGemvCounters * sizeof(unsigned), c->stream));
       SLM_CUDA(cudaHostAlloc(reinterpret_cast<void**>(&c->mbox), 64, cudaHostAllocMapped));
       c->mbox[0] = c->mbox[1] = 0;
       SLM_CUDA(cudaHostGetDevicePointer(reinterpret_cast<void**>(&c->mbox_dev), c->mbox, 0));
