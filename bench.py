@@ -673,7 +673,8 @@ def run_b200(args, rank: int, world: int, local: int) -> dict | None:
         # 0..63) partitioned over the ranks, each rank's share decoded as one
         # batch (weights read once per step), 256 greedy steps; the total is
         # fixed, so this part scales strongly.
-        mine = c5_partition(64, rank, world)
+        n_seq = args.c5_sequences
+        mine = c5_partition(n_seq, rank, world)
         sessions = []
         firsts = []
         for q in mine:
@@ -701,7 +702,7 @@ def run_b200(args, rank: int, world: int, local: int) -> dict | None:
             bt.decode(nxt, 2)
             torch.cuda.synchronize(dev)
             torch.cuda.cudart().cudaProfilerStop()
-        extra["C5"] = {"value": 64 * 256 / (c5_ms / 1000.0), "unit": "tok/s (all ranks)", "sequences": 64,
+        extra["C5"] = {"value": n_seq * 256 / (c5_ms / 1000.0), "unit": "tok/s (all ranks)", "sequences": n_seq,
                        "per_rank": len(mine), "prompt": 2048, "decode_steps": 256, "loops": args.loops,
                        "scaling": "strong", "ms_per_step": c5_ms / 256, "sampling": "greedy",
                        "path": "slm_batch_decode (one graph-replayed step for the rank's sequences)"}
@@ -739,6 +740,8 @@ def main():
     ap.add_argument("--quick", action="store_true", help="skip the extra legs (R=8/16, C4, C5)")
     ap.add_argument("--profile-c5", action="store_true", help="bracket two C5 batched steps (after the timed "
                     "region) with cudaProfilerStart/Stop, for ncu --profile-from-start off")
+    ap.add_argument("--c5-sequences", type=int, default=64, help="sequences of the C5 leg (configs[4]: 64; "
+                    "64/N on one GPU reproduces one rank's share at N GPUs)")
     ap.add_argument("--extras", default="", help="comma list of extra legs to run (R8,R16,C4,C5); default all, "
                     "none with --quick")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
