@@ -243,7 +243,13 @@ uint64_t slm_rng_seed(uint64_t seed);
  * Greedy without a penalty, right after this session's slm_step on the
  * persistent kernel: returns the arg-max that step computed, as soon as the
  * step's mailbox (mapped pinned host memory) shows it, busy-waiting the
- * calling thread for the step (about one step's time, 0.2 ms at R = 4). */
+ * calling thread for the step (about one step's time, 0.2 ms at R = 4).
+ * In such a greedy slm_step/slm_sample loop, slm_step also queues the next
+ * persistent step behind the one it issues ("armed": it waits on the GPU,
+ * for at most 20 ms, for the token the next slm_step writes to mapped
+ * memory); any other call on the context cancels it, and one that times out
+ * is replaced by a plain launch.  SLM_MEGA_ARM=0 in the environment turns
+ * this off. */
 int slm_sample(slm_session* se, const slm_sampling* s, const uint32_t* recent, size_t n_recent,
                uint64_t* rng_state, uint32_t* out_id);
 

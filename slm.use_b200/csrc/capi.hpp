@@ -21,9 +21,18 @@ struct slm_ctx {
   // Mapped pinned words a persistent step launched by slm_step writes when it
   // ends: [0] its sequence number, [1] its arg-max | error word << 32
   // (slm_sample polls them instead of a copy and a stream synchronisation).
+  // [2]: the sequence number of an armed launch that ended without its step;
+  // [8] (its own cache line): the host's gate word for an armed launch,
+  // sequence << 32 | token (token 0xFFFFFFFF cancels).
   unsigned long long* mbox = nullptr;      // host address
   unsigned long long* mbox_dev = nullptr;  // device address of the same words
   unsigned long long mbox_seq = 0;         // last sequence number given to a launch
+  // An armed launch (a persistent step queued before its token is known,
+  // waiting on mbox[8]): any library call on the context other than the
+  // owner's slm_step cancels it (Device's constructor).
+  bool armed = false;
+  unsigned long long armed_seq = 0;
+  const void* armed_owner = nullptr;
   void* stage = nullptr;        // staging buffer for host arrays (ids, factors)
   size_t stage_bytes = 0;
   void* gemm_ws = nullptr;      // tensor-core GEMM workspace (grown on demand, outside captures)
@@ -55,9 +64,14 @@ void set_error(const std::string& s);
 // Makes the context's device current for the lifetime of the object.
 struct Device {
   int prev;
-  explicit Device(slm_ctx* c);
+  // Also cancels the context's armed launch, unless keep_armed.
+  explicit Device(slm_ctx* c, bool keep_armed = false);
   ~Device();
 };
+
+// Cancels the context's armed launch, if any: one host write (the kernel ends
+// without running its step).
+void disarm(slm_ctx* c);
 
 // Takes / drops a reference to a context (see slm_ctx::refs).
 void ctx_retain(slm_ctx* c);

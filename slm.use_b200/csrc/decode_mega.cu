@@ -209,6 +209,12 @@ __device__ __forceinline__ ulonglong2 ld_relaxed_u64x2(const unsigned long long*
   asm volatile("ld.relaxed.gpu.global.v2.u64 {%0,%1}, [%2];" : "=l"(v.x), "=l"(v.y) : "l"(p) : "memory");
   return v;
 }
+// A word the host writes (mapped pinned memory): system scope.
+__device__ __forceinline__ unsigned long long ld_sys_u64(const volatile unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
 __device__ __forceinline__ void st_relaxed_u64(unsigned long long* p, unsigned long long v) {
   asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
@@ -516,6 +522,7 @@ struct Smem {
   int flag;
   uint32_t cur_id;   // the token of the running step (steps after the first: the previous arg-max)
   unsigned step_ok;  // steps whose start the consumers have seen (the producer may read caches after it)
+  unsigned gate;     // armed launch: 0 undecided, 1 go, 2 cancelled
 };
 
 // ---------------------------------------------------------------------------
@@ -540,7 +547,18 @@ __device__ void producer(const Plan& P, Smem& sm, char* ring, long long pos) {
   unsigned k = 0;
   const unsigned inflight = P.inflight >= 1 && P.inflight < kStages ? (unsigned)P.inflight : (unsigned)kStages;
   int ready = 0;  // the last step whose caches and states this thread may read
+  bool gated = P.host_gate == nullptr;
   while (ring_w.next(T)) {
+    if (!gated && k == (unsigned)kStages) {
+      // Armed launch: the first ring of tiles is in flight; issue more only
+      // once the consumers know the step goes ahead (drain and end if not).
+      Spin sp;
+      unsigned g = 0;
+      while ((g = ld_acquire_cta_shared(&sm.gate)) == 0)
+        if (!sp.again(P.err)) break;
+      if (g != 1) break;
+      gated = true;
+    }
     if (T.mut && T.step > ready) {
       // K/V and GLA state of step s were written by step s - 1: wait until
       // the consumers have seen that step end (their acquire of its arg-max),
@@ -1832,9 +1850,56 @@ struct Cons {
     }
   }
 
+  // Armed launch: wait for the host's token (see Plan::host_gate).  True when
+  // the step goes ahead (its token in sm.cur_id); false when it was
+  // cancelled, which every CTA learns before any state is touched.
+  __device__ bool gate() {
+    const unsigned gtag = (unsigned)(P.gate_seq & 0x7fffffffu);
+    if (tid == 0) {
+      unsigned id = 0xffffffffu;
+      if (blockIdx.x == 0) {
+        const unsigned long long t0 = now_ns();
+        for (unsigned it = 0;; it++) {
+          const unsigned long long w = ld_sys_u64(P.host_gate);
+          if ((unsigned)(w >> 32) == (unsigned)P.gate_seq) {
+            id = (unsigned)w;
+            break;
+          }
+          if ((it & 15) == 15 && now_ns() - t0 > kArmNs) break;  // no token in time: cancel
+        }
+        st_relaxed_u64(P.next_tagged, ((unsigned long long)gtag << 32) | id);
+      }
+      // Every CTA takes the decision from CTA 0 (bounded like every other wait;
+      // CTA 0's own wait is far shorter).
+      Spin sp;
+      unsigned long long w = 0;
+      bool got = true;
+      while (((w = ld_relaxed_u64(P.next_tagged)) >> 32) != gtag)
+        if (!sp.again(P.err)) {
+          got = false;
+          break;
+        }
+      id = got ? (unsigned)w : 0xffffffffu;
+      if (id != 0xffffffffu) sm.cur_id = id;
+      sm.flag = id != 0xffffffffu ? 1 : 2;
+      st_release_cta_shared(&sm.gate, id != 0xffffffffu ? 1u : 2u);  // the producer may go on, or drain
+    }
+    consumers_sync();
+    const bool go = sm.flag == 1;
+    consumers_sync();  // sm.flag is reused by the step's waits
+    if (tid == 0) sm.flag = 0;
+    if (!go && blockIdx.x == 0 && tid == 0) {
+      // Tell the host this launch ended without running its step.
+      *(volatile unsigned long long*)(P.host_mbox + 2) = P.gate_seq;
+      __threadfence_system();
+    }
+    return go;
+  }
+
   __device__ void run() {
     if (tid < kDH / 2 && P.inv_freq) sm.inv_freq[tid] = __ldg(P.inv_freq + tid);
     if (tid == 0) sm.cur_id = P.host_id >= 0 ? (uint32_t)P.host_id : P.ids[0];
+    if (P.host_gate && !gate()) return;  // an armed launch whose step was cancelled
     const int np = P.nphases;
     stage_phase(0, 0);
     stage_wait();
@@ -1924,6 +1989,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_mega(const __grid_consta
     }
     sm.flag = 0;
     sm.step_ok = 0;
+    sm.gate = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   __syncthreads();

@@ -201,7 +201,17 @@ struct Plan {
   // arg-max back and synchronising the stream.
   unsigned long long* host_mbox;
   unsigned long long host_seq;
+  // Optional gate (an armed launch, queued before the host knows the step's
+  // token): CTA 0 polls host_gate (mapped pinned memory) for a word
+  // (gate_seq << 32 | token), bounded by kArmNs; the token 0xFFFFFFFF, or no
+  // word in time, cancels the step (the kernel then writes host_mbox[2] =
+  // gate_seq and ends without touching the session's state).  The decision
+  // reaches the other CTAs through next_tagged, tagged with gate_seq (bit 31
+  // clear, so it never matches a step's arg-max tag).
+  const volatile unsigned long long* host_gate;
+  unsigned long long gate_seq;
 };
+constexpr unsigned long long kArmNs = 20000000ull;  // 20 ms without a token: the armed step cancels itself
 
 }  // namespace mega
 }  // namespace slm

@@ -139,6 +139,12 @@ struct slm_session {
   unsigned* merge_cnt = nullptr;         // attention slice counters of the graph path (zero between launches)
   bool argmax_valid = false;             // the logits come from a persistent step
   unsigned long long mbox_want = 0;      // mailbox sequence number of this session's pending slm_step (0: none)
+  // The armed launch this session's last slm_step fed (sequence number and
+  // token), kept so a launch that ran out of time before the token reached
+  // it can be replaced by a plain one.
+  unsigned long long fed_seq = 0;
+  uint32_t fed_id = 0;
+  bool greedy_loop = false;  // the last slm_sample took the mailbox: slm_step arms the next step
   // Pinned host words for the per-token transfers (ids in and out, RNG state).
   struct HostIO {
     uint32_t id_in, id_out;
@@ -1035,6 +1041,35 @@ void mega_step(slm_session* se, long long host_id = -1) {
   se->ctx->argmax_owner = se;
 }
 
+// Arming: in a greedy step/sample loop, slm_step queues the next persistent
+// step right behind the one it issues, waiting (bounded) on the context's gate
+// word; the next slm_step only writes its token there.  The launch and the
+// kernel's start then overlap the running step and the host's turn-around
+// instead of following them.  SLM_MEGA_ARM=0 disables it.
+bool arm_enabled() {
+  static const bool on = [] {
+    const char* e = std::getenv("SLM_MEGA_ARM");
+    return !(e && *e == '0');
+  }();
+  return on;
+}
+
+void arm(slm_session* se) {
+  slm_ctx* c = se->ctx;
+  ensure_caps(se, 1);
+  if (se->plan_stale) build_plan(se, true);
+  if (se->keys_stale) refresh_next_keys(se);
+  mega::Plan p = se->plan_host;
+  p.host_gate = c->mbox_dev + 8;
+  p.gate_seq = ++c->mbox_seq;
+  p.host_mbox = c->mbox_dev;
+  p.host_seq = p.gate_seq;
+  mega::launch(p, se->grid, c->stream);
+  c->armed = true;
+  c->armed_seq = p.gate_seq;
+  c->armed_owner = se;
+}
+
 // n greedy persistent steps for the id in ids_dev[0], as few launches as the
 // plan allows: one launch runs the steps back to back (each step's arg-max is
 // the next one's token), so later steps pay neither a launch nor a cold
@@ -1784,6 +1819,7 @@ int slm_session_loops(const slm_session* se, size_t* out) {
 int slm_session_set(slm_session* se, int option, int64_t value) {
   return guard([&] {
     SLM_REQUIRE(se, "session is null");
+    disarm(se->ctx);  // a launch armed with the old settings must not run
     if (option == SLM_OPT_GRAPH) {
       Device dev(se->ctx);
       se->use_graph = value != 0;
@@ -1886,14 +1922,33 @@ int slm_step(slm_session* se, uint32_t id) {
   return guard([&] {
     SLM_REQUIRE(se, "session is null");
     SLM_REQUIRE(id < se->model->cfg.vocab, "token id out of range");
-    Device dev(se->ctx);
-    // The pinned word is read by the copy engine in stream order; wait for an
-    // earlier step's copy of it before overwriting.
+    slm_ctx* c = se->ctx;
+    const volatile unsigned long long* mb = c->mbox;
+    if (se->use_mega && c->armed && c->armed_owner == se && mb[2] != c->armed_seq) {
+      // This session's armed launch is waiting: hand it the token.
+      *(volatile unsigned long long*)(c->mbox + 8) = (c->armed_seq << 32) | id;
+      se->mbox_want = se->fed_seq = c->armed_seq;
+      se->fed_id = id;
+      c->armed = false;
+      c->armed_owner = nullptr;
+      se->pos += 1;
+      se->argmax_valid = true;
+      c->argmax_owner = se;
+      if (se->greedy_loop && arm_enabled()) {
+        Device dev(c, true);
+        arm(se);
+      }
+      return;
+    }
+    Device dev(se->ctx);  // (cancels an armed launch that is not this step's)
     if (se->use_mega) {  // the id travels with the launch
       ensure_caps(se, 1);
       mega_step(se, id);
+      if (se->greedy_loop && arm_enabled()) arm(se);
       return;
     }
+    // The pinned word is read by the copy engine in stream order; wait for an
+    // earlier step's copy of it before overwriting.
     if (se->io_busy) SLM_CUDA(cudaEventSynchronize(se->io_event));
     se->io->id_in = id;
     SLM_CUDA(cudaMemcpyAsync(se->ids_dev, &se->io->id_in, sizeof(uint32_t), cudaMemcpyHostToDevice, se->ctx->stream));
@@ -2011,34 +2066,47 @@ int slm_sample(slm_session* se, const slm_sampling* sp, const uint32_t* recent, 
   return guard([&] {
     SLM_REQUIRE(se && rng_state && out_id && (recent || n_recent == 0), "bad arguments");
     check_sampling(sp);
-    Device dev(se->ctx);
     cudaStream_t s = se->ctx->stream;
     // Greedy without a penalty on logits of a persistent step: that step
     // already computed the arg-max (same order: first maximum, NaN never
     // wins) and pick draws nothing from the RNG (src/sample.rs:33-45).
     const bool fast = se->argmax_valid && sp->temperature <= 0.0f && (sp->repeat_penalty == 1.0f || n_recent == 0);
-    if (fast) {
+    se->greedy_loop = false;
+    {
       slm_ctx* c = se->ctx;
-      if (c->argmax_owner == se && se->mbox_want) {
+      if (fast && c->argmax_owner == se && se->mbox_want) {
+        // (This session's armed next step, queued behind, stays armed.)
+        Device dev(c, true);
         // slm_step's launch hands its arg-max over in the mailbox: poll it
         // while the stream runs; a step that gave up writes none, so once the
         // stream is idle without it, the copy below reports the error.
-        const unsigned long long want = se->mbox_want;
+        unsigned long long want = se->mbox_want;
         se->mbox_want = 0;
         const volatile unsigned long long* mb = c->mbox;
         bool got = false;
-        for (unsigned it = 1;; it++) {
-          if (mb[0] == want) {
-            got = true;
-            break;
-          }
-          if ((it & 255) == 0 && cudaStreamQuery(s) != cudaErrorNotReady) {
-            got = mb[0] == want;
-            break;
-          }
+        for (int attempt = 0; attempt < 2; attempt++) {
+          for (unsigned it = 1;; it++) {
+            if (mb[0] == want) {
+              got = true;
+              break;
+            }
+            if ((it & 255) == 0 && cudaStreamQuery(s) != cudaErrorNotReady) {
+              got = mb[0] == want;
+              break;
+            }
 #if defined(__x86_64__)
-          __builtin_ia32_pause();
+            __builtin_ia32_pause();
 #endif
+          }
+          if (got || se->fed_seq != want || mb[2] != want) break;
+          // The armed launch ran out of time before slm_step's token reached
+          // it and ended without its step: run that step now (after ending
+          // the launch armed behind it).
+          disarm(c);
+          se->pos -= 1;
+          mega_step(se, se->fed_id);
+          want = se->mbox_want;
+          se->mbox_want = 0;
         }
         if (cudaPeekAtLastError() == cudaErrorNotReady) (void)cudaGetLastError();  // the queries' answer, not an error
         if (got) {
@@ -2047,10 +2115,15 @@ int slm_sample(slm_session* se, const slm_sampling* sp, const uint32_t* recent, 
           if ((w >> 32) == 0) {
             se->io_busy = false;
             *out_id = static_cast<uint32_t>(w);
+            se->greedy_loop = se->use_mega;  // slm_step arms the steps after the next one
             return;
           }
         }
       }
+    }
+    Device dev(se->ctx);
+    if (fast) {
+      slm_ctx* c = se->ctx;
       if (c->argmax_owner == se) {  // one copy: the error word and this step's arg-max beside it
         SLM_CUDA(cudaMemcpyAsync(c->err_host, c->err, 2 * sizeof(int), cudaMemcpyDeviceToHost, s));
         SLM_CUDA(cudaStreamSynchronize(s));

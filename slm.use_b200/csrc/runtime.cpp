@@ -19,7 +19,15 @@ thread_local std::string g_last_error;
 
 void set_error(const std::string& s) { g_last_error = s; }
 
-Device::Device(slm_ctx* c) : prev(-1) {
+void disarm(slm_ctx* c) {
+  if (!c->armed) return;
+  *(volatile unsigned long long*)(c->mbox + 8) = (c->armed_seq << 32) | 0xffffffffull;
+  c->armed = false;
+  c->armed_owner = nullptr;
+}
+
+Device::Device(slm_ctx* c, bool keep_armed) : prev(-1) {
+  if (!keep_armed) disarm(c);
   cudaGetDevice(&prev);
   if (prev != c->device) SLM_CUDA(cudaSetDevice(c->device));
 }
@@ -167,8 +175,8 @@ int slm_ctx_new(int device, slm_ctx** out) {
       SLM_CUDA(cudaHostAlloc(reinterpret_cast<void**>(&c->err_host), sizeof(int) * 4, cudaHostAllocDefault));
       c->gemv_cnt = static_cast<unsigned*>(dev_alloc(kGemvCounters * sizeof(unsigned)));
       SLM_CUDA(cudaMemsetAsync(c->gemv_cnt, 0, kGemvCounters * sizeof(unsigned), c->stream));
-      SLM_CUDA(cudaHostAlloc(reinterpret_cast<void**>(&c->mbox), 64, cudaHostAllocMapped));
-      c->mbox[0] = c->mbox[1] = 0;
+      SLM_CUDA(cudaHostAlloc(reinterpret_cast<void**>(&c->mbox), 128, cudaHostAllocMapped));
+      for (int i = 0; i < 16; i++) c->mbox[i] = 0;
       SLM_CUDA(cudaHostGetDevicePointer(reinterpret_cast<void**>(&c->mbox_dev), c->mbox, 0));
     } catch (...) {
       delete c;
