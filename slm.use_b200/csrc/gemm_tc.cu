@@ -45,8 +45,10 @@ using OpClass = cutlass::arch::OpClassTensorOp;
 #ifndef SLM_TC_TILE_K
 #define SLM_TC_TILE_K 32
 #endif
+// 64 × 64 × 32 tiles: measured on prefill (4096 ids, R = 4) 134.8k tok/s against 131.0k with
+// 128 × 64, 129.0k with 64 × 128, 130.7k with a K tile of 64, 122.6k with 64 × 32.
 #ifndef SLM_TC_TILE_M
-#define SLM_TC_TILE_M 128
+#define SLM_TC_TILE_M 64
 #endif
 using TileShape = Shape<Int<SLM_TC_TILE_M>, Int<SLM_TC_TILE_N>, Int<SLM_TC_TILE_K>>;
 // The split A operand kept in shared memory (the "Smem" schedule) measured
