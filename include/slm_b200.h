@@ -249,7 +249,8 @@ uint64_t slm_rng_seed(uint64_t seed);
  * for at most 20 ms, for the token the next slm_step writes to mapped
  * memory); any other call on the context cancels it, and one that times out
  * is replaced by a plain launch.  SLM_MEGA_ARM=0 in the environment turns
- * this off. */
+ * this off; so do CUDA_LAUNCH_BLOCKING=1 and any tool that makes launches
+ * return only after the kernel ends (detected at the first armed launch). */
 int slm_sample(slm_session* se, const slm_sampling* s, const uint32_t* recent, size_t n_recent,
                uint64_t* rng_state, uint32_t* out_id);
 

@@ -1046,12 +1046,20 @@ void mega_step(slm_session* se, long long host_id = -1) {
 // word; the next slm_step only writes its token there.  The launch and the
 // kernel's start then overlap the running step and the host's turn-around
 // instead of following them.  SLM_MEGA_ARM=0 disables it.
+// It is off where launches are serialised (CUDA_LAUNCH_BLOCKING=1, or a
+// profiler that waits for each kernel): there an armed step runs while the
+// host is still inside the launch call, so it can only run out of time.  arm()
+// notices that (the stream is already idle when the launch returns) and turns
+// arming off for the rest of the process.
+std::atomic<bool> g_arm_serialised{false};
 bool arm_enabled() {
   static const bool on = [] {
     const char* e = std::getenv("SLM_MEGA_ARM");
-    return !(e && *e == '0');
+    if (e && *e == '0') return false;
+    const char* b = std::getenv("CUDA_LAUNCH_BLOCKING");
+    return !(b && *b == '1');
   }();
-  return on;
+  return on && !g_arm_serialised.load(std::memory_order_relaxed);
 }
 
 void arm(slm_session* se) {
@@ -1068,6 +1076,16 @@ void arm(slm_session* se) {
   c->armed = true;
   c->armed_seq = p.gate_seq;
   c->armed_owner = se;
+  // The armed kernel waits for a token no one has written yet: an idle stream
+  // here means the launch returned only after the kernel had given up.
+  const cudaError_t q = cudaStreamQuery(c->stream);
+  if (q == cudaErrorNotReady) {
+    if (cudaPeekAtLastError() == cudaErrorNotReady) (void)cudaGetLastError();  // the query's answer, not an error
+  } else if (q == cudaSuccess) {
+    g_arm_serialised.store(true, std::memory_order_relaxed);
+    c->armed = false;
+    c->armed_owner = nullptr;
+  }
 }
 
 // n greedy persistent steps for the id in ids_dev[0], as few launches as the
