@@ -615,6 +615,55 @@ __global__ void __launch_bounds__(256) k_attn_combine(const float* __restrict__ 
   }
 }
 
+// The same merge for head size 64, one warp per (query, head): the splits'
+// weights e^{m_s − M} live in the lanes (32 splits at a time) and every lane
+// adds its two dims over the splits in order.  One wave for a chunk's
+// 256 × 12 pairs, instead of a 256-thread CTA with block reductions each.
+__global__ void __launch_bounds__(256) k_attn_combine64(const float* __restrict__ part, int nsplit, int m, int heads,
+                                                        float* __restrict__ y, int ldy) {
+  constexpr int DH = 64;
+  const int lane = threadIdx.x & 31;
+  const int pair = blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (pair >= m * heads) return;  // whole warps
+  const int i = pair / heads, h = pair % heads;
+  const size_t stride = (size_t)m * heads * (DH + 2);
+  const float* p0 = part + ((size_t)i * heads + h) * (DH + 2);
+  float M = -INFINITY;
+  for (int s = lane; s < nsplit; s += 32) M = fmaxf(M, __ldcg(p0 + s * stride + DH));
+  M = warp_max(M);
+  float L = 0.0f, a0 = 0.0f, a1 = 0.0f;
+  for (int s0 = 0; s0 < nsplit; s0 += 32) {
+    const int s = s0 + lane;
+    float c = 0.0f;
+    if (s < nsplit) {
+      const float ms = __ldcg(p0 + s * stride + DH);
+      c = (M == -INFINITY || ms == -INFINITY) ? 0.0f : expf(ms - M);
+      L = fmaf(__ldcg(p0 + s * stride + DH + 1), c, L);
+    }
+    const int n = min(32, nsplit - s0);
+    for (int k = 0; k < n; k++) {
+      const float ck = __shfl_sync(0xffffffffu, c, k);
+      const float* ps = p0 + (size_t)(s0 + k) * stride;
+      a0 = fmaf(__ldcg(ps + lane), ck, a0);
+      a1 = fmaf(__ldcg(ps + 32 + lane), ck, a1);
+    }
+  }
+  L = warp_sum(L);
+  float* yo = y + (size_t)i * ldy + (size_t)h * DH;
+  yo[lane] = L > 0.0f ? a0 / L : 0.0f;
+  yo[32 + lane] = L > 0.0f ? a1 / L : 0.0f;
+}
+
+void combine(const float* part, int nsplit, const AttnGeom& g, float* y, int ldy, cudaStream_t st) {
+  if (g.dh == 64) {
+    k_attn_combine64<<<(g.m * g.heads + 7) / 8, 256, 0, st>>>(part, nsplit, g.m, g.heads, y, ldy);
+    SLM_LAUNCHED("k_attn_combine64");
+    return;
+  }
+  k_attn_combine<<<g.m * g.heads, 256, 0, st>>>(part, nsplit, g.m, g.heads, g.dh, y, ldy);
+  SLM_LAUNCHED("k_attn_combine");
+}
+
 template <int DH>
 void launch_tile(const float* q, int ldq, const float* K, const float* V, const AttnGeom& g, const long long* pos_ptr,
                  int nsplit, float* part, cudaStream_t st) {
@@ -698,8 +747,7 @@ void attention(const float* q, int ldq, const float* K, const float* V, const At
     default: fail(SLM_ERR_INVALID, "attend: head size must be one of 8, 16, 32, 64, 128, 256");
   }
   if (merged) return;
-  k_attn_combine<<<g.m * g.heads, 256, 0, st>>>(part, nsplit, g.m, g.heads, g.dh, y, ldy);
-  SLM_LAUNCHED("k_attn_combine");
+  combine(part, nsplit, g, y, ldy, st);
 }
 
 void attention_rows(const float* q, int ldq, const AttnRows& rows, const AttnGeom& g, int nsplit, float* part,
@@ -722,8 +770,7 @@ void attention_rows(const float* q, int ldq, const AttnRows& rows, const AttnGeo
 #undef SLM_ROWS
   SLM_LAUNCHED("k_attn_split");
   if (cnt) return;
-  k_attn_combine<<<g.m * g.heads, 256, 0, st>>>(part, nsplit, g.m, g.heads, g.dh, y, ldy);
-  SLM_LAUNCHED("k_attn_combine");
+  combine(part, nsplit, g, y, ldy, st);
 }
 
 }  // namespace slm
