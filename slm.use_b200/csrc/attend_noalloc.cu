@@ -74,6 +74,7 @@ extern "C" int slm_op_attend_noalloc(slm_ctx* c, float* y, const float* q, const
     g.reach = at->reach == SIZE_MAX ? 0 : (long long)at->reach;
     g.gap = (long long)at->gap, g.cap = (long long)at->cap;
     g.heads = (int)at->heads, g.key_heads = (int)at->key_heads, g.dh = (int)at->dh, g.scale = at->scale;
+    g.err = c->err;
     // Span of positions any query sees (Attn::span, reference src/ops.rs:54-59).
     long long base = g.reach == 0 ? 0 : ((long long)at->pos > g.reach - 1 ? (long long)at->pos - (g.reach - 1) : 0);
     long long span = (long long)(at->pos + at->m) - g.gap - base;

@@ -21,22 +21,11 @@
 
 #include "common.cuh"
 #include "kernels.cuh"
+#include "window.cuh"
 
 namespace slm {
 
 namespace {
-
-struct Range {
-  long long lo, hi;
-};
-
-__device__ __forceinline__ Range visible(long long p, long long reach, long long gap) {
-  Range r;
-  r.lo = (reach <= 0 || p < reach - 1) ? 0 : p - (reach - 1);
-  r.hi = p + 1 - gap;
-  if (r.hi < r.lo) r.hi = r.lo;
-  return r;
-}
 
 // Merge two online-softmax partials (m, l, acc) into the first.
 __device__ __forceinline__ void merge(float& m, float& l, float* acc, float om, float ol, const float* oacc, int n) {
@@ -668,6 +657,10 @@ template <int DH>
 void launch_tile(const float* q, int ldq, const float* K, const float* V, const AttnGeom& g, const long long* pos_ptr,
                  int nsplit, float* part, cudaStream_t st) {
   if constexpr (DH == 64) {
+    if (attention_tc_on()) {
+      attention_tc(q, ldq, K, V, g, pos_ptr, nsplit, part, st);
+      return;
+    }
     // The shared-memory limit is a per-device function attribute: set it on
     // the first launch on each device (a process may drive several).
     constexpr int kDevices = 64;
@@ -708,7 +701,9 @@ bool launch_dh(const float* q, int ldq, const float* K, const float* V, const At
 
 int attn_splits(const AttnGeom& g, long long max_span) {
   if (max_span < 1) max_span = 1;
+  const bool tc = g.m > 8 && g.dh == 64 && attention_tc_on();
   long long ctas = (g.m <= 8 || g.dh > 128) ? (long long)g.heads * g.m
+                  : tc                       ? (long long)g.heads * ((g.m + 127) / 128)
                   : g.dh == 64               ? (long long)g.heads * ((g.m + FQ - 1) / FQ)
                                              : (long long)g.heads * ((g.m + 15) / 16);
   // Decode-sized calls (the slice pass): at most two 256-thread CTAs per SM
@@ -719,7 +714,9 @@ int attn_splits(const AttnGeom& g, long long max_span) {
   // exactly two per SM, so their count rounds down to one full wave.
   const bool slices = g.m <= 8 || g.dh > 128;
   constexpr long long per_sm = 2, min_pos = 256;
-  long long want = (g.m > 8 && g.dh == 64) ? std::max(1ll, (2 * 148) / ctas)
+  // The tensor-core pass holds one CTA per SM: one wave of them.
+  long long want = tc                       ? std::max(1ll, 148 / ctas)
+                   : (g.m > 8 && g.dh == 64) ? std::max(1ll, (2 * 148) / ctas)
                    : slices                ? (per_sm * 148 + ctas - 1) / ctas
                                            : (2 * 148 + ctas - 1) / ctas;
   const long long step = slices ? min_pos : 128;  // positions per slice at least

@@ -61,6 +61,7 @@ struct AttnGeom {
   int heads, key_heads, dh;
   float scale;
   long long pos0 = 0;  // position of the first query when no device position pointer is given
+  int* err = nullptr;  // device error word (bit 32: a bounded wait of the tensor-core pass expired)
 };
 // Per-row sequences of a batched decode step (device arrays of g.m entries).
 struct AttnRows {
@@ -70,6 +71,11 @@ struct AttnRows {
   const long long* cap = nullptr;  // per-row capacities (global caches of different sizes), or null: g.cap
 };
 int attn_splits(const AttnGeom& g, long long max_span);
+// Prefill slice pass on the tensor cores (head size 64, m > 8): on unless
+// SLM_ATTN_TC=0 (read once); attn_splits and attention() follow it.
+bool attention_tc_on();
+void attention_tc(const float* q, int ldq, const float* K, const float* V, const AttnGeom& g,
+                  const long long* pos_ptr, int nsplit, float* part, cudaStream_t st);
 size_t attn_part_floats(const AttnGeom& g, int nsplit);
 // y[i][h·dh + e]; part holds attn_part_floats(g, nsplit) floats.  With cnt
 // (heads·m counters, zero on entry and left zero) decode-sized calls merge

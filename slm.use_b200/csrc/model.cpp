@@ -430,6 +430,7 @@ void block(slm_session* se, const Block& b, LState& st, float* x, size_t m) {
     run_linear(s, b.qkv, se->n, id, im, se->mix, (int)(3 * d), EPI_STORE, nullptr, 0, 0, np);
     ew_rope_store(se->mix, 3 * d, md->inv_freq, se->pos_dev, m, heads, dh, st.cap, se->q, st.k, st.v, s);
     AttnGeom g{im, (long long)c.window, 0, (long long)st.cap, (int)heads, (int)heads, (int)dh, scale};
+    g.err = se->ctx->err;
     int ns = attn_splits(g, (long long)(c.window + m - 1));
     attention(se->q, id, st.k, st.v, g, se->pos_dev, ns, se->part, se->y, id, s, se->merge_cnt);
   } else if (b.kind == 'L') {
@@ -475,6 +476,7 @@ void block(slm_session* se, const Block& b, LState& st, float* x, size_t m) {
     size_t far = c.far ? c.window : 0;
     if (se->capturing || se->pos + m > far) {
       AttnGeom g{im, 0, (long long)far, (long long)st.cap, (int)heads, (int)kh, (int)dh, scale};
+      g.err = se->ctx->err;
       long long span = (long long)(se->capturing ? st.cap : se->pos + m);
       int ns = attn_splits(g, span);
       attention(se->q, id, st.k, st.v, g, se->pos_dev, ns, se->part, se->y, id, s, se->merge_cnt);
@@ -1190,6 +1192,7 @@ void check_device_error(slm_ctx* c, slm_session* se = nullptr) {
     std::string why;
     if (h & 1) why += " token id out of range;";
     if (h & 8) why += " a bounded wait in the decode kernel expired (state of this step is undefined);";
+    if (h & 32) why += " a bounded wait in the tensor-core attention pass expired (its output is undefined);";
     if (h & 16)
       why += " a residual value in the decode kernel was non-finite or beyond 2^22 in magnitude (state of this step "
              "is undefined);";

@@ -163,6 +163,29 @@ def test_attend(ops, oracle, pos, m, reach, gap, cap, heads, kh, dh):
     close(y.read(m * heads * dh), want, atol=2e-5)
 
 
+@pytest.mark.parametrize("growth", [4.0, 6.5])
+def test_attend_with_scores_growing_along_the_window(ops, oracle, growth):
+    # Scores step up by `growth` nats every 64 positions (four steps, then
+    # back down), so a query's running max grows across the first tiles of
+    # its slice: the tensor-core pass rescales the output it holds in tensor
+    # memory (each tile at 6.5 nats, every other at 4, when the max has moved
+    # past 2^8).
+    pos, m, reach, gap, cap, heads, kh, dh = 3840, 256, 4096, 0, 4352, 2, 2, 64
+    scale = 0.125
+    qv = rand(dh)
+    qv *= np.float32(8.0 / np.linalg.norm(qv))  # |q| = 8: score = scale·|q|·(k along q)
+    q = (np.tile(qv, m * heads) + rand(m * heads * dh, scale=0.05)).astype(np.float32)
+    level = growth * ((np.arange(cap) // 64) % 4)  # slot = position: no wrap below 4352
+    k1 = (level[:, None] * (qv / 8.0)[None, :] / np.float32(scale * 8.0)).astype(np.float32)
+    k = (np.tile(k1.ravel(), kh) + rand(kh * cap * dh, scale=0.1)).astype(np.float32)
+    v = rand(kh * cap * dh)
+    y, scores = ops.zeros(1), ops.zeros(1)
+    ops.attend(y, scores, ops.upload(q), ops.upload(k), ops.upload(v), pos=pos, m=m, reach=reach, gap=gap, cap=cap,
+               heads=heads, key_heads=kh, dh=dh, scale=scale)
+    want = oracle.attend(q, k, v, pos, m, reach, gap, cap, heads, kh, dh, scale)
+    close(y.read(m * heads * dh), want, atol=2e-5)
+
+
 def test_attend_reads_q_at_an_odd_offset(ops, oracle):
     # q at a view offset that is not a multiple of 4 floats: staged, not faulted.
     pos, m, reach, gap, cap, heads, kh, dh = 300, 20, 64, 0, 320, 4, 4, 64
