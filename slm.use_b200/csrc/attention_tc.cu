@@ -7,30 +7,33 @@
 // (hi = bf16(x), lo = bf16(x − hi); |x − hi − lo| ≤ 2^-18 |x|) and each
 // product is taken as hi·hi + hi·lo + lo·hi, accumulated in fp32 in tensor
 // memory: three kind::f16 MMAs per k-step, the dropped lo·lo term below
-// 2^-16 of the product.  The softmax itself (mask, max, exp, sums) and the
-// output accumulators stay in fp32 registers.
+// 2^-16 of the product.  The softmax itself (mask, max, exp, sums) stays in
+// fp32 registers.
 //
 // One CTA = 128 queries of one head × one slice of their key range
-// (grid (nsplit, ceil(m/128), heads)), 288 threads:
+// (grid (nsplit, ceil(m/128), heads)), 320 threads, one CTA per SM:
 //  * warp 8 (one thread) fetches each 64-position tile's fp32 K and V rows
-//    from the ring with bulk copies into one of three buffers, as soon as the
-//    MMAs of the tile three back are done with it;
+//    from the ring with bulk copies into one of four shared buffers, as soon
+//    as the MMAs of the tile four back are done with it;
 //  * warps 4–7 split each landed tile in place into the layout the MMA reads;
-//  * warps 0–3 own one query row per thread (tensor-memory lane = row).
-//    Thread 0 issues the MMAs: QKᵀ two tiles ahead into two score buffers,
-//    P·V accumulating into one output in tensor memory.  Every thread reads
+//  * warp 9 (one thread) issues the MMAs: QKᵀ two tiles ahead into two score
+//    buffers, P·V accumulating into one output, all in tensor memory;
+//  * warps 0–3 own one query row per thread (tensor-memory lane = row).  Each
+//    writes its row of Q (split) into tensor memory once; per tile it reads
 //    its row of scores, masks it to its window, runs the online softmax and
-//    writes its row of P (split) to one of two shared buffers.  P is taken
-//    against a reference max that trails the running max by at most 2^8, so
-//    the output in tensor memory is rescaled (read, scaled, written back)
-//    only in the rare tiles where a row's max grows past that.
-// Shared tiles use the no-swizzle core-matrix layout: element (r, c) of an
-// [R][64] bf16 tile sits at (r % 8)·16 + (r / 8)·1024 + (c / 8)·128 +
-// (c % 8)·2 bytes (core matrices of 8 rows × 16 bytes).  Q, K and P are
-// K-major operands in it (leading byte offset 128 along K, stride byte
-// offset 1024 along M/N); V, stored the same way as [key][dh], is the
-// MN-major B operand of P·V (K = key: 1024 bytes between 8-key groups; N =
-// dh: 128 bytes between 8-dim groups).
+//    writes its row of P (split) into one of two tensor-memory buffers.  P is
+//    taken against a reference max that trails the running max by at most
+//    2^8, so the output in tensor memory is rescaled (read, scaled, written
+//    back) only in the rare tiles where a row's max grows past that.
+// Q and P are the A operands of their MMAs straight from tensor memory (one
+// row per lane, two bf16 of K per 32-bit column): the tensor core reads only
+// K and V from shared memory.  Shared tiles use the no-swizzle core-matrix
+// layout: element (r, c) of an [R][64] bf16 tile sits at (r % 8)·16 +
+// (r / 8)·1024 + (c / 8)·128 + (c % 8)·2 bytes (core matrices of 8 rows × 16
+// bytes).  K is the K-major B operand of QKᵀ in it (leading byte offset 128
+// along K, stride byte offset 1024 along N); V, stored the same way as
+// [key][dh], is the MN-major B operand of P·V (K = key: 1024 bytes between
+// 8-key groups; N = dh: 128 bytes between 8-dim groups).
 // Partials have the layout of the other slice passes (acc[64], max, sum per
 // (slice, query, head)) and are merged by the same combine.
 //
@@ -51,16 +54,16 @@ namespace slm {
 namespace {
 
 constexpr int TQ = 128, TK = 64, TDH = 64;
-constexpr uint32_t kTile = 16384;          // one [128][64] bf16 tile
 constexpr uint32_t kHalf = 8192;           // one [64][64] bf16 tile
-constexpr uint32_t kQh = 0, kQl = kTile;   // Q split, 128 × 64
-constexpr int kBufs = 3;                   // K/V tile buffers
-constexpr uint32_t kKV = 2 * kTile;        // buffers of Kh, Kl, Vh, Vl
+constexpr int kBufs = 4;                   // K/V tile buffers
+constexpr uint32_t kKV = 0;                // buffers of Kh, Kl, Vh, Vl
 constexpr uint32_t kKVBuf = 4 * kHalf;
-constexpr uint32_t kP = kKV + kBufs * kKVBuf;  // two buffers of P split (h, l), 128 × 64 each
-constexpr uint32_t kBars = kP + 4 * kTile;  // mbarriers, tensor-memory address, abort flag
-constexpr size_t kTcSmem = kBars + 192 + 1024;  // + slack to align the base to 1024
-constexpr uint32_t kTmemCols = 256;        // scores: two buffers at columns 0 and 64; output: 128–191
+constexpr uint32_t kBars = kKV + kBufs * kKVBuf;  // mbarriers, tensor-memory address, abort flag
+constexpr size_t kTcSmem = kBars + 192 + 1024;     // + slack to align the base to 1024
+// Tensor-memory columns: two score buffers, the output, Q split (bf16 pairs,
+// two per column), two buffers of P split.
+constexpr uint32_t kColS = 0, kColO = 128, kColQ = 192, kColP = 256;
+constexpr uint32_t kTmemCols = 512;
 constexpr float kLazy = 8.0f;              // rescale a row's output only when its max rises by more (log2 units)
 constexpr unsigned long long kTcWaitNs = 2000000000ull;
 
@@ -91,30 +94,28 @@ __device__ __forceinline__ uint64_t mdesc(uint32_t a, uint32_t lbo, uint32_t sbo
          (1ull << 46);
 }
 
-__device__ __forceinline__ void umma(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+// An MMA with A in tensor memory (one row per lane, two bf16 of K per column).
+__device__ __forceinline__ void umma_ts(uint32_t d, uint32_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
   asm volatile(
       "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n}\n" ::"r"(d),
-      "l"(a), "l"(b), "r"(idesc), "r"(acc), "r"(0u), "r"(0u), "r"(0u), "r"(0u));
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, {%5, %6, %7, %8}, p;\n}\n" ::"r"(d),
+      "r"(a), "l"(b), "r"(idesc), "r"(acc), "r"(0u), "r"(0u), "r"(0u), "r"(0u));
 }
 
-// d (+)= ah·bh + ah·bl + al·bh over K = 64 in four k-steps of 16: A K-major
-// (256 bytes a step); B K-major (QKᵀ: 256 bytes a step) or MN-major (P·V:
-// two 8-key groups, 2048 bytes, a step).
+// d (+)= ah·bh + ah·bl + al·bh over K = 64 in four k-steps of 16, A in tensor
+// memory at columns ah, al (8 columns a step); B K-major (QKᵀ: 256 bytes a
+// step) or MN-major (P·V: two 8-key groups, 2048 bytes, a step).
 template <bool kBmn>
-__device__ __forceinline__ void umma3(uint32_t d, uint32_t ah, uint32_t al, uint32_t bh, uint32_t bl,
-                                      bool accumulate = false) {
+__device__ __forceinline__ void umma3t(uint32_t d, uint32_t ah, uint32_t al, uint32_t bh, uint32_t bl,
+                                       bool accumulate = false) {
   constexpr uint32_t idesc = kBmn ? kIdescO : kIdescS;
   constexpr uint32_t bstep = kBmn ? 2048 : 256, blbo = kBmn ? 1024 : 128, bsbo = kBmn ? 128 : 1024;
 #pragma unroll
-  for (int k = 0; k < 4; k++)
-    umma(d, mdesc(ah + 256 * k, 128, 1024), mdesc(bh + bstep * k, blbo, bsbo), idesc, accumulate || k > 0);
+  for (int k = 0; k < 4; k++) umma_ts(d, ah + 8 * k, mdesc(bh + bstep * k, blbo, bsbo), idesc, accumulate || k > 0);
 #pragma unroll
-  for (int k = 0; k < 4; k++)
-    umma(d, mdesc(ah + 256 * k, 128, 1024), mdesc(bl + bstep * k, blbo, bsbo), idesc, 1);
+  for (int k = 0; k < 4; k++) umma_ts(d, ah + 8 * k, mdesc(bl + bstep * k, blbo, bsbo), idesc, 1);
 #pragma unroll
-  for (int k = 0; k < 4; k++)
-    umma(d, mdesc(al + 256 * k, 128, 1024), mdesc(bh + bstep * k, blbo, bsbo), idesc, 1);
+  for (int k = 0; k < 4; k++) umma_ts(d, al + 8 * k, mdesc(bh + bstep * k, blbo, bsbo), idesc, 1);
 }
 
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
@@ -197,6 +198,31 @@ __device__ __forceinline__ void tmem_st32(uint32_t a, const float* v) {
       "f"(v[19]), "f"(v[20]), "f"(v[21]), "f"(v[22]), "f"(v[23]), "f"(v[24]), "f"(v[25]), "f"(v[26]), "f"(v[27]),
       "f"(v[28]), "f"(v[29]), "f"(v[30]), "f"(v[31])
       : "memory");
+}
+
+// Store 32 columns of 32-bit words (bf16 pairs) for this warp's lanes, waited for.
+__device__ __forceinline__ void tmem_st32u(uint32_t a, const uint32_t* v) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};\n"
+      "tcgen05.wait::st.sync.aligned;\n" ::"r"(a),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
+      "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]), "r"(v[16]), "r"(v[17]), "r"(v[18]),
+      "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]), "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]),
+      "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31])
+      : "memory");
+}
+
+// 64 floats as 32 bf16 pairs of high parts and 32 of low parts.
+__device__ __forceinline__ void split64(const float* x, uint32_t* hi, uint32_t* lo) {
+#pragma unroll
+  for (int i = 0; i < 32; i++) {
+    const __nv_bfloat162 a = __floats2bfloat162_rn(x[2 * i], x[2 * i + 1]);
+    const float2 af = __bfloat1622float2(a);
+    const __nv_bfloat162 b = __floats2bfloat162_rn(x[2 * i] - af.x, x[2 * i + 1] - af.y);
+    hi[i] = *reinterpret_cast<const uint32_t*>(&a);
+    lo[i] = *reinterpret_cast<const uint32_t*>(&b);
+  }
 }
 
 // Eight floats as 16 bytes of bf16 high parts and 16 bytes of low parts
@@ -307,8 +333,9 @@ __global__ void __launch_bounds__(320, 1)
   uint64_t* fin = s_done + 4;           // drain after a stop
   uint64_t* landed = fin + 1;           // [kBufs]: a tile's fp32 rows arrived (bulk copies)
   uint64_t* p_full = landed + kBufs;    // [2]: the 128 rows wrote P of tile j (P buffer j % 2)
-  uint32_t* tmem_word = reinterpret_cast<uint32_t*>(sm + kBars + 128);
-  volatile int* abort = reinterpret_cast<volatile int*>(sm + kBars + 132);
+  uint64_t* q_full = p_full + 2;        // the 128 rows wrote Q
+  uint32_t* tmem_word = reinterpret_cast<uint32_t*>(sm + kBars + 160);
+  volatile int* abort = reinterpret_cast<volatile int*>(sm + kBars + 164);
 
   const int s = blockIdx.x, i0 = blockIdx.y * TQ, h = blockIdx.z, t = threadIdx.x, warp = t >> 5;
   const long long pos = pos_ptr ? pos_ptr[0] : g.pos0;
@@ -354,6 +381,7 @@ __global__ void __launch_bounds__(320, 1)
       bar_init(&o_done[b], 1);
       bar_init(&p_full[b], 128);
     }
+    bar_init(q_full, 128);
     bar_init(fin, 1);
     *abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -366,41 +394,23 @@ __global__ void __launch_bounds__(320, 1)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
-  if (t < 256) {  // Q, split: thread → row t / 2, dims 32·(t % 2) .. + 31 (rows past m as zeros)
-    const int row = t >> 1, c0 = (t & 1) * 32;
-    const bool ok = i0 + row < g.m;
-    const float* src = q + (size_t)(i0 + row) * ldq + (size_t)h * TDH + c0;
-#pragma unroll
-    for (int c = 0; c < 32; c += 8) {
-      float4 a = make_float4(0.f, 0.f, 0.f, 0.f), b = a;
-      if (ok) {
-        a = *reinterpret_cast<const float4*>(src + c);
-        b = *reinterpret_cast<const float4*>(src + c + 4);
-      }
-      const float x[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
-      uint4 hi, lo;
-      split8(x, hi, lo);
-      st16(sm + kQh, cm_off(row, c0 + c), hi);
-      st16(sm + kQl, cm_off(row, c0 + c), lo);
-    }
-  }
   fence_async_smem();
   tc_before();
   __syncthreads();
   tc_after();
   const uint32_t tmem = *tmem_word;
-  const uint32_t tO = tmem + 128;
+  const uint32_t tO = tmem + kColO;
 
   if (warp == 9) {  // MMA issuer (thread 288)
     if (t == 288) {
-      const uint32_t qh = saddr(sm + kQh), ql = saddr(sm + kQl);
-      bool ok = true;
+      const uint32_t qh = tmem + kColQ, ql = tmem + kColQ + 32;
+      bool ok = tc_wait(q_full, 0, abort, g.err);
       for (int j = 0; j < 2 && j < ntiles && ok; j++) {  // the scores of the first two tiles
         ok = tc_wait(&kv_full[j], 0, abort, g.err);
         if (ok) {
           tc_after();
           const uint32_t kb = saddr(sm + kKV + j * kKVBuf);
-          umma3<false>(tmem + 64 * j, qh, ql, kb, kb + kHalf);
+          umma3t<false>(tmem + kColS + 64 * j, qh, ql, kb, kb + kHalf);
           umma_commit(&s_done[j]);
         }
       }
@@ -408,8 +418,8 @@ __global__ void __launch_bounds__(320, 1)
         const int sb = j & 1;
         if (!tc_wait(&p_full[sb], (j >> 1) & 1, abort, g.err)) break;
         tc_after();
-        const uint32_t kb = saddr(sm + kKV + b * kKVBuf), pa = saddr(sm + kP + sb * 2 * kTile);
-        umma3<true>(tO, pa, pa + kTile, kb + 2 * kHalf, kb + 3 * kHalf, j > 0);
+        const uint32_t kb = saddr(sm + kKV + b * kKVBuf), pa = tmem + kColP + 64 * sb;
+        umma3t<true>(tO, pa, pa + 32, kb + 2 * kHalf, kb + 3 * kHalf, j > 0);
         umma_commit(&o_done[sb]);
         umma_commit(&kv_empty[b]);
         // The scores of tile j + 2 into this score buffer (its rows have read it).
@@ -418,7 +428,7 @@ __global__ void __launch_bounds__(320, 1)
           if (!tc_wait(&kv_full[b2], ((j + 2) / kBufs) & 1, abort, g.err)) break;
           tc_after();
           const uint32_t kn = saddr(sm + kKV + b2 * kKVBuf);
-          umma3<false>(tmem + 64 * sb, qh, ql, kn, kn + kHalf);
+          umma3t<false>(tmem + kColS + 64 * sb, qh, ql, kn, kn + kHalf);
           umma_commit(&s_done[sb]);
         }
         b = b + 1 == kBufs ? 0 : b + 1;
@@ -466,6 +476,21 @@ __global__ void __launch_bounds__(320, 1)
     // are taken against (within kLazy of the running max), l their sum.
     float mu = -INFINITY, l = 0.0f;
     const uint32_t lanes = tmem + ((uint32_t)(warp * 32) << 16);
+    {  // this row of Q, split, into tensor memory (rows past m as zeros)
+      float x[TDH];
+      const float* src = q + (size_t)i * ldq + (size_t)h * TDH;
+#pragma unroll
+      for (int c = 0; c < TDH; c += 4) {
+        const float4 v = i < g.m ? *reinterpret_cast<const float4*>(src + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+        x[c] = v.x, x[c + 1] = v.y, x[c + 2] = v.z, x[c + 3] = v.w;
+      }
+      uint32_t hi[32], lo[32];
+      split64(x, hi, lo);
+      tmem_st32u(lanes + kColQ, hi);
+      tmem_st32u(lanes + kColQ + 32, lo);
+      tc_before();
+      bar_arrive(q_full);
+    }
     const float k2 = g.scale * kLog2e;  // scores in log2 units: exp(x) = exp2(x · log2 e)
     for (int j = 0; j < ntiles; j++) {
       const long long base = start + (long long)j * TK;
@@ -477,8 +502,8 @@ __global__ void __launch_bounds__(320, 1)
       if (!__all_sync(0xffffffffu, ok)) break;
       tc_after();
       float sc[TK];
-      tmem_ld32(lanes + 64 * sb, sc);
-      tmem_ld32(lanes + 64 * sb + 32, sc + 32);
+      tmem_ld32(lanes + kColS + 64 * sb, sc);
+      tmem_ld32(lanes + kColS + 64 * sb + 32, sc + 32);
       // This row's visible columns of the tile: [c0, c1).
       const long long lo_p = qlo > base ? qlo : base, hi_p = min(min(qhi, end), base + TK);
       const long long d0 = lo_p - base;
@@ -513,10 +538,10 @@ __global__ void __launch_bounds__(320, 1)
           float ov[32];
 #pragma unroll
           for (int hh = 0; hh < 2; hh++) {
-            tmem_ld32(lanes + 128 + 32 * hh, ov);
+            tmem_ld32(lanes + kColO + 32 * hh, ov);
 #pragma unroll
             for (int e = 0; e < 32; e++) ov[e] *= f;
-            tmem_st32(lanes + 128 + 32 * hh, ov);
+            tmem_st32(lanes + kColO + 32 * hh, ov);
           }
         }
       }
@@ -528,21 +553,18 @@ __global__ void __launch_bounds__(320, 1)
         rq[c & 3] += sc[c];
       }
       l = l * f + ((rq[0] + rq[1]) + (rq[2] + rq[3]));
-      char* ph = sm + kP + sb * 2 * kTile;
-#pragma unroll
-      for (int c = 0; c < TK; c += 8) {
-        uint4 hi, lo;
-        split8(sc + c, hi, lo);
-        st16(ph, cm_off(t, c), hi);
-        st16(ph + kTile, cm_off(t, c), lo);
+      {
+        uint32_t hi[32], lo[32];
+        split64(sc, hi, lo);
+        tmem_st32u(lanes + kColP + 64 * sb, hi);
+        tmem_st32u(lanes + kColP + 64 * sb + 32, lo);
       }
-      fence_async_smem();
       tc_before();
       bar_arrive(&p_full[sb]);
     }
     // The output: wait for the last two tiles' P·V (each barrier is at most
     // one phase short of them), read this row, and stage it in shared memory
-    // (the P buffers, free now) so the partial rows go out coalesced.
+    // (the tile buffers, free now) so the partial rows go out coalesced.
     bool ok = true;
     for (int j = ntiles - 2; j < ntiles; j++)
       if (j >= 0 && ok) ok = tc_wait(&o_done[j & 1], (j >> 1) & 1, abort, g.err);
@@ -550,13 +572,13 @@ __global__ void __launch_bounds__(320, 1)
     float o[TDH];
     if (__all_sync(0xffffffffu, ok)) {
       tc_after();
-      tmem_ld32(lanes + 128, o);
-      tmem_ld32(lanes + 160, o + 32);
+      tmem_ld32(lanes + kColO, o);
+      tmem_ld32(lanes + kColO + 32, o + 32);
     } else {
 #pragma unroll
       for (int e = 0; e < TDH; e++) o[e] = 0.0f;
     }
-    float2* row = reinterpret_cast<float2*>(sm + kP + (size_t)t * (TDH + 2) * sizeof(float));
+    float2* row = reinterpret_cast<float2*>(sm + kKV + (size_t)t * (TDH + 2) * sizeof(float));
 #pragma unroll
     for (int e = 0; e < TDH / 2; e++) row[e] = make_float2(o[2 * e], o[2 * e + 1]);
     row[TDH / 2] = make_float2(mu == -INFINITY ? mu : mu / kLog2e, l);  // max back to natural-log units
@@ -564,7 +586,7 @@ __global__ void __launch_bounds__(320, 1)
     asm volatile("bar.sync 1, 128;" ::: "memory");
     const int lane = t & 31;
     for (int r = warp; r < TQ && i0 + r < g.m; r += 4) {
-      const float* src = reinterpret_cast<const float*>(sm + kP + (size_t)r * (TDH + 2) * sizeof(float));
+      const float* src = reinterpret_cast<const float*>(sm + kKV + (size_t)r * (TDH + 2) * sizeof(float));
       float* out = part + (((size_t)s * g.m + i0 + r) * g.heads + h) * (TDH + 2);
       out[lane] = src[lane];
       out[32 + lane] = src[32 + lane];
