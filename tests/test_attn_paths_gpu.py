@@ -1,7 +1,8 @@
 """Both slice passes for prefill-sized attention (head size 64, m > 8) against
 the oracle: the tensor-core pass (the default) runs in this process through
-test_ops_gpu.py; the FP32 flash-tile pass, which SLM_ATTN_TC=0 selects when
-the library loads, runs here in a child process on the same cases."""
+test_ops_gpu.py; the FP32 flash-tile pass, which SLM_ATTN_TC=0 selects (read
+once, at the first attention call), runs here in a child process on the same
+kinds of cases."""
 import os
 import subprocess
 import sys
