@@ -27,13 +27,10 @@
 //    back) only in the rare tiles where a row's max grows past that.
 // Q and P are the A operands of their MMAs straight from tensor memory (one
 // row per lane, two bf16 of K per 32-bit column): the tensor core reads only
-// K and V from shared memory.  Shared tiles use the no-swizzle core-matrix
-// layout: element (r, c) of an [R][64] bf16 tile sits at (r % 8)·16 +
-// (r / 8)·1024 + (c / 8)·128 + (c % 8)·2 bytes (core matrices of 8 rows × 16
-// bytes).  K is the K-major B operand of QKᵀ in it (leading byte offset 128
-// along K, stride byte offset 1024 along N); V, stored the same way as
-// [key][dh], is the MN-major B operand of P·V (K = key: 1024 bytes between
-// 8-key groups; N = dh: 128 bytes between 8-dim groups).
+// K and V from shared memory.  K/V tiles are [key][dh] bf16 rows of 128 bytes
+// in the 128-byte swizzled layout (8-key atoms of 1024 bytes, the 16-byte
+// chunk c of key r at chunk c ^ (r % 8)): K is the K-major B operand of QKᵀ,
+// V the MN-major B operand of P·V (K = key), with no transposition.
 // Partials have the layout of the other slice passes (acc[64], max, sum per
 // (slice, query, head)) and are merged by the same combine.
 //
@@ -82,16 +79,18 @@ __device__ __forceinline__ unsigned long long tc_now() {
   return t;
 }
 
-// Byte offset of element (r, c) of a K-major [R][64] bf16 tile (c a multiple of 8).
-__device__ __forceinline__ uint32_t cm_off(int r, int c) {
-  return (uint32_t)((r & 7) * 16 + (r >> 3) * 1024 + (c >> 3) * 128);
+// Byte offset of the 16-byte chunk c (elements 8c .. 8c + 7) of row r of a
+// [64][64] bf16 tile in the 128-byte swizzled layout: rows of 128 bytes, 8-row
+// atoms of 1024 bytes, chunk c of row r stored at chunk c ^ (r % 8).
+__device__ __forceinline__ uint32_t sw_off(int r, int c) {
+  return (uint32_t)((r >> 3) * 1024 + (r & 7) * 128 + ((c ^ (r & 7)) << 4));
 }
 
-// Shared-memory matrix descriptor (no swizzle): start address, leading and
-// stride byte offsets, descriptor version 1.
+// Shared-memory matrix descriptor, 128-byte swizzle: start address, leading
+// and stride byte offsets, descriptor version 1, layout type 2.
 __device__ __forceinline__ uint64_t mdesc(uint32_t a, uint32_t lbo, uint32_t sbo) {
   return (uint64_t)((a >> 4) & 0x3FFFu) | ((uint64_t)(lbo >> 4) << 16) | ((uint64_t)(sbo >> 4) << 32) |
-         (1ull << 46);
+         (1ull << 46) | (2ull << 61);
 }
 
 // An MMA with A in tensor memory (one row per lane, two bf16 of K per column).
@@ -103,13 +102,15 @@ __device__ __forceinline__ void umma_ts(uint32_t d, uint32_t a, uint64_t b, uint
 }
 
 // d (+)= ah·bh + ah·bl + al·bh over K = 64 in four k-steps of 16, A in tensor
-// memory at columns ah, al (8 columns a step); B K-major (QKᵀ: 256 bytes a
-// step) or MN-major (P·V: two 8-key groups, 2048 bytes, a step).
+// memory at columns ah, al (8 columns a step); B from a swizzled [key][dh]
+// tile: K-major for QKᵀ (a step is 32 bytes along the 128-byte rows; 8-key
+// atoms 1024 bytes apart) or MN-major for P·V (a step is two 8-key atoms,
+// 2048 bytes; the 64 dims are one atom wide, so the leading offset is unused).
 template <bool kBmn>
 __device__ __forceinline__ void umma3t(uint32_t d, uint32_t ah, uint32_t al, uint32_t bh, uint32_t bl,
                                        bool accumulate = false) {
   constexpr uint32_t idesc = kBmn ? kIdescO : kIdescS;
-  constexpr uint32_t bstep = kBmn ? 2048 : 256, blbo = kBmn ? 1024 : 128, bsbo = kBmn ? 128 : 1024;
+  constexpr uint32_t bstep = kBmn ? 2048 : 32, blbo = kBmn ? 8192 : 16, bsbo = 1024;
 #pragma unroll
   for (int k = 0; k < 4; k++) umma_ts(d, ah + 8 * k, mdesc(bh + bstep * k, blbo, bsbo), idesc, accumulate || k > 0);
 #pragma unroll
@@ -278,16 +279,16 @@ __device__ __forceinline__ void fetch_tile(char* buf, uint64_t* bar, const float
 
 // Split a landed tile in place into the MMA layout (Kh, Kl, Vh, Vl at 0, 8,
 // 16, 24 KB; rows at or past `end` as zeros).  Loader thread lt (0..127)
-// takes, for e = lt + 128 i (i < 4), key 8·((e / 8) % 8) + e % 8 and dims
-// 8·((e / 64 + e) % 8) .. + 7 of K and of V: reads in the fp32 rows, writes in
-// the core matrices without bank conflicts; every loader reads before any
-// writes (barrier 2).  False when the CTA has stopped.
+// takes, for e = lt + 128 i (i < 4), key e / 8 and dims 8·(e % 8) .. + 7 of K
+// and of V: eight lanes read one fp32 row and write the eight swizzled chunks
+// of its bf16 rows, both without bank conflicts; every loader reads before
+// any writes (barrier 2).  False when the CTA has stopped.
 __device__ __forceinline__ bool split_tile(char* buf, long long base, long long end, int lt, bool ok,
                                            volatile int* abort) {
   float4 ka[4][2], va[4][2];
 #pragma unroll
   for (int i = 0; i < 4; i++) {
-    const int e = lt + 128 * i, key = 8 * ((e >> 3) & 7) + (e & 7), c = 8 * (((e >> 6) + e) & 7);
+    const int e = lt + 128 * i, key = e >> 3, c = 8 * (e & 7);
     if (ok && base + key < end) {
       const float4* ks = reinterpret_cast<const float4*>(buf + (size_t)key * TDH * sizeof(float) + c * 4);
       const float4* vs = reinterpret_cast<const float4*>(buf + 2 * kHalf + (size_t)key * TDH * sizeof(float) + c * 4);
@@ -303,8 +304,8 @@ __device__ __forceinline__ bool split_tile(char* buf, long long base, long long 
   if (warps4_any<2>(!ok || *abort)) return false;
 #pragma unroll
   for (int i = 0; i < 4; i++) {
-    const int e = lt + 128 * i, key = 8 * ((e >> 3) & 7) + (e & 7), c = 8 * (((e >> 6) + e) & 7);
-    const uint32_t off = cm_off(key, c);
+    const int e = lt + 128 * i, key = e >> 3;
+    const uint32_t off = sw_off(key, e & 7);
     uint4 hi, lo;
     const float xk[8] = {ka[i][0].x, ka[i][0].y, ka[i][0].z, ka[i][0].w,
                          ka[i][1].x, ka[i][1].y, ka[i][1].z, ka[i][1].w};
