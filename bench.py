@@ -545,6 +545,29 @@ def run_b200(args, rank: int, world: int, local: int) -> dict | None:
         b.record(stream)
         torch.cuda.synchronize(dev)
         attn_us = a.elapsed_time(b) * 1000.0 / 36
+
+        # Prefill attention on its own (the tensor-core pass k_attn_tc and the
+        # slice merge k_attn_combine64): a 256-query chunk at positions
+        # 3840-4095 over the same rings, every query seeing all positions up to
+        # its own; the six rings rotate, so each call streams its K/V from HBM.
+        qp, yp = ops.upload(rng.standard_normal(256 * H * dh, dtype=np.float32)), ops.zeros(256 * H * dh)
+
+        def attend_chunk(i):
+            ops.attend(yp, sa, qp, caches[i % 6][0], caches[i % 6][1], pos=W - 256, m=256, reach=W, gap=0, cap=cap,
+                       heads=H, key_heads=H, dh=dh, scale=1.0 / math.sqrt(dh))
+
+        for i in range(6):
+            attend_chunk(i)
+        a, b = events()
+        queue_behind_sleep(torch, stream)
+        a.record(stream)
+        for i in range(24):
+            attend_chunk(i)
+        b.record(stream)
+        torch.cuda.synchronize(dev)
+        pattn_us = a.elapsed_time(b) * 1000.0 / 24
+        qp.close()
+        yp.close()
         for kb, vb in caches:
             kb.close()
             vb.close()
@@ -720,7 +743,7 @@ def run_b200(args, rank: int, world: int, local: int) -> dict | None:
     step_kernels = se.step_kernels
     mega = se.mega
     res = {"dec_ms": dec_ms, "e2e_s": e2e_s, "prefill_ms": prefill_ms, "prefill_host_s": prefill_host_s,
-           "gemv_us": gemv_us, "attn_us": attn_us, "attn_phase": attn_phase, "clocks": clocks.summary(), "extra": extra, "step_kernels": step_kernels, "mega": mega, "load_s": load_s,
+           "gemv_us": gemv_us, "attn_us": attn_us, "pattn_us": pattn_us, "attn_phase": attn_phase, "clocks": clocks.summary(), "extra": extra, "step_kernels": step_kernels, "mega": mega, "load_s": load_s,
            "device": ctx.name, "state_bytes": se.state_bytes()}
     res["dec_ms"], res["e2e_s"], res["prefill_ms"] = max_over_ranks([dec_ms, e2e_s, prefill_ms], dist, dev)
     se.close()
@@ -866,6 +889,23 @@ def main():
                        "how": "slm_model_load: safetensors read, f32 upload through pinned double buffers, "
                               "derived layouts (bf16x3 parts, transposed down, per-head o) on the device"},
     }
+    if res.get("pattn_us"):
+        # Algorithmic work of the chunk: QKᵀ and P·V over every visible
+        # position, 2 flops per multiply-add; the pass runs each fp32 product
+        # as three bf16 products, so its tensor work is three times that.
+        span = sum(p + 1 for p in range(cfg["window"] - 256, cfg["window"]))
+        fl = 4.0 * span * dh * H
+        bf16_peak = peaks.get("bf16_tflops") or 1590.0
+        ach = 3 * fl / (res["pattn_us"] * 1e-6) / 1e12
+        line["roofline"]["prefill_attention"] = {
+            "kernel": "k_attn_tc + k_attn_combine64 (256 queries at positions 3840-4095, 12 heads, each over all "
+                      "positions up to its own: 6 slices x 2 query tiles x 12 heads)",
+            "bound": "tensor", "achieved": ach, "peak": bf16_peak, "unit": "TFLOP/s (bf16 products)",
+            "frac": ach / bf16_peak, "fp32_tflops": fl / (res["pattn_us"] * 1e-6) / 1e12,
+            "us_per_call": res["pattn_us"], "flops_fp32_per_call": fl,
+            "peak_source": "measured" if peaks.get("bf16_tflops") else "fallback",
+            "how": "24 calls (two launches each) queued behind a device sleep, CUDA events around them; six "
+                   "K/V rings rotate (160 MB)"}
     if res.get("attn_phase"):
         ap = res["attn_phase"]
         line["roofline"]["attention_in_step"] = {
